@@ -1,0 +1,235 @@
+/*
+ * osm_b200.h -- C ABI of the B200 (sm_100a) routed-MoE sublayer.
+ *
+ * Plain pointers, sizes and int status codes; no C++ or torch types.  Every
+ * entry point names the interface of the reference (ingeniusvictor/
+ * orbi-streammoe, paths inside that project) that it replaces.  The C++
+ * drop-in layer (orbi-streammoe_b200/host) implements the reference's own
+ * class and function names on top of these calls.
+ *
+ * Conventions
+ *  - Return 0 on success, a negative OSM_E* code on failure; the text of the
+ *    last failure of a context is osm_last_error(ctx).  No C++ exception
+ *    crosses this boundary (the reference's entry points are noexcept and
+ *    report `executed=false` + `diagnostic`, e.g. src/model/routed_moe.cpp).
+ *  - Pointers named *_dev are device pointers; *_host are host pointers.
+ *  - Work is enqueued on the context's stream.  Functions documented as
+ *    "synchronous" wait for the stream before returning, like the reference's
+ *    fence waits (src/backend/vulkan_q4_gemv.cpp:1645-1657).
+ *  - Geometry: Q4 = MLX affine 4-bit, eight nibbles per uint32 LSB first,
+ *    group 64 along the input dimension, BF16 scale and bias
+ *    (src/cpu/reference_ops.cpp:11-67, shaders/q4_gemv.comp:32-63).
+ */
+#ifndef OSM_B200_H
+#define OSM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OSM_OK 0
+#define OSM_EINVAL (-1)   /* invalid argument (reference: std::invalid_argument) */
+#define OSM_ERUNTIME (-2) /* runtime failure (reference: std::runtime_error) */
+#define OSM_ECUDA (-3)    /* a CUDA call failed */
+#define OSM_ENOMEM (-4)   /* device or pinned allocation failed */
+#define OSM_ENOTRES (-5)  /* a routed expert is not resident in the slab */
+#define OSM_ETIMEOUT (-6) /* a bounded wait gave up */
+
+/* Flags for osm_moe_forward / osm_moe_route / osm_rms_norm. */
+#define OSM_ROUTE_EXACT 0x1u      /* route every token on the exact path */
+#define OSM_RMSNORM_EXACT 0x2u    /* sequential RMSNorm sum (bit-exact)   */
+#define OSM_ADD_RESIDUAL 0x4u     /* out = residual + MoE(...)            */
+
+typedef struct osm_context osm_context;
+typedef struct osm_layer osm_layer;
+typedef struct osm_slab osm_slab;
+
+/* Byte offsets of the nine qpack sections inside one expert slot
+ * (gate_proj/up_proj/down_proj . weight/scales/biases; the section table of
+ * the reference's layout.json, src/container/qpack.cpp:67-97). */
+typedef struct {
+  uint32_t hidden;       /* H: input of gate/up, output of down        */
+  uint32_t inter;        /* I: moe_intermediate_size                   */
+  uint32_t group;        /* quantisation group (64)                    */
+  uint32_t reserved;
+  uint64_t gate_w, gate_s, gate_b;
+  uint64_t up_w, up_s, up_b;
+  uint64_t down_w, down_s, down_b;
+  uint64_t stride;       /* bytes per slot                              */
+} osm_expert_layout;
+
+/* Fill `out` with the packed back-to-back layout (U32 weights, BF16
+ * metadata) used by the reference's fixtures and the synthetic configs. */
+int osm_expert_layout_packed(uint32_t hidden, uint32_t inter, uint32_t group,
+                             osm_expert_layout* out);
+
+/* ---- context: replaces VulkanComputeContext
+ *      (include/orbi/streammoe/backend/vulkan_compute_context.hpp:19-49) ---- */
+int osm_context_create(int device, uint32_t max_tokens, osm_context** out);
+int osm_context_destroy(osm_context* ctx);
+const char* osm_last_error(const osm_context* ctx);
+int osm_context_device(const osm_context* ctx);
+void* osm_context_stream(const osm_context* ctx); /* cudaStream_t */
+/* Use a caller-owned stream (NULL restores the context's own stream). */
+int osm_context_set_stream(osm_context* ctx, void* cuda_stream);
+int osm_context_synchronize(osm_context* ctx);
+/* Device status word accumulated by kernels since the last call (bit 0
+ * non-finite router input, bit 1 invalid softmax/mass, bit 2 non-resident
+ * expert, bit 3 bad slot); the count of tokens routed on the exact path. */
+int osm_context_status(osm_context* ctx, uint32_t* status,
+                       uint64_t* exact_tokens);
+
+/* ---- buffers: replaces VulkanFloatBuffer
+ *      (include/orbi/streammoe/backend/vulkan_float_buffer.hpp:23-58) ---- */
+int osm_device_alloc(osm_context* ctx, size_t bytes, void** dev);
+int osm_device_free(osm_context* ctx, void* dev);
+int osm_upload(osm_context* ctx, void* dev, const void* host, size_t bytes);
+int osm_download(osm_context* ctx, void* host, const void* dev, size_t bytes);
+int osm_host_alloc_pinned(size_t bytes, void** host);
+int osm_host_free_pinned(void* host);
+
+/* ---- element-wise ops (each replaces one Vulkan kernel) ---- */
+
+/* run_vulkan_q4_dequant (src/backend/vulkan_q4_dequant.cpp:270,
+ * shaders/q4_dequant.comp): out[r][c] = scale*q + bias, bit-exact with
+ * cpu::dequantize_affine_rows (separate multiply and add, no FMA). */
+int osm_q4_dequant(osm_context* ctx, const uint32_t* packed_dev,
+                   const uint16_t* scales_bf16_dev,
+                   const uint16_t* biases_bf16_dev, uint32_t rows,
+                   uint32_t in_dim, uint32_t group, float* out_dev);
+
+/* run_vulkan_q4_gemv_preloaded (include/orbi/streammoe/backend/
+ * vulkan_q4_gemv.hpp:53-57): y[t][r] = sum_c w[r][c] * x[t][c] for `tokens`
+ * input vectors (batched; the reference is tokens == 1). */
+int osm_q4_gemv(osm_context* ctx, const uint32_t* packed_dev,
+                const uint16_t* scales_bf16_dev,
+                const uint16_t* biases_bf16_dev, uint32_t out_dim,
+                uint32_t in_dim, uint32_t group, const float* x_dev,
+                uint32_t tokens, float* y_dev);
+
+/* run_vulkan_swiglu_buffers (include/orbi/streammoe/backend/
+ * vulkan_swiglu.hpp:26-30): out = silu(gate) * up. */
+int osm_swiglu(osm_context* ctx, const float* gate_dev, const float* up_dev,
+               float* out_dev, size_t count);
+
+/* run_vulkan_weighted_accumulate (include/orbi/streammoe/backend/
+ * vulkan_weighted_accumulate.hpp:12-16): acc += weight * src. */
+int osm_weighted_accumulate(osm_context* ctx, const float* src_dev,
+                            float weight, float* acc_dev, size_t count);
+
+/* run_vulkan_rms_norm (include/orbi/streammoe/backend/vulkan_rmsnorm.hpp:
+ * 25-31): in place, rows x dim, weight_dev may be NULL (unit weight).
+ * flags & OSM_RMSNORM_EXACT sums squares sequentially (bit-exact with
+ * cpu::rms_norm_inplace); otherwise a block reduction (within 1e-6). */
+int osm_rms_norm(osm_context* ctx, float* values_dev, uint32_t rows,
+                 uint32_t dim, const float* weight_dev, float eps,
+                 uint32_t flags);
+
+/* VulkanResidentExpert::run_from_buffer (include/orbi/streammoe/backend/
+ * vulkan_resident_expert.hpp:64-66): one expert's gate/up -> SwiGLU -> down
+ * on `tokens` inputs; slot_dev points at one expert slot of `layout`. */
+int osm_expert_forward(osm_context* ctx, const void* slot_dev,
+                       const osm_expert_layout* layout, const float* x_dev,
+                       uint32_t tokens, float* out_dev);
+
+/* ---- expert slab: the HBM side of VulkanResidentExpertCache
+ *      (include/orbi/streammoe/backend/vulkan_resident_expert_cache.hpp:
+ *      27-83); the policy lives in the host layer ---- */
+int osm_slab_create(osm_context* ctx, const osm_expert_layout* layout,
+                    uint32_t slots, osm_slab** out);
+int osm_slab_destroy(osm_slab* slab);
+uint32_t osm_slab_slots(const osm_slab* slab);
+void* osm_slab_slot_ptr(const osm_slab* slab, uint32_t slot);
+/* Copy one slot's bytes from (ideally pinned) host memory on the slab's side
+ * stream; the copy is ordered before the next kernel on the context stream
+ * that reads the slab (an event is recorded and waited on). */
+int osm_slab_fill_async(osm_slab* slab, uint32_t slot, const void* host_src);
+/* Block until every fill issued so far has landed, with a time limit. */
+int osm_slab_fill_wait(osm_slab* slab, uint32_t timeout_ms);
+/* Bytes copied host->device by fills since creation. */
+uint64_t osm_slab_h2d_bytes(const osm_slab* slab);
+
+/* ---- one MoE layer: the dense state QwenCheckpointSparseMoeLayer keeps
+ *      (src/model/checkpoint_sparse_moe.cpp:112-220): router, shared expert
+ *      and its scalar gate, plus the table expert -> slab slot ---- */
+typedef struct {
+  uint32_t hidden;          /* H                                         */
+  uint32_t experts;         /* E (<= 1024)                               */
+  uint32_t top_k;           /* k (<= 32)                                 */
+  uint32_t norm_topk_prob;  /* renormalise the selected weights          */
+  const float* router_weight_host;   /* [E][H] fp32, row-major; values
+                                        must be bf16-representable       */
+  const float* logit_bias_host;      /* [E] or NULL                      */
+  const void* shared_slot_host;      /* one slot of shared_layout or NULL */
+  osm_expert_layout shared_layout;   /* ignored without a shared expert  */
+  const float* shared_gate_host;     /* [H] scalar gate (fp32)           */
+  const float* norm_weight_host;     /* [H] post-attention norm or NULL  */
+  float norm_eps;
+} osm_layer_desc;
+
+int osm_layer_create(osm_context* ctx, const osm_layer_desc* desc,
+                     osm_layer** out);
+int osm_layer_destroy(osm_layer* layer);
+/* Bind routed experts to slab slots: slot_of_expert[e] = slot, or -1 when
+ * expert e is not resident (routing to it then fails with OSM_ENOTRES). */
+int osm_layer_bind_slab(osm_layer* layer, osm_slab* slab,
+                        const int32_t* slot_of_expert_host);
+/* Rebind a single expert (cache fill / eviction). */
+int osm_layer_set_slot(osm_layer* layer, uint32_t expert, int32_t slot);
+
+/* route_qwen_top_k_cpu (include/orbi/streammoe/model/qwen_router.hpp:42-45):
+ * logits = W x (+ bias), softmax, top-k, renormalise, for `tokens` rows of
+ * x_dev.  ids_dev [tokens][k] u32, weights_dev [tokens][k], mass_dev
+ * [tokens] (selected probability mass); any output may be NULL. */
+int osm_moe_route(osm_layer* layer, const float* x_dev, uint32_t tokens,
+                  uint32_t* ids_dev, float* weights_dev, float* mass_dev,
+                  uint32_t flags);
+
+/* run_qwen_sparse_moe_vulkan_accum (include/orbi/streammoe/model/
+ * routed_moe.hpp:58-65), batched: route, run the picked experts and the
+ * shared expert, combine in pick order.  Every picked expert must be bound
+ * to a slab slot.  shared_gate_dev [tokens] receives sigmoid(g . x) (or 0
+ * without a shared expert).  With OSM_ADD_RESIDUAL, residual_dev is added. */
+int osm_moe_forward(osm_layer* layer, const float* x_dev, uint32_t tokens,
+                    float* out_dev, uint32_t* ids_dev, float* weights_dev,
+                    float* mass_dev, float* shared_gate_dev,
+                    const float* residual_dev, uint32_t flags);
+
+/* Expert half of osm_moe_forward for a routing already in device memory
+ * (after osm_moe_route and host-side cache fills). */
+int osm_moe_experts(osm_layer* layer, const float* x_dev, uint32_t tokens,
+                    const uint32_t* ids_dev, const float* weights_dev,
+                    float* out_dev, float* shared_gate_dev,
+                    const float* residual_dev, uint32_t flags);
+
+/* QwenCheckpointMoeSublayer::run (include/orbi/streammoe/model/
+ * checkpoint_moe_sublayer.hpp:55-58): normalized = RMSNorm(residual),
+ * out = residual + MoE(normalized).  normalized_dev may be NULL. */
+int osm_moe_sublayer_forward(osm_layer* layer, const float* residual_dev,
+                             uint32_t tokens, float* out_dev,
+                             float* normalized_dev, uint32_t* ids_dev,
+                             float* weights_dev, float* mass_dev,
+                             float* shared_gate_dev, uint32_t flags);
+
+/* Number of kernels this library launched on `ctx` since creation. */
+uint64_t osm_context_launches(const osm_context* ctx);
+
+/* ---- synthetic data (seeded; identical stream on host and device) ---- */
+/* N(0, sigma) fp32 values of stream (seed, tensor), elements
+ * [first, first + n), into device memory. */
+int osm_gen_normal(osm_context* ctx, uint64_t seed, uint64_t tensor,
+                   float sigma, float* out_dev, size_t n, size_t first);
+/* Generate `count` expert slots of `layout` into consecutive slab slots
+ * starting at first_slot: gate/up/down ~ N(0, sigma) from tensors
+ * tensor_base + 3*i + {0,1,2}, quantised with the reference quantiser
+ * (src/conversion/single_expert_pilot.cpp:276-346), bf16 (RNE) metadata. */
+int osm_gen_expert_slots(osm_slab* slab, uint64_t seed, uint64_t tensor_base,
+                         float sigma, uint32_t first_slot, uint32_t count);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,936 @@
+// osm_capi.cu -- the extern "C" boundary (include/osm_b200.h) over the sm_100a
+// kernels: contexts with their stream and scratch, the HBM expert slab, MoE
+// layers, and every entry point.  No exception crosses the boundary.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/osm_b200.h"
+#include "osm_common.cuh"
+#include "osm_kernels.cuh"
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device scratch of one context, carved from a single allocation.  Sized for
+// (tokens T, hidden H, experts E, top-k k, intermediate I, projection K).
+struct Scratch {
+  size_t T = 0, H = 0, E = 0, k = 0, I = 0, K = 0;
+  void* base = nullptr;
+  size_t bytes = 0;
+  float* logits = nullptr;
+  float* bounds = nullptr;
+  uint32_t* ids = nullptr;
+  float* weights = nullptr;
+  float* mass = nullptr;
+  float* sgate = nullptr;
+  uint4* xfrag = nullptr;
+  float* xfsum8 = nullptr;
+  unsigned int* ticket = nullptr;
+  int* counts = nullptr;
+  int* n_active = nullptr;
+  int* act_kind = nullptr;
+  const uint8_t** act_ptr = nullptr;
+  int* act_off = nullptr;
+  int* act_cnt = nullptr;
+  int* pair_tok = nullptr;
+  int* pair_pick = nullptr;
+  int* cursor = nullptr;
+  int* out_row = nullptr;
+  uint4* hfrag = nullptr;
+  float* hfsum8 = nullptr;
+  float* partial = nullptr;
+  float* normalized = nullptr;
+  uint32_t* status = nullptr;
+  unsigned long long* exact_count = nullptr;
+};
+
+}  // namespace
+
+struct osm_context {
+  int device = 0;
+  uint32_t max_tokens = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  uint64_t launches = 0;
+  Scratch sc;
+};
+
+struct osm_slab {
+  osm_context* ctx = nullptr;
+  osm_expert_layout layout{};
+  uint32_t slots = 0;
+  uint8_t* base = nullptr;
+  cudaStream_t side = nullptr;
+  cudaEvent_t ev = nullptr;
+  uint64_t h2d_bytes = 0;
+};
+
+struct osm_layer {
+  osm_context* ctx = nullptr;
+  osm::RouterGeom g{};
+  uint32_t norm = 0;
+  void* wp = nullptr;          // permuted router
+  float* bias = nullptr;
+  float* sgate_w = nullptr;
+  uint8_t* shared_slot = nullptr;
+  osm_expert_layout shared_layout{};
+  float* norm_w = nullptr;
+  float norm_eps = 1e-6f;
+  int* slot_of = nullptr;
+  std::vector<int32_t> slot_host;
+  osm_slab* slab = nullptr;
+};
+
+namespace {
+
+int fail(osm_context* ctx, int code, const std::string& msg) {
+  if (ctx) ctx->err = msg;
+  return code;
+}
+
+int cuda_fail(osm_context* ctx, cudaError_t e, const char* what) {
+  return fail(ctx, OSM_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define OSM_CUDA(ctx, call)                                   \
+  do {                                                        \
+    cudaError_t e_ = (call);                                  \
+    if (e_ != cudaSuccess) return cuda_fail((ctx), e_, #call); \
+  } while (0)
+
+int check_launch(osm_context* ctx, const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  return OSM_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Grow the scratch to cover the request (no shrink).
+int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, size_t I,
+                   size_t K) {
+  Scratch& s = ctx->sc;
+  T = std::max<size_t>(T, 1);
+  if (s.base && T <= s.T && H <= s.H && E <= s.E && k <= s.k && I <= s.I && K <= s.K)
+    return OSM_OK;
+  T = std::max(T, s.T);
+  H = std::max(H, s.H);
+  E = std::max(E, s.E);
+  k = std::max(k, s.k);
+  I = std::max(I, s.I);
+  K = std::max(K, s.K);
+  const size_t kp1 = k + 1;
+  const size_t P = T * kp1;
+  const size_t Kx = std::max(H, K);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, kAlign);
+    return o;
+  };
+  const size_t o_logits = take(T * E * 4), o_bounds = take(T * E * 4);
+  const size_t o_ids = take(T * k * 4), o_w = take(T * k * 4), o_mass = take(T * 4);
+  const size_t o_sg = take(T * 4);
+  const size_t o_xf = take(T * (Kx / 8) * 32), o_xs = take(T * (Kx / 8) * 4);
+  const size_t o_ticket = take(4), o_counts = take((E + 1) * 4), o_nact = take(4);
+  const size_t o_akind = take((E + 1) * 4), o_aptr = take((E + 1) * 8);
+  const size_t o_aoff = take((E + 1) * 4), o_acnt = take((E + 1) * 4);
+  const size_t o_ptok = take(P * 4), o_ppick = take(P * 4), o_cursor = take((E + 1) * 4);
+  const size_t o_orow = take(P * 4);
+  const size_t o_hf = take(P * (I / 8) * 32), o_hs = take(P * (I / 8) * 4);
+  const size_t o_part = take(P * H * 4), o_norm = take(T * H * 4);
+  const size_t o_status = take(4), o_exact = take(8);
+  void* base = nullptr;
+  cudaError_t e = cudaMalloc(&base, off);
+  if (e != cudaSuccess) return fail(ctx, OSM_ENOMEM, "scratch allocation failed");
+  // Keep status / exact counters across growth.
+  uint32_t st = 0;
+  unsigned long long ex = 0;
+  if (s.base) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaMemcpy(&st, s.status, 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(&ex, s.exact_count, 8, cudaMemcpyDeviceToHost);
+    cudaFree(s.base);
+  }
+  cudaMemset(base, 0, off);
+  char* b = static_cast<char*>(base);
+  s.base = base;
+  s.bytes = off;
+  s.T = T; s.H = H; s.E = E; s.k = k; s.I = I; s.K = K;
+  s.logits = reinterpret_cast<float*>(b + o_logits);
+  s.bounds = reinterpret_cast<float*>(b + o_bounds);
+  s.ids = reinterpret_cast<uint32_t*>(b + o_ids);
+  s.weights = reinterpret_cast<float*>(b + o_w);
+  s.mass = reinterpret_cast<float*>(b + o_mass);
+  s.sgate = reinterpret_cast<float*>(b + o_sg);
+  s.xfrag = reinterpret_cast<uint4*>(b + o_xf);
+  s.xfsum8 = reinterpret_cast<float*>(b + o_xs);
+  s.ticket = reinterpret_cast<unsigned int*>(b + o_ticket);
+  s.counts = reinterpret_cast<int*>(b + o_counts);
+  s.n_active = reinterpret_cast<int*>(b + o_nact);
+  s.act_kind = reinterpret_cast<int*>(b + o_akind);
+  s.act_ptr = reinterpret_cast<const uint8_t**>(b + o_aptr);
+  s.act_off = reinterpret_cast<int*>(b + o_aoff);
+  s.act_cnt = reinterpret_cast<int*>(b + o_acnt);
+  s.pair_tok = reinterpret_cast<int*>(b + o_ptok);
+  s.pair_pick = reinterpret_cast<int*>(b + o_ppick);
+  s.cursor = reinterpret_cast<int*>(b + o_cursor);
+  s.out_row = reinterpret_cast<int*>(b + o_orow);
+  s.hfrag = reinterpret_cast<uint4*>(b + o_hf);
+  s.hfsum8 = reinterpret_cast<float*>(b + o_hs);
+  s.partial = reinterpret_cast<float*>(b + o_part);
+  s.normalized = reinterpret_cast<float*>(b + o_norm);
+  s.status = reinterpret_cast<uint32_t*>(b + o_status);
+  s.exact_count = reinterpret_cast<unsigned long long*>(b + o_exact);
+  cudaMemcpy(s.status, &st, 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(s.exact_count, &ex, 8, cudaMemcpyHostToDevice);
+  return OSM_OK;
+}
+
+bool layout_ok(const osm_expert_layout* L) {
+  if (!L || L->group != 64 || L->hidden == 0 || L->inter == 0) return false;
+  if (L->hidden % 64 || L->inter % 64) return false;
+  if (L->hidden > 2048 || L->inter > 2048) return false;  // K <= 2048 per projection
+  if (L->hidden % 16 || L->inter % 8) return false;
+  const uint64_t H = L->hidden, I = L->inter;
+  const uint64_t gu_w = I * H / 2, gu_m = I * (H / 64) * 2, dn_w = H * I / 2,
+                 dn_m = H * (I / 64) * 2;
+  auto in = [&](uint64_t o, uint64_t n) { return o % 4 == 0 && o + n <= L->stride; };
+  return in(L->gate_w, gu_w) && in(L->up_w, gu_w) && in(L->down_w, dn_w) && in(L->gate_s, gu_m) &&
+         in(L->gate_b, gu_m) && in(L->up_s, gu_m) && in(L->up_b, gu_m) && in(L->down_s, dn_m) &&
+         in(L->down_b, dn_m) && (L->gate_w % 8 == 0) && (L->up_w % 8 == 0) &&
+         (L->down_w % 8 == 0);
+}
+
+void fill_sections(osm::ProjSections& s, const osm_expert_layout& r, const osm_expert_layout& sh,
+                   bool gate_up) {
+  const osm_expert_layout* L[2] = {&r, &sh};
+  for (int i = 0; i < 2; ++i) {
+    if (gate_up) {
+      s.w[i] = L[i]->gate_w; s.s[i] = L[i]->gate_s; s.b[i] = L[i]->gate_b;
+      s.w2[i] = L[i]->up_w; s.s2[i] = L[i]->up_s; s.b2[i] = L[i]->up_b;
+      s.rows[i] = (int)L[i]->inter;
+      s.K[i] = (int)L[i]->hidden;
+    } else {
+      s.w[i] = L[i]->down_w; s.s[i] = L[i]->down_s; s.b[i] = L[i]->down_b;
+      s.w2[i] = s.w[i]; s.s2[i] = s.s[i]; s.b2[i] = s.b[i];
+      s.rows[i] = (int)L[i]->hidden;
+      s.K[i] = (int)L[i]->inter;
+    }
+  }
+}
+
+// Router args common to route / forward / experts.
+osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
+  osm_context* ctx = L->ctx;
+  Scratch& s = ctx->sc;
+  osm::RouterArgs a{};
+  a.g = L->g;
+  a.wp = static_cast<const uint4*>(L->wp);
+  a.bias = L->bias;
+  a.x = x;
+  a.B = (int)T;
+  a.norm = (int)L->norm;
+  a.logits = s.logits;
+  a.bounds = s.bounds;
+  a.ids = s.ids;
+  a.weights = s.weights;
+  a.mass = s.mass;
+  a.sgate_w = L->shared_slot ? L->sgate_w : nullptr;
+  a.sgate = s.sgate;
+  a.xfrag = s.xfrag;
+  a.xfsum8 = s.xfsum8;
+  a.slot_of = L->slot_of;
+  a.slab = L->slab ? L->slab->base : nullptr;
+  a.slab_stride = L->slab ? L->slab->layout.stride : 0;
+  a.shared_slot = L->shared_slot;
+  a.ticket = s.ticket;
+  a.counts = s.counts;
+  a.n_active = s.n_active;
+  a.act_kind = s.act_kind;
+  a.act_ptr = s.act_ptr;
+  a.act_off = s.act_off;
+  a.act_cnt = s.act_cnt;
+  a.pair_tok = s.pair_tok;
+  a.pair_pick = s.pair_pick;
+  a.cursor = s.cursor;
+  a.status = s.status;
+  a.exact_count = s.exact_count;
+  return a;
+}
+
+int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
+  osm_context* ctx = L->ctx;
+  Scratch& s = ctx->sc;
+  const osm_expert_layout& R = L->slab->layout;
+  const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
+  const int Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
+  const int max_active = (int)std::min<size_t>(L->g.E, (size_t)T * L->g.k) + (L->shared_slot ? 1 : 0);
+  osm::ProjArgs gu{};
+  fill_sections(gu.sec, R, S, true);
+  gu.n_active = s.n_active;
+  gu.act_kind = s.act_kind;
+  gu.act_ptr = s.act_ptr;
+  gu.act_off = s.act_off;
+  gu.act_cnt = s.act_cnt;
+  gu.pair_tok = s.pair_tok;
+  gu.frag_by_pair = 0;
+  gu.raw = 0;
+  gu.frag_stride = L->g.H / 8;
+  gu.frag = s.xfrag;
+  gu.fsum8 = s.xfsum8;
+  gu.hfrag = s.hfrag;
+  gu.hfsum8 = s.hfsum8;
+  gu.hK = Imax;
+  osm::launch_proj(gu, true, Imax, max_active, ctx->stream, &ctx->launches);
+  int rc = check_launch(ctx, "gate/up projection");
+  if (rc) return rc;
+  osm::ProjArgs dn = gu;
+  fill_sections(dn.sec, R, S, false);
+  dn.frag_by_pair = 1;
+  dn.frag_stride = Imax / 8;
+  dn.frag = s.hfrag;
+  dn.fsum8 = s.hfsum8;
+  dn.hfrag = nullptr;
+  dn.hfsum8 = nullptr;
+  dn.out = s.partial;
+  dn.out_row = nullptr;
+  dn.pair_pick = s.pair_pick;
+  dn.kp1 = (int)L->g.k + 1;
+  dn.ostride = L->g.H;
+  osm::launch_proj(dn, false, L->g.H, max_active, ctx->stream, &ctx->launches);
+  rc = check_launch(ctx, "down projection");
+  if (rc) return rc;
+  osm::CombineArgs c{};
+  c.partial = s.partial;
+  c.weights = s.weights;
+  c.sgate = L->shared_slot ? s.sgate : nullptr;
+  c.residual = residual;
+  c.out = out;
+  c.B = (int)T;
+  c.H = L->g.H;
+  c.k = L->g.k;
+  osm::launch_combine(c, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "combine");
+}
+
+int layer_ready(osm_layer* L, uint32_t T, bool need_slab) {
+  if (!L || !L->ctx) return OSM_EINVAL;
+  osm_context* ctx = L->ctx;
+  if (T == 0) return fail(ctx, OSM_EINVAL, "token count must be non-zero");
+  if (T > ctx->max_tokens) return fail(ctx, OSM_EINVAL, "token count exceeds context max_tokens");
+  if (need_slab && !L->slab) return fail(ctx, OSM_EINVAL, "layer has no expert slab bound");
+  const size_t I = std::max<size_t>(L->slab ? L->slab->layout.inter : 64,
+                                    L->shared_slot ? L->shared_layout.inter : 0);
+  return ensure_scratch(ctx, T, L->g.H, L->g.E, L->g.k, I, L->g.H);
+}
+
+}  // namespace
+
+extern "C" {
+
+int osm_expert_layout_packed(uint32_t hidden, uint32_t inter, uint32_t group,
+                             osm_expert_layout* out) {
+  if (!out || group == 0 || hidden % group || inter % group || hidden % 8 || inter % 8)
+    return OSM_EINVAL;
+  const uint64_t H = hidden, I = inter;
+  const uint64_t gu_w = I * H / 2, gu_m = I * (H / group) * 2, dn_w = H * I / 2,
+                 dn_m = H * (I / group) * 2;
+  osm_expert_layout L{};
+  L.hidden = hidden;
+  L.inter = inter;
+  L.group = group;
+  L.gate_w = 0;
+  L.gate_s = L.gate_w + gu_w;
+  L.gate_b = L.gate_s + gu_m;
+  L.up_w = L.gate_b + gu_m;
+  L.up_s = L.up_w + gu_w;
+  L.up_b = L.up_s + gu_m;
+  L.down_w = L.up_b + gu_m;
+  L.down_s = L.down_w + dn_w;
+  L.down_b = L.down_s + dn_m;
+  L.stride = L.down_b + dn_m;
+  *out = L;
+  return OSM_OK;
+}
+
+int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
+  if (!out) return OSM_EINVAL;
+  *out = nullptr;
+  if (max_tokens == 0) return OSM_EINVAL;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return OSM_ECUDA;
+  DeviceGuard dg(device);
+  auto* ctx = new (std::nothrow) osm_context();
+  if (!ctx) return OSM_ENOMEM;
+  ctx->device = device;
+  ctx->max_tokens = max_tokens;
+  if (cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    delete ctx;
+    return OSM_ECUDA;
+  }
+  ctx->stream = ctx->own_stream;
+  *out = ctx;
+  return OSM_OK;
+}
+
+int osm_context_destroy(osm_context* ctx) {
+  if (!ctx) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (ctx->sc.base) cudaFree(ctx->sc.base);
+  if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+  delete ctx;
+  return OSM_OK;
+}
+
+const char* osm_last_error(const osm_context* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+int osm_context_device(const osm_context* ctx) { return ctx ? ctx->device : -1; }
+void* osm_context_stream(const osm_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+uint64_t osm_context_launches(const osm_context* ctx) { return ctx ? ctx->launches : 0; }
+
+int osm_context_set_stream(osm_context* ctx, void* stream) {
+  if (!ctx) return OSM_EINVAL;
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  return OSM_OK;
+}
+
+int osm_context_synchronize(osm_context* ctx) {
+  if (!ctx) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return OSM_OK;
+}
+
+int osm_context_status(osm_context* ctx, uint32_t* status, uint64_t* exact_tokens) {
+  if (!ctx) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  uint32_t st = 0;
+  unsigned long long ex = 0;
+  if (ctx->sc.base) {
+    OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    OSM_CUDA(ctx, cudaMemcpy(&st, ctx->sc.status, 4, cudaMemcpyDeviceToHost));
+    OSM_CUDA(ctx, cudaMemcpy(&ex, ctx->sc.exact_count, 8, cudaMemcpyDeviceToHost));
+    OSM_CUDA(ctx, cudaMemset(ctx->sc.status, 0, 4));
+  }
+  if (status) *status = st;
+  if (exact_tokens) *exact_tokens = ex;
+  return OSM_OK;
+}
+
+int osm_device_alloc(osm_context* ctx, size_t bytes, void** dev) {
+  if (!ctx || !dev) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  if (cudaMalloc(dev, std::max<size_t>(bytes, 1)) != cudaSuccess)
+    return fail(ctx, OSM_ENOMEM, "device allocation failed");
+  return OSM_OK;
+}
+
+int osm_device_free(osm_context* ctx, void* dev) {
+  if (!ctx) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaFree(dev));
+  return OSM_OK;
+}
+
+int osm_upload(osm_context* ctx, void* dev, const void* host, size_t bytes) {
+  if (!ctx || (!dev && bytes) || (!host && bytes)) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return OSM_OK;
+}
+
+int osm_download(osm_context* ctx, void* host, const void* dev, size_t bytes) {
+  if (!ctx || (!dev && bytes) || (!host && bytes)) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return OSM_OK;
+}
+
+int osm_host_alloc_pinned(size_t bytes, void** host) {
+  if (!host) return OSM_EINVAL;
+  if (cudaHostAlloc(host, std::max<size_t>(bytes, 1), cudaHostAllocDefault) != cudaSuccess)
+    return OSM_ENOMEM;
+  return OSM_OK;
+}
+
+int osm_host_free_pinned(void* host) {
+  return cudaFreeHost(host) == cudaSuccess ? OSM_OK : OSM_ECUDA;
+}
+
+int osm_q4_dequant(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
+                   const uint16_t* bi, uint32_t rows, uint32_t in_dim, uint32_t group,
+                   float* out) {
+  if (!ctx) return OSM_EINVAL;
+  if (group != 64 || in_dim % 64 || rows == 0 || !packed || !sc || !bi || !out)
+    return fail(ctx, OSM_EINVAL, "q4 dequant: group must be 64 and in_dim a multiple of 64");
+  DeviceGuard dg(ctx->device);
+  osm::launch_dequant(packed, sc, bi, (int)rows, (int)in_dim, out, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "q4 dequant");
+}
+
+int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
+                const uint16_t* bi, uint32_t out_dim, uint32_t in_dim, uint32_t group,
+                const float* x, uint32_t tokens, float* y) {
+  if (!ctx) return OSM_EINVAL;
+  if (group != 64 || in_dim % 64 || in_dim > 2048 || out_dim % 16 || out_dim == 0 || !packed ||
+      !sc || !bi || !x || !y || tokens == 0)
+    return fail(ctx, OSM_EINVAL,
+                "q4 gemv: group 64, in_dim a multiple of 64 (<= 2048), out_dim a multiple of 16");
+  if (tokens > ctx->max_tokens) return fail(ctx, OSM_EINVAL, "q4 gemv: tokens > max_tokens");
+  DeviceGuard dg(ctx->device);
+  int rc = ensure_scratch(ctx, tokens, 0, 1, 1, 64, in_dim);
+  if (rc) return rc;
+  Scratch& s = ctx->sc;
+  osm::launch_frag_prep(x, (int)tokens, (int)in_dim, s.xfrag, s.xfsum8, ctx->stream, &ctx->launches);
+  osm::launch_setup_single((int)tokens, nullptr, s.n_active, s.act_kind, s.act_ptr, s.act_off,
+                           s.act_cnt, s.pair_tok, s.pair_pick, s.out_row, ctx->stream,
+                           &ctx->launches);
+  osm::ProjArgs a{};
+  for (int i = 0; i < 2; ++i) {
+    a.sec.w[i] = a.sec.w2[i] = (uint64_t)(uintptr_t)packed;
+    a.sec.s[i] = a.sec.s2[i] = (uint64_t)(uintptr_t)sc;
+    a.sec.b[i] = a.sec.b2[i] = (uint64_t)(uintptr_t)bi;
+    a.sec.rows[i] = (int)out_dim;
+    a.sec.K[i] = (int)in_dim;
+  }
+  a.n_active = s.n_active;
+  a.act_kind = s.act_kind;
+  a.act_ptr = s.act_ptr;
+  a.act_off = s.act_off;
+  a.act_cnt = s.act_cnt;
+  a.pair_tok = s.pair_tok;
+  a.frag_by_pair = 0;
+  a.raw = 1;
+  a.frag_stride = (int)in_dim / 8;
+  a.frag = s.xfrag;
+  a.fsum8 = s.xfsum8;
+  a.out = y;
+  a.out_row = s.out_row;
+  a.pair_pick = s.pair_pick;
+  a.kp1 = 1;
+  a.ostride = (int)out_dim;
+  osm::launch_proj(a, false, (int)out_dim, 1, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "q4 gemv");
+}
+
+int osm_swiglu(osm_context* ctx, const float* g, const float* u, float* out, size_t n) {
+  if (!ctx || (n && (!g || !u || !out))) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  if (n == 0) return OSM_OK;
+  osm::launch_swiglu(g, u, out, n, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "swiglu");
+}
+
+int osm_weighted_accumulate(osm_context* ctx, const float* src, float w, float* acc, size_t n) {
+  if (!ctx || (n && (!src || !acc))) return OSM_EINVAL;
+  if (!std::isfinite(w)) return fail(ctx, OSM_EINVAL, "weighted accumulate: non-finite weight");
+  DeviceGuard dg(ctx->device);
+  if (n == 0) return OSM_OK;
+  osm::launch_waccum(src, w, acc, n, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "weighted accumulate");
+}
+
+int osm_rms_norm(osm_context* ctx, float* values, uint32_t rows, uint32_t dim, const float* w,
+                 float eps, uint32_t flags) {
+  if (!ctx) return OSM_EINVAL;
+  if (rows == 0 || dim == 0 || !values) return fail(ctx, OSM_EINVAL, "rms_norm: invalid shape");
+  if (!(eps >= 0.0f)) return fail(ctx, OSM_EINVAL, "rms_norm: eps must be non-negative");
+  DeviceGuard dg(ctx->device);
+  osm::launch_rmsnorm(values, values, (int)rows, (int)dim, w, eps, (flags & OSM_RMSNORM_EXACT) != 0,
+                      ctx->stream, &ctx->launches);
+  return check_launch(ctx, "rms_norm");
+}
+
+int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layout* layout,
+                       const float* x, uint32_t tokens, float* out) {
+  if (!ctx) return OSM_EINVAL;
+  if (!slot || !x || !out || tokens == 0 || !layout_ok(layout))
+    return fail(ctx, OSM_EINVAL, "expert forward: invalid arguments or unsupported layout");
+  if (tokens > ctx->max_tokens) return fail(ctx, OSM_EINVAL, "expert forward: tokens > max_tokens");
+  DeviceGuard dg(ctx->device);
+  const osm_expert_layout& L = *layout;
+  int rc = ensure_scratch(ctx, tokens, L.hidden, 1, 1, L.inter, L.hidden);
+  if (rc) return rc;
+  Scratch& s = ctx->sc;
+  osm::launch_frag_prep(x, (int)tokens, (int)L.hidden, s.xfrag, s.xfsum8, ctx->stream,
+                        &ctx->launches);
+  osm::launch_setup_single((int)tokens, static_cast<const uint8_t*>(slot), s.n_active, s.act_kind,
+                           s.act_ptr, s.act_off, s.act_cnt, s.pair_tok, s.pair_pick, s.out_row,
+                           ctx->stream, &ctx->launches);
+  osm::ProjArgs gu{};
+  fill_sections(gu.sec, L, L, true);
+  gu.n_active = s.n_active;
+  gu.act_kind = s.act_kind;
+  gu.act_ptr = s.act_ptr;
+  gu.act_off = s.act_off;
+  gu.act_cnt = s.act_cnt;
+  gu.pair_tok = s.pair_tok;
+  gu.frag_stride = (int)L.hidden / 8;
+  gu.frag = s.xfrag;
+  gu.fsum8 = s.xfsum8;
+  gu.hfrag = s.hfrag;
+  gu.hfsum8 = s.hfsum8;
+  gu.hK = (int)L.inter;
+  osm::launch_proj(gu, true, (int)L.inter, 1, ctx->stream, &ctx->launches);
+  rc = check_launch(ctx, "expert gate/up");
+  if (rc) return rc;
+  osm::ProjArgs dn = gu;
+  fill_sections(dn.sec, L, L, false);
+  dn.frag_by_pair = 1;
+  dn.frag_stride = (int)L.inter / 8;
+  dn.frag = s.hfrag;
+  dn.fsum8 = s.hfsum8;
+  dn.out = out;
+  dn.out_row = s.out_row;
+  dn.pair_pick = s.pair_pick;
+  dn.kp1 = 1;
+  dn.ostride = (int)L.hidden;
+  osm::launch_proj(dn, false, (int)L.hidden, 1, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "expert down");
+}
+
+int osm_slab_create(osm_context* ctx, const osm_expert_layout* layout, uint32_t slots,
+                    osm_slab** out) {
+  if (!ctx || !out) return OSM_EINVAL;
+  *out = nullptr;
+  if (slots == 0 || !layout_ok(layout))
+    return fail(ctx, OSM_EINVAL, "slab: zero slots or unsupported expert layout");
+  DeviceGuard dg(ctx->device);
+  auto* s = new (std::nothrow) osm_slab();
+  if (!s) return OSM_ENOMEM;
+  s->ctx = ctx;
+  s->layout = *layout;
+  s->slots = slots;
+  if (cudaMalloc(&s->base, (size_t)slots * layout->stride) != cudaSuccess) {
+    delete s;
+    return fail(ctx, OSM_ENOMEM, "slab: device allocation failed");
+  }
+  if (cudaStreamCreateWithFlags(&s->side, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&s->ev, cudaEventDisableTiming) != cudaSuccess) {
+    cudaFree(s->base);
+    delete s;
+    return fail(ctx, OSM_ECUDA, "slab: stream/event creation failed");
+  }
+  *out = s;
+  return OSM_OK;
+}
+
+int osm_slab_destroy(osm_slab* s) {
+  if (!s) return OSM_EINVAL;
+  DeviceGuard dg(s->ctx->device);
+  cudaStreamSynchronize(s->side);
+  cudaStreamSynchronize(s->ctx->stream);
+  cudaFree(s->base);
+  cudaEventDestroy(s->ev);
+  cudaStreamDestroy(s->side);
+  delete s;
+  return OSM_OK;
+}
+
+uint32_t osm_slab_slots(const osm_slab* s) { return s ? s->slots : 0; }
+
+void* osm_slab_slot_ptr(const osm_slab* s, uint32_t slot) {
+  if (!s || slot >= s->slots) return nullptr;
+  return s->base + (size_t)slot * s->layout.stride;
+}
+
+uint64_t osm_slab_h2d_bytes(const osm_slab* s) { return s ? s->h2d_bytes : 0; }
+
+int osm_slab_fill_async(osm_slab* s, uint32_t slot, const void* host) {
+  if (!s || !host) return OSM_EINVAL;
+  osm_context* ctx = s->ctx;
+  if (slot >= s->slots) return fail(ctx, OSM_EINVAL, "slab fill: slot out of range");
+  DeviceGuard dg(ctx->device);
+  // A fill must not overwrite a slot that queued kernels still read.
+  OSM_CUDA(ctx, cudaEventRecord(s->ev, ctx->stream));
+  OSM_CUDA(ctx, cudaStreamWaitEvent(s->side, s->ev, 0));
+  OSM_CUDA(ctx, cudaMemcpyAsync(s->base + (size_t)slot * s->layout.stride, host, s->layout.stride,
+                                cudaMemcpyHostToDevice, s->side));
+  OSM_CUDA(ctx, cudaEventRecord(s->ev, s->side));
+  OSM_CUDA(ctx, cudaStreamWaitEvent(ctx->stream, s->ev, 0));
+  s->h2d_bytes += s->layout.stride;
+  return OSM_OK;
+}
+
+int osm_slab_fill_wait(osm_slab* s, uint32_t timeout_ms) {
+  if (!s) return OSM_EINVAL;
+  osm_context* ctx = s->ctx;
+  DeviceGuard dg(ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t e = cudaEventQuery(s->ev);
+    if (e == cudaSuccess) return OSM_OK;
+    if (e != cudaErrorNotReady) return cuda_fail(ctx, e, "slab fill wait");
+    const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
+                        std::chrono::steady_clock::now() - t0).count();
+    if (ms >= (long long)timeout_ms)
+      return fail(ctx, OSM_ETIMEOUT, "slab fill wait: timed out");
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+int osm_layer_create(osm_context* ctx, const osm_layer_desc* d, osm_layer** out) {
+  if (!ctx || !d || !out) return OSM_EINVAL;
+  *out = nullptr;
+  if (d->hidden == 0 || d->experts == 0 || d->top_k == 0)
+    return fail(ctx, OSM_EINVAL, "qwen router: dimensions and top_k must be non-zero");
+  if (d->top_k > d->experts) return fail(ctx, OSM_EINVAL, "qwen router: top_k cannot exceed expert_count");
+  if (d->experts > (uint32_t)osm::kMaxExperts - 1 || d->top_k > (uint32_t)osm::kMaxTopK)
+    return fail(ctx, OSM_EINVAL, "router: at most 1023 experts and top_k 32 are supported");
+  if (d->hidden > 8192 || d->hidden % 8)
+    return fail(ctx, OSM_EINVAL, "router: hidden must be a multiple of 8 and <= 8192");
+  if (!d->router_weight_host) return fail(ctx, OSM_EINVAL, "router weight missing");
+  const size_t EH = (size_t)d->experts * d->hidden;
+  bool bf16_exact = true;
+  for (size_t i = 0; i < EH; ++i) {
+    const float v = d->router_weight_host[i];
+    if (!std::isfinite(v))
+      return fail(ctx, OSM_EINVAL, "qwen router: router weight contains non-finite value");
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    if (u & 0xFFFFu) bf16_exact = false;
+  }
+  if (d->shared_slot_host) {
+    if (!layout_ok(&d->shared_layout) || d->shared_layout.hidden != d->hidden)
+      return fail(ctx, OSM_EINVAL, "shared expert layout unsupported or hidden mismatch");
+    if (!d->shared_gate_host) return fail(ctx, OSM_EINVAL, "shared expert scalar gate missing");
+  }
+  DeviceGuard dg(ctx->device);
+  auto* L = new (std::nothrow) osm_layer();
+  if (!L) return OSM_ENOMEM;
+  L->ctx = ctx;
+  osm::RouterGeom g{};
+  g.H = (int)d->hidden;
+  g.Hp = (int)align_up(d->hidden, 256);
+  g.c = g.Hp / 32;
+  g.nvec = g.c / 8;
+  g.E = (int)d->experts;
+  g.k = (int)d->top_k;
+  g.f32w = bf16_exact ? 0 : 1;
+  L->g = g;
+  L->norm = d->norm_topk_prob ? 1 : 0;
+  L->norm_eps = d->norm_eps;
+  auto cleanup = [&](int code, const char* msg) {
+    osm_layer_destroy(L);
+    return fail(ctx, code, msg);
+  };
+  float* tmp = nullptr;
+  if (cudaMalloc(&L->wp, (size_t)g.E * g.Hp * (g.f32w ? 4 : 2)) != cudaSuccess ||
+      cudaMalloc(&tmp, EH * 4) != cudaSuccess)
+    return cleanup(OSM_ENOMEM, "layer: router allocation failed");
+  cudaMemcpyAsync(tmp, d->router_weight_host, EH * 4, cudaMemcpyHostToDevice, ctx->stream);
+  osm::launch_router_pack(tmp, g, L->wp, ctx->stream, &ctx->launches);
+  cudaStreamSynchronize(ctx->stream);
+  cudaFree(tmp);
+  if (d->logit_bias_host) {
+    for (uint32_t e = 0; e < d->experts; ++e)
+      if (!std::isfinite(d->logit_bias_host[e])) return cleanup(OSM_EINVAL, "logit bias non-finite");
+    if (cudaMalloc(&L->bias, d->experts * 4) != cudaSuccess)
+      return cleanup(OSM_ENOMEM, "layer: bias allocation failed");
+    cudaMemcpy(L->bias, d->logit_bias_host, d->experts * 4, cudaMemcpyHostToDevice);
+  }
+  if (d->shared_slot_host) {
+    L->shared_layout = d->shared_layout;
+    if (cudaMalloc(&L->shared_slot, d->shared_layout.stride) != cudaSuccess ||
+        cudaMalloc(&L->sgate_w, d->hidden * 4) != cudaSuccess)
+      return cleanup(OSM_ENOMEM, "layer: shared expert allocation failed");
+    cudaMemcpy(L->shared_slot, d->shared_slot_host, d->shared_layout.stride, cudaMemcpyHostToDevice);
+    cudaMemcpy(L->sgate_w, d->shared_gate_host, d->hidden * 4, cudaMemcpyHostToDevice);
+  }
+  if (d->norm_weight_host) {
+    if (cudaMalloc(&L->norm_w, d->hidden * 4) != cudaSuccess)
+      return cleanup(OSM_ENOMEM, "layer: norm weight allocation failed");
+    cudaMemcpy(L->norm_w, d->norm_weight_host, d->hidden * 4, cudaMemcpyHostToDevice);
+  }
+  if (cudaMalloc(&L->slot_of, d->experts * 4) != cudaSuccess)
+    return cleanup(OSM_ENOMEM, "layer: slot table allocation failed");
+  L->slot_host.assign(d->experts, -1);
+  cudaMemcpy(L->slot_of, L->slot_host.data(), d->experts * 4, cudaMemcpyHostToDevice);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cleanup(OSM_ECUDA, cudaGetErrorString(e));
+  *out = L;
+  return OSM_OK;
+}
+
+int osm_layer_destroy(osm_layer* L) {
+  if (!L) return OSM_EINVAL;
+  DeviceGuard dg(L->ctx->device);
+  cudaStreamSynchronize(L->ctx->stream);
+  cudaFree(L->wp);
+  cudaFree(L->bias);
+  cudaFree(L->sgate_w);
+  cudaFree(L->shared_slot);
+  cudaFree(L->norm_w);
+  cudaFree(L->slot_of);
+  delete L;
+  return OSM_OK;
+}
+
+int osm_layer_bind_slab(osm_layer* L, osm_slab* slab, const int32_t* slot_of) {
+  if (!L || !slab || !slot_of) return OSM_EINVAL;
+  osm_context* ctx = L->ctx;
+  if (slab->ctx != ctx) return fail(ctx, OSM_EINVAL, "slab belongs to another context");
+  if (slab->layout.hidden != (uint32_t)L->g.H)
+    return fail(ctx, OSM_EINVAL, "slab expert geometry does not match the router hidden size");
+  for (int e = 0; e < L->g.E; ++e)
+    if (slot_of[e] >= (int32_t)slab->slots) return fail(ctx, OSM_EINVAL, "slot index out of range");
+  DeviceGuard dg(ctx->device);
+  L->slab = slab;
+  L->slot_host.assign(slot_of, slot_of + L->g.E);
+  OSM_CUDA(ctx, cudaMemcpyAsync(L->slot_of, L->slot_host.data(), L->g.E * 4,
+                                cudaMemcpyHostToDevice, ctx->stream));
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return OSM_OK;
+}
+
+int osm_layer_set_slot(osm_layer* L, uint32_t expert, int32_t slot) {
+  if (!L) return OSM_EINVAL;
+  osm_context* ctx = L->ctx;
+  if (expert >= (uint32_t)L->g.E) return fail(ctx, OSM_EINVAL, "expert out of range");
+  if (L->slab && slot >= (int32_t)L->slab->slots) return fail(ctx, OSM_EINVAL, "slot out of range");
+  DeviceGuard dg(ctx->device);
+  L->slot_host[expert] = slot;
+  // pageable-source copy: the value is staged before the call returns
+  OSM_CUDA(ctx, cudaMemcpyAsync(L->slot_of + expert, &L->slot_host[expert], 4,
+                                cudaMemcpyHostToDevice, ctx->stream));
+  return OSM_OK;
+}
+
+int osm_moe_route(osm_layer* L, const float* x, uint32_t T, uint32_t* ids, float* w, float* mass,
+                  uint32_t flags) {
+  int rc = layer_ready(L, T, false);
+  if (rc) return rc;
+  if (!x) return fail(L->ctx, OSM_EINVAL, "route: null input");
+  osm_context* ctx = L->ctx;
+  DeviceGuard dg(ctx->device);
+  osm::RouterArgs a = router_args(L, x, T);
+  a.force_exact = (flags & OSM_ROUTE_EXACT) ? 1 : 0;
+  a.ids_out = ids;
+  a.weights_out = w;
+  a.mass_out = mass;
+  a.do_group = 0;
+  a.xfrag = nullptr;
+  a.sgate_w = nullptr;
+  osm::launch_router(a, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "router");
+}
+
+int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32_t* ids, float* w,
+                    float* mass, float* sgate, const float* residual, uint32_t flags) {
+  int rc = layer_ready(L, T, true);
+  if (rc) return rc;
+  osm_context* ctx = L->ctx;
+  if (!x || !out) return fail(ctx, OSM_EINVAL, "forward: null input/output");
+  if ((flags & OSM_ADD_RESIDUAL) && !residual) return fail(ctx, OSM_EINVAL, "forward: residual missing");
+  DeviceGuard dg(ctx->device);
+  osm::RouterArgs a = router_args(L, x, T);
+  a.force_exact = (flags & OSM_ROUTE_EXACT) ? 1 : 0;
+  a.ids_out = ids;
+  a.weights_out = w;
+  a.mass_out = mass;
+  a.sgate_out = sgate;
+  a.do_group = 1;
+  osm::launch_router(a, ctx->stream, &ctx->launches);
+  rc = check_launch(ctx, "router");
+  if (rc) return rc;
+  return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
+}
+
+int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, const float* w,
+                    float* out, float* sgate, const float* residual, uint32_t flags) {
+  int rc = layer_ready(L, T, true);
+  if (rc) return rc;
+  osm_context* ctx = L->ctx;
+  if (!x || !out || !ids || !w) return fail(ctx, OSM_EINVAL, "experts: null argument");
+  if ((flags & OSM_ADD_RESIDUAL) && !residual) return fail(ctx, OSM_EINVAL, "experts: residual missing");
+  DeviceGuard dg(ctx->device);
+  Scratch& s = ctx->sc;
+  const size_t nk = (size_t)T * L->g.k;
+  OSM_CUDA(ctx, cudaMemcpyAsync(s.ids, ids, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  OSM_CUDA(ctx, cudaMemcpyAsync(s.weights, w, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  osm::RouterArgs a = router_args(L, x, T);
+  a.skip_route = 1;
+  a.sgate_out = sgate;
+  a.do_group = 1;
+  osm::launch_router(a, ctx->stream, &ctx->launches);
+  rc = check_launch(ctx, "expert grouping");
+  if (rc) return rc;
+  return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
+}
+
+int osm_moe_sublayer_forward(osm_layer* L, const float* residual, uint32_t T, float* out,
+                             float* normalized, uint32_t* ids, float* w, float* mass,
+                             float* sgate, uint32_t flags) {
+  int rc = layer_ready(L, T, true);
+  if (rc) return rc;
+  osm_context* ctx = L->ctx;
+  if (!residual || !out) return fail(ctx, OSM_EINVAL, "sublayer: null input/output");
+  DeviceGuard dg(ctx->device);
+  float* nrm = normalized ? normalized : ctx->sc.normalized;
+  osm::launch_rmsnorm(residual, nrm, (int)T, L->g.H, L->norm_w, L->norm_eps,
+                      (flags & OSM_RMSNORM_EXACT) != 0, ctx->stream, &ctx->launches);
+  rc = check_launch(ctx, "sublayer rmsnorm");
+  if (rc) return rc;
+  return osm_moe_forward(L, nrm, T, out, ids, w, mass, sgate, residual, flags | OSM_ADD_RESIDUAL);
+}
+
+int osm_gen_normal(osm_context* ctx, uint64_t seed, uint64_t tensor, float sigma, float* out,
+                   size_t n, size_t first) {
+  if (!ctx || (n && !out)) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  if (n == 0) return OSM_OK;
+  osm::launch_gen_normal(seed, tensor, sigma, out, n, first, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "gen normal");
+}
+
+int osm_gen_expert_slots(osm_slab* s, uint64_t seed, uint64_t tensor_base, float sigma,
+                         uint32_t first, uint32_t count) {
+  if (!s) return OSM_EINVAL;
+  osm_context* ctx = s->ctx;
+  if ((uint64_t)first + count > s->slots) return fail(ctx, OSM_EINVAL, "gen: slot range");
+  DeviceGuard dg(ctx->device);
+  const osm_expert_layout& L = s->layout;
+  for (uint32_t i = 0; i < count; ++i) {
+    uint8_t* b = s->base + (size_t)(first + i) * L.stride;
+    const uint64_t t = tensor_base + 3ull * i;
+    osm::launch_gen_quant(seed, t + 0, sigma, (int)L.inter, (int)L.hidden,
+                          reinterpret_cast<uint32_t*>(b + L.gate_w), reinterpret_cast<uint16_t*>(b + L.gate_s),
+                          reinterpret_cast<uint16_t*>(b + L.gate_b), ctx->stream, &ctx->launches);
+    osm::launch_gen_quant(seed, t + 1, sigma, (int)L.inter, (int)L.hidden,
+                          reinterpret_cast<uint32_t*>(b + L.up_w), reinterpret_cast<uint16_t*>(b + L.up_s),
+                          reinterpret_cast<uint16_t*>(b + L.up_b), ctx->stream, &ctx->launches);
+    osm::launch_gen_quant(seed, t + 2, sigma, (int)L.hidden, (int)L.inter,
+                          reinterpret_cast<uint32_t*>(b + L.down_w), reinterpret_cast<uint16_t*>(b + L.down_s),
+                          reinterpret_cast<uint16_t*>(b + L.down_b), ctx->stream, &ctx->launches);
+  }
+  return check_launch(ctx, "gen expert slots");
+}
+
+}  // extern "C"

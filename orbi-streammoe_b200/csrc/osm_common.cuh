@@ -1,0 +1,93 @@
+// osm_common.cuh -- device helpers shared by the sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace osm {
+
+constexpr int kWarp = 32;
+constexpr int kGroup = 64;          // quantisation group along the input dim
+constexpr int kMaxExperts = 1024;   // router width supported by the selectors
+constexpr int kMaxTopK = 32;
+
+// Device status bits (osm_context_status).
+constexpr uint32_t kStatusNonFinite = 1u << 0;
+constexpr uint32_t kStatusBadMass = 1u << 1;
+constexpr uint32_t kStatusNotResident = 1u << 2;
+constexpr uint32_t kStatusBadSlot = 1u << 3;
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
+  return __uint_as_float(bits16 << 16);
+}
+
+// Round-to-nearest-even fp32 -> bf16 bits (finite inputs).
+__device__ __forceinline__ uint32_t f32_to_bf16_rne(float v) {
+  uint32_t u = __float_as_uint(v);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu) != 0)
+    return (u >> 16) | 0x40u;
+  return (u + 0x7FFFu + ((u >> 16) & 1u)) >> 16;
+}
+
+// x ~= hi + lo with hi = bf16(x), lo = bf16(x - hi): 16 significant bits,
+// relative error <= 2^-17.  x - hi is exact in fp32.
+__device__ __forceinline__ void split_bf16(float x, uint32_t& hi, uint32_t& lo) {
+  hi = f32_to_bf16_rne(x);
+  const float r = __fsub_rn(x, bf16_bits_to_f32(hi));
+  lo = f32_to_bf16_rne(r);
+}
+
+__device__ __forceinline__ uint32_t pack2(uint32_t lo16, uint32_t hi16) {
+  return (lo16 & 0xFFFFu) | (hi16 << 16);
+}
+
+// Nibble pair k (0..3) of a Q4 word as a bf16x2 register holding exactly
+// (q_k, q_{k+4}): OR the nibbles into the mantissa of 128.0 (0x4300) and
+// subtract 128 (exact).
+__device__ __forceinline__ uint32_t nibble_pair_bf16(uint32_t w, int k) {
+  uint32_t v;
+  const uint32_t s = w >> (4 * k);
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(v) : "r"(s), "r"(0x000F000Fu), "r"(0x43004300u));
+  uint32_t out;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(out) : "r"(v), "r"(0x43004300u));
+  return out;
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float d[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Reference sigmoid / silu op order (reference_ops.cpp:214-220):
+// sigmoid(v) = 1 / (1 + exp(-v)); silu(v) = v * sigmoid(v).
+__device__ __forceinline__ float ref_sigmoid(float v) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
+}
+__device__ __forceinline__ float ref_silu(float v) { return __fmul_rn(v, ref_sigmoid(v)); }
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+  uint64_t z = x + 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+}  // namespace osm

@@ -1,0 +1,145 @@
+// osm_kernels.cuh -- launch interfaces of the sm_100a kernels (osm_kernels.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace osm {
+
+// Router weight layout in HBM.  Row e is padded to Hp = roundup(H, 256) and
+// split into 32 contiguous lane chunks of c = Hp/32 elements; lane l's chunk
+// is stored as nvec = c/8 vectors of 8 bf16, vector m of every lane adjacent:
+//   element (e, h), l = h / c, o = h % c  ->  ((e*nvec + o/8)*32 + l)*8 + o%8
+// so the 32 lanes of a warp read 512 contiguous bytes per step while each lane
+// walks its own contiguous chunk (needed by the error bound of the router).
+struct RouterGeom {
+  int H, Hp, c, nvec, E, k;
+  int f32w;                 // router stored as fp32 (else bf16)
+};
+
+struct RouterArgs {
+  RouterGeom g;
+  const uint4* wp;          // permuted router rows (bf16 or fp32)
+  const float* bias;        // [E] or null
+  const float* x;           // [B][H]
+  int B;
+  int norm;                 // norm_topk_prob
+  int force_exact;
+  int skip_route;           // routing given (osm_moe_experts): gate, fragments, grouping only
+  float* logits;            // scratch [B][E]
+  float* bounds;            // scratch [B][E]
+  uint32_t* ids;            // scratch [B][k]
+  float* weights;           // scratch [B][k]
+  float* mass;              // scratch [B]
+  uint32_t* ids_out;        // optional user copies
+  float* weights_out;
+  float* mass_out;
+  // shared expert scalar gate
+  const float* sgate_w;     // [H] or null
+  float* sgate;             // scratch [B]
+  float* sgate_out;         // optional
+  // fragments of x for the expert kernels
+  uint4* xfrag;             // [B][H/8][2]
+  float* xfsum8;            // [B][H/8]
+  // grouping (done by the last block)
+  int do_group;
+  const int* slot_of;       // [E]
+  const uint8_t* slab;
+  uint64_t slab_stride;
+  const uint8_t* shared_slot;  // null without shared expert
+  unsigned int* ticket;
+  int* counts;              // [E+1] scratch (zeroed by the last block)
+  int* n_active;
+  int* act_kind;            // 0 routed layout, 1 shared layout
+  const uint8_t** act_ptr;
+  int* act_off;
+  int* act_cnt;
+  int* pair_tok;            // [B*(k+1)]
+  int* pair_pick;
+  int* cursor;              // [E+1]
+  uint32_t* status;
+  unsigned long long* exact_count;
+};
+
+void launch_router(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
+
+// Grouping alone (expert list from a routing already in scratch).
+void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
+
+// Fragments of activations for the projection kernel: per 8-element chunk
+// c of row r, two uint4 (hi, lo) holding bf16x2 pairs (x0,x4) (x1,x5)
+// (x2,x6) (x3,x7), and the fp32 sequential sum of the 8 values.
+void launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8,
+                      cudaStream_t s, uint64_t* launches);
+
+// Section offsets of one projection (weight, scales, biases) for the two
+// slot layouts (0 routed, 1 shared); for a raw projection, base pointers are
+// null and offsets carry the addresses.
+struct ProjSections {
+  uint64_t w[2], s[2], b[2];     // first (gate / single) projection
+  uint64_t w2[2], s2[2], b2[2];  // paired projection (up)
+  int rows[2];                   // output rows per layout
+  int K[2];                      // input dim per layout
+};
+
+struct ProjArgs {
+  ProjSections sec;
+  const int* n_active;
+  const int* act_kind;
+  const uint8_t* const* act_ptr;
+  const int* act_off;
+  const int* act_cnt;
+  const int* pair_tok;           // pair -> input fragment row (for paired)
+  int frag_by_pair;              // 1: input row = pair position
+  int raw;                       // 1: sections are absolute addresses
+  int frag_stride;               // chunks (of 8) per fragment row
+  const uint4* frag;             // [row][frag_stride][2]
+  const float* fsum8;            // [row][frag_stride]
+  // paired outputs
+  uint4* hfrag;                  // [pair][Kd/8][2]
+  float* hfsum8;                 // [pair][Kd/8]
+  int hK;                        // row length of hfrag (intermediate, max)
+  // single outputs
+  float* out;                    // [out_row][ostride]
+  const int* out_row;            // pair -> output row, or null (row = pair_tok)
+  const int* pair_pick;          // pair -> pick (used with kp1)
+  int kp1;                       // k+1 (out row = tok*kp1 + pick) when out_row null
+  int ostride;
+};
+
+void launch_proj(const ProjArgs& a, bool paired, int max_rows, int max_active,
+                 cudaStream_t s, uint64_t* launches);
+
+struct CombineArgs {
+  const float* partial;          // [B][k+1][H]
+  const float* weights;          // [B][k]
+  const float* sgate;            // [B] or null (no shared expert)
+  const float* residual;         // [B][H] or null
+  float* out;                    // [B][H]
+  int B, H, k;
+};
+void launch_combine(const CombineArgs& a, cudaStream_t s, uint64_t* launches);
+
+void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float* w,
+                    float eps, bool exact, cudaStream_t s, uint64_t* launches);
+void launch_dequant(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi,
+                    int rows, int K, float* out, cudaStream_t s, uint64_t* launches);
+void launch_swiglu(const float* g, const float* u, float* out, size_t n, cudaStream_t s,
+                   uint64_t* launches);
+void launch_waccum(const float* src, float w, float* acc, size_t n, cudaStream_t s,
+                   uint64_t* launches);
+void launch_gen_normal(uint64_t seed, uint64_t tensor, float sigma, float* out, size_t n,
+                       size_t first, cudaStream_t s, uint64_t* launches);
+// Quantise `rows` x `cols` N(0, sigma) values of (seed, tensor) with the
+// reference quantiser into packed/scales/biases (bf16) destinations.
+void launch_gen_quant(uint64_t seed, uint64_t tensor, float sigma, int rows, int cols,
+                      uint32_t* packed, uint16_t* sc, uint16_t* bi, cudaStream_t s,
+                      uint64_t* launches);
+// Permute fp32 [E][H] router rows (bf16-representable) into the router layout.
+void launch_router_pack(const float* w, const RouterGeom& g, void* wp, cudaStream_t s,
+                        uint64_t* launches);
+void launch_setup_single(int T, const uint8_t* ptr, int* n_active, int* act_kind,
+                         const uint8_t** act_ptr, int* act_off, int* act_cnt, int* pair_tok,
+                         int* pair_pick, int* out_row, cudaStream_t s, uint64_t* launches);
+
+}  // namespace osm

@@ -1,0 +1,239 @@
+"""Python handle on the B200 routed-MoE sublayer (C ABI in include/osm_b200.h).
+
+Device buffers are torch CUDA tensors (plumbing only: allocation, streams);
+every computation is a call into libosm_b200.so.  Names follow the reference
+(ingeniusvictor/orbi-streammoe): ``Context`` <-> VulkanComputeContext,
+``Slab`` <-> the device side of VulkanResidentExpertCache, ``Layer`` <->
+QwenCheckpointSparseMoeLayer, ``route_qwen_top_k`` <-> route_qwen_top_k_cpu,
+``run_qwen_sparse_moe`` <-> run_qwen_sparse_moe_vulkan_accum, and so on.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _lib
+from ._lib import (OSM_ADD_RESIDUAL, OSM_RMSNORM_EXACT, OSM_ROUTE_EXACT,  # noqa: F401
+                   ExpertLayout, LayerDesc)
+
+
+class OsmError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"osm error {code}: {msg}")
+        self.code = code
+
+
+def lib():
+    return _lib.load()
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    return C.c_void_p(t.data_ptr())
+
+
+def expert_layout(hidden: int, inter: int, group: int = 64) -> ExpertLayout:
+    L = ExpertLayout()
+    rc = lib().osm_expert_layout_packed(hidden, inter, group, C.byref(L))
+    if rc:
+        raise OsmError(rc, "invalid expert geometry")
+    return L
+
+
+class Context:
+    """One device, one stream, scratch for up to ``max_tokens`` rows."""
+
+    def __init__(self, device: int = 0, max_tokens: int = 256):
+        self.h = C.c_void_p()
+        rc = lib().osm_context_create(device, max_tokens, C.byref(self.h))
+        if rc:
+            raise OsmError(rc, "context creation failed")
+        self.device = device
+        self.max_tokens = max_tokens
+
+    def check(self, rc: int, what: str = ""):
+        if rc:
+            msg = lib().osm_last_error(self.h).decode()
+            raise OsmError(rc, f"{what}: {msg}" if what else msg)
+
+    def close(self):
+        if self.h:
+            lib().osm_context_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def stream_handle(self) -> int:
+        return lib().osm_context_stream(self.h) or 0
+
+    def set_stream(self, stream_handle: int | None):
+        self.check(lib().osm_context_set_stream(self.h, C.c_void_p(stream_handle or 0)))
+
+    def synchronize(self):
+        self.check(lib().osm_context_synchronize(self.h))
+
+    def status(self):
+        st = C.c_uint32()
+        ex = C.c_uint64()
+        self.check(lib().osm_context_status(self.h, C.byref(st), C.byref(ex)))
+        return st.value, ex.value
+
+    @property
+    def launches(self) -> int:
+        return lib().osm_context_launches(self.h)
+
+    # ---- element-wise ops (Vulkan kernel replacements) ----
+    def q4_dequant(self, packed, scales_bf16, biases_bf16, rows, in_dim, out, group=64):
+        self.check(lib().osm_q4_dequant(self.h, _ptr(packed), _ptr(scales_bf16), _ptr(biases_bf16),
+                                        rows, in_dim, group, _ptr(out)), "q4_dequant")
+
+    def q4_gemv(self, packed, scales_bf16, biases_bf16, out_dim, in_dim, x, tokens, y, group=64):
+        self.check(lib().osm_q4_gemv(self.h, _ptr(packed), _ptr(scales_bf16), _ptr(biases_bf16),
+                                     out_dim, in_dim, group, _ptr(x), tokens, _ptr(y)), "q4_gemv")
+
+    def swiglu(self, gate, up, out):
+        self.check(lib().osm_swiglu(self.h, _ptr(gate), _ptr(up), _ptr(out), gate.numel()), "swiglu")
+
+    def weighted_accumulate(self, src, weight, acc):
+        self.check(lib().osm_weighted_accumulate(self.h, _ptr(src), float(weight), _ptr(acc),
+                                                 src.numel()), "weighted_accumulate")
+
+    def rms_norm(self, values, rows, dim, weight, eps, exact=False):
+        self.check(lib().osm_rms_norm(self.h, _ptr(values), rows, dim, _ptr(weight), eps,
+                                      OSM_RMSNORM_EXACT if exact else 0), "rms_norm")
+
+    def expert_forward(self, slot_ptr: int, layout: ExpertLayout, x, tokens, out):
+        self.check(lib().osm_expert_forward(self.h, C.c_void_p(slot_ptr), C.byref(layout), _ptr(x),
+                                            tokens, _ptr(out)), "expert_forward")
+
+    def gen_normal(self, seed, tensor, sigma, out, first=0):
+        self.check(lib().osm_gen_normal(self.h, seed, tensor, sigma, _ptr(out), out.numel(), first),
+                   "gen_normal")
+
+
+class Slab:
+    """Fixed-stride expert slots in HBM."""
+
+    def __init__(self, ctx: Context, layout: ExpertLayout, slots: int):
+        self.ctx = ctx
+        self.layout = layout
+        self.h = C.c_void_p()
+        ctx.check(lib().osm_slab_create(ctx.h, C.byref(layout), slots, C.byref(self.h)), "slab")
+        self.slots = slots
+
+    def close(self):
+        if self.h:
+            lib().osm_slab_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def slot_ptr(self, slot: int) -> int:
+        return lib().osm_slab_slot_ptr(self.h, slot) or 0
+
+    def fill_async(self, slot: int, host_ptr: int):
+        self.ctx.check(lib().osm_slab_fill_async(self.h, slot, C.c_void_p(host_ptr)), "slab fill")
+
+    def fill_wait(self, timeout_ms: int = 5000):
+        self.ctx.check(lib().osm_slab_fill_wait(self.h, timeout_ms), "slab fill wait")
+
+    @property
+    def h2d_bytes(self) -> int:
+        return lib().osm_slab_h2d_bytes(self.h)
+
+    def generate(self, seed: int, tensor_base: int, sigma: float, first: int, count: int):
+        self.ctx.check(lib().osm_gen_expert_slots(self.h, seed, tensor_base, sigma, first, count),
+                       "gen_expert_slots")
+
+
+class Layer:
+    """One MoE layer: router (+ optional logit bias), shared expert and its
+    scalar gate, optional post-attention norm weight, and the expert slab."""
+
+    def __init__(self, ctx: Context, router_weight, top_k: int, norm_topk_prob: bool = True,
+                 logit_bias=None, shared_slot=None, shared_layout: ExpertLayout | None = None,
+                 shared_gate=None, norm_weight=None, norm_eps: float = 1e-6):
+        import numpy as np
+
+        self.ctx = ctx
+        rw = np.ascontiguousarray(router_weight, np.float32)
+        E, H = rw.shape
+        keep = [rw]
+        d = LayerDesc()
+        d.hidden, d.experts, d.top_k, d.norm_topk_prob = H, E, top_k, int(bool(norm_topk_prob))
+        d.router_weight_host = rw.ctypes.data
+        if logit_bias is not None:
+            lb = np.ascontiguousarray(logit_bias, np.float32)
+            keep.append(lb)
+            d.logit_bias_host = lb.ctypes.data
+        if shared_slot is not None:
+            ss = np.ascontiguousarray(shared_slot, np.uint8)
+            sg = np.ascontiguousarray(shared_gate, np.float32)
+            keep += [ss, sg]
+            d.shared_slot_host = ss.ctypes.data
+            d.shared_layout = shared_layout
+            d.shared_gate_host = sg.ctypes.data
+        if norm_weight is not None:
+            nw = np.ascontiguousarray(norm_weight, np.float32)
+            keep.append(nw)
+            d.norm_weight_host = nw.ctypes.data
+        d.norm_eps = norm_eps
+        self.h = C.c_void_p()
+        ctx.check(lib().osm_layer_create(ctx.h, C.byref(d), C.byref(self.h)), "layer")
+        self.hidden, self.experts, self.top_k = H, E, top_k
+        self.has_shared = shared_slot is not None
+
+    def close(self):
+        if self.h:
+            lib().osm_layer_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def bind_slab(self, slab: Slab, slot_of_expert):
+        import numpy as np
+
+        so = np.ascontiguousarray(slot_of_expert, np.int32)
+        self.slab = slab
+        self.ctx.check(lib().osm_layer_bind_slab(self.h, slab.h, C.c_void_p(so.ctypes.data)), "bind")
+
+    def set_slot(self, expert: int, slot: int):
+        self.ctx.check(lib().osm_layer_set_slot(self.h, expert, slot), "set_slot")
+
+    def route_qwen_top_k(self, x, tokens, ids, weights, mass=None, exact=False):
+        self.ctx.check(lib().osm_moe_route(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
+                                           _ptr(mass), OSM_ROUTE_EXACT if exact else 0), "route")
+
+    def run_qwen_sparse_moe(self, x, tokens, out, ids=None, weights=None, mass=None,
+                            shared_gate=None, residual=None, exact_route=False):
+        flags = (OSM_ROUTE_EXACT if exact_route else 0) | (OSM_ADD_RESIDUAL if residual is not None else 0)
+        self.ctx.check(lib().osm_moe_forward(self.h, _ptr(x), tokens, _ptr(out), _ptr(ids),
+                                             _ptr(weights), _ptr(mass), _ptr(shared_gate),
+                                             _ptr(residual), flags), "moe_forward")
+
+    def run_experts(self, x, tokens, ids, weights, out, shared_gate=None, residual=None):
+        flags = OSM_ADD_RESIDUAL if residual is not None else 0
+        self.ctx.check(lib().osm_moe_experts(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
+                                             _ptr(out), _ptr(shared_gate), _ptr(residual), flags),
+                       "moe_experts")
+
+    def run_sublayer(self, residual, tokens, out, normalized=None, ids=None, weights=None,
+                     mass=None, shared_gate=None, exact_route=False, exact_rmsnorm=False):
+        flags = (OSM_ROUTE_EXACT if exact_route else 0) | (OSM_RMSNORM_EXACT if exact_rmsnorm else 0)
+        self.ctx.check(lib().osm_moe_sublayer_forward(self.h, _ptr(residual), tokens, _ptr(out),
+                                                      _ptr(normalized), _ptr(ids), _ptr(weights),
+                                                      _ptr(mass), _ptr(shared_gate), flags),
+                       "sublayer")
