@@ -217,6 +217,16 @@ int osm_moe_sublayer_forward(osm_layer* layer, const float* residual_dev,
 /* Number of kernels this library launched on `ctx` since creation. */
 uint64_t osm_context_launches(const osm_context* ctx);
 
+/* Per-kernel timing (no counterpart in the reference, which has no GPU
+ * timers): while enabled, every launch is bracketed by CUDA events on the
+ * context stream.  _read synchronises, adds each kind's elapsed milliseconds
+ * and launch count into ms[OSM_KERNEL_KINDS] / launches[OSM_KERNEL_KINDS]
+ * (either may be NULL) and clears the records. */
+#define OSM_KERNEL_KINDS 8
+int osm_context_profile(osm_context* ctx, int enable);
+int osm_context_profile_read(osm_context* ctx, double* ms, uint64_t* launches);
+const char* osm_kernel_kind_name(int kind);
+
 /* ---- synthetic data (seeded; identical stream on host and device) ---- */
 /* N(0, sigma) fp32 values of stream (seed, tensor), elements
  * [first, first + n), into device memory. */

@@ -58,6 +58,27 @@ struct Scratch {
 
 }  // namespace
 
+namespace {
+enum KernelKind {
+  kKRouterLogits = 0,
+  kKRouterSelect,
+  kKGateUp,
+  kKDown,
+  kKCombine,
+  kKRmsNorm,
+  kKPrep,
+  kKOther,
+};
+const char* const kKindNames[OSM_KERNEL_KINDS] = {
+    "router_logits", "router_select", "proj_gate_up", "proj_down",
+    "combine",       "rmsnorm",       "prep",         "other"};
+
+struct ProfRec {
+  int kind;
+  cudaEvent_t a, b;
+};
+}  // namespace
+
 struct osm_context {
   int device = 0;
   uint32_t max_tokens = 0;
@@ -66,6 +87,9 @@ struct osm_context {
   std::string err;
   uint64_t launches = 0;
   Scratch sc;
+  bool prof_on = false;
+  std::vector<cudaEvent_t> ev_pool;
+  std::vector<ProfRec> recs;
 };
 
 struct osm_slab {
@@ -116,6 +140,33 @@ int check_launch(osm_context* ctx, const char* what) {
   if (e != cudaSuccess) return cuda_fail(ctx, e, what);
   return OSM_OK;
 }
+
+cudaEvent_t pool_event(osm_context* ctx) {
+  if (!ctx->ev_pool.empty()) {
+    cudaEvent_t e = ctx->ev_pool.back();
+    ctx->ev_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// Bracket one launch with events on the context stream when profiling.
+struct Prof {
+  osm_context* ctx;
+  int idx = -1;
+  Prof(osm_context* c, int kind) : ctx(c) {
+    if (!ctx->prof_on) return;
+    ProfRec r{kind, pool_event(ctx), pool_event(ctx)};
+    cudaEventRecord(r.a, ctx->stream);
+    ctx->recs.push_back(r);
+    idx = (int)ctx->recs.size() - 1;
+  }
+  ~Prof() {
+    if (idx >= 0) cudaEventRecord(ctx->recs[idx].b, ctx->stream);
+  }
+};
 
 struct DeviceGuard {
   int prev = -1;
@@ -283,6 +334,15 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   return a;
 }
 
+void launch_router_pair(osm_context* ctx, const osm::RouterArgs& a) {
+  if (!a.skip_route) {
+    Prof p(ctx, kKRouterLogits);
+    osm::launch_router_logits(a, ctx->stream, &ctx->launches);
+  }
+  Prof p(ctx, kKRouterSelect);
+  osm::launch_router_select(a, ctx->stream, &ctx->launches);
+}
+
 int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
@@ -306,7 +366,10 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   gu.hfrag = s.hfrag;
   gu.hfsum8 = s.hfsum8;
   gu.hK = Imax;
-  osm::launch_proj(gu, true, Imax, max_active, ctx->stream, &ctx->launches);
+  {
+    Prof p(ctx, kKGateUp);
+    osm::launch_proj(gu, true, Imax, max_active, ctx->stream, &ctx->launches);
+  }
   int rc = check_launch(ctx, "gate/up projection");
   if (rc) return rc;
   osm::ProjArgs dn = gu;
@@ -322,7 +385,10 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   dn.pair_pick = s.pair_pick;
   dn.kp1 = (int)L->g.k + 1;
   dn.ostride = L->g.H;
-  osm::launch_proj(dn, false, L->g.H, max_active, ctx->stream, &ctx->launches);
+  {
+    Prof p(ctx, kKDown);
+    osm::launch_proj(dn, false, L->g.H, max_active, ctx->stream, &ctx->launches);
+  }
   rc = check_launch(ctx, "down projection");
   if (rc) return rc;
   osm::CombineArgs c{};
@@ -334,7 +400,10 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   c.B = (int)T;
   c.H = L->g.H;
   c.k = L->g.k;
-  osm::launch_combine(c, ctx->stream, &ctx->launches);
+  {
+    Prof p(ctx, kKCombine);
+    osm::launch_combine(c, ctx->stream, &ctx->launches);
+  }
   return check_launch(ctx, "combine");
 }
 
@@ -403,6 +472,11 @@ int osm_context_destroy(osm_context* ctx) {
   DeviceGuard dg(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->sc.base) cudaFree(ctx->sc.base);
+  for (const ProfRec& r : ctx->recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
   return OSM_OK;
@@ -412,6 +486,34 @@ const char* osm_last_error(const osm_context* ctx) { return ctx ? ctx->err.c_str
 int osm_context_device(const osm_context* ctx) { return ctx ? ctx->device : -1; }
 void* osm_context_stream(const osm_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
 uint64_t osm_context_launches(const osm_context* ctx) { return ctx ? ctx->launches : 0; }
+
+int osm_context_profile(osm_context* ctx, int enable) {
+  if (!ctx) return OSM_EINVAL;
+  ctx->prof_on = enable != 0;
+  return OSM_OK;
+}
+
+int osm_context_profile_read(osm_context* ctx, double* ms, uint64_t* launches) {
+  if (!ctx) return OSM_EINVAL;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  for (const ProfRec& r : ctx->recs) {
+    float t = 0.0f;
+    if (cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess && r.kind >= 0 &&
+        r.kind < OSM_KERNEL_KINDS) {
+      if (ms) ms[r.kind] += t;
+      if (launches) launches[r.kind] += 1;
+    }
+    ctx->ev_pool.push_back(r.a);
+    ctx->ev_pool.push_back(r.b);
+  }
+  ctx->recs.clear();
+  return OSM_OK;
+}
+
+const char* osm_kernel_kind_name(int kind) {
+  return (kind >= 0 && kind < OSM_KERNEL_KINDS) ? kKindNames[kind] : "unknown";
+}
 
 int osm_context_set_stream(osm_context* ctx, void* stream) {
   if (!ctx) return OSM_EINVAL;
@@ -704,8 +806,7 @@ int osm_layer_create(osm_context* ctx, const osm_layer_desc* d, osm_layer** out)
   if (d->top_k > d->experts) return fail(ctx, OSM_EINVAL, "qwen router: top_k cannot exceed expert_count");
   if (d->experts > (uint32_t)osm::kMaxExperts - 1 || d->top_k > (uint32_t)osm::kMaxTopK)
     return fail(ctx, OSM_EINVAL, "router: at most 1023 experts and top_k 32 are supported");
-  if (d->hidden > 8192 || d->hidden % 8)
-    return fail(ctx, OSM_EINVAL, "router: hidden must be a multiple of 8 and <= 8192");
+  if (d->hidden > 8192) return fail(ctx, OSM_EINVAL, "router: hidden must be <= 8192");
   if (!d->router_weight_host) return fail(ctx, OSM_EINVAL, "router weight missing");
   const size_t EH = (size_t)d->experts * d->hidden;
   bool bf16_exact = true;
@@ -838,7 +939,7 @@ int osm_moe_route(osm_layer* L, const float* x, uint32_t T, uint32_t* ids, float
   a.do_group = 0;
   a.xfrag = nullptr;
   a.sgate_w = nullptr;
-  osm::launch_router(a, ctx->stream, &ctx->launches);
+  launch_router_pair(ctx, a);
   return check_launch(ctx, "router");
 }
 
@@ -857,7 +958,7 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   a.mass_out = mass;
   a.sgate_out = sgate;
   a.do_group = 1;
-  osm::launch_router(a, ctx->stream, &ctx->launches);
+  launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");
   if (rc) return rc;
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
@@ -879,7 +980,7 @@ int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* id
   a.skip_route = 1;
   a.sgate_out = sgate;
   a.do_group = 1;
-  osm::launch_router(a, ctx->stream, &ctx->launches);
+  launch_router_pair(ctx, a);
   rc = check_launch(ctx, "expert grouping");
   if (rc) return rc;
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
@@ -894,8 +995,11 @@ int osm_moe_sublayer_forward(osm_layer* L, const float* residual, uint32_t T, fl
   if (!residual || !out) return fail(ctx, OSM_EINVAL, "sublayer: null input/output");
   DeviceGuard dg(ctx->device);
   float* nrm = normalized ? normalized : ctx->sc.normalized;
-  osm::launch_rmsnorm(residual, nrm, (int)T, L->g.H, L->norm_w, L->norm_eps,
-                      (flags & OSM_RMSNORM_EXACT) != 0, ctx->stream, &ctx->launches);
+  {
+    Prof p(ctx, kKRmsNorm);
+    osm::launch_rmsnorm(residual, nrm, (int)T, L->g.H, L->norm_w, L->norm_eps,
+                        (flags & OSM_RMSNORM_EXACT) != 0, ctx->stream, &ctx->launches);
+  }
   rc = check_launch(ctx, "sublayer rmsnorm");
   if (rc) return rc;
   return osm_moe_forward(L, nrm, T, out, ids, w, mass, sgate, residual, flags | OSM_ADD_RESIDUAL);

@@ -907,7 +907,7 @@ inline int grid_for(size_t n, int threads) {
 
 }  // namespace
 
-void launch_router(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
+void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
   const RouterGeom& g = a.g;
   const dim3 grid1((g.E + kRtExp * kRtWarps - 1) / (kRtExp * kRtWarps),
                    (a.B + kRtTok - 1) / kRtTok);
@@ -916,6 +916,11 @@ void launch_router(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
     cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)sm1);
   router_logits_kernel<<<grid1, kRtWarps * 32, sm1, s>>>(a);
+  if (launches) *launches += 1;
+}
+
+void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
+  const RouterGeom& g = a.g;
   const size_t sm_tok = (size_t)(g.H + 2 * g.E) * sizeof(float);
   const size_t sm_grp = (size_t)3 * (g.E + 1) * sizeof(int);
   const size_t sm2 = sm_tok > sm_grp ? sm_tok : sm_grp;
@@ -923,7 +928,7 @@ void launch_router(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
     cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)sm2);
   router_select_kernel<<<a.B, kSelThreads, sm2, s>>>(a);
-  if (launches) *launches += 2;
+  if (launches) *launches += 1;
 }
 
 void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {

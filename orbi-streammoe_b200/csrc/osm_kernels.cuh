@@ -61,7 +61,8 @@ struct RouterArgs {
   unsigned long long* exact_count;
 };
 
-void launch_router(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
+void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
+void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
 
 // Grouping alone (expert list from a routing already in scratch).
 void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches);

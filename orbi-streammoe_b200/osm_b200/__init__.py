@@ -87,6 +87,18 @@ class Context:
     def launches(self) -> int:
         return lib().osm_context_launches(self.h)
 
+    def profile(self, enable: bool):
+        self.check(lib().osm_context_profile(self.h, int(bool(enable))))
+
+    def profile_read(self) -> dict:
+        """{kernel kind: (total ms, launches)} since the last read."""
+        n = _lib.KERNEL_KINDS
+        ms = (C.c_double * n)()
+        cnt = (C.c_uint64 * n)()
+        self.check(lib().osm_context_profile_read(self.h, ms, cnt))
+        return {lib().osm_kernel_kind_name(i).decode(): (ms[i], cnt[i]) for i in range(n)
+                if cnt[i]}
+
     # ---- element-wise ops (Vulkan kernel replacements) ----
     def q4_dequant(self, packed, scales_bf16, biases_bf16, rows, in_dim, out, group=64):
         self.check(lib().osm_q4_dequant(self.h, _ptr(packed), _ptr(scales_bf16), _ptr(biases_bf16),

@@ -22,6 +22,8 @@ OSM_ROUTE_EXACT = 0x1
 OSM_RMSNORM_EXACT = 0x2
 OSM_ADD_RESIDUAL = 0x4
 
+KERNEL_KINDS = 8
+
 STATUS_NONFINITE = 1
 STATUS_BADMASS = 2
 STATUS_NOTRESIDENT = 4
@@ -59,6 +61,9 @@ _SIGS = {
     "osm_context_synchronize": (C.c_int, [_P]),
     "osm_context_status": (C.c_int, [_P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)]),
     "osm_context_launches": (C.c_uint64, [_P]),
+    "osm_context_profile": (C.c_int, [_P, C.c_int]),
+    "osm_context_profile_read": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "osm_kernel_kind_name": (C.c_char_p, [C.c_int]),
     "osm_device_alloc": (C.c_int, [_P, C.c_size_t, C.POINTER(_P)]),
     "osm_device_free": (C.c_int, [_P, _P]),
     "osm_upload": (C.c_int, [_P, _P, _P, C.c_size_t]),
