@@ -1,0 +1,470 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 routed-MoE sublayer (Qwen3-Next-80B-A3B shape).
+
+Workload: one sublayer with all 512 Q4 experts resident
+in HBM (hidden 2048, top-10 renormalised, inter 512, shared expert 512,
+sigmoid scalar gate), router logits biased by Zipf(1.1) over a seeded expert
+permutation, decode batches B = 1, 8, 32, 64, 128, 256.  One step = one
+sublayer call per batch size (489 tokens).  Synthetic seeded data.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Timing: L2 (126 MB) is flushed by a 256 MiB write before every call; each call
+is bracketed by CUDA events on the stream it runs on; value = tokens / sum of
+call intervals (max over ranks).  e2e = the same calls through pinned host
+buffers, H2D of x and D2H of the output inside the intervals.  The roofline
+names the kernel with the largest share of device time, timed by the
+library's per-kernel events on its stream.  --gpus N > 1 runs N independent
+replicas (the decode path does not shard): scaling "weak".
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "orbi-streammoe_b200"))
+
+import numpy as np  # noqa: E402
+
+SWEEP = (1, 8, 32, 64, 128, 256)
+H, E, I, K, SHI, GROUP = 2048, 512, 512, 10, 512, 64
+SEED = 20241201
+ZIPF_S = 1.1
+METRIC = "routed-MoE sublayer tokens/s (Qwen3-Next-80B-A3B shape); decode µs/layer; HBM GB/s"
+WORKLOAD = ("configs[1]: Qwen3-Next-80B-A3B routed-MoE sublayer, decode batches "
+            "1,8,32,64,128,256, Zipf(1.1) router bias, all 512 Q4 experts in HBM")
+# bytes of one Q4 expert slot (gate/up/down U32 + BF16 scale/bias)
+S_EXPERT = 1769472
+S_GATEUP = 1179648   # gate + up sections
+S_DOWN = 589824
+S_ROUTER = E * H * 2
+S_SGATE = H * 2
+# Per-launch DRAM traffic of proj_gate_up, B=1 launch (ncu, see profiles/);
+# None until a capture exists for the current kernel.
+NCU_GATEUP_TRAFFIC_B1 = None
+
+
+def bf16_round(v: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(v, np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint32) << 16
+    return r.astype(np.uint32).view(np.float32)
+
+
+def zipf_bias(E: int, s: float, seed: int) -> np.ndarray:
+    r = np.arange(1, E + 1, dtype=np.float64)
+    perm = np.random.default_rng(seed).permutation(E)
+    b = np.zeros(E, np.float32)
+    b[perm] = np.log(r ** -s / (r ** -s).sum()).astype(np.float32)
+    return b
+
+
+def load_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of this GPU while the timed work runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_id}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.t:
+            self.t.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [s for s, p in zip(sm, power) if p > 200.0] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+def build_sublayer(torch, ctx, osm):
+    lay = osm.expert_layout(H, I, GROUP)
+    slab = osm.Slab(ctx, lay, E)
+    slab.generate(SEED, 1000, 0.02, 0, E)
+    sh_slab = osm.Slab(ctx, lay, 1)
+    sh_slab.generate(SEED, 1000 + 3 * E, 0.02, 0, 1)
+    buf = torch.empty(E * H, device="cuda")
+    ctx.gen_normal(SEED, 1, 0.02, buf)
+    W = bf16_round(buf.cpu().numpy()).reshape(E, H)
+    g = torch.empty(H, device="cuda")
+    ctx.gen_normal(SEED, 2, 0.02, g)
+    sg = bf16_round(g.cpu().numpy())
+    ctx.synchronize()
+    import ctypes
+
+    shared = np.zeros(lay.stride, np.uint8)
+    ctx.check(osm.lib().osm_download(ctx.h, ctypes.c_void_p(shared.ctypes.data),
+                                     ctypes.c_void_p(sh_slab.slot_ptr(0)), lay.stride))
+    sh_slab.close()
+    bias = zipf_bias(E, ZIPF_S, SEED)
+    layer = osm.Layer(ctx, W, K, True, logit_bias=bias, shared_slot=shared, shared_layout=lay,
+                      shared_gate=sg)
+    layer.bind_slab(slab, np.arange(E, dtype=np.int32))
+    return layer, slab, W, sg, bias, shared
+
+
+def sublayer_bytes(B: int, U: int) -> int:
+    """Algorithmic bytes of one call (U distinct routed experts)."""
+    return U * S_EXPERT + S_EXPERT + S_ROUTER + S_SGATE + B * H * 8
+
+
+def kernel_bytes(kind: str, B: int, U: int) -> int:
+    P = B * (K + 1)
+    if kind == "proj_gate_up":
+        return (U + 1) * S_GATEUP + B * H * 4 + P * I * 4
+    if kind == "proj_down":
+        return (U + 1) * S_DOWN + P * I * 4 + P * H * 4
+    if kind == "router_logits":
+        return S_ROUTER + B * H * 4 + B * E * 8
+    if kind == "router_select":
+        return B * E * 8 + B * H * 4 + B * H * 8
+    if kind == "combine":
+        return P * H * 4 + B * H * 4
+    return 0
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    import osm_b200 as osm
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.current_stream()
+    ctx = osm.Context(local_rank, max_tokens=max(SWEEP))
+    ctx.set_stream(stream.cuda_stream)
+    layer, slab, W, sg, bias, shared = build_sublayer(torch, ctx, osm)
+    xs, outs, hx, hout = {}, {}, {}, {}
+    ids_d = {}
+    for B in SWEEP:
+        x = torch.empty(B, H, device=dev)
+        ctx.gen_normal(SEED, 5000 + B, 1.0, x)
+        xs[B] = x
+        outs[B] = torch.empty(B, H, device=dev)
+        ids_d[B] = torch.empty(B, K, dtype=torch.int32, device=dev)
+        hx[B] = x.cpu().pin_memory()
+        hout[B] = torch.empty(B, H).pin_memory()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def call(B, e2e):
+        if e2e:
+            xs[B].copy_(hx[B], non_blocking=True)
+        layer.run_qwen_sparse_moe(xs[B], B, outs[B], ids=ids_d[B])
+        if e2e:
+            hout[B].copy_(outs[B], non_blocking=True)
+
+    def timed_pass(steps, e2e):
+        evs = []
+        for _ in range(steps):
+            for B in SWEEP:
+                flush.zero_()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                call(B, e2e)
+                b.record(stream)
+                evs.append((B, a, b))
+        return evs
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    gpu_uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local_rank))
+    if gpu_uuid and not gpu_uuid.startswith("GPU-") and len(gpu_uuid) > 8:
+        gpu_uuid = "GPU-" + gpu_uuid
+    clocks = ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else str(local_rank))
+
+    timed_pass(args.warmup, False)
+    timed_pass(max(1, args.warmup // 2), True)
+    torch.cuda.synchronize()
+    ctx.status()
+    clocks.start()
+    # ---- value: inputs resident in HBM ----
+    barrier()
+    torch.cuda.synchronize()
+    l0 = ctx.launches
+    t_wall = time.perf_counter()
+    evs = timed_pass(args.steps, False)
+    torch.cuda.synchronize()
+    barrier()
+    bracket_s = time.perf_counter() - t_wall
+    launches = ctx.launches - l0
+    per_b = {B: 0.0 for B in SWEEP}
+    for B, a, b in evs:
+        per_b[B] += a.elapsed_time(b)
+    total_ms = sum(per_b.values())
+    # ---- e2e: host buffers, copies inside the intervals ----
+    barrier()
+    torch.cuda.synchronize()
+    evs2 = timed_pass(args.steps, True)
+    torch.cuda.synchronize()
+    barrier()
+    total_ms_e2e = sum(a.elapsed_time(b) for _, a, b in evs2)
+    # ---- per-kernel profile pass (roofline) ----
+    uniq = {}
+    for B in SWEEP:
+        layer.run_qwen_sparse_moe(xs[B], B, outs[B], ids=ids_d[B])
+        torch.cuda.synchronize()
+        uniq[B] = int(np.unique(ids_d[B].cpu().numpy()).size)
+    ctx.profile_read()
+    ctx.profile(True)
+    prof_steps = max(1, min(args.steps, 50))
+    kbytes = {}
+    for _ in range(prof_steps):
+        for B in SWEEP:
+            flush.zero_()
+            layer.run_qwen_sparse_moe(xs[B], B, outs[B], ids=ids_d[B])
+            for kind in ("proj_gate_up", "proj_down", "router_logits", "router_select", "combine"):
+                kbytes[kind] = kbytes.get(kind, 0) + kernel_bytes(kind, B, uniq[B])
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    clk = clocks.stop()
+    status, exact_tokens = ctx.status()
+    if status:
+        raise RuntimeError(f"device status {status} during the benchmark")
+
+    tokens_per_step = sum(SWEEP)
+    total_ms = max_over_ranks(total_ms)
+    total_ms_e2e = max_over_ranks(total_ms_e2e)
+    value = world * tokens_per_step * args.steps / (total_ms / 1e3)
+    e2e_value = world * tokens_per_step * args.steps / (total_ms_e2e / 1e3)
+    peaks = load_peaks()
+    dom = max(prof.items(), key=lambda kv: kv[1][0])
+    dom_kind, (dom_ms, dom_n) = dom
+    achieved = kbytes[dom_kind] / (dom_ms / 1e3) / 1e9
+    sweep = {}
+    for B in SWEEP:
+        us = per_b[B] / args.steps * 1e3
+        byt = sublayer_bytes(B, uniq[B])
+        sweep[str(B)] = {"us_per_call": round(us, 2), "distinct_experts": uniq[B],
+                         "alg_bytes": byt, "gbs": round(byt / us / 1e3, 1),
+                         "frac_hbm": round(byt / us / 1e3 / peaks["hbm_gbs"], 3)}
+    kernels = {k: {"ms": round(v[0], 3), "launches": int(v[1]),
+                   "share": round(v[0] / sum(x[0] for x in prof.values()), 3)} for k, v in prof.items()}
+    traffic = None
+    if NCU_GATEUP_TRAFFIC_B1 is not None and dom_kind == "proj_gate_up":
+        traffic = NCU_GATEUP_TRAFFIC_B1
+    h2d = sum(B * H * 4 for B in SWEEP)
+    line = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp32",
+        "data": "synthetic (seeded N(0,0.02) weights, reference quantiser, bf16 scale/bias; x~N(0,1))",
+        "config": {"workload": WORKLOAD, "tokens_per_step": tokens_per_step,
+                   "hidden": H, "experts": E, "top_k": K, "moe_inter": I, "shared_inter": SHI,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
+                   "timing": "sum of per-call CUDA-event intervals on the launching stream",
+                   "bracket_wall_s": round(bracket_s, 3),
+                   "exact_route_tokens": int(exact_tokens),
+                   "per_batch": sweep, "kernels": kernels},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": h2d},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": dom_kind, "achieved": round(achieved, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_leg(torch, ctx, slab, W, sg, bias, shared, xs, osm)
+    return line
+
+
+def cpu_baseline_leg(torch, ctx, slab, W, sg, bias, shared, xs, osm):
+    """The reference CPU path on the host cores on a bounded sample (the B=32
+    batch of the sweep), token-parallel over all threads."""
+    import ctypes
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import cpu_baseline as cb
+
+    lay = osm.expert_layout(H, I, GROUP)
+    slots = np.zeros((E, lay.stride), np.uint8)
+    ctx.check(osm.lib().osm_download(ctx.h, ctypes.c_void_p(slots.ctypes.data),
+                                     ctypes.c_void_p(slab.slot_ptr(0)), E * lay.stride))
+    x = xs[32].cpu().numpy()
+    threads = cb.cpu_count()
+    sub = cb.Sublayer(slots, shared, W, sg, bias, H, I, K, threads)
+    sub.prepare(x)
+    secs, n = 0.0, 0
+    while secs < 5.0 and n < 200:
+        secs += sub.run(x, threads)
+        n += 1
+    st = sub.run(x[:4], 1)
+    return {"value": round(n * x.shape[0] / secs, 2), "unit": "tokens/s", "cores": threads,
+            "kind": sub.kind,
+            "sample": f"the B=32 decode batch of the sweep, {n} passes, {threads} threads; "
+                      f"dequantisation of {len(sub.deq)} experts excluded ({sub.dequant_s:.1f} s)",
+            "single_thread_tokens_per_s": round(4 / st, 2), "cpu_model": cb.cpu_model()}
+
+
+# ----------------------------------------------------------------------------
+# reference arm
+# ----------------------------------------------------------------------------
+def run_reference(args, rank, world):
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import cpu_baseline as cb
+    import pyoracle
+
+    if rank != 0:
+        return None
+    port = pyoracle.Oracle("port")
+    threads = cb.cpu_count()
+    W = bf16_round(port.gen_normal(SEED, 1, 0.02, E * H)).reshape(E, H)
+    sg = bf16_round(port.gen_normal(SEED, 2, 0.02, H))
+    bias = zipf_bias(E, ZIPF_S, SEED)
+    shared = port.gen_expert_slot(SEED, 1000 + 3 * E, 0.02, H, I)
+    # bounded sample: the B=1, B=8 and B=32 batches of the sweep (41 tokens)
+    x = np.concatenate([port.gen_normal(SEED, 5000 + B, 1.0, B * H).reshape(B, H)
+                        for B in (1, 8, 32)])
+    stride = pyoracle.slot_stride(H, I)
+    slots = np.zeros((E, stride), np.uint8)
+    sub = cb.Sublayer(slots, shared, W, sg, bias, H, I, K, threads)
+    need = sorted(sub.route_ids(x))
+    from concurrent.futures import ThreadPoolExecutor
+
+    def gen(e):
+        slots[e] = port.gen_expert_slot(SEED, 1000 + 3 * e, 0.02, H, I)
+
+    with ThreadPoolExecutor(threads) as ex:
+        list(ex.map(gen, need))
+    sub.prepare(x)
+    for _ in range(args.warmup):
+        sub.run(x, threads)
+    secs = sum(sub.run(x, threads) for _ in range(args.steps))
+    value = args.steps * x.shape[0] / secs
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "impl": "reference",
+        "data": "synthetic (same seeds as our arm)",
+        "config": {"workload": WORKLOAD, "tokens_per_step": int(x.shape[0]),
+                   "sample": "B=1, 8 and 32 batches of the sweep per step"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads,
+                         "kind": sub.kind,
+                         "sample": f"{x.shape[0]} tokens per step (B=1,8,32 batches), "
+                                   f"{len(sub.deq)} experts dequantised once "
+                                   f"({sub.dequant_s:.1f} s, excluded)",
+                         "cpu_model": cb.cpu_model()},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch
+
+            torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
