@@ -265,7 +265,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
 bool layout_ok(const osm_expert_layout* L) {
   if (!L || L->group != 64 || L->hidden == 0 || L->inter == 0) return false;
   if (L->hidden % 64 || L->inter % 64) return false;
-  if (L->hidden > 2048 || L->inter > 2048) return false;  // K <= 2048 per projection
+  if (L->hidden > 2048 || L->inter > 768) return false;  // gate/up K <= 2048, down K <= 768
   if (L->hidden % 16 || L->inter % 8) return false;
   const uint64_t H = L->hidden, I = L->inter;
   const uint64_t gu_w = I * H / 2, gu_m = I * (H / 64) * 2, dn_w = H * I / 2,
@@ -360,6 +360,8 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   gu.pair_tok = s.pair_tok;
   gu.frag_by_pair = 0;
   gu.raw = 0;
+  gu.shared_first = L->shared_slot ? 1 : 0;
+  gu.shared_ptr = L->shared_slot;
   gu.frag_stride = L->g.H / 8;
   gu.frag = s.xfrag;
   gu.fsum8 = s.xfsum8;
@@ -368,7 +370,7 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   gu.hK = Imax;
   {
     Prof p(ctx, kKGateUp);
-    osm::launch_proj(gu, true, Imax, max_active, ctx->stream, &ctx->launches);
+    osm::launch_proj(gu, osm::ProjKind::kGateUp, Imax, max_active, ctx->stream, &ctx->launches);
   }
   int rc = check_launch(ctx, "gate/up projection");
   if (rc) return rc;
@@ -387,7 +389,8 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   dn.ostride = L->g.H;
   {
     Prof p(ctx, kKDown);
-    osm::launch_proj(dn, false, L->g.H, max_active, ctx->stream, &ctx->launches);
+    osm::launch_proj(dn, Imax <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12, L->g.H,
+                     max_active, ctx->stream, &ctx->launches);
   }
   rc = check_launch(ctx, "down projection");
   if (rc) return rc;
@@ -638,7 +641,7 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
   a.pair_pick = s.pair_pick;
   a.kp1 = 1;
   a.ostride = (int)out_dim;
-  osm::launch_proj(a, false, (int)out_dim, 1, ctx->stream, &ctx->launches);
+  osm::launch_proj(a, osm::ProjKind::kSingle, (int)out_dim, 1, ctx->stream, &ctx->launches);
   return check_launch(ctx, "q4 gemv");
 }
 
@@ -700,7 +703,7 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   gu.hfrag = s.hfrag;
   gu.hfsum8 = s.hfsum8;
   gu.hK = (int)L.inter;
-  osm::launch_proj(gu, true, (int)L.inter, 1, ctx->stream, &ctx->launches);
+  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, 1, ctx->stream, &ctx->launches);
   rc = check_launch(ctx, "expert gate/up");
   if (rc) return rc;
   osm::ProjArgs dn = gu;
@@ -714,7 +717,8 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   dn.pair_pick = s.pair_pick;
   dn.kp1 = 1;
   dn.ostride = (int)L.hidden;
-  osm::launch_proj(dn, false, (int)L.hidden, 1, ctx->stream, &ctx->launches);
+  osm::launch_proj(dn, L.inter <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12,
+                   (int)L.hidden, 1, ctx->stream, &ctx->launches);
   return check_launch(ctx, "expert down");
 }
 

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <math.h>
 #include <stdint.h>
 
 namespace osm {
@@ -82,6 +83,46 @@ __device__ __forceinline__ float ref_sigmoid(float v) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v)));
 }
 __device__ __forceinline__ float ref_silu(float v) { return __fmul_rn(v, ref_sigmoid(v)); }
+
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialisation attribute may start before its predecessor ends;
+// pdl_wait() blocks until the predecessor has completed and flushed memory
+// (a no-op for ordinary launches), pdl_trigger() lets the successor start.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Monotone map of finite floats (and -inf) to unsigned keys.
+__device__ __forceinline__ uint32_t ord_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Block reductions over blockDim.x threads (<= 1024); `red` holds 32 floats.
+__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.0f;
+  const int nw = blockDim.x >> 5;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  return s;
+}
+
+__device__ __forceinline__ float block_reduce_max(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = -INFINITY;
+  const int nw = blockDim.x >> 5;
+  for (int w = 0; w < nw; ++w) s = fmaxf(s, red[w]);
+  return s;
+}
 
 __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
   uint64_t z = x + 0x9E3779B97F4A7C15ull;

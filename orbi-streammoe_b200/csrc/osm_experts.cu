@@ -1,0 +1,330 @@
+// osm_experts.cu -- Q4 expert projections on sm_100a (replace
+// shaders/q4_gemv.comp, shaders/swiglu.comp and the per-expert submits of
+// src/backend/vulkan_resident_expert.cpp:286-365).
+//
+// proj_kernel<PAIRED, KSPLIT, MAXG> computes, for every active expert and
+// every token routed to it, one output tile with mma.sync m16n8k16:
+//   A = 16 weight rows x 16 inputs: the Q4 nibbles as exact bf16 integers,
+//   B = 16 inputs x 8 tokens: the activation split into bf16 hi + lo,
+//   D = fp32 per 64-input group, then acc += s * D + b * sum(x)
+// (the group identity of shaders/q4_gemv.comp:44-60 with the reference's
+// dequantised value s*q + b).  PAIRED tiles hold gate rows r..r+7 in MMA rows
+// 0-7 and the matching up rows in MMA rows 8-15, so each thread owns gate and
+// up of the same (row, token) and applies SwiGLU in registers; the result is
+// written as the next projection's activation fragments.  KSPLIT warps share
+// one tile's input range; 4 / KSPLIT tiles per CTA.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "osm_common.cuh"
+#include "osm_kernels.cuh"
+
+namespace osm {
+namespace {
+
+constexpr int kWarps = 4;
+
+__device__ __forceinline__ void mma_group(float d[4], uint2 wl, uint2 wh, const uint4 (&xf)[4]) {
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    const uint32_t wlo = jj ? wl.y : wl.x;
+    const uint32_t whi = jj ? wh.y : wh.x;
+    const uint4 xh = xf[2 * jj], xl = xf[2 * jj + 1];
+    {
+      const uint32_t a0 = nibble_pair_bf16(wlo, 0), a2 = nibble_pair_bf16(wlo, 1);
+      const uint32_t a1 = nibble_pair_bf16(whi, 0), a3 = nibble_pair_bf16(whi, 1);
+      mma_bf16_16816(d, a0, a1, a2, a3, xh.x, xh.y);
+      mma_bf16_16816(d, a0, a1, a2, a3, xl.x, xl.y);
+    }
+    {
+      const uint32_t a0 = nibble_pair_bf16(wlo, 2), a2 = nibble_pair_bf16(wlo, 3);
+      const uint32_t a1 = nibble_pair_bf16(whi, 2), a3 = nibble_pair_bf16(whi, 3);
+      mma_bf16_16816(d, a0, a1, a2, a3, xh.z, xh.w);
+      mma_bf16_16816(d, a0, a1, a2, a3, xl.z, xl.w);
+    }
+  }
+}
+
+template <bool PAIRED, int KSPLIT, int MAXG>
+__global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjArgs a) {
+  constexpr int TILES = kWarps / KSPLIT;
+  constexpr int TROWS = PAIRED ? 8 : 16;
+  const int j = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, t = lane & 3;
+  const int tile = warp / KSPLIT, ks = warp - tile * KSPLIT;
+  // The shared expert is active entry 0: its weights are known before the
+  // routing is, so they are fetched before waiting on the router.
+  const bool early = a.shared_first && j == 0;
+  const uint8_t* base = early ? a.shared_ptr : nullptr;
+  int kind = 1;
+  uint2 wl[MAXG], wh[MAXG];
+  uint32_t sp[MAXG], bp[MAXG];  // bf16 pairs (lo row, hi row) of scale / bias
+  int rows = 0, K = 0, r0 = 0, G = 0, KW = 0;
+  auto fetch = [&]() {
+    rows = a.sec.rows[kind];
+    K = a.sec.K[kind];
+    G = K >> 6;
+    KW = K >> 3;
+    r0 = (blockIdx.x * TILES + tile) * TROWS;
+    const uintptr_t ub = reinterpret_cast<uintptr_t>(base);
+    const uint32_t* Wlo = reinterpret_cast<const uint32_t*>(ub + a.sec.w[kind]);
+    const uint16_t* Slo = reinterpret_cast<const uint16_t*>(ub + a.sec.s[kind]);
+    const uint16_t* Blo = reinterpret_cast<const uint16_t*>(ub + a.sec.b[kind]);
+    const uint32_t* Whi = PAIRED ? reinterpret_cast<const uint32_t*>(ub + a.sec.w2[kind]) : Wlo;
+    const uint16_t* Shi = PAIRED ? reinterpret_cast<const uint16_t*>(ub + a.sec.s2[kind]) : Slo;
+    const uint16_t* Bhi = PAIRED ? reinterpret_cast<const uint16_t*>(ub + a.sec.b2[kind]) : Blo;
+    const int row_lo = r0 + gid;
+    const int row_hi = PAIRED ? r0 + gid : r0 + 8 + gid;
+    const bool live = r0 < rows;
+#pragma unroll
+    for (int i = 0; i < MAXG; ++i) {
+      const int g = ks + KSPLIT * i;
+      if (live && g < G) {
+        wl[i] = __ldg(reinterpret_cast<const uint2*>(Wlo + (size_t)row_lo * KW + g * 8 + 2 * t));
+        wh[i] = __ldg(reinterpret_cast<const uint2*>(Whi + (size_t)row_hi * KW + g * 8 + 2 * t));
+        sp[i] = pack2(__ldg(Slo + (size_t)row_lo * G + g), __ldg(Shi + (size_t)row_hi * G + g));
+        bp[i] = pack2(__ldg(Blo + (size_t)row_lo * G + g), __ldg(Bhi + (size_t)row_hi * G + g));
+      } else {
+        wl[i] = wh[i] = make_uint2(0u, 0u);
+        sp[i] = bp[i] = 0u;
+      }
+    }
+  };
+  if (early) fetch();
+  pdl_wait();
+  pdl_trigger();
+  if (j >= *a.n_active) return;
+  if (!early) {
+    base = a.act_ptr[j];
+    kind = a.act_kind[j];
+    if (base == nullptr && !a.raw) return;  // non-resident expert (status already set)
+    fetch();
+  }
+  if ((blockIdx.x * TILES) * TROWS >= rows) return;
+
+  __shared__ float fsg[8][33];
+  __shared__ int rowof[8];
+  __shared__ float red[kWarps][32][4];
+  __shared__ float hs[TILES][8][9];
+  const int off = a.act_off[j], cnt = a.act_cnt[j];
+  const bool live = r0 < rows;
+  for (int c0 = 0; c0 < cnt; c0 += 8) {
+    const int nv = min(8, cnt - c0);
+    if (threadIdx.x < 8) {
+      const int p = off + c0 + threadIdx.x;
+      rowof[threadIdx.x] = threadIdx.x < nv ? (a.frag_by_pair ? p : a.pair_tok[p]) : 0;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 8 * G; i += blockDim.x) {
+      const int n = i / G, g = i - n * G;
+      float s = 0.0f;
+      if (n < nv) {
+        const float4* f = reinterpret_cast<const float4*>(a.fsum8 + (size_t)rowof[n] * a.frag_stride + g * 8);
+        const float4 u = f[0], w = f[1];
+        s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(u.x, u.y), u.z), u.w), w.x), w.y), w.z), w.w);
+      }
+      fsg[n][g] = s;
+    }
+    __syncthreads();
+    const bool has_tok = gid < nv;
+    const uint4* xf = a.frag + (size_t)rowof[has_tok ? gid : 0] * a.frag_stride * 2;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    uint4 cur[4], nxt[4];
+    auto load_x = [&](int i, uint4 (&dst)[4]) {
+      const int g = ks + KSPLIT * i;
+      if (has_tok && live && g < G) {
+        const int c = 8 * g + 2 * t;
+        dst[0] = __ldg(xf + 2 * c);
+        dst[1] = __ldg(xf + 2 * c + 1);
+        dst[2] = __ldg(xf + 2 * c + 2);
+        dst[3] = __ldg(xf + 2 * c + 3);
+      } else {
+        dst[0] = dst[1] = dst[2] = dst[3] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    load_x(0, cur);
+#pragma unroll
+    for (int i = 0; i < MAXG; ++i) {
+      const int g = ks + KSPLIT * i;
+      if (i + 1 < MAXG) load_x(i + 1, nxt);
+      if (g < G) {
+        float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        mma_group(d, wl[i], wh[i], cur);
+        const float f0 = fsg[2 * t][g], f1 = fsg[2 * t + 1][g];
+        const float sl = bf16_bits_to_f32(sp[i] & 0xFFFFu), sh = bf16_bits_to_f32(sp[i] >> 16);
+        const float bl = bf16_bits_to_f32(bp[i] & 0xFFFFu), bh = bf16_bits_to_f32(bp[i] >> 16);
+        acc[0] = fmaf(bl, f0, fmaf(sl, d[0], acc[0]));
+        acc[1] = fmaf(bl, f1, fmaf(sl, d[1], acc[1]));
+        acc[2] = fmaf(bh, f0, fmaf(sh, d[2], acc[2]));
+        acc[3] = fmaf(bh, f1, fmaf(sh, d[3], acc[3]));
+      }
+      if (i + 1 < MAXG) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
+      }
+    }
+    float tot[4] = {acc[0], acc[1], acc[2], acc[3]};
+    if (KSPLIT > 1) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) red[warp][lane][q] = acc[q];
+      __syncthreads();
+      if (ks == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float s = red[warp][lane][q];
+#pragma unroll
+          for (int w = 1; w < KSPLIT; ++w) s = __fadd_rn(s, red[warp + w][lane][q]);
+          tot[q] = s;
+        }
+      }
+    }
+    if (ks == 0 && live) {
+      if (PAIRED) {
+        // thread (gid, t): gate/up of intermediate row r0+gid, tokens 2t, 2t+1
+        hs[tile][gid][2 * t] = __fmul_rn(ref_silu(tot[0]), tot[2]);
+        hs[tile][gid][2 * t + 1] = __fmul_rn(ref_silu(tot[1]), tot[3]);
+        __syncwarp();
+        if (lane < nv) {
+          const int p = off + c0 + lane;
+          const int hch = a.hK >> 3;
+          uint32_t hi[8], lo[8];
+          float fs = hs[tile][0][lane];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) split_bf16(hs[tile][r][lane], hi[r], lo[r]);
+#pragma unroll
+          for (int r = 1; r < 8; ++r) fs = __fadd_rn(fs, hs[tile][r][lane]);
+          uint4* dst = a.hfrag + ((size_t)p * hch + (r0 >> 3)) * 2;
+          dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
+                              pack2(hi[3], hi[7]));
+          dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
+                              pack2(lo[3], lo[7]));
+          a.hfsum8[(size_t)p * hch + (r0 >> 3)] = fs;
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int n = 2 * t + q;
+          if (n < nv) {
+            const int p = off + c0 + n;
+            const int orow = a.out_row ? a.out_row[p] : a.pair_tok[p] * a.kp1 + a.pair_pick[p];
+            float* o = a.out + (size_t)orow * a.ostride;
+            o[r0 + gid] = tot[q];
+            o[r0 + 8 + gid] = tot[2 + q];
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void frag_prep_kernel(const float* __restrict__ x, int rows, int K,
+                                 uint4* __restrict__ frag, float* __restrict__ fsum8) {
+  pdl_wait();
+  pdl_trigger();
+  const int nch = K >> 3;
+  const size_t total = (size_t)rows * nch;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / nch, c = i - r * nch;
+    const float* xc = x + r * K + c * 8;
+    const float4 p = *reinterpret_cast<const float4*>(xc);
+    const float4 q = *reinterpret_cast<const float4*>(xc + 4);
+    const float v[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+    uint32_t hi[8], lo[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) split_bf16(v[j], hi[j], lo[j]);
+    float fs = v[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, v[j]);
+    frag[i * 2] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
+                             pack2(hi[3], hi[7]));
+    frag[i * 2 + 1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
+                                 pack2(lo[3], lo[7]));
+    fsum8[i] = fs;
+  }
+}
+
+// Expert list for a single expert over `T` tokens (standalone projections).
+__global__ void setup_single_kernel(int T, const uint8_t* ptr, int* n_active, int* act_kind,
+                                    const uint8_t** act_ptr, int* act_off, int* act_cnt,
+                                    int* pair_tok, int* pair_pick, int* out_row) {
+  pdl_wait();
+  pdl_trigger();
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    *n_active = 1;
+    act_kind[0] = 0;
+    act_ptr[0] = ptr;
+    act_off[0] = 0;
+    act_cnt[0] = T;
+  }
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x) {
+    pair_tok[i] = i;
+    pair_pick[i] = 0;
+    out_row[i] = i;
+  }
+}
+
+template <typename K, typename... Args>
+void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int grid_for(size_t n, int threads) {
+  size_t b = (n + threads - 1) / threads;
+  if (b > 148 * 64) b = 148 * 64;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace
+
+void launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8, cudaStream_t s,
+                      uint64_t* launches) {
+  const size_t n = (size_t)rows * (K >> 3);
+  launch_pdl(frag_prep_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, rows, K, frag, fsum8);
+  if (launches) *launches += 1;
+}
+
+void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active, cudaStream_t s,
+                 uint64_t* launches) {
+  switch (kind) {
+    case ProjKind::kGateUp:  // 8 intermediate rows per CTA, input split over 4 warps
+      launch_pdl(proj_kernel<true, 4, 8>, dim3((max_rows + 7) / 8, max_active), dim3(kWarps * 32),
+                 0, s, a);
+      break;
+    case ProjKind::kDown:    // 64 output rows per CTA, one warp per 16-row tile (K <= 512)
+      launch_pdl(proj_kernel<false, 1, 8>, dim3((max_rows + 63) / 64, max_active),
+                 dim3(kWarps * 32), 0, s, a);
+      break;
+    case ProjKind::kDown12:  // the same for K <= 768
+      launch_pdl(proj_kernel<false, 1, 12>, dim3((max_rows + 63) / 64, max_active),
+                 dim3(kWarps * 32), 0, s, a);
+      break;
+    case ProjKind::kSingle:  // 16 rows per CTA, input split over 4 warps (K <= 2048)
+      launch_pdl(proj_kernel<false, 4, 8>, dim3((max_rows + 15) / 16, max_active),
+                 dim3(kWarps * 32), 0, s, a);
+      break;
+  }
+  if (launches) *launches += 1;
+}
+
+void launch_setup_single(int T, const uint8_t* ptr, int* n_active, int* act_kind,
+                         const uint8_t** act_ptr, int* act_off, int* act_cnt, int* pair_tok,
+                         int* pair_pick, int* out_row, cudaStream_t s, uint64_t* launches) {
+  launch_pdl(setup_single_kernel, dim3(grid_for((size_t)T, 256)), dim3(256), 0, s, T, ptr,
+             n_active, act_kind, act_ptr, act_off, act_cnt, pair_tok, pair_pick, out_row);
+  if (launches) *launches += 1;
+}
+
+}  // namespace osm

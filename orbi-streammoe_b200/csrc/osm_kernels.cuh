@@ -85,6 +85,8 @@ struct ProjSections {
 
 struct ProjArgs {
   ProjSections sec;
+  int shared_first;              // active entry 0 is the shared expert (layout 1)
+  const uint8_t* shared_ptr;     // its slot, readable before the routing exists
   const int* n_active;
   const int* act_kind;
   const uint8_t* const* act_ptr;
@@ -108,7 +110,8 @@ struct ProjArgs {
   int ostride;
 };
 
-void launch_proj(const ProjArgs& a, bool paired, int max_rows, int max_active,
+enum class ProjKind { kGateUp, kDown, kDown12, kSingle };
+void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active,
                  cudaStream_t s, uint64_t* launches);
 
 struct CombineArgs {

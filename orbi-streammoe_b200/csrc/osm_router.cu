@@ -1,0 +1,731 @@
+// osm_router.cu -- the Qwen router on sm_100a (replaces route_qwen_top_k_cpu,
+// src/model/qwen_router.cpp:11-94, and the host grouping of
+// src/model/routed_moe.cpp:320-370).
+//
+// router_logits_kernel<EXP, TOKS>
+//   fp32 logits on CUDA cores.  Lane l of a warp owns the contiguous chunk
+//   [l*c, (l+1)*c) of the hidden dimension (weights stored in that order, see
+//   osm_kernels.cuh), so each logit comes with a rigorous bound on its distance
+//   to the reference's sequential fp32 sum (reference_ops.cpp:85-91): the
+//   running-error bound u * sum_i |s_i| of the sequential order, whose partial
+//   sums s_i are bounded by the chunk prefix |P_l| plus the in-chunk partials,
+//   plus the error of this kernel's own order.
+// router_select_kernel (one block per token)
+//   1. top-(k+1) by (logit desc, id asc) with redux.sync; certified when every
+//      adjacent gap exceeds twice the largest bound plus a floor that keeps
+//      distinct logits at distinct probabilities;
+//   2. otherwise the candidates within twice the bound of the k-th logit get
+//      their logits recomputed exactly as the reference does (sequential fp32,
+//      rows staged in shared memory) and are ordered by them;
+//   3. if exact logits are themselves (near) equal, the whole token is routed
+//      by the reference's arithmetic: all logits sequential, softmax with a
+//      sequential sum, stable top-k (reference_ops.cpp:130-212).
+//   Then the shared-expert scalar gate, the activation fragments and, in the
+//   last block, the grouping of (token, pick) pairs by expert.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "osm_common.cuh"
+#include "osm_kernels.cuh"
+
+namespace osm {
+namespace {
+
+constexpr float kU = 5.9604644775390625e-8f;  // 2^-24
+constexpr int kLogitWarps = 4;
+constexpr int kMaxVec = 8;                    // H <= 2048 on the register path
+constexpr int kSelThreads = 512;
+constexpr int kMaxCand = 16;                  // candidates of the partial exact path
+constexpr int kFullTile = 32;                 // h per tile on the full exact path
+
+__device__ __forceinline__ void unpack8(const uint4 q, float w[8]) {
+  const uint32_t ww[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj) w[jj] = bf16_bits_to_f32((ww[jj >> 1] >> ((jj & 1) * 16)) & 0xFFFFu);
+}
+
+// Eight consecutive weights of vector (e, m, lane) of the router layout.
+__device__ __forceinline__ void load8(const RouterArgs& a, int e, int m, int lane, float w[8]) {
+  const size_t v = ((size_t)e * a.g.nvec + m) * 32 + lane;
+  if (a.g.f32w) {
+    const float4* p = reinterpret_cast<const float4*>(a.wp) + 2 * v;
+    const float4 x0 = __ldg(p), x1 = __ldg(p + 1);
+    w[0] = x0.x; w[1] = x0.y; w[2] = x0.z; w[3] = x0.w;
+    w[4] = x1.x; w[5] = x1.y; w[6] = x1.z; w[7] = x1.w;
+  } else {
+    unpack8(__ldg(a.wp + v), w);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// logits
+// ----------------------------------------------------------------------------
+template <int EXP, int TOKS>
+__global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(RouterArgs a) {
+  extern __shared__ float4 smem4[];
+  const RouterGeom g = a.g;
+  const int cp = g.c + 4;  // padded lane chunk: conflict-free float4 reads
+  float* xs = reinterpret_cast<float*>(smem4);  // [TOKS][32][cp]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = (blockIdx.x * kLogitWarps + warp) * EXP;
+  const bool reg_path = !g.f32w && g.nvec <= kMaxVec;
+  // The weights are immutable: fetch them before waiting on the predecessor.
+  uint4 wv[EXP][kMaxVec];
+#pragma unroll
+  for (int q = 0; q < EXP; ++q)
+#pragma unroll
+    for (int m = 0; m < kMaxVec; ++m) {
+      wv[q][m] = make_uint4(0u, 0u, 0u, 0u);
+      if (reg_path && m < g.nvec && e0 + q < g.E)
+        wv[q][m] = __ldg(a.wp + ((size_t)(e0 + q) * g.nvec + m) * 32 + lane);
+    }
+  pdl_wait();
+  const int t0 = blockIdx.y * TOKS;
+  const int nv4 = g.Hp >> 2;
+  const bool vec_ok = (g.H & 3) == 0;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < TOKS * nv4; i += blockDim.x) {
+    const int t = i / nv4, h = (i - t * nv4) * 4;
+    float4 val = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (t0 + t < a.B && h < g.H) {
+      const float* src = a.x + (size_t)(t0 + t) * g.H + h;
+      if (vec_ok) {
+        val = *reinterpret_cast<const float4*>(src);
+      } else {
+        val.x = src[0];
+        if (h + 1 < g.H) val.y = src[1];
+        if (h + 2 < g.H) val.z = src[2];
+        if (h + 3 < g.H) val.w = src[3];
+      }
+    }
+    const int l = h / g.c, o = h - l * g.c;
+    *reinterpret_cast<float4*>(xs + (t * 32 + l) * cp + o) = val;
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (e0 >= g.E) return;
+  float tacc[EXP][TOKS], aacc[EXP][TOKS], sacc[EXP][TOKS];
+#pragma unroll
+  for (int q = 0; q < EXP; ++q)
+#pragma unroll
+    for (int t = 0; t < TOKS; ++t) tacc[q][t] = aacc[q][t] = sacc[q][t] = 0.0f;
+  auto step = [&](int m, const float (&w)[EXP][8]) {
+#pragma unroll
+    for (int t = 0; t < TOKS; ++t) {
+      const float4* xp = reinterpret_cast<const float4*>(xs + (t * 32 + lane) * cp + 8 * m);
+      const float4 xa = xp[0], xb = xp[1];
+      const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+      for (int q = 0; q < EXP; ++q) {
+        // |partial sum| at the start of this 8-element block: the partial
+        // sums inside the block are bounded by it plus the block's |w x|.
+        sacc[q][t] += fabsf(tacc[q][t]);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          tacc[q][t] = fmaf(w[q][jj], xv[jj], tacc[q][t]);
+          aacc[q][t] = fmaf(fabsf(w[q][jj]), fabsf(xv[jj]), aacc[q][t]);
+        }
+      }
+    }
+  };
+  if (reg_path) {
+#pragma unroll
+    for (int m = 0; m < kMaxVec; ++m) {
+      if (m < g.nvec) {
+        float w[EXP][8];
+#pragma unroll
+        for (int q = 0; q < EXP; ++q) unpack8(wv[q][m], w[q]);
+        step(m, w);
+      }
+    }
+  } else {
+    for (int m = 0; m < g.nvec; ++m) {
+      float w[EXP][8];
+#pragma unroll
+      for (int q = 0; q < EXP; ++q) {
+        if (e0 + q < g.E) {
+          load8(a, e0 + q, m, lane, w[q]);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 8; ++jj) w[q][jj] = 0.0f;
+        }
+      }
+      step(m, w);
+    }
+  }
+  const float n = (float)g.Hp;
+  const float gam = n * kU / (1.0f - n * kU);
+#pragma unroll
+  for (int q = 0; q < EXP; ++q) {
+#pragma unroll
+    for (int t = 0; t < TOKS; ++t) {
+      const float T = tacc[q][t];
+      float incl = T;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      float P = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+      if (lane == 0) P = 0.0f;
+      const float logit = warp_sum(T);
+      const float Q = warp_sum(fabsf(T));
+      const float S = warp_sum(8.0f * (sacc[q][t] + aacc[q][t]));
+      const float Pa = warp_sum(fabsf(P));
+      const float A = warp_sum(aacc[q][t]);
+      float bound = 1.001f * kU *
+                    ((float)g.c * Pa + 2.0f * S + 5.0f * Q + A * (1.0f + 3.0f * n * gam));
+      float outl = logit;
+      const int e = e0 + q;
+      if (a.bias != nullptr && e < g.E) {
+        outl = __fadd_rn(logit, a.bias[e]);
+        bound = bound + 2.002f * kU * (fabsf(outl) + bound);
+      }
+      if (lane == 0 && e < g.E && t0 + t < a.B) {
+        a.logits[(size_t)(t0 + t) * g.E + e] = outl;
+        a.bounds[(size_t)(t0 + t) * g.E + e] = bound;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// selection
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+// Best n (<= number of valid entries) of the lane-strided values v[i]
+// (index i*32 + lane, valid when < E) by (value desc, index asc), one
+// redux.sync max and min per pick.  All lanes receive sel_id / sel_v.
+__device__ void warp_select(const float (&v)[32], int E, int n, int* sel_id, float* sel_v) {
+  const int lane = threadIdx.x & 31;
+  uint32_t taken = 0;
+  uint32_t bk = 0;
+  int bi = 0x7FFFFFFF;
+  float bv = -INFINITY;
+  auto rescan = [&]() {
+    bk = 0;
+    bi = 0x7FFFFFFF;
+    bv = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int id = i * 32 + lane;
+      if (id < E && !((taken >> i) & 1u)) {
+        const uint32_t key = ord_key(v[i]);
+        if (key > bk || (key == bk && id < bi)) {
+          bk = key;
+          bi = id;
+          bv = v[i];
+        }
+      }
+    }
+  };
+  rescan();
+  for (int r = 0; r < n; ++r) {
+    const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, bk);
+    const uint32_t win = __reduce_min_sync(0xFFFFFFFFu, bk == m ? (uint32_t)bi : 0xFFFFFFFFu);
+    const float wv = __shfl_sync(0xFFFFFFFFu, bv, (int)(win & 31u));
+    if (lane == 0) {
+      sel_id[r] = (int)win;
+      sel_v[r] = wv;
+    }
+    if ((int)(win & 31u) == lane) {
+      taken |= 1u << (win >> 5);
+      rescan();
+    }
+  }
+  __syncwarp();
+}
+
+// Block-wide exclusive scan of n (<= 4*blockDim) ints in smem `v`, in place;
+// returns the total.  `red` holds 32 ints.
+__device__ int block_exclusive_scan(int* v, int n, int* red) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int C = (n + blockDim.x - 1) / blockDim.x;
+  const int i0 = tid * C;
+  int loc[4];
+  int s = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    loc[q] = (q < C && i0 + q < n) ? v[i0 + q] : 0;
+    s += loc[q];
+  }
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  __syncthreads();
+  if (lane == 31) red[warp] = incl;
+  __syncthreads();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += red[w];
+  int total = 0;
+  const int nw = blockDim.x >> 5;
+  for (int w = 0; w < nw; ++w) total += red[w];
+  int run = base + incl - s;
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if (q < C && i0 + q < n) v[i0 + q] = run;
+    run += loc[q];
+  }
+  __syncthreads();
+  return total;
+}
+
+// Group (token, pick) pairs by expert.  The shared expert (id E) is active
+// index 0 when present, so later kernels can fetch its weights early.  The
+// order of the other experts and of tokens inside an expert is arbitrary:
+// every token's result is computed independently of its position.
+__device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
+  const int E = a.g.E, k = a.g.k, B = a.B;
+  const int has_sh = a.shared_slot != nullptr;
+  const int NE = E + has_sh;
+  int* cnt = sm;
+  int* actidx = sm + NE;
+  int* cur = sm + 2 * NE;
+  int* expert_of = sm + 3 * NE;
+  int* off = sm + 4 * NE;
+  __shared__ int s_nact;
+  for (int i = threadIdx.x; i < NE; i += blockDim.x) {
+    cnt[i] = 0;
+    cur[i] = 0;
+    actidx[i] = -1;
+  }
+  if (threadIdx.x == 0) s_nact = has_sh;
+  __syncthreads();
+  if (has_sh && threadIdx.x == 0) {
+    actidx[E] = 0;
+    cnt[E] = B;
+  }
+  for (int p = threadIdx.x; p < B * k; p += blockDim.x) {
+    const uint32_t e = __ldcg(a.ids + p);
+    if (e >= (uint32_t)E) {
+      atomicOr(a.status, kStatusBadSlot);
+      continue;
+    }
+    if (atomicAdd(&cnt[e], 1) == 0) actidx[e] = atomicAdd(&s_nact, 1);
+  }
+  __syncthreads();
+  const int n_active = s_nact;
+  for (int e = threadIdx.x; e < NE; e += blockDim.x)
+    if (actidx[e] >= 0) expert_of[actidx[e]] = e;
+  __syncthreads();
+  for (int j = threadIdx.x; j < n_active; j += blockDim.x) off[j] = cnt[expert_of[j]];
+  __syncthreads();
+  block_exclusive_scan(off, n_active, red);
+  for (int j = threadIdx.x; j < n_active; j += blockDim.x) {
+    const int e = expert_of[j];
+    a.act_off[j] = off[j];
+    a.act_cnt[j] = cnt[e];
+    if (e == E) {
+      a.act_kind[j] = 1;
+      a.act_ptr[j] = a.shared_slot;
+    } else {
+      a.act_kind[j] = 0;
+      const int slot = a.slot_of[e];
+      if (slot < 0) {
+        atomicOr(a.status, kStatusNotResident);
+        a.act_ptr[j] = nullptr;
+      } else {
+        a.act_ptr[j] = a.slab + (size_t)slot * a.slab_stride;
+      }
+    }
+  }
+  for (int p = threadIdx.x; p < B * k; p += blockDim.x) {
+    const uint32_t e = __ldcg(a.ids + p);
+    if (e >= (uint32_t)E) continue;
+    const int pos = off[actidx[e]] + atomicAdd(&cur[e], 1);
+    a.pair_tok[pos] = p / k;
+    a.pair_pick[pos] = p % k;
+  }
+  if (has_sh)
+    for (int t = threadIdx.x; t < B; t += blockDim.x) {
+      a.pair_tok[off[0] + t] = t;
+      a.pair_pick[off[0] + t] = k;
+    }
+  if (threadIdx.x == 0) *a.n_active = n_active;
+}
+
+// Softmax weights of the picks from logits lsel[0..k) (lsel[0] the largest)
+// with the sum over the fast logits v[] (lane-strided); lane 0 writes.
+__device__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32],
+                              const int* sid, const float* lsel) {
+  const int lane = threadIdx.x & 31;
+  const int k = a.g.k;
+  const float mx = lsel[0];
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (i * 32 + lane < a.g.E) s += expf(__fsub_rn(v[i], mx));
+  s = warp_sum(s);
+  if (lane == 0) {
+    float p[kMaxTopK];
+    float mass = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      p[j] = __fdiv_rn(expf(__fsub_rn(lsel[j], mx)), s);
+      mass = __fadd_rn(mass, p[j]);
+    }
+    if (!(mass > 0.0f) || !isfinite(mass) || !(s > 0.0f) || !isfinite(s))
+      atomicOr(a.status, kStatusBadMass);
+    for (int j = 0; j < k; ++j) {
+      a.ids[(size_t)tok * k + j] = (uint32_t)sid[j];
+      a.weights[(size_t)tok * k + j] = a.norm ? __fdiv_rn(p[j], mass) : p[j];
+    }
+    a.mass[tok] = mass;
+  }
+}
+
+// True when consecutive (exact) logits are far enough apart that their
+// probabilities cannot round to the same value.
+__device__ __forceinline__ bool distinct_p(float hi, float lo, float mx) {
+  return __fsub_rd(hi, lo) > 1e-6f + 3e-7f * (fabsf(hi - mx) + fabsf(lo - mx));
+}
+
+__global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a) {
+  extern __shared__ float4 smem4[];
+  float* xs = reinterpret_cast<float*>(smem4);  // [H]
+  char* uni = reinterpret_cast<char*>(xs + ((a.g.H + 3) & ~3));
+  __shared__ float red[32];
+  __shared__ int sel_id[kMaxTopK + 1];
+  __shared__ float sel_v[kMaxTopK + 1];
+  __shared__ int cand_id[kMaxCand];
+  __shared__ float cand_l[kMaxCand];
+  __shared__ int s_flag, s_ncand;
+  __shared__ float s_bm, s_bcast;
+  const RouterGeom g = a.g;
+  const int tok = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int k = g.k;
+  pdl_wait();
+  pdl_trigger();
+  const float* x = a.x + (size_t)tok * g.H;
+  int nonfinite = 0;
+  if ((g.H & 3) == 0) {
+    for (int i = tid; i < (g.H >> 2); i += blockDim.x) {
+      const float4 v = reinterpret_cast<const float4*>(x)[i];
+      reinterpret_cast<float4*>(xs)[i] = v;
+      if (!isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w)) nonfinite = 1;
+    }
+  } else {
+    for (int h = tid; h < g.H; h += blockDim.x) {
+      const float v = x[h];
+      xs[h] = v;
+      if (!isfinite(v)) nonfinite = 1;
+    }
+  }
+  if (tid == 0) {
+    s_flag = 0;
+    s_ncand = 0;
+  }
+  nonfinite = __syncthreads_or(nonfinite);
+  if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
+  const bool route = !nonfinite && !a.skip_route;
+  // ---- 1. fast path: certified top-k over the fast logits ----
+  float v[32];
+  if (warp == 0 && route) {
+    float bm = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int id = i * 32 + lane;
+      v[i] = id < g.E ? a.logits[(size_t)tok * g.E + id] : -INFINITY;
+      if (id < g.E) bm = fmaxf(bm, a.bounds[(size_t)tok * g.E + id]);
+    }
+    bm = warp_max(bm);
+    const int nsel = k + 1 <= g.E ? k + 1 : k;
+    warp_select(v, g.E, nsel, sel_id, sel_v);
+    bool ok = !a.force_exact && isfinite(sel_v[0]);
+    const float mx0 = sel_v[0];
+    for (int j = 0; j + 1 < nsel; ++j) {
+      const float need = 2.0f * bm * 1.0001f + 1e-6f +
+                         3e-7f * (fabsf(sel_v[j] - mx0) + fabsf(sel_v[j + 1] - mx0));
+      if (!(__fsub_rd(sel_v[j], sel_v[j + 1]) > need)) ok = false;
+    }
+    if (ok) {
+      write_weights(a, tok, v, sel_id, sel_v);
+    } else if (lane == 0) {
+      s_flag = a.force_exact ? 2 : 1;
+      s_bm = bm;
+    }
+  }
+  __syncthreads();
+  // ---- 2. partial exact path: recompute the ambiguous candidates ----
+  if (s_flag == 1) {
+    if (tid == 0) atomicAdd(a.exact_count, 1ull);
+    const float thr = sel_v[k - 1] - 2.0f * s_bm * 1.0001f - 1e-6f;
+    for (int e = tid; e < g.E; e += blockDim.x) {
+      if (a.logits[(size_t)tok * g.E + e] >= thr) {
+        const int idx = atomicAdd(&s_ncand, 1);
+        if (idx < kMaxCand) cand_id[idx] = e;
+      }
+    }
+    __syncthreads();
+    const int nc = s_ncand;
+    if (nc > kMaxCand || g.f32w || nc < k) {
+      if (tid == 0) s_flag = 2;
+    } else {
+      // rows of the candidates, transposed: wt[h * kMaxCand + j] (bf16)
+      uint16_t* wt = reinterpret_cast<uint16_t*>(uni);
+      const int vpr = g.Hp >> 3;  // 8-element vectors per row
+      for (int i = tid; i < nc * vpr; i += blockDim.x) {
+        const int j = i / vpr, vi = i - j * vpr;
+        const int m = vi >> 5, l = vi & 31;
+        const uint4 q = __ldg(a.wp + ((size_t)cand_id[j] * g.nvec + m) * 32 + l);
+        const uint32_t ww[4] = {q.x, q.y, q.z, q.w};
+        const int h0 = l * g.c + 8 * m;
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj)
+          if (h0 + jj < g.H) wt[(h0 + jj) * kMaxCand + j] = (uint16_t)((ww[jj >> 1] >> ((jj & 1) * 16)) & 0xFFFFu);
+      }
+      __syncthreads();
+      if (tid < nc) {
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int h = 0; h < g.H; ++h)
+          acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wt[h * kMaxCand + tid]), xs[h]));
+        if (a.bias != nullptr) acc = __fadd_rn(acc, a.bias[cand_id[tid]]);
+        cand_l[tid] = acc;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // rank the candidates by (exact logit desc, id asc)
+        const float myl = lane < nc ? cand_l[lane] : -INFINITY;
+        const int myid = lane < nc ? cand_id[lane] : 0x7FFFFFFF;
+        int rank = 0;
+        for (int i = 0; i < nc; ++i) {
+          const float ol = cand_l[i];
+          const int oi = cand_id[i];
+          if (better(ol, oi, myl, myid)) ++rank;
+        }
+        __syncwarp();
+        if (lane < nc) {
+          sel_id[rank] = myid;
+          sel_v[rank] = myl;
+        }
+        __syncwarp();
+        bool ok = isfinite(sel_v[0]);
+        const int npair = k < nc ? k : nc - 1;  // pairs (r, r+1) that decide ids/order
+        for (int r = 0; r < npair; ++r)
+          if (!distinct_p(sel_v[r], sel_v[r + 1], sel_v[0])) ok = false;
+        if (ok) write_weights(a, tok, v, sel_id, sel_v);
+        else if (lane == 0) s_flag = 2;
+      }
+    }
+    __syncthreads();
+  }
+  // ---- 3. full exact path: the reference's arithmetic for the whole token ----
+  if (s_flag == 2) {
+    float* lex = reinterpret_cast<float*>(uni);                  // [E]
+    uint16_t* tile = reinterpret_cast<uint16_t*>(lex + g.E);      // [kFullTile][E]
+    float* tilef = reinterpret_cast<float*>(lex + g.E);           // fp32 router tiles
+    float acc[2] = {0.0f, 0.0f};  // experts tid, tid + 512
+    for (int h0 = 0; h0 < g.H; h0 += kFullTile) {
+      // stage h in [h0, h0 + kFullTile) of every row, transposed [hh][e]
+      const int nvt = kFullTile / 8;
+      for (int i = tid; i < g.E * nvt; i += blockDim.x) {
+        const int e = i / nvt, vv = i - e * nvt;
+        const int h = h0 + vv * 8;
+        if (h >= g.Hp) continue;
+        const int l = h / g.c, o = h - l * g.c;
+        float w8[8];
+        load8(a, e, o >> 3, l, w8);
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          if (g.f32w) tilef[(vv * 8 + jj) * g.E + e] = w8[jj];
+          else tile[(vv * 8 + jj) * g.E + e] = (uint16_t)(__float_as_uint(w8[jj]) >> 16);
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int e = tid + r * kSelThreads;
+        if (e < g.E) {
+          for (int hh = 0; hh < kFullTile && h0 + hh < g.H; ++hh) {
+            const float w = g.f32w ? tilef[hh * g.E + e] : bf16_bits_to_f32(tile[hh * g.E + e]);
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(w, xs[h0 + hh]));
+          }
+        }
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int e = tid + r * kSelThreads;
+      if (e < g.E) lex[e] = a.bias != nullptr ? __fadd_rn(acc[r], a.bias[e]) : acc[r];
+    }
+    __syncthreads();
+    float m = -INFINITY;
+    for (int e = tid; e < g.E; e += blockDim.x) m = fmaxf(m, lex[e]);
+    const float mx = block_reduce_max(m, red);
+    for (int e = tid; e < g.E; e += blockDim.x)
+      lex[e] = (float)exp((double)__fsub_rn(lex[e], mx));
+    __syncthreads();
+    if (tid == 0) {
+      float s = 0.0f;
+      for (int e = 0; e < g.E; ++e) s = __fadd_rn(s, lex[e]);
+      s_bcast = s;
+      if (!(s > 0.0f) || !isfinite(s)) atomicOr(a.status, kStatusBadMass);
+    }
+    __syncthreads();
+    const float sum = s_bcast;
+    for (int e = tid; e < g.E; e += blockDim.x) lex[e] = __fdiv_rn(lex[e], sum);
+    __syncthreads();
+    if (warp == 0) {
+      float pv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int id = i * 32 + lane;
+        pv[i] = id < g.E ? lex[id] : -INFINITY;
+      }
+      warp_select(pv, g.E, k, sel_id, sel_v);
+      if (lane == 0) {
+        float mass = 0.0f;
+        for (int j = 0; j < k; ++j) mass = __fadd_rn(mass, sel_v[j]);
+        if (!(mass > 0.0f) || !isfinite(mass)) atomicOr(a.status, kStatusBadMass);
+        for (int j = 0; j < k; ++j) {
+          a.ids[(size_t)tok * k + j] = (uint32_t)sel_id[j];
+          a.weights[(size_t)tok * k + j] = a.norm ? __fdiv_rn(sel_v[j], mass) : sel_v[j];
+        }
+        a.mass[tok] = mass;
+      }
+    }
+    if (tid == 0 && !a.force_exact) atomicAdd(a.exact_count, 0ull);
+  }
+  if (s_flag == 2 && a.force_exact && tid == 0) atomicAdd(a.exact_count, 1ull);
+  if (nonfinite && tid == 0 && !a.skip_route) {
+    for (int j = 0; j < k; ++j) {
+      a.ids[(size_t)tok * k + j] = 0;
+      a.weights[(size_t)tok * k + j] = 0.0f;
+    }
+    a.mass[tok] = 0.0f;
+  }
+  __syncthreads();
+  if (tid < k && !a.skip_route) {
+    if (a.ids_out) a.ids_out[(size_t)tok * k + tid] = a.ids[(size_t)tok * k + tid];
+    if (a.weights_out) a.weights_out[(size_t)tok * k + tid] = a.weights[(size_t)tok * k + tid];
+  }
+  if (tid == 0 && a.mass_out && !a.skip_route) a.mass_out[tok] = a.mass[tok];
+  // ---- shared expert scalar gate: sigmoid(g . x) ----
+  if (a.sgate_w != nullptr) {
+    float d = 0.0f;
+    for (int h = tid; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
+    const float dot = block_reduce_sum(d, red);
+    if (tid == 0) {
+      const float s = ref_sigmoid(dot);
+      a.sgate[tok] = s;
+      if (a.sgate_out) a.sgate_out[tok] = s;
+    }
+  } else if (tid == 0) {
+    if (a.sgate) a.sgate[tok] = 0.0f;
+    if (a.sgate_out) a.sgate_out[tok] = 0.0f;
+  }
+  // ---- activation fragments for the expert kernels ----
+  if (a.xfrag != nullptr) {
+    const int nch = g.H >> 3;
+    for (int c = tid; c < nch; c += blockDim.x) {
+      const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
+      const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
+      const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+      uint32_t hi[8], lo[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
+      float fs = xc[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
+      uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
+      dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
+                          pack2(hi[3], hi[7]));
+      dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
+                          pack2(lo[3], lo[7]));
+      a.xfsum8[(size_t)tok * nch + c] = fs;
+    }
+  }
+  if (!a.do_group) return;
+  // ---- the last block groups (token, pick) pairs by expert ----
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned int prev = atomicAdd(a.ticket, 1u);
+    s_flag = (prev == gridDim.x - 1) ? 3 : 0;
+  }
+  __syncthreads();
+  if (s_flag != 3) return;
+  __threadfence();
+  group_pairs(a, reinterpret_cast<int*>(uni), reinterpret_cast<int*>(red));
+  if (tid == 0) *a.ticket = 0u;
+}
+
+__global__ void __launch_bounds__(kSelThreads) group_kernel(RouterArgs a) {
+  extern __shared__ float4 smem4[];
+  __shared__ int red[32];
+  pdl_wait();
+  pdl_trigger();
+  group_pairs(a, reinterpret_cast<int*>(smem4), red);
+}
+
+template <typename K, typename... Args>
+void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+template <int EXP, int TOKS>
+void launch_logits_t(const RouterArgs& a, cudaStream_t s) {
+  const RouterGeom& g = a.g;
+  const dim3 grid((g.E + EXP * kLogitWarps - 1) / (EXP * kLogitWarps), (a.B + TOKS - 1) / TOKS);
+  const size_t sm = (size_t)TOKS * 32 * (g.c + 4) * sizeof(float);
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(router_logits_kernel<EXP, TOKS>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  launch_pdl(router_logits_kernel<EXP, TOKS>, grid, dim3(kLogitWarps * 32), sm, s, a);
+}
+
+size_t select_smem(const RouterGeom& g) {
+  const size_t xs = (size_t)((g.H + 3) & ~3) * sizeof(float);
+  const size_t partial = (size_t)g.H * kMaxCand * sizeof(uint16_t);
+  const size_t full = (size_t)g.E * sizeof(float) + (size_t)kFullTile * g.E * sizeof(float);
+  const size_t grp = (size_t)5 * (g.E + 1) * sizeof(int);
+  size_t u = partial;
+  if (full > u) u = full;
+  if (grp > u) u = grp;
+  return xs + u;
+}
+
+}  // namespace
+
+void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
+  if (a.B <= 2) launch_logits_t<1, 1>(a, s);
+  else launch_logits_t<2, 4>(a, s);
+  if (launches) *launches += 1;
+}
+
+void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
+  const size_t sm = select_smem(a.g);
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)sm);
+  launch_pdl(router_select_kernel, dim3(a.B), dim3(kSelThreads), sm, s, a);
+  if (launches) *launches += 1;
+}
+
+void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
+  const size_t sm = (size_t)5 * (a.g.E + 1) * sizeof(int);
+  launch_pdl(group_kernel, dim3(1), dim3(kSelThreads), sm, s, a);
+  if (launches) *launches += 1;
+}
+
+}  // namespace osm
