@@ -87,6 +87,7 @@ struct osm_context {
   std::string err;
   uint64_t launches = 0;
   Scratch sc;
+  int grid_cap = 148 * 4;       // resident CTAs of the projection kernels
   bool prof_on = false;
   std::vector<cudaEvent_t> ev_pool;
   std::vector<ProfRec> recs;
@@ -370,7 +371,7 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   gu.hK = Imax;
   {
     Prof p(ctx, kKGateUp);
-    osm::launch_proj(gu, osm::ProjKind::kGateUp, Imax, max_active, ctx->stream, &ctx->launches);
+    osm::launch_proj(gu, osm::ProjKind::kGateUp, Imax, max_active, ctx->grid_cap, ctx->stream, &ctx->launches);
   }
   int rc = check_launch(ctx, "gate/up projection");
   if (rc) return rc;
@@ -390,7 +391,7 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   {
     Prof p(ctx, kKDown);
     osm::launch_proj(dn, Imax <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12, L->g.H,
-                     max_active, ctx->stream, &ctx->launches);
+                     max_active, ctx->grid_cap, ctx->stream, &ctx->launches);
   }
   rc = check_launch(ctx, "down projection");
   if (rc) return rc;
@@ -466,6 +467,9 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
     return OSM_ECUDA;
   }
   ctx->stream = ctx->own_stream;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+    ctx->grid_cap = sms * 4;
   *out = ctx;
   return OSM_OK;
 }
@@ -641,7 +645,8 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
   a.pair_pick = s.pair_pick;
   a.kp1 = 1;
   a.ostride = (int)out_dim;
-  osm::launch_proj(a, osm::ProjKind::kSingle, (int)out_dim, 1, ctx->stream, &ctx->launches);
+  osm::launch_proj(a, osm::ProjKind::kSingle, (int)out_dim, 1, ctx->grid_cap, ctx->stream,
+                   &ctx->launches);
   return check_launch(ctx, "q4 gemv");
 }
 
@@ -703,7 +708,8 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   gu.hfrag = s.hfrag;
   gu.hfsum8 = s.hfsum8;
   gu.hK = (int)L.inter;
-  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, 1, ctx->stream, &ctx->launches);
+  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, 1, ctx->grid_cap, ctx->stream,
+                   &ctx->launches);
   rc = check_launch(ctx, "expert gate/up");
   if (rc) return rc;
   osm::ProjArgs dn = gu;
@@ -718,7 +724,7 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   dn.kp1 = 1;
   dn.ostride = (int)L.hidden;
   osm::launch_proj(dn, L.inter <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12,
-                   (int)L.hidden, 1, ctx->stream, &ctx->launches);
+                   (int)L.hidden, 1, ctx->grid_cap, ctx->stream, &ctx->launches);
   return check_launch(ctx, "expert down");
 }
 

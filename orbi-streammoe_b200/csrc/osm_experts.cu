@@ -45,16 +45,18 @@ __device__ __forceinline__ void mma_group(float d[4], uint2 wl, uint2 wh, const 
   }
 }
 
+// One work item: CTA tile `bx` (TILES row tiles) of active expert j.
 template <bool PAIRED, int KSPLIT, int MAXG>
-__global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjArgs a) {
+__device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles, bool first,
+                                          int& n_items) {
   constexpr int TILES = kWarps / KSPLIT;
   constexpr int TROWS = PAIRED ? 8 : 16;
-  const int j = blockIdx.y;
+  const int j = item / tiles, bx = item - (item / tiles) * tiles;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, t = lane & 3;
   const int tile = warp / KSPLIT, ks = warp - tile * KSPLIT;
   // The shared expert is active entry 0: its weights are known before the
   // routing is, so they are fetched before waiting on the router.
-  const bool early = a.shared_first && j == 0;
+  const bool early = first && a.shared_first && j == 0;
   const uint8_t* base = early ? a.shared_ptr : nullptr;
   int kind = 1;
   uint2 wl[MAXG], wh[MAXG];
@@ -65,7 +67,7 @@ __global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjA
     K = a.sec.K[kind];
     G = K >> 6;
     KW = K >> 3;
-    r0 = (blockIdx.x * TILES + tile) * TROWS;
+    r0 = (bx * TILES + tile) * TROWS;
     const uintptr_t ub = reinterpret_cast<uintptr_t>(base);
     const uint32_t* Wlo = reinterpret_cast<const uint32_t*>(ub + a.sec.w[kind]);
     const uint16_t* Slo = reinterpret_cast<const uint16_t*>(ub + a.sec.s[kind]);
@@ -91,16 +93,19 @@ __global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjA
     }
   };
   if (early) fetch();
-  pdl_wait();
-  pdl_trigger();
-  if (j >= *a.n_active) return;
+  if (first) {
+    pdl_wait();
+    pdl_trigger();
+    n_items = *a.n_active * tiles;
+  }
+  if (item >= n_items) return;
   if (!early) {
     base = a.act_ptr[j];
     kind = a.act_kind[j];
     if (base == nullptr && !a.raw) return;  // non-resident expert (status already set)
     fetch();
   }
-  if ((blockIdx.x * TILES) * TROWS >= rows) return;
+  if ((bx * TILES) * TROWS >= rows) return;
 
   __shared__ float fsg[8][33];
   __shared__ int rowof[8];
@@ -218,6 +223,21 @@ __global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjA
   }
 }
 
+// Persistent grid: CTAs stride over (active expert, CTA tile) items; the
+// number of active experts is only known on the device.  Items 0..tiles-1
+// belong to active entry 0 (the shared expert when present), whose weights
+// are fetched before the wait on the router.
+template <bool PAIRED, int KSPLIT, int MAXG>
+__global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjArgs a, int tiles) {
+  int n_items = 0x7FFFFFFF;
+  bool first = true;
+  for (int item = blockIdx.x; first || item < n_items; item += gridDim.x) {
+    if (!first) __syncthreads();
+    proj_item<PAIRED, KSPLIT, MAXG>(a, item, tiles, first, n_items);
+    first = false;
+  }
+}
+
 __global__ void frag_prep_kernel(const float* __restrict__ x, int rows, int K,
                                  uint4* __restrict__ frag, float* __restrict__ fsum8) {
   pdl_wait();
@@ -296,24 +316,30 @@ void launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8
   if (launches) *launches += 1;
 }
 
-void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active, cudaStream_t s,
-                 uint64_t* launches) {
+void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active, int grid_cap,
+                 cudaStream_t s, uint64_t* launches) {
+  auto go = [&](auto kernel, int rows_per_cta) {
+    const int tiles = (max_rows + rows_per_cta - 1) / rows_per_cta;
+    long long items = (long long)tiles * max_active;
+    // the gate/up kernel is register-limited to 5 resident CTAs per SM, the
+    // others to 4 (grid_cap counts 4 per SM)
+    const int cap = kind == ProjKind::kGateUp ? grid_cap / 4 * 5 : grid_cap;
+    int grid = (int)(items < cap ? items : cap);
+    if (grid < 1) grid = 1;
+    launch_pdl(kernel, dim3(grid), dim3(kWarps * 32), 0, s, a, tiles);
+  };
   switch (kind) {
-    case ProjKind::kGateUp:  // 8 intermediate rows per CTA, input split over 4 warps
-      launch_pdl(proj_kernel<true, 4, 8>, dim3((max_rows + 7) / 8, max_active), dim3(kWarps * 32),
-                 0, s, a);
+    case ProjKind::kGateUp:  // 8 intermediate rows per CTA tile, input split over 4 warps
+      go(proj_kernel<true, 4, 8>, 8);
       break;
-    case ProjKind::kDown:    // 64 output rows per CTA, one warp per 16-row tile (K <= 512)
-      launch_pdl(proj_kernel<false, 1, 8>, dim3((max_rows + 63) / 64, max_active),
-                 dim3(kWarps * 32), 0, s, a);
+    case ProjKind::kDown:    // 64 output rows per CTA tile, one warp per 16 rows (K <= 512)
+      go(proj_kernel<false, 1, 8>, 64);
       break;
     case ProjKind::kDown12:  // the same for K <= 768
-      launch_pdl(proj_kernel<false, 1, 12>, dim3((max_rows + 63) / 64, max_active),
-                 dim3(kWarps * 32), 0, s, a);
+      go(proj_kernel<false, 1, 12>, 64);
       break;
-    case ProjKind::kSingle:  // 16 rows per CTA, input split over 4 warps (K <= 2048)
-      launch_pdl(proj_kernel<false, 4, 8>, dim3((max_rows + 15) / 16, max_active),
-                 dim3(kWarps * 32), 0, s, a);
+    case ProjKind::kSingle:  // 16 rows per CTA tile, input split over 4 warps (K <= 2048)
+      go(proj_kernel<false, 4, 8>, 16);
       break;
   }
   if (launches) *launches += 1;

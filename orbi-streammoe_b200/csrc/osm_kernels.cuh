@@ -111,7 +111,9 @@ struct ProjArgs {
 };
 
 enum class ProjKind { kGateUp, kDown, kDown12, kSingle };
-void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active,
+// grid_cap: resident CTAs the device holds (SMs x CTAs per SM); the grid is
+// persistent and strides over (active expert, tile) items.
+void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active, int grid_cap,
                  cudaStream_t s, uint64_t* launches);
 
 struct CombineArgs {
