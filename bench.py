@@ -189,7 +189,8 @@ def run_ours(args, rank, world, local_rank):
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
     ctx = osm.Context(local_rank, max_tokens=max(SWEEP))
     ctx.set_stream(stream.cuda_stream)
     layer, slab, W, sg, bias, shared = build_sublayer(torch, ctx, osm)

@@ -73,8 +73,11 @@ int osm_context_destroy(osm_context* ctx);
 const char* osm_last_error(const osm_context* ctx);
 int osm_context_device(const osm_context* ctx);
 void* osm_context_stream(const osm_context* ctx); /* cudaStream_t */
-/* Use a caller-owned stream (NULL restores the context's own stream). */
+/* Enqueue all later work on `cuda_stream` (caller-owned; NULL is the CUDA
+ * default stream).  osm_context_reset_stream returns to the context's own
+ * non-blocking stream. */
 int osm_context_set_stream(osm_context* ctx, void* cuda_stream);
+int osm_context_reset_stream(osm_context* ctx);
 int osm_context_synchronize(osm_context* ctx);
 /* Device status word accumulated by kernels since the last call (bit 0
  * non-finite router input, bit 1 invalid softmax/mass, bit 2 non-resident

@@ -524,7 +524,13 @@ const char* osm_kernel_kind_name(int kind) {
 
 int osm_context_set_stream(osm_context* ctx, void* stream) {
   if (!ctx) return OSM_EINVAL;
-  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return OSM_OK;
+}
+
+int osm_context_reset_stream(osm_context* ctx) {
+  if (!ctx) return OSM_EINVAL;
+  ctx->stream = ctx->own_stream;
   return OSM_OK;
 }
 

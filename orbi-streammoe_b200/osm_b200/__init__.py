@@ -71,8 +71,13 @@ class Context:
     def stream_handle(self) -> int:
         return lib().osm_context_stream(self.h) or 0
 
-    def set_stream(self, stream_handle: int | None):
-        self.check(lib().osm_context_set_stream(self.h, C.c_void_p(stream_handle or 0)))
+    def set_stream(self, stream_handle: int):
+        """Run on this CUDA stream (0 is the default stream, e.g. torch's
+        default ``torch.cuda.current_stream().cuda_stream``)."""
+        self.check(lib().osm_context_set_stream(self.h, C.c_void_p(stream_handle)))
+
+    def reset_stream(self):
+        self.check(lib().osm_context_reset_stream(self.h))
 
     def synchronize(self):
         self.check(lib().osm_context_synchronize(self.h))

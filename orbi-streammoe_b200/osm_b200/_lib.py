@@ -58,6 +58,7 @@ _SIGS = {
     "osm_context_device": (C.c_int, [_P]),
     "osm_context_stream": (_P, [_P]),
     "osm_context_set_stream": (C.c_int, [_P, _P]),
+    "osm_context_reset_stream": (C.c_int, [_P]),
     "osm_context_synchronize": (C.c_int, [_P]),
     "osm_context_status": (C.c_int, [_P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)]),
     "osm_context_launches": (C.c_uint64, [_P]),
