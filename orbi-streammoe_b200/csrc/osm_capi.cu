@@ -40,10 +40,10 @@ struct Scratch {
   unsigned int* ticket = nullptr;
   int* counts = nullptr;
   int* n_active = nullptr;
-  int* act_kind = nullptr;
-  const uint8_t** act_ptr = nullptr;
-  int* act_off = nullptr;
-  int* act_cnt = nullptr;
+  osm::ActEntry* act = nullptr;
+  int* n_tg = nullptr;
+  int* tg_expert = nullptr;
+  int* tg_begin = nullptr;
   int* pair_tok = nullptr;
   int* pair_pick = nullptr;
   int* cursor = nullptr;
@@ -209,8 +209,9 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t o_sg = take(T * 4);
   const size_t o_xf = take(T * (Kx / 8) * 32), o_xs = take(T * (Kx / 8) * 4);
   const size_t o_ticket = take(4), o_counts = take((E + 1) * 4), o_nact = take(4);
-  const size_t o_akind = take((E + 1) * 4), o_aptr = take((E + 1) * 8);
-  const size_t o_aoff = take((E + 1) * 4), o_acnt = take((E + 1) * 4);
+  const size_t o_act = take((E + 1) * sizeof(osm::ActEntry)), o_ntg = take(4);
+  const size_t max_tg = P / osm::kTokGroup + E + 2;
+  const size_t o_tge = take(max_tg * 4), o_tgb = take(max_tg * 4);
   const size_t o_ptok = take(P * 4), o_ppick = take(P * 4), o_cursor = take((E + 1) * 4);
   const size_t o_orow = take(P * 4);
   const size_t o_hf = take(P * (I / 8) * 32), o_hs = take(P * (I / 8) * 4);
@@ -244,10 +245,10 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.ticket = reinterpret_cast<unsigned int*>(b + o_ticket);
   s.counts = reinterpret_cast<int*>(b + o_counts);
   s.n_active = reinterpret_cast<int*>(b + o_nact);
-  s.act_kind = reinterpret_cast<int*>(b + o_akind);
-  s.act_ptr = reinterpret_cast<const uint8_t**>(b + o_aptr);
-  s.act_off = reinterpret_cast<int*>(b + o_aoff);
-  s.act_cnt = reinterpret_cast<int*>(b + o_acnt);
+  s.act = reinterpret_cast<osm::ActEntry*>(b + o_act);
+  s.n_tg = reinterpret_cast<int*>(b + o_ntg);
+  s.tg_expert = reinterpret_cast<int*>(b + o_tge);
+  s.tg_begin = reinterpret_cast<int*>(b + o_tgb);
   s.pair_tok = reinterpret_cast<int*>(b + o_ptok);
   s.pair_pick = reinterpret_cast<int*>(b + o_ppick);
   s.cursor = reinterpret_cast<int*>(b + o_cursor);
@@ -323,10 +324,10 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.ticket = s.ticket;
   a.counts = s.counts;
   a.n_active = s.n_active;
-  a.act_kind = s.act_kind;
-  a.act_ptr = s.act_ptr;
-  a.act_off = s.act_off;
-  a.act_cnt = s.act_cnt;
+  a.act = s.act;
+  a.n_tg = s.n_tg;
+  a.tg_expert = s.tg_expert;
+  a.tg_begin = s.tg_begin;
   a.pair_tok = s.pair_tok;
   a.pair_pick = s.pair_pick;
   a.cursor = s.cursor;
@@ -351,13 +352,14 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
   const int Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
   const int max_active = (int)std::min<size_t>(L->g.E, (size_t)T * L->g.k) + (L->shared_slot ? 1 : 0);
+  const int max_tg = (int)((size_t)T * (L->g.k + 1) / osm::kTokGroup) + max_active + 1;
+  const int tchunk = (int)std::min<uint32_t>(T, 8);
   osm::ProjArgs gu{};
   fill_sections(gu.sec, R, S, true);
-  gu.n_active = s.n_active;
-  gu.act_kind = s.act_kind;
-  gu.act_ptr = s.act_ptr;
-  gu.act_off = s.act_off;
-  gu.act_cnt = s.act_cnt;
+  gu.n_tg = s.n_tg;
+  gu.act = s.act;
+  gu.tg_expert = s.tg_expert;
+  gu.tg_begin = s.tg_begin;
   gu.pair_tok = s.pair_tok;
   gu.frag_by_pair = 0;
   gu.raw = 0;
@@ -371,7 +373,8 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   gu.hK = Imax;
   {
     Prof p(ctx, kKGateUp);
-    osm::launch_proj(gu, osm::ProjKind::kGateUp, Imax, max_active, ctx->grid_cap, ctx->stream, &ctx->launches);
+    osm::launch_proj(gu, osm::ProjKind::kGateUp, Imax, max_tg, ctx->grid_cap, tchunk, ctx->stream,
+                     &ctx->launches);
   }
   int rc = check_launch(ctx, "gate/up projection");
   if (rc) return rc;
@@ -391,7 +394,7 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   {
     Prof p(ctx, kKDown);
     osm::launch_proj(dn, Imax <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12, L->g.H,
-                     max_active, ctx->grid_cap, ctx->stream, &ctx->launches);
+                     max_tg, ctx->grid_cap, tchunk, ctx->stream, &ctx->launches);
   }
   rc = check_launch(ctx, "down projection");
   if (rc) return rc;
@@ -551,6 +554,7 @@ int osm_context_status(osm_context* ctx, uint32_t* status, uint64_t* exact_token
     OSM_CUDA(ctx, cudaMemcpy(&st, ctx->sc.status, 4, cudaMemcpyDeviceToHost));
     OSM_CUDA(ctx, cudaMemcpy(&ex, ctx->sc.exact_count, 8, cudaMemcpyDeviceToHost));
     OSM_CUDA(ctx, cudaMemset(ctx->sc.status, 0, 4));
+    OSM_CUDA(ctx, cudaMemset(ctx->sc.exact_count, 0, 8));
   }
   if (status) *status = st;
   if (exact_tokens) *exact_tokens = ex;
@@ -624,8 +628,8 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
   if (rc) return rc;
   Scratch& s = ctx->sc;
   osm::launch_frag_prep(x, (int)tokens, (int)in_dim, s.xfrag, s.xfsum8, ctx->stream, &ctx->launches);
-  osm::launch_setup_single((int)tokens, nullptr, s.n_active, s.act_kind, s.act_ptr, s.act_off,
-                           s.act_cnt, s.pair_tok, s.pair_pick, s.out_row, ctx->stream,
+  osm::launch_setup_single((int)tokens, nullptr, s.n_active, s.act, s.n_tg, s.tg_expert,
+                           s.tg_begin, s.pair_tok, s.pair_pick, s.out_row, ctx->stream,
                            &ctx->launches);
   osm::ProjArgs a{};
   for (int i = 0; i < 2; ++i) {
@@ -635,11 +639,10 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
     a.sec.rows[i] = (int)out_dim;
     a.sec.K[i] = (int)in_dim;
   }
-  a.n_active = s.n_active;
-  a.act_kind = s.act_kind;
-  a.act_ptr = s.act_ptr;
-  a.act_off = s.act_off;
-  a.act_cnt = s.act_cnt;
+  a.n_tg = s.n_tg;
+  a.act = s.act;
+  a.tg_expert = s.tg_expert;
+  a.tg_begin = s.tg_begin;
   a.pair_tok = s.pair_tok;
   a.frag_by_pair = 0;
   a.raw = 1;
@@ -651,8 +654,9 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
   a.pair_pick = s.pair_pick;
   a.kp1 = 1;
   a.ostride = (int)out_dim;
-  osm::launch_proj(a, osm::ProjKind::kSingle, (int)out_dim, 1, ctx->grid_cap, ctx->stream,
-                   &ctx->launches);
+  osm::launch_proj(a, osm::ProjKind::kSingle, (int)out_dim,
+                   (int)((tokens + osm::kTokGroup - 1) / osm::kTokGroup), ctx->grid_cap,
+                   (int)std::min<uint32_t>(tokens, 8), ctx->stream, &ctx->launches);
   return check_launch(ctx, "q4 gemv");
 }
 
@@ -697,16 +701,15 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   Scratch& s = ctx->sc;
   osm::launch_frag_prep(x, (int)tokens, (int)L.hidden, s.xfrag, s.xfsum8, ctx->stream,
                         &ctx->launches);
-  osm::launch_setup_single((int)tokens, static_cast<const uint8_t*>(slot), s.n_active, s.act_kind,
-                           s.act_ptr, s.act_off, s.act_cnt, s.pair_tok, s.pair_pick, s.out_row,
+  osm::launch_setup_single((int)tokens, static_cast<const uint8_t*>(slot), s.n_active, s.act,
+                           s.n_tg, s.tg_expert, s.tg_begin, s.pair_tok, s.pair_pick, s.out_row,
                            ctx->stream, &ctx->launches);
   osm::ProjArgs gu{};
   fill_sections(gu.sec, L, L, true);
-  gu.n_active = s.n_active;
-  gu.act_kind = s.act_kind;
-  gu.act_ptr = s.act_ptr;
-  gu.act_off = s.act_off;
-  gu.act_cnt = s.act_cnt;
+  gu.n_tg = s.n_tg;
+  gu.act = s.act;
+  gu.tg_expert = s.tg_expert;
+  gu.tg_begin = s.tg_begin;
   gu.pair_tok = s.pair_tok;
   gu.frag_stride = (int)L.hidden / 8;
   gu.frag = s.xfrag;
@@ -714,7 +717,9 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   gu.hfrag = s.hfrag;
   gu.hfsum8 = s.hfsum8;
   gu.hK = (int)L.inter;
-  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, 1, ctx->grid_cap, ctx->stream,
+  const int ntg1 = (int)((tokens + osm::kTokGroup - 1) / osm::kTokGroup);
+  const int tch1 = (int)std::min<uint32_t>(tokens, 8);
+  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, ntg1, ctx->grid_cap, tch1, ctx->stream,
                    &ctx->launches);
   rc = check_launch(ctx, "expert gate/up");
   if (rc) return rc;
@@ -730,7 +735,7 @@ int osm_expert_forward(osm_context* ctx, const void* slot, const osm_expert_layo
   dn.kp1 = 1;
   dn.ostride = (int)L.hidden;
   osm::launch_proj(dn, L.inter <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12,
-                   (int)L.hidden, 1, ctx->grid_cap, ctx->stream, &ctx->launches);
+                   (int)L.hidden, ntg1, ctx->grid_cap, tch1, ctx->stream, &ctx->launches);
   return check_launch(ctx, "expert down");
 }
 

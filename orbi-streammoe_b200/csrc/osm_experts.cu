@@ -45,18 +45,21 @@ __device__ __forceinline__ void mma_group(float d[4], uint2 wl, uint2 wh, const 
   }
 }
 
-// One work item: CTA tile `bx` (TILES row tiles) of active expert j.
+// One work item: token group `tg` (up to kTokGroup tokens of one active
+// expert) x CTA tile `bx` (TILES row tiles).  Activation fragments of each
+// 8-token chunk are staged in shared memory by the whole CTA at once (xs:
+// [8][KW*2 + 1] uint4, padded against bank conflicts).
 template <bool PAIRED, int KSPLIT, int MAXG>
 __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles, bool first,
-                                          int& n_items) {
+                                          int& n_items, uint4* xs) {
   constexpr int TILES = kWarps / KSPLIT;
   constexpr int TROWS = PAIRED ? 8 : 16;
-  const int j = item / tiles, bx = item - (item / tiles) * tiles;
+  const int tg = item / tiles, bx = item - (item / tiles) * tiles;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, gid = lane >> 2, t = lane & 3;
   const int tile = warp / KSPLIT, ks = warp - tile * KSPLIT;
-  // The shared expert is active entry 0: its weights are known before the
-  // routing is, so they are fetched before waiting on the router.
-  const bool early = first && a.shared_first && j == 0;
+  // Token group 0 belongs to the shared expert when there is one: its weights
+  // are known before the routing is, so they are fetched before the wait.
+  const bool early = first && a.shared_first && tg == 0;
   const uint8_t* base = early ? a.shared_ptr : nullptr;
   int kind = 1;
   uint2 wl[MAXG], wh[MAXG];
@@ -96,12 +99,14 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
   if (first) {
     pdl_wait();
     pdl_trigger();
-    n_items = *a.n_active * tiles;
+    n_items = *a.n_tg * tiles;
   }
   if (item >= n_items) return;
+  const int j = a.tg_expert[tg];
+  const ActEntry en = a.act[j];
   if (!early) {
-    base = a.act_ptr[j];
-    kind = a.act_kind[j];
+    base = en.ptr;
+    kind = en.kind;
     if (base == nullptr && !a.raw) return;  // non-resident expert (status already set)
     fetch();
   }
@@ -111,15 +116,24 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
   __shared__ int rowof[8];
   __shared__ float red[kWarps][32][4];
   __shared__ float hs[TILES][8][9];
-  const int off = a.act_off[j], cnt = a.act_cnt[j];
+  const int t_begin = a.tg_begin[tg];
+  const int t_end = min(en.cnt, t_begin + kTokGroup);
   const bool live = r0 < rows;
-  for (int c0 = 0; c0 < cnt; c0 += 8) {
-    const int nv = min(8, cnt - c0);
+  const int xstride = KW * 2 + 1;
+  for (int c0 = t_begin; c0 < t_end; c0 += 8) {
+    const int nv = min(8, t_end - c0);
     if (threadIdx.x < 8) {
-      const int p = off + c0 + threadIdx.x;
+      const int p = en.off + c0 + threadIdx.x;
       rowof[threadIdx.x] = threadIdx.x < nv ? (a.frag_by_pair ? p : a.pair_tok[p]) : 0;
     }
     __syncthreads();
+    // stage the chunk's activation fragments and group sums (all loads in flight)
+    const int per_tok = KW * 2;
+#pragma unroll 8
+    for (int i = threadIdx.x; i < nv * per_tok; i += blockDim.x) {
+      const int n = i / per_tok, r = i - n * per_tok;
+      xs[n * xstride + r] = __ldg(a.frag + (size_t)rowof[n] * a.frag_stride * 2 + r);
+    }
     for (int i = threadIdx.x; i < 8 * G; i += blockDim.x) {
       const int n = i / G, g = i - n * G;
       float s = 0.0f;
@@ -132,29 +146,24 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
     }
     __syncthreads();
     const bool has_tok = gid < nv;
-    const uint4* xf = a.frag + (size_t)rowof[has_tok ? gid : 0] * a.frag_stride * 2;
+    const uint4* xrow = xs + (has_tok ? gid : 0) * xstride;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    uint4 cur[4], nxt[4];
-    auto load_x = [&](int i, uint4 (&dst)[4]) {
-      const int g = ks + KSPLIT * i;
-      if (has_tok && live && g < G) {
-        const int c = 8 * g + 2 * t;
-        dst[0] = __ldg(xf + 2 * c);
-        dst[1] = __ldg(xf + 2 * c + 1);
-        dst[2] = __ldg(xf + 2 * c + 2);
-        dst[3] = __ldg(xf + 2 * c + 3);
-      } else {
-        dst[0] = dst[1] = dst[2] = dst[3] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    };
-    load_x(0, cur);
 #pragma unroll
     for (int i = 0; i < MAXG; ++i) {
       const int g = ks + KSPLIT * i;
-      if (i + 1 < MAXG) load_x(i + 1, nxt);
       if (g < G) {
+        uint4 xf[4];
+        if (has_tok) {
+          const int c = 8 * g + 2 * t;
+          xf[0] = xrow[2 * c];
+          xf[1] = xrow[2 * c + 1];
+          xf[2] = xrow[2 * c + 2];
+          xf[3] = xrow[2 * c + 3];
+        } else {
+          xf[0] = xf[1] = xf[2] = xf[3] = make_uint4(0u, 0u, 0u, 0u);
+        }
         float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        mma_group(d, wl[i], wh[i], cur);
+        mma_group(d, wl[i], wh[i], xf);
         const float f0 = fsg[2 * t][g], f1 = fsg[2 * t + 1][g];
         const float sl = bf16_bits_to_f32(sp[i] & 0xFFFFu), sh = bf16_bits_to_f32(sp[i] >> 16);
         const float bl = bf16_bits_to_f32(bp[i] & 0xFFFFu), bh = bf16_bits_to_f32(bp[i] >> 16);
@@ -162,10 +171,6 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
         acc[1] = fmaf(bl, f1, fmaf(sl, d[1], acc[1]));
         acc[2] = fmaf(bh, f0, fmaf(sh, d[2], acc[2]));
         acc[3] = fmaf(bh, f1, fmaf(sh, d[3], acc[3]));
-      }
-      if (i + 1 < MAXG) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) cur[q] = nxt[q];
       }
     }
     float tot[4] = {acc[0], acc[1], acc[2], acc[3]};
@@ -190,7 +195,7 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
         hs[tile][gid][2 * t + 1] = __fmul_rn(ref_silu(tot[1]), tot[3]);
         __syncwarp();
         if (lane < nv) {
-          const int p = off + c0 + lane;
+          const int p = en.off + c0 + lane;
           const int hch = a.hK >> 3;
           uint32_t hi[8], lo[8];
           float fs = hs[tile][0][lane];
@@ -210,7 +215,7 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
         for (int q = 0; q < 2; ++q) {
           const int n = 2 * t + q;
           if (n < nv) {
-            const int p = off + c0 + n;
+            const int p = en.off + c0 + n;
             const int orow = a.out_row ? a.out_row[p] : a.pair_tok[p] * a.kp1 + a.pair_pick[p];
             float* o = a.out + (size_t)orow * a.ostride;
             o[r0 + gid] = tot[q];
@@ -223,17 +228,16 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
   }
 }
 
-// Persistent grid: CTAs stride over (active expert, CTA tile) items; the
-// number of active experts is only known on the device.  Items 0..tiles-1
-// belong to active entry 0 (the shared expert when present), whose weights
-// are fetched before the wait on the router.
+// Persistent grid: CTAs stride over (token group, CTA tile) items; the number
+// of token groups is only known on the device.
 template <bool PAIRED, int KSPLIT, int MAXG>
 __global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjArgs a, int tiles) {
+  extern __shared__ uint4 xs_dyn[];
   int n_items = 0x7FFFFFFF;
   bool first = true;
   for (int item = blockIdx.x; first || item < n_items; item += gridDim.x) {
     if (!first) __syncthreads();
-    proj_item<PAIRED, KSPLIT, MAXG>(a, item, tiles, first, n_items);
+    proj_item<PAIRED, KSPLIT, MAXG>(a, item, tiles, first, n_items, xs_dyn);
     first = false;
   }
 }
@@ -266,22 +270,32 @@ __global__ void frag_prep_kernel(const float* __restrict__ x, int rows, int K,
 }
 
 // Expert list for a single expert over `T` tokens (standalone projections).
-__global__ void setup_single_kernel(int T, const uint8_t* ptr, int* n_active, int* act_kind,
-                                    const uint8_t** act_ptr, int* act_off, int* act_cnt,
-                                    int* pair_tok, int* pair_pick, int* out_row) {
+__global__ void setup_single_kernel(int T, const uint8_t* ptr, int* n_active, ActEntry* act,
+                                    int* n_tg, int* tg_expert, int* tg_begin, int* pair_tok,
+                                    int* pair_pick, int* out_row) {
   pdl_wait();
   pdl_trigger();
+  const int ng = (T + kTokGroup - 1) / kTokGroup;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     *n_active = 1;
-    act_kind[0] = 0;
-    act_ptr[0] = ptr;
-    act_off[0] = 0;
-    act_cnt[0] = T;
+    *n_tg = ng;
+    ActEntry en;
+    en.ptr = ptr;
+    en.off = 0;
+    en.cnt = T;
+    en.kind = 0;
+    en.tg0 = 0;
+    en.pad0 = en.pad1 = 0;
+    act[0] = en;
   }
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T; i += gridDim.x * blockDim.x) {
     pair_tok[i] = i;
     pair_pick[i] = 0;
     out_row[i] = i;
+    if (i < ng) {
+      tg_expert[i] = 0;
+      tg_begin[i] = i * kTokGroup;
+    }
   }
 }
 
@@ -316,40 +330,47 @@ void launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8
   if (launches) *launches += 1;
 }
 
-void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active, int grid_cap,
-                 cudaStream_t s, uint64_t* launches) {
-  auto go = [&](auto kernel, int rows_per_cta) {
+void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
+                 int max_tokens_chunk, cudaStream_t s, uint64_t* launches) {
+  auto go = [&](auto kernel, int rows_per_cta, int K, int ctas_per_sm) {
     const int tiles = (max_rows + rows_per_cta - 1) / rows_per_cta;
-    long long items = (long long)tiles * max_active;
-    // the gate/up kernel is register-limited to 5 resident CTAs per SM, the
-    // others to 4 (grid_cap counts 4 per SM)
-    const int cap = kind == ProjKind::kGateUp ? grid_cap / 4 * 5 : grid_cap;
+    const int tc = max_tokens_chunk < 8 ? (max_tokens_chunk < 1 ? 1 : max_tokens_chunk) : 8;
+    const size_t smem = (size_t)tc * ((K >> 3) * 2 + 1) * sizeof(uint4);
+    // resident CTAs: registers allow ctas_per_sm, shared memory (227 KB) may allow fewer
+    int per_sm = ctas_per_sm;
+    const int by_smem = (int)((227u * 1024u) / (smem + 8192));
+    if (by_smem < per_sm) per_sm = by_smem < 1 ? 1 : by_smem;
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int cap = grid_cap / 4 * per_sm;
+    long long items = (long long)tiles * max_tg;
     int grid = (int)(items < cap ? items : cap);
     if (grid < 1) grid = 1;
-    launch_pdl(kernel, dim3(grid), dim3(kWarps * 32), 0, s, a, tiles);
+    launch_pdl(kernel, dim3(grid), dim3(kWarps * 32), smem, s, a, tiles);
   };
+  const int Kmax = a.sec.K[0] > a.sec.K[1] ? a.sec.K[0] : a.sec.K[1];
   switch (kind) {
     case ProjKind::kGateUp:  // 8 intermediate rows per CTA tile, input split over 4 warps
-      go(proj_kernel<true, 4, 8>, 8);
+      go(proj_kernel<true, 4, 8>, 8, Kmax, 5);
       break;
     case ProjKind::kDown:    // 64 output rows per CTA tile, one warp per 16 rows (K <= 512)
-      go(proj_kernel<false, 1, 8>, 64);
+      go(proj_kernel<false, 1, 8>, 64, Kmax, 4);
       break;
     case ProjKind::kDown12:  // the same for K <= 768
-      go(proj_kernel<false, 1, 12>, 64);
+      go(proj_kernel<false, 1, 12>, 64, Kmax, 4);
       break;
     case ProjKind::kSingle:  // 16 rows per CTA tile, input split over 4 warps (K <= 2048)
-      go(proj_kernel<false, 4, 8>, 16);
+      go(proj_kernel<false, 4, 8>, 16, Kmax, 4);
       break;
   }
   if (launches) *launches += 1;
 }
 
-void launch_setup_single(int T, const uint8_t* ptr, int* n_active, int* act_kind,
-                         const uint8_t** act_ptr, int* act_off, int* act_cnt, int* pair_tok,
-                         int* pair_pick, int* out_row, cudaStream_t s, uint64_t* launches) {
+void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
+                         int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
+                         int* out_row, cudaStream_t s, uint64_t* launches) {
   launch_pdl(setup_single_kernel, dim3(grid_for((size_t)T, 256)), dim3(256), 0, s, T, ptr,
-             n_active, act_kind, act_ptr, act_off, act_cnt, pair_tok, pair_pick, out_row);
+             n_active, act, n_tg, tg_expert, tg_begin, pair_tok, pair_pick, out_row);
   if (launches) *launches += 1;
 }
 

@@ -12,6 +12,17 @@ namespace osm {
 //   element (e, h), l = h / c, o = h % c  ->  ((e*nvec + o/8)*32 + l)*8 + o%8
 // so the 32 lanes of a warp read 512 contiguous bytes per step while each lane
 // walks its own contiguous chunk (needed by the error bound of the router).
+// One active expert of a call (written by the grouping step): 32 bytes.
+struct ActEntry {
+  const uint8_t* ptr;  // slot base (null: not resident)
+  int off;             // first pair position of its tokens
+  int cnt;             // tokens routed to it
+  int kind;            // 0 routed layout, 1 shared layout
+  int tg0;             // first token group (groups of kTokGroup tokens)
+  int pad0, pad1;
+};
+constexpr int kTokGroup = 32;  // tokens per projection work item
+
 struct RouterGeom {
   int H, Hp, c, nvec, E, k;
   int f32w;                 // router stored as fp32 (else bf16)
@@ -50,10 +61,10 @@ struct RouterArgs {
   unsigned int* ticket;
   int* counts;              // [E+1] scratch (zeroed by the last block)
   int* n_active;
-  int* act_kind;            // 0 routed layout, 1 shared layout
-  const uint8_t** act_ptr;
-  int* act_off;
-  int* act_cnt;
+  ActEntry* act;            // [E+1]
+  int* n_tg;                // token groups of the call
+  int* tg_expert;           // token group -> active entry
+  int* tg_begin;            // token group -> first token within the entry
   int* pair_tok;            // [B*(k+1)]
   int* pair_pick;
   int* cursor;              // [E+1]
@@ -87,11 +98,10 @@ struct ProjArgs {
   ProjSections sec;
   int shared_first;              // active entry 0 is the shared expert (layout 1)
   const uint8_t* shared_ptr;     // its slot, readable before the routing exists
-  const int* n_active;
-  const int* act_kind;
-  const uint8_t* const* act_ptr;
-  const int* act_off;
-  const int* act_cnt;
+  const int* n_tg;
+  const ActEntry* act;
+  const int* tg_expert;
+  const int* tg_begin;
   const int* pair_tok;           // pair -> input fragment row (for paired)
   int frag_by_pair;              // 1: input row = pair position
   int raw;                       // 1: sections are absolute addresses
@@ -113,8 +123,9 @@ struct ProjArgs {
 enum class ProjKind { kGateUp, kDown, kDown12, kSingle };
 // grid_cap: resident CTAs the device holds (SMs x CTAs per SM); the grid is
 // persistent and strides over (active expert, tile) items.
-void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_active, int grid_cap,
-                 cudaStream_t s, uint64_t* launches);
+// max_tg: upper bound of the call's token groups (grid sizing only).
+void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
+                 int max_tokens_chunk, cudaStream_t s, uint64_t* launches);
 
 struct CombineArgs {
   const float* partial;          // [B][k+1][H]
@@ -144,8 +155,8 @@ void launch_gen_quant(uint64_t seed, uint64_t tensor, float sigma, int rows, int
 // Permute fp32 [E][H] router rows (bf16-representable) into the router layout.
 void launch_router_pack(const float* w, const RouterGeom& g, void* wp, cudaStream_t s,
                         uint64_t* launches);
-void launch_setup_single(int T, const uint8_t* ptr, int* n_active, int* act_kind,
-                         const uint8_t** act_ptr, int* act_off, int* act_cnt, int* pair_tok,
-                         int* pair_pick, int* out_row, cudaStream_t s, uint64_t* launches);
+void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
+                         int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
+                         int* out_row, cudaStream_t s, uint64_t* launches);
 
 }  // namespace osm

@@ -319,24 +319,41 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
   for (int j = threadIdx.x; j < n_active; j += blockDim.x) off[j] = cnt[expert_of[j]];
   __syncthreads();
   block_exclusive_scan(off, n_active, red);
+  // token groups per active expert (cur[] is free until the scatter)
+  for (int j = threadIdx.x; j < n_active; j += blockDim.x)
+    cur[j] = (cnt[expert_of[j]] + kTokGroup - 1) / kTokGroup;
+  __syncthreads();
+  const int n_tg = block_exclusive_scan(cur, n_active, red);
   for (int j = threadIdx.x; j < n_active; j += blockDim.x) {
     const int e = expert_of[j];
-    a.act_off[j] = off[j];
-    a.act_cnt[j] = cnt[e];
+    ActEntry en;
+    en.off = off[j];
+    en.cnt = cnt[e];
+    en.tg0 = cur[j];
+    en.pad0 = en.pad1 = 0;
     if (e == E) {
-      a.act_kind[j] = 1;
-      a.act_ptr[j] = a.shared_slot;
+      en.kind = 1;
+      en.ptr = a.shared_slot;
     } else {
-      a.act_kind[j] = 0;
+      en.kind = 0;
       const int slot = a.slot_of[e];
       if (slot < 0) {
         atomicOr(a.status, kStatusNotResident);
-        a.act_ptr[j] = nullptr;
+        en.ptr = nullptr;
       } else {
-        a.act_ptr[j] = a.slab + (size_t)slot * a.slab_stride;
+        en.ptr = a.slab + (size_t)slot * a.slab_stride;
       }
     }
+    a.act[j] = en;
+    const int ng = (en.cnt + kTokGroup - 1) / kTokGroup;
+    for (int q = 0; q < ng; ++q) {
+      a.tg_expert[en.tg0 + q] = j;
+      a.tg_begin[en.tg0 + q] = q * kTokGroup;
+    }
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NE; i += blockDim.x) cur[i] = 0;
+  __syncthreads();
   for (int p = threadIdx.x; p < B * k; p += blockDim.x) {
     const uint32_t e = __ldcg(a.ids + p);
     if (e >= (uint32_t)E) continue;
@@ -349,13 +366,16 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
       a.pair_tok[off[0] + t] = t;
       a.pair_pick[off[0] + t] = k;
     }
-  if (threadIdx.x == 0) *a.n_active = n_active;
+  if (threadIdx.x == 0) {
+    *a.n_active = n_active;
+    *a.n_tg = n_tg;
+  }
 }
 
 // Softmax weights of the picks from logits lsel[0..k) (lsel[0] the largest)
-// with the sum over the fast logits v[] (lane-strided); lane 0 writes.
-__device__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32],
-                              const int* sid, const float* lsel) {
+// with the sum over the fast logits v[] (lane-strided); lane j handles pick j.
+__device__ __noinline__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32],
+                                           const int* sid, const float* lsel) {
   const int lane = threadIdx.x & 31;
   const int k = a.g.k;
   const float mx = lsel[0];
@@ -364,21 +384,15 @@ __device__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32]
   for (int i = 0; i < 32; ++i)
     if (i * 32 + lane < a.g.E) s += expf(__fsub_rn(v[i], mx));
   s = warp_sum(s);
-  if (lane == 0) {
-    float p[kMaxTopK];
-    float mass = 0.0f;
-    for (int j = 0; j < k; ++j) {
-      p[j] = __fdiv_rn(expf(__fsub_rn(lsel[j], mx)), s);
-      mass = __fadd_rn(mass, p[j]);
-    }
-    if (!(mass > 0.0f) || !isfinite(mass) || !(s > 0.0f) || !isfinite(s))
-      atomicOr(a.status, kStatusBadMass);
-    for (int j = 0; j < k; ++j) {
-      a.ids[(size_t)tok * k + j] = (uint32_t)sid[j];
-      a.weights[(size_t)tok * k + j] = a.norm ? __fdiv_rn(p[j], mass) : p[j];
-    }
-    a.mass[tok] = mass;
+  const float p = lane < k ? __fdiv_rn(expf(__fsub_rn(lsel[lane], mx)), s) : 0.0f;
+  const float mass = warp_sum(p);
+  if (lane == 0 && (!(mass > 0.0f) || !isfinite(mass) || !(s > 0.0f) || !isfinite(s)))
+    atomicOr(a.status, kStatusBadMass);
+  if (lane < k) {
+    a.ids[(size_t)tok * k + lane] = (uint32_t)sid[lane];
+    a.weights[(size_t)tok * k + lane] = a.norm ? __fdiv_rn(p, mass) : p;
   }
+  if (lane == 0) a.mass[tok] = mass;
 }
 
 // True when consecutive (exact) logits are far enough apart that their
@@ -398,6 +412,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   __shared__ float cand_l[kMaxCand];
   __shared__ int s_flag, s_ncand;
   __shared__ float s_bm, s_bcast;
+  __shared__ float sg_part[kSelThreads / 32];
   const RouterGeom g = a.g;
   const int tok = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -426,6 +441,37 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   nonfinite = __syncthreads_or(nonfinite);
   if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
   const bool route = !nonfinite && !a.skip_route;
+  // ---- warps 1..: activation fragments and the shared-gate dot, while
+  //      warp 0 selects ----
+  if (warp != 0) {
+    const int nt = blockDim.x - 32, me = tid - 32;
+    if (a.xfrag != nullptr) {
+      const int nch = g.H >> 3;
+      for (int c = me; c < nch; c += nt) {
+        const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
+        const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
+        const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
+        float fs = xc[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
+        uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
+        dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
+                            pack2(hi[3], hi[7]));
+        dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
+                            pack2(lo[3], lo[7]));
+        a.xfsum8[(size_t)tok * nch + c] = fs;
+      }
+    }
+    if (a.sgate_w != nullptr) {
+      float d = 0.0f;
+      for (int h = me; h < g.H; h += nt) d = fmaf(a.sgate_w[h], xs[h], d);
+      d = warp_sum(d);
+      if (lane == 0) sg_part[warp] = d;
+    }
+  }
   // ---- 1. fast path: certified top-k over the fast logits ----
   float v[32];
   if (warp == 0 && route) {
@@ -610,39 +656,17 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
     if (a.weights_out) a.weights_out[(size_t)tok * k + tid] = a.weights[(size_t)tok * k + tid];
   }
   if (tid == 0 && a.mass_out && !a.skip_route) a.mass_out[tok] = a.mass[tok];
-  // ---- shared expert scalar gate: sigmoid(g . x) ----
-  if (a.sgate_w != nullptr) {
-    float d = 0.0f;
-    for (int h = tid; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
-    const float dot = block_reduce_sum(d, red);
-    if (tid == 0) {
-      const float s = ref_sigmoid(dot);
-      a.sgate[tok] = s;
-      if (a.sgate_out) a.sgate_out[tok] = s;
-    }
-  } else if (tid == 0) {
-    if (a.sgate) a.sgate[tok] = 0.0f;
-    if (a.sgate_out) a.sgate_out[tok] = 0.0f;
-  }
-  // ---- activation fragments for the expert kernels ----
-  if (a.xfrag != nullptr) {
-    const int nch = g.H >> 3;
-    for (int c = tid; c < nch; c += blockDim.x) {
-      const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
-      const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
-      const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
-      uint32_t hi[8], lo[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
-      float fs = xc[0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
-      uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
-      dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
-                          pack2(hi[3], hi[7]));
-      dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
-                          pack2(lo[3], lo[7]));
-      a.xfsum8[(size_t)tok * nch + c] = fs;
+  // ---- shared expert scalar gate (partials of warps 1.. summed here) ----
+  if (tid == 0) {
+    if (a.sgate_w != nullptr) {
+      float dot = 0.0f;
+      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) dot += sg_part[w];
+      const float sgv = ref_sigmoid(dot);
+      a.sgate[tok] = sgv;
+      if (a.sgate_out) a.sgate_out[tok] = sgv;
+    } else {
+      if (a.sgate) a.sgate[tok] = 0.0f;
+      if (a.sgate_out) a.sgate_out[tok] = 0.0f;
     }
   }
   if (!a.do_group) return;
