@@ -217,6 +217,27 @@ int osm_moe_sublayer_forward(osm_layer* layer, const float* residual_dev,
                              float* weights_dev, float* mass_dev,
                              float* shared_gate_dev, uint32_t flags);
 
+/* ---- execution plans: one call captured as a CUDA graph (no counterpart in
+ *      the reference, whose every GPU op is a synchronous submit + fence,
+ *      src/backend/vulkan_q4_gemv.cpp:1645-1657).  A plan replays
+ *      osm_moe_forward (or, with OSM_PLAN_SUBLAYER, osm_moe_sublayer_forward)
+ *      on fixed device buffers with one graph launch.  When x_host / out_host
+ *      (pinned) are given, the H2D copy of x and the D2H copy of out are part
+ *      of the plan.  With OSM_PLAN_PROFILE each kernel is bracketed by event
+ *      nodes, read by osm_plan_profile_read. ---- */
+#define OSM_PLAN_SUBLAYER 0x100u
+#define OSM_PLAN_PROFILE 0x200u
+typedef struct osm_plan osm_plan;
+int osm_plan_create(osm_layer* layer, uint32_t tokens, const float* x_dev, float* out_dev,
+                    uint32_t* ids_dev, float* weights_dev, const float* x_host,
+                    float* out_host, uint32_t flags, osm_plan** out);
+int osm_plan_launch(osm_plan* plan);
+int osm_plan_destroy(osm_plan* plan);
+/* Adds the last replay's per-kernel times (OSM_PLAN_PROFILE plans). */
+int osm_plan_profile_read(osm_plan* plan, double* ms, uint64_t* launches);
+/* Kernels one replay launches. */
+uint32_t osm_plan_kernels(const osm_plan* plan);
+
 /* Number of kernels this library launched on `ctx` since creation. */
 uint64_t osm_context_launches(const osm_context* ctx);
 

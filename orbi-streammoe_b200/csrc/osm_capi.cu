@@ -103,6 +103,13 @@ struct osm_slab {
   uint64_t h2d_bytes = 0;
 };
 
+struct osm_plan {
+  osm_layer* layer = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::vector<ProfRec> recs;
+  uint32_t kernels = 0;
+};
+
 struct osm_layer {
   osm_context* ctx = nullptr;
   osm::RouterGeom g{};
@@ -1025,6 +1032,104 @@ int osm_moe_sublayer_forward(osm_layer* L, const float* residual, uint32_t T, fl
   if (rc) return rc;
   return osm_moe_forward(L, nrm, T, out, ids, w, mass, sgate, residual, flags | OSM_ADD_RESIDUAL);
 }
+
+int osm_plan_create(osm_layer* L, uint32_t T, const float* x, float* out, uint32_t* ids,
+                    float* w, const float* x_host, float* out_host, uint32_t flags,
+                    osm_plan** res) {
+  if (!res) return OSM_EINVAL;
+  *res = nullptr;
+  int rc = layer_ready(L, T, true);
+  if (rc) return rc;
+  osm_context* ctx = L->ctx;
+  if (!x || !out) return fail(ctx, OSM_EINVAL, "plan: null input/output");
+  if (ctx->stream == nullptr || ctx->stream == cudaStreamLegacy || ctx->stream == cudaStreamPerThread)
+    return fail(ctx, OSM_EINVAL, "plan: capture needs a non-default stream");
+  DeviceGuard dg(ctx->device);
+  auto* plan = new (std::nothrow) osm_plan();
+  if (!plan) return OSM_ENOMEM;
+  plan->layer = L;
+  const bool prof = (flags & OSM_PLAN_PROFILE) != 0;
+  const bool saved_prof = ctx->prof_on;
+  std::vector<ProfRec> saved_recs;
+  saved_recs.swap(ctx->recs);
+  ctx->prof_on = prof;
+  const uint64_t l0 = ctx->launches;
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) {
+    ctx->prof_on = saved_prof;
+    ctx->recs.swap(saved_recs);
+    delete plan;
+    return cuda_fail(ctx, e, "plan: begin capture");
+  }
+  const size_t bytes = (size_t)T * L->g.H * sizeof(float);
+  if (x_host) cudaMemcpyAsync(const_cast<float*>(x), x_host, bytes, cudaMemcpyHostToDevice, ctx->stream);
+  const uint32_t fw = flags & (OSM_ROUTE_EXACT | OSM_RMSNORM_EXACT);
+  if (flags & OSM_PLAN_SUBLAYER)
+    rc = osm_moe_sublayer_forward(L, x, T, out, nullptr, ids, w, nullptr, nullptr, fw);
+  else
+    rc = osm_moe_forward(L, x, T, out, ids, w, nullptr, nullptr, nullptr, fw);
+  if (out_host) cudaMemcpyAsync(out_host, out, bytes, cudaMemcpyDeviceToHost, ctx->stream);
+  e = cudaStreamEndCapture(ctx->stream, &graph);
+  plan->kernels = (uint32_t)(ctx->launches - l0);
+  ctx->launches = l0;
+  plan->recs.swap(ctx->recs);
+  ctx->recs.swap(saved_recs);
+  ctx->prof_on = saved_prof;
+  if (rc == OSM_OK && e != cudaSuccess) rc = cuda_fail(ctx, e, "plan: end capture");
+  if (rc == OSM_OK) {
+    e = cudaGraphInstantiate(&plan->exec, graph, 0);
+    if (e != cudaSuccess) rc = cuda_fail(ctx, e, "plan: instantiate");
+  }
+  if (graph) cudaGraphDestroy(graph);
+  if (rc != OSM_OK) {
+    osm_plan_destroy(plan);
+    return rc;
+  }
+  *res = plan;
+  return OSM_OK;
+}
+
+int osm_plan_launch(osm_plan* plan) {
+  if (!plan || !plan->exec) return OSM_EINVAL;
+  osm_context* ctx = plan->layer->ctx;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaGraphLaunch(plan->exec, ctx->stream));
+  ctx->launches += plan->kernels;
+  return OSM_OK;
+}
+
+int osm_plan_destroy(osm_plan* plan) {
+  if (!plan) return OSM_EINVAL;
+  osm_context* ctx = plan->layer->ctx;
+  DeviceGuard dg(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  if (plan->exec) cudaGraphExecDestroy(plan->exec);
+  for (const ProfRec& r : plan->recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  delete plan;
+  return OSM_OK;
+}
+
+int osm_plan_profile_read(osm_plan* plan, double* ms, uint64_t* launches) {
+  if (!plan) return OSM_EINVAL;
+  osm_context* ctx = plan->layer->ctx;
+  DeviceGuard dg(ctx->device);
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  for (const ProfRec& r : plan->recs) {
+    float t = 0.0f;
+    if (cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess && r.kind >= 0 &&
+        r.kind < OSM_KERNEL_KINDS) {
+      if (ms) ms[r.kind] += t;
+      if (launches) launches[r.kind] += 1;
+    }
+  }
+  return OSM_OK;
+}
+
+uint32_t osm_plan_kernels(const osm_plan* plan) { return plan ? plan->kernels : 0; }
 
 int osm_gen_normal(osm_context* ctx, uint64_t seed, uint64_t tensor, float sigma, float* out,
                    size_t n, size_t first) {

@@ -254,3 +254,42 @@ class Layer:
                                                       _ptr(normalized), _ptr(ids), _ptr(weights),
                                                       _ptr(mass), _ptr(shared_gate), flags),
                        "sublayer")
+
+
+class Plan:
+    """One sublayer call captured as a CUDA graph on fixed device buffers
+    (optionally with the pinned-host H2D of x and D2H of out)."""
+
+    def __init__(self, layer: Layer, tokens: int, x, out, ids=None, weights=None, x_host=None,
+                 out_host=None, exact_route=False, sublayer=False, profile=False):
+        self.layer = layer
+        flags = ((_lib.OSM_ROUTE_EXACT if exact_route else 0)
+                 | (_lib.OSM_PLAN_SUBLAYER if sublayer else 0)
+                 | (_lib.OSM_PLAN_PROFILE if profile else 0))
+        self.h = C.c_void_p()
+        layer.ctx.check(lib().osm_plan_create(layer.h, _ptr(x), tokens, _ptr(out), _ptr(ids),
+                                              _ptr(weights), _ptr(x_host), _ptr(out_host), flags,
+                                              C.byref(self.h)), "plan")
+        self.kernels = lib().osm_plan_kernels(self.h)
+
+    def launch(self):
+        self.layer.ctx.check(lib().osm_plan_launch(self.h), "plan launch")
+
+    def profile_read(self) -> dict:
+        n = _lib.KERNEL_KINDS
+        ms = (C.c_double * n)()
+        cnt = (C.c_uint64 * n)()
+        self.layer.ctx.check(lib().osm_plan_profile_read(self.h, ms, cnt))
+        return {lib().osm_kernel_kind_name(i).decode(): (ms[i], cnt[i]) for i in range(n)
+                if cnt[i]}
+
+    def close(self):
+        if self.h:
+            lib().osm_plan_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -21,6 +21,8 @@ OSM_ETIMEOUT = -6
 OSM_ROUTE_EXACT = 0x1
 OSM_RMSNORM_EXACT = 0x2
 OSM_ADD_RESIDUAL = 0x4
+OSM_PLAN_SUBLAYER = 0x100
+OSM_PLAN_PROFILE = 0x200
 
 KERNEL_KINDS = 8
 
@@ -92,6 +94,11 @@ _SIGS = {
     "osm_moe_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_experts": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_sublayer_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
+    "osm_plan_create": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32, C.POINTER(_P)]),
+    "osm_plan_launch": (C.c_int, [_P]),
+    "osm_plan_destroy": (C.c_int, [_P]),
+    "osm_plan_profile_read": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "osm_plan_kernels": (C.c_uint32, [_P]),
     "osm_gen_normal": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_float, _P, C.c_size_t, C.c_size_t]),
     "osm_gen_expert_slots": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_float, C.c_uint32, C.c_uint32]),
 }

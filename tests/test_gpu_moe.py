@@ -305,3 +305,37 @@ def test_sublayer_rmsnorm_residual(torch, port):
             refy = r[b] + ref
             assert normwise_rel(got[b] - r[b], ref) <= 1e-4
             assert float(np.abs(got[b] - refy).max()) <= 0.03
+
+
+def test_plan_replay_matches_direct_call(torch):
+    """A captured plan (CUDA graph) gives bit-identical results to the direct
+    call, with and without host buffers inside the plan."""
+    import osm_b200 as osm
+
+    fx = _q3n_fixture(torch)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        fx.ctx.set_stream(stream.cuda_stream)
+        try:
+            for B in (1, 5):
+                x = fx.port.gen_normal(9, 40 + B, 1.0, B * fx.H).reshape(B, fx.H)
+                out_ref, ids_ref, _, _, _ = fx.run(torch, x)
+                xd = torch.from_numpy(x).cuda()
+                out = torch.empty(B, fx.H, device="cuda")
+                ids = torch.empty(B, fx.K, dtype=torch.int32, device="cuda")
+                plan = osm.Plan(fx.layer, B, xd, out, ids=ids)
+                for _ in range(3):
+                    plan.launch()
+                torch.cuda.synchronize()
+                assert np.array_equal(out.cpu().numpy().view(np.uint32), out_ref.view(np.uint32))
+                assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_ref)
+                xh = torch.from_numpy(x).pin_memory()
+                oh = torch.empty(B, fx.H).pin_memory()
+                plan2 = osm.Plan(fx.layer, B, xd, out, x_host=xh, out_host=oh)
+                plan2.launch()
+                torch.cuda.synchronize()
+                assert np.array_equal(oh.numpy().view(np.uint32), out_ref.view(np.uint32))
+                plan.close()
+                plan2.close()
+        finally:
+            fx.ctx.set_stream(torch.cuda.current_stream().cuda_stream)
