@@ -267,7 +267,7 @@ class Plan:
                  | (_lib.OSM_PLAN_SUBLAYER if sublayer else 0)
                  | (_lib.OSM_PLAN_PROFILE if profile else 0))
         self.h = C.c_void_p()
-        layer.ctx.check(lib().osm_plan_create(layer.h, _ptr(x), tokens, _ptr(out), _ptr(ids),
+        layer.ctx.check(lib().osm_plan_create(layer.h, tokens, _ptr(x), _ptr(out), _ptr(ids),
                                               _ptr(weights), _ptr(x_host), _ptr(out_host), flags,
                                               C.byref(self.h)), "plan")
         self.kernels = lib().osm_plan_kernels(self.h)

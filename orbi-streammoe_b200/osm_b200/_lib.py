@@ -94,7 +94,7 @@ _SIGS = {
     "osm_moe_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_experts": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_sublayer_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
-    "osm_plan_create": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32, C.POINTER(_P)]),
+    "osm_plan_create": (C.c_int, [_P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32, C.POINTER(_P)]),
     "osm_plan_launch": (C.c_int, [_P]),
     "osm_plan_destroy": (C.c_int, [_P]),
     "osm_plan_profile_read": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),

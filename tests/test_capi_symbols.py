@@ -34,6 +34,24 @@ def test_library_exports_every_declared_symbol(lib):
     assert not missing, missing
 
 
+def declared_arity():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for m in re.finditer(r"\b(osm_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
+        params = m.group(2).strip()
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_python_signatures_match_header_arity(lib):
+    from osm_b200 import _lib
+
+    ar = declared_arity()
+    for name, (_, args) in _lib._SIGS.items():
+        assert len(args) == ar[name], (name, len(args), ar[name])
+
+
 def test_python_binding_covers_header(lib):
     from osm_b200 import _lib
 
