@@ -480,6 +480,17 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
     ctx->grid_cap = sms * 4;
+  int max_smem = 0;
+  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  if (max_smem <= 0) max_smem = 48 * 1024;
+  osm::init_router_attributes(max_smem);
+  osm::init_expert_attributes(max_smem);
+  const cudaError_t ae = cudaGetLastError();
+  if (ae != cudaSuccess) {
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return OSM_ECUDA;
+  }
   *out = ctx;
   return OSM_OK;
 }
@@ -520,6 +531,8 @@ int osm_context_profile_read(osm_context* ctx, double* ms, uint64_t* launches) {
         r.kind < OSM_KERNEL_KINDS) {
       if (ms) ms[r.kind] += t;
       if (launches) launches[r.kind] += 1;
+    } else {
+      cudaGetLastError();  // an unrecorded pair is skipped, not a sticky error
     }
     ctx->ev_pool.push_back(r.a);
     ctx->ev_pool.push_back(r.b);
@@ -1124,6 +1137,8 @@ int osm_plan_profile_read(osm_plan* plan, double* ms, uint64_t* launches) {
         r.kind < OSM_KERNEL_KINDS) {
       if (ms) ms[r.kind] += t;
       if (launches) launches[r.kind] += 1;
+    } else {
+      cudaGetLastError();
     }
   }
   return OSM_OK;

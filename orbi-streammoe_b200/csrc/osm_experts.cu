@@ -340,8 +340,6 @@ void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int
     int per_sm = ctas_per_sm;
     const int by_smem = (int)((227u * 1024u) / (smem + 8192));
     if (by_smem < per_sm) per_sm = by_smem < 1 ? 1 : by_smem;
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int cap = grid_cap / 4 * per_sm;
     long long items = (long long)tiles * max_tg;
     int grid = (int)(items < cap ? items : cap);
@@ -364,6 +362,13 @@ void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int
       break;
   }
   if (launches) *launches += 1;
+}
+
+void init_expert_attributes(int max_smem) {
+  cudaFuncSetAttribute(proj_kernel<true, 4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(proj_kernel<false, 1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(proj_kernel<false, 1, 12>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(proj_kernel<false, 4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
 
 void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,

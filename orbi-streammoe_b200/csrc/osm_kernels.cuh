@@ -72,6 +72,11 @@ struct RouterArgs {
   unsigned long long* exact_count;
 };
 
+// Allow up to max_smem bytes of dynamic shared memory for every kernel that
+// uses it (once per device, before any launch or capture).
+void init_router_attributes(int max_smem);
+void init_expert_attributes(int max_smem);
+
 void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
 void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
 

@@ -712,9 +712,6 @@ void launch_logits_t(const RouterArgs& a, cudaStream_t s) {
   const RouterGeom& g = a.g;
   const dim3 grid((g.E + EXP * kLogitWarps - 1) / (EXP * kLogitWarps), (a.B + TOKS - 1) / TOKS);
   const size_t sm = (size_t)TOKS * 32 * (g.c + 4) * sizeof(float);
-  if (sm > 48 * 1024)
-    cudaFuncSetAttribute(router_logits_kernel<EXP, TOKS>,
-                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   launch_pdl(router_logits_kernel<EXP, TOKS>, grid, dim3(kLogitWarps * 32), sm, s, a);
 }
 
@@ -739,11 +736,15 @@ void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launche
 
 void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
   const size_t sm = select_smem(a.g);
-  if (sm > 48 * 1024)
-    cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)sm);
   launch_pdl(router_select_kernel, dim3(a.B), dim3(kSelThreads), sm, s, a);
   if (launches) *launches += 1;
+}
+
+void init_router_attributes(int max_smem) {
+  cudaFuncSetAttribute(router_logits_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_logits_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
 
 void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
