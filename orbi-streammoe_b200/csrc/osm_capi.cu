@@ -482,7 +482,8 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
     ctx->grid_cap = sms * 4;
   int max_smem = 0;
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-  if (max_smem <= 0) max_smem = 48 * 1024;
+  // dynamic limit = opt-in maximum minus room for each kernel's static smem
+  max_smem = max_smem > 64 * 1024 ? max_smem - 16 * 1024 : 48 * 1024;
   osm::init_router_attributes(max_smem);
   osm::init_expert_attributes(max_smem);
   const cudaError_t ae = cudaGetLastError();
