@@ -19,6 +19,13 @@
 #include "osm_common.cuh"
 #include "osm_kernels.cuh"
 
+#ifdef OSM_PHASE_TIMING
+#include <cstdio>
+#define OSM_PSTAMP(i) do { if (threadIdx.x == 0) pts_[(i)] = clock64(); } while (0)
+#else
+#define OSM_PSTAMP(i) do { } while (0)
+#endif
+
 namespace osm {
 namespace {
 
@@ -95,21 +102,28 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
       }
     }
   };
+#ifdef OSM_PHASE_TIMING
+  __shared__ long long pts_[12];
+#endif
+  OSM_PSTAMP(0);
   if (early) fetch();
   if (first) {
     pdl_wait();
     pdl_trigger();
     n_items = *a.n_tg * tiles;
   }
+  OSM_PSTAMP(1);
   if (item >= n_items) return;
   const int j = a.tg_expert[tg];
   const ActEntry en = a.act[j];
+  OSM_PSTAMP(2);
   if (!early) {
     base = en.ptr;
     kind = en.kind;
     if (base == nullptr && !a.raw) return;  // non-resident expert (status already set)
     fetch();
   }
+  OSM_PSTAMP(3);
   if ((bx * TILES) * TROWS >= rows) return;
 
   __shared__ float fsg[8][33];
@@ -127,6 +141,7 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
       rowof[threadIdx.x] = threadIdx.x < nv ? (a.frag_by_pair ? p : a.pair_tok[p]) : 0;
     }
     __syncthreads();
+    OSM_PSTAMP(4);
     // stage the chunk's activation fragments and group sums (all loads in flight)
     const int per_tok = KW * 2;
 #pragma unroll 8
@@ -145,6 +160,7 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
       fsg[n][g] = s;
     }
     __syncthreads();
+    OSM_PSTAMP(5);
     const bool has_tok = gid < nv;
     const uint4* xrow = xs + (has_tok ? gid : 0) * xstride;
     float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -173,6 +189,7 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
         acc[3] = fmaf(bh, f1, fmaf(sh, d[3], acc[3]));
       }
     }
+    OSM_PSTAMP(6);
     float tot[4] = {acc[0], acc[1], acc[2], acc[3]};
     if (KSPLIT > 1) {
 #pragma unroll
@@ -225,7 +242,14 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
       }
     }
     __syncthreads();
+    OSM_PSTAMP(7);
   }
+#ifdef OSM_PHASE_TIMING
+  if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 300 || blockIdx.x == 700))
+    printf("proj%d cta %d item %d: 1:%lld 2:%lld 3:%lld 4:%lld 5:%lld 6:%lld 7:%lld\n", (int)PAIRED,
+           (int)blockIdx.x, item, pts_[1] - pts_[0], pts_[2] - pts_[0], pts_[3] - pts_[0],
+           pts_[4] - pts_[0], pts_[5] - pts_[0], pts_[6] - pts_[0], pts_[7] - pts_[0]);
+#endif
 }
 
 // Persistent grid: CTAs stride over (token group, CTA tile) items; the number

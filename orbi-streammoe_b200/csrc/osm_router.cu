@@ -29,6 +29,13 @@
 #include "osm_common.cuh"
 #include "osm_kernels.cuh"
 
+#ifdef OSM_PHASE_TIMING
+#include <cstdio>
+#define OSM_STAMP(i) do { if (threadIdx.x == 0 || threadIdx.x == 32) ts_[(i)] = clock64(); } while (0)
+#else
+#define OSM_STAMP(i) do { } while (0)
+#endif
+
 namespace osm {
 namespace {
 
@@ -278,6 +285,26 @@ __device__ int block_exclusive_scan(int* v, int n, int* red) {
   return total;
 }
 
+// Exclusive scan of n ints in smem; one warp when n <= 32.  Returns the total.
+__device__ int small_or_block_scan(int* v, int n, int* red) {
+  if (n > 32) return block_exclusive_scan(v, n, red);
+  __shared__ int s_tot;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int x = lane < n ? v[lane] : 0;
+    int incl = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    if (lane < n) v[lane] = incl - x;
+    if (lane == 31) s_tot = incl;
+  }
+  __syncthreads();
+  return s_tot;
+}
+
 // Group (token, pick) pairs by expert.  The shared expert (id E) is active
 // index 0 when present, so later kernels can fetch its weights early.  The
 // order of the other experts and of tokens inside an expert is arbitrary:
@@ -318,12 +345,12 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
   __syncthreads();
   for (int j = threadIdx.x; j < n_active; j += blockDim.x) off[j] = cnt[expert_of[j]];
   __syncthreads();
-  block_exclusive_scan(off, n_active, red);
+  small_or_block_scan(off, n_active, red);
   // token groups per active expert (cur[] is free until the scatter)
   for (int j = threadIdx.x; j < n_active; j += blockDim.x)
     cur[j] = (cnt[expert_of[j]] + kTokGroup - 1) / kTokGroup;
   __syncthreads();
-  const int n_tg = block_exclusive_scan(cur, n_active, red);
+  const int n_tg = small_or_block_scan(cur, n_active, red);
   for (int j = threadIdx.x; j < n_active; j += blockDim.x) {
     const int e = expert_of[j];
     ActEntry en;
@@ -374,8 +401,8 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
 
 // Softmax weights of the picks from logits lsel[0..k) (lsel[0] the largest)
 // with the sum over the fast logits v[] (lane-strided); lane j handles pick j.
-__device__ __noinline__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32],
-                                           const int* sid, const float* lsel) {
+__device__ __forceinline__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32],
+                                              const int* sid, const float* lsel) {
   const int lane = threadIdx.x & 31;
   const int k = a.g.k;
   const float mx = lsel[0];
@@ -417,8 +444,13 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   const int tok = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = g.k;
+#ifdef OSM_PHASE_TIMING
+  __shared__ long long ts_[16];
+#endif
+  OSM_STAMP(0);
   pdl_wait();
   pdl_trigger();
+  OSM_STAMP(1);
   const float* x = a.x + (size_t)tok * g.H;
   int nonfinite = 0;
   if ((g.H & 3) == 0) {
@@ -439,6 +471,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
     s_ncand = 0;
   }
   nonfinite = __syncthreads_or(nonfinite);
+  OSM_STAMP(2);
   if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
   const bool route = !nonfinite && !a.skip_route;
   // ---- warps 1..: activation fragments and the shared-gate dot, while
@@ -475,6 +508,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   // ---- 1. fast path: certified top-k over the fast logits ----
   float v[32];
   if (warp == 0 && route) {
+    OSM_STAMP(3);
     float bm = 0.0f;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -483,8 +517,10 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
       if (id < g.E) bm = fmaxf(bm, a.bounds[(size_t)tok * g.E + id]);
     }
     bm = warp_max(bm);
+    OSM_STAMP(4);
     const int nsel = k + 1 <= g.E ? k + 1 : k;
     warp_select(v, g.E, nsel, sel_id, sel_v);
+    OSM_STAMP(5);
     bool ok = !a.force_exact && isfinite(sel_v[0]);
     const float mx0 = sel_v[0];
     for (int j = 0; j + 1 < nsel; ++j) {
@@ -498,8 +534,11 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
       s_flag = a.force_exact ? 2 : 1;
       s_bm = bm;
     }
+    OSM_STAMP(6);
   }
+  if (warp == 1) OSM_STAMP(7);
   __syncthreads();
+  OSM_STAMP(8);
   // ---- 2. partial exact path: recompute the ambiguous candidates ----
   if (s_flag == 1) {
     if (tid == 0) atomicAdd(a.exact_count, 1ull);
@@ -530,9 +569,19 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
       }
       __syncthreads();
       if (tid < nc) {
+        // the reference's sequential sum: products are independent of the
+        // running sum, so a batch of them is formed ahead of the add chain
         float acc = 0.0f;
-#pragma unroll 8
-        for (int h = 0; h < g.H; ++h)
+        int h = 0;
+        for (; h + 64 <= g.H; h += 64) {
+          float pr[64];
+#pragma unroll
+          for (int u = 0; u < 64; ++u)
+            pr[u] = __fmul_rn(bf16_bits_to_f32(wt[(h + u) * kMaxCand + tid]), xs[h + u]);
+#pragma unroll
+          for (int u = 0; u < 64; ++u) acc = __fadd_rn(acc, pr[u]);
+        }
+        for (; h < g.H; ++h)
           acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wt[h * kMaxCand + tid]), xs[h]));
         if (a.bias != nullptr) acc = __fadd_rn(acc, a.bias[cand_id[tid]]);
         cand_l[tid] = acc;
@@ -591,10 +640,16 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
       for (int r = 0; r < 2; ++r) {
         const int e = tid + r * kSelThreads;
         if (e < g.E) {
-          for (int hh = 0; hh < kFullTile && h0 + hh < g.H; ++hh) {
-            const float w = g.f32w ? tilef[hh * g.E + e] : bf16_bits_to_f32(tile[hh * g.E + e]);
-            acc[r] = __fadd_rn(acc[r], __fmul_rn(w, xs[h0 + hh]));
+          const int nh = min(kFullTile, g.H - h0);
+          float pr[kFullTile];
+#pragma unroll
+          for (int hh = 0; hh < kFullTile; ++hh) {
+            const float w = hh < nh ? (g.f32w ? tilef[hh * g.E + e] : bf16_bits_to_f32(tile[hh * g.E + e])) : 0.0f;
+            pr[hh] = __fmul_rn(w, xs[h0 + (hh < nh ? hh : 0)]);
           }
+#pragma unroll
+          for (int hh = 0; hh < kFullTile; ++hh)
+            if (hh < nh) acc[r] = __fadd_rn(acc[r], pr[hh]);
         }
       }
       __syncthreads();
@@ -669,19 +724,32 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
       if (a.sgate_out) a.sgate_out[tok] = 0.0f;
     }
   }
+  OSM_STAMP(9);
   if (!a.do_group) return;
   // ---- the last block groups (token, pick) pairs by expert ----
-  __threadfence();
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
   __syncthreads();
+  OSM_STAMP(10);
   if (tid == 0) {
     const unsigned int prev = atomicAdd(a.ticket, 1u);
     s_flag = (prev == gridDim.x - 1) ? 3 : 0;
   }
   __syncthreads();
+  OSM_STAMP(11);
   if (s_flag != 3) return;
-  __threadfence();
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  OSM_STAMP(12);
   group_pairs(a, reinterpret_cast<int*>(uni), reinterpret_cast<int*>(red));
   if (tid == 0) *a.ticket = 0u;
+  __syncthreads();
+  OSM_STAMP(13);
+#ifdef OSM_PHASE_TIMING
+  if (tid == 0) {
+    printf("select tok %d:", tok);
+    for (int i = 1; i < 14; ++i) printf(" %d:%lld", i, ts_[i] - ts_[0]);
+    printf("\n");
+  }
+#endif
 }
 
 __global__ void __launch_bounds__(kSelThreads) group_kernel(RouterArgs a) {

@@ -106,11 +106,13 @@ _SIGS = {
 _lib = None
 
 
-def load(path: str = LIB_PATH) -> C.CDLL:
-    """Load libosm_b200.so (raises if it is missing: no fallback exists)."""
+def load(path: str | None = None) -> C.CDLL:
+    """Load libosm_b200.so (raises if it is missing: no fallback exists).
+    OSM_LIB_PATH selects another build of the same library."""
     global _lib
     if _lib is not None:
         return _lib
+    path = path or os.environ.get("OSM_LIB_PATH") or LIB_PATH
     if not os.path.exists(path):
         raise RuntimeError(
             f"{path} is missing: build it with __graft_entry__.build() "
