@@ -20,6 +20,7 @@
 namespace {
 
 constexpr size_t kAlign = 256;
+constexpr uint32_t kGemvMaxTokens = 2;  // calls with at most this many tokens use osm_gemv.cu
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -46,6 +47,7 @@ struct Scratch {
   int* tg_begin = nullptr;
   int* pair_tok = nullptr;
   int* pair_pick = nullptr;
+  int* tp_pos = nullptr;
   int* cursor = nullptr;
   int* out_row = nullptr;
   uint4* hfrag = nullptr;
@@ -89,6 +91,7 @@ struct osm_context {
   Scratch sc;
   int grid_cap = 148 * 4;       // resident CTAs of the projection kernels
   bool prof_on = false;
+  const float* cur_x = nullptr;  // activations of the call in flight (expert kernels)
   std::vector<cudaEvent_t> ev_pool;
   std::vector<ProfRec> recs;
 };
@@ -220,6 +223,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t max_tg = P / osm::kTokGroup + E + 2;
   const size_t o_tge = take(max_tg * 4), o_tgb = take(max_tg * 4);
   const size_t o_ptok = take(P * 4), o_ppick = take(P * 4), o_cursor = take((E + 1) * 4);
+  const size_t o_tpp = take(P * 4);
   const size_t o_orow = take(P * 4);
   const size_t o_hf = take(P * (I / 8) * 32), o_hs = take(P * (I / 8) * 4);
   const size_t o_part = take(P * H * 4), o_norm = take(T * H * 4);
@@ -258,6 +262,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.tg_begin = reinterpret_cast<int*>(b + o_tgb);
   s.pair_tok = reinterpret_cast<int*>(b + o_ptok);
   s.pair_pick = reinterpret_cast<int*>(b + o_ppick);
+  s.tp_pos = reinterpret_cast<int*>(b + o_tpp);
   s.cursor = reinterpret_cast<int*>(b + o_cursor);
   s.out_row = reinterpret_cast<int*>(b + o_orow);
   s.hfrag = reinterpret_cast<uint4*>(b + o_hf);
@@ -337,6 +342,7 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.tg_begin = s.tg_begin;
   a.pair_tok = s.pair_tok;
   a.pair_pick = s.pair_pick;
+  a.tp_pos = s.tp_pos;
   a.cursor = s.cursor;
   a.status = s.status;
   a.exact_count = s.exact_count;
@@ -359,6 +365,38 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
   const int Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
   const int max_active = (int)std::min<size_t>(L->g.E, (size_t)T * L->g.k) + (L->shared_slot ? 1 : 0);
+  if (T <= kGemvMaxTokens) {
+    // 1-2 tokens: CUDA-core latency path, combine fused into the down kernel
+    osm::GemvArgs g{};
+    fill_sections(g.gu, R, S, true);
+    fill_sections(g.dn, R, S, false);
+    g.x = ctx->cur_x;
+    g.B = (int)T;
+    g.H = L->g.H;
+    g.Imax = Imax;
+    g.k = L->g.k;
+    g.has_shared = L->shared_slot ? 1 : 0;
+    g.n_active = s.n_active;
+    g.act = s.act;
+    g.pair_tok = s.pair_tok;
+    g.tp_pos = s.tp_pos;
+    g.h = s.partial;
+    g.weights = s.weights;
+    g.sgate = s.sgate;
+    g.residual = residual;
+    g.out = out;
+    {
+      Prof p(ctx, kKGateUp);
+      osm::launch_gemv_gateup(g, max_active, ctx->grid_cap, ctx->stream, &ctx->launches);
+    }
+    int rc = check_launch(ctx, "gate/up gemv");
+    if (rc) return rc;
+    {
+      Prof p(ctx, kKDown);
+      osm::launch_gemv_down(g, ctx->stream, &ctx->launches);
+    }
+    return check_launch(ctx, "down gemv + combine");
+  }
   const int max_tg = (int)((size_t)T * (L->g.k + 1) / osm::kTokGroup) + max_active + 1;
   const int tchunk = (int)std::min<uint32_t>(T, 8);
   osm::ProjArgs gu{};
@@ -486,6 +524,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   max_smem = max_smem > 64 * 1024 ? max_smem - 16 * 1024 : 48 * 1024;
   osm::init_router_attributes(max_smem);
   osm::init_expert_attributes(max_smem);
+  osm::init_gemv_attributes(max_smem);
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {
     cudaStreamDestroy(ctx->own_stream);
@@ -1000,6 +1039,7 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   a.mass_out = mass;
   a.sgate_out = sgate;
   a.do_group = 1;
+  ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");
   if (rc) return rc;
@@ -1022,6 +1062,7 @@ int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* id
   a.skip_route = 1;
   a.sgate_out = sgate;
   a.do_group = 1;
+  ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "expert grouping");
   if (rc) return rc;

@@ -67,6 +67,7 @@ struct RouterArgs {
   int* tg_begin;            // token group -> first token within the entry
   int* pair_tok;            // [B*(k+1)]
   int* pair_pick;
+  int* tp_pos;              // (token, pick) -> pair position
   int* cursor;              // [E+1]
   uint32_t* status;
   unsigned long long* exact_count;
@@ -131,6 +132,26 @@ enum class ProjKind { kGateUp, kDown, kDown12, kSingle };
 // max_tg: upper bound of the call's token groups (grid sizing only).
 void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
                  int max_tokens_chunk, cudaStream_t s, uint64_t* launches);
+
+// The 1-2 token path (osm_gemv.cu).
+struct GemvArgs {
+  ProjSections gu, dn;           // gate/up and down sections, both layouts
+  const float* x;                // [B][H]
+  int B, H, Imax, k, has_shared;
+  const int* n_active;
+  const ActEntry* act;
+  const int* pair_tok;
+  const int* tp_pos;
+  float* h;                      // [pairs][Imax] SwiGLU output
+  const float* weights;          // [B][k]
+  const float* sgate;            // [B]
+  const float* residual;         // [B][H] or null
+  float* out;                    // [B][H]
+};
+void init_gemv_attributes(int max_smem);
+void launch_gemv_gateup(const GemvArgs& a, int max_active, int grid_cap, cudaStream_t s,
+                        uint64_t* launches);
+void launch_gemv_down(const GemvArgs& a, cudaStream_t s, uint64_t* launches);
 
 struct CombineArgs {
   const float* partial;          // [B][k+1][H]

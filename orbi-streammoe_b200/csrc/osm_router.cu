@@ -387,11 +387,13 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     const int pos = off[actidx[e]] + atomicAdd(&cur[e], 1);
     a.pair_tok[pos] = p / k;
     a.pair_pick[pos] = p % k;
+    if (a.tp_pos) a.tp_pos[(p / k) * (k + has_sh) + p % k] = pos;
   }
   if (has_sh)
     for (int t = threadIdx.x; t < B; t += blockDim.x) {
       a.pair_tok[off[0] + t] = t;
       a.pair_pick[off[0] + t] = k;
+      if (a.tp_pos) a.tp_pos[t * (k + 1) + k] = off[0] + t;
     }
   if (threadIdx.x == 0) {
     *a.n_active = n_active;
