@@ -83,23 +83,31 @@ __device__ __forceinline__ float chunk_dot(uint4 q, const float* xp) {
 }
 
 // Stage activations of length K (token rows of `src`) as pre-scaled chunks:
-// dst[t][c][kChunkPad], and the plain chunk sums sums[t][c].
-__device__ void stage_chunks(const float* __restrict__ src, int rows, const int* row_of, int K,
-                             float* dst, float* sums) {
+// dst[t][c][kChunkPad], and the plain chunk sums sums[t][c].  One thread per
+// 32-value chunk: its 8 float4 loads are all in flight at once.
+__device__ void stage_chunks(const float* __restrict__ src, int rows, int K, float* dst,
+                             float* sums) {
   const int nch = K >> 5;
-  for (int i = threadIdx.x; i < rows * K; i += blockDim.x) {
-    const int t = i / K, h = i - t * K;
-    const float v = src[(size_t)(row_of ? row_of[t] : t) * K + h];
-    dst[(t * nch + (h >> 5)) * kChunkPad + (h & 31)] = v * pos_scale(h & 7);
-  }
-  __syncthreads();
   for (int i = threadIdx.x; i < rows * nch; i += blockDim.x) {
     const int t = i / nch, c = i - t * nch;
-    const float* s = src + (size_t)(row_of ? row_of[t] : t) * K + c * 32;
+    const float4* s4 = reinterpret_cast<const float4*>(src + (size_t)t * K + c * 32);
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = s4[u];
     float acc = 0.0f;
-#pragma unroll 8
-    for (int j = 0; j < 32; ++j) acc += s[j];
-    sums[t * nch + c] = acc;
+    float4* d4 = reinterpret_cast<float4*>(dst + (size_t)i * kChunkPad);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc += v[u].x;
+      acc += v[u].y;
+      acc += v[u].z;
+      acc += v[u].w;
+      // positions 4u..4u+3 of the chunk: word position (4u + e) & 7
+      const int k0 = (4 * u) & 7;
+      d4[u] = make_float4(v[u].x * pos_scale(k0), v[u].y * pos_scale(k0 + 1),
+                          v[u].z * pos_scale(k0 + 2), v[u].w * pos_scale(k0 + 3));
+    }
+    sums[i] = acc;
   }
 }
 
@@ -113,7 +121,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, 
   const int nch = a.H >> 5;
   float* xsum = xs + a.B * nch * kChunkPad;              // [B][H/32]
   // x is complete when this kernel starts (the router's predecessor).
-  stage_chunks(a.x, a.B, nullptr, a.H, xs, xsum);
+  stage_chunks(a.x, a.B, a.H, xs, xsum);
   pdl_wait();
   pdl_trigger();
   __syncthreads();
@@ -188,7 +196,7 @@ __global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a)
   float* ys = hsum + P * nch;                        // [P][8]
   pdl_wait();
   pdl_trigger();
-  stage_chunks(a.h, P, nullptr, a.Imax, hs, hsum);
+  stage_chunks(a.h, P, a.Imax, hs, hsum);
   __syncthreads();
   const int n_active = *a.n_active;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -205,41 +205,44 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 }
 
 // Best n (<= number of valid entries) of the lane-strided values v[i]
-// (index i*32 + lane, valid when < E) by (value desc, index asc), one
-// redux.sync max and min per pick.  All lanes receive sel_id / sel_v.
-__device__ void warp_select(const float (&v)[32], int E, int n, int* sel_id, float* sel_v) {
+// (index i*32 + lane, valid when < E) by (value desc, index asc).  The lane
+// candidates are compared as 64-bit keys (order key of the value, then the
+// complement of the index) with a shuffle butterfly; only the winning lane
+// rescans its values.  Lane 0 writes sel_id / sel_v.
+__device__ __forceinline__ void warp_select(const float (&v)[32], int E, int n, int* sel_id,
+                                            float* sel_v) {
   const int lane = threadIdx.x & 31;
   uint32_t taken = 0;
-  uint32_t bk = 0;
-  int bi = 0x7FFFFFFF;
-  float bv = -INFINITY;
+  unsigned long long best = 0;
   auto rescan = [&]() {
-    bk = 0;
-    bi = 0x7FFFFFFF;
-    bv = -INFINITY;
+    best = 0;
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int id = i * 32 + lane;
       if (id < E && !((taken >> i) & 1u)) {
-        const uint32_t key = ord_key(v[i]);
-        if (key > bk || (key == bk && id < bi)) {
-          bk = key;
-          bi = id;
-          bv = v[i];
-        }
+        const unsigned long long key =
+            ((unsigned long long)ord_key(v[i]) << 32) | (0xFFFFFFFFu - (uint32_t)id);
+        if (key > best) best = key;
       }
     }
   };
   rescan();
   for (int r = 0; r < n; ++r) {
-    const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, bk);
-    const uint32_t win = __reduce_min_sync(0xFFFFFFFFu, bk == m ? (uint32_t)bi : 0xFFFFFFFFu);
-    const float wv = __shfl_sync(0xFFFFFFFFu, bv, (int)(win & 31u));
-    if (lane == 0) {
-      sel_id[r] = (int)win;
-      sel_v[r] = wv;
+    unsigned long long m = best;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, m, o);
+      if (other > m) m = other;
     }
-    if ((int)(win & 31u) == lane) {
+    const int win = (int)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFull));
+    const uint32_t kk = (uint32_t)(m >> 32);
+    // invert the order key
+    const uint32_t u = (kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk;
+    if (lane == 0) {
+      sel_id[r] = win;
+      sel_v[r] = __uint_as_float(u);
+    }
+    if ((win & 31) == lane) {
       taken |= 1u << (win >> 5);
       rescan();
     }
