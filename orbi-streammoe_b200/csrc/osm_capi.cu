@@ -380,6 +380,13 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
     g.act = s.act;
     g.pair_tok = s.pair_tok;
     g.tp_pos = s.tp_pos;
+    g.direct = T == 1 ? 1 : 0;
+    g.ids = s.ids;
+    g.slot_of = L->slot_of;
+    g.slab = L->slab->base;
+    g.slab_stride = L->slab->layout.stride;
+    g.shared_ptr = L->shared_slot;
+    g.status = s.status;
     g.h = s.partial;
     g.weights = s.weights;
     g.sgate = s.sgate;
@@ -1038,7 +1045,10 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   a.weights_out = w;
   a.mass_out = mass;
   a.sgate_out = sgate;
-  a.do_group = 1;
+  // one token: the expert kernels read the picks directly (no grouping, no
+  // tensor-core fragments)
+  a.do_group = T == 1 ? 0 : 1;
+  if (T <= kGemvMaxTokens) a.xfrag = nullptr;
   ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");

@@ -111,6 +111,36 @@ __device__ void stage_chunks(const float* __restrict__ src, int rows, int K, flo
   }
 }
 
+// Active entry j: from the grouping step, or in direct mode pick j of the one
+// token (j == k: the shared expert).
+__device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
+  if (!a.direct) return a.act[j];
+  ActEntry en;
+  en.off = j;
+  en.cnt = 1;
+  en.tg0 = 0;
+  en.pad0 = en.pad1 = 0;
+  if (j < a.k) {
+    en.kind = 0;
+    const uint32_t e = a.ids[j];
+    const int slot = a.slot_of[e];
+    if (slot < 0) {
+      if (threadIdx.x == 0) atomicOr(a.status, kStatusNotResident);
+      en.ptr = nullptr;
+    } else {
+      en.ptr = a.slab + (size_t)slot * a.slab_stride;
+    }
+  } else {
+    en.kind = 1;
+    en.ptr = a.shared_ptr;
+  }
+  return en;
+}
+
+__device__ __forceinline__ int gemv_entries(const GemvArgs& a) {
+  return a.direct ? a.k + a.has_shared : *a.n_active;
+}
+
 // ----------------------------------------------------------------------------
 // gate/up + SwiGLU.  Item = (active expert j, 16 row pairs); warp w owns row
 // pairs r0 + 2w, r0 + 2w + 1.
@@ -125,11 +155,11 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, 
   pdl_wait();
   pdl_trigger();
   __syncthreads();
-  const int n_items = *a.n_active * tiles;
+  const int n_items = gemv_entries(a) * tiles;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
     const int j = item / tiles, tile = item - (item / tiles) * tiles;
-    const ActEntry en = a.act[j];
+    const ActEntry en = gemv_entry(a, j);
     if (en.ptr == nullptr) continue;
     const int kind = en.kind;
     const int rows = a.gu.rows[kind];
@@ -163,7 +193,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, 
       }
       for (int i = 0; i < en.cnt; ++i) {
         const int pos = en.off + i;
-        const int t = a.pair_tok[pos];
+        const int t = a.direct ? 0 : a.pair_tok[pos];
         float gacc = 0.0f, uacc = 0.0f;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
@@ -198,12 +228,12 @@ __global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a)
   pdl_trigger();
   stage_chunks(a.h, P, a.Imax, hs, hsum);
   __syncthreads();
-  const int n_active = *a.n_active;
+  const int n_active = gemv_entries(a);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = lane >> 4, hl = lane & 15;
   const int r0 = blockIdx.x * 8;
   for (int j = warp; j < n_active; j += kGvWarps) {
-    const ActEntry en = a.act[j];
+    const ActEntry en = gemv_entry(a, j);
     if (en.ptr == nullptr) continue;
     const int kind = en.kind;
     const int K = a.dn.K[kind];
@@ -253,10 +283,13 @@ __global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a)
     const int t = i >> 3, rr = i & 7;
     float acc = 0.0f;
     for (int p = 0; p < a.k; ++p) {
-      const int pos = a.tp_pos[t * kp1 + p];
+      const int pos = a.direct ? p : a.tp_pos[t * kp1 + p];
       acc = __fadd_rn(acc, __fmul_rn(a.weights[t * a.k + p], ys[pos * 8 + rr]));
     }
-    if (a.has_shared) acc = __fadd_rn(acc, __fmul_rn(a.sgate[t], ys[a.tp_pos[t * kp1 + a.k] * 8 + rr]));
+    if (a.has_shared) {
+      const int pos = a.direct ? a.k : a.tp_pos[t * kp1 + a.k];
+      acc = __fadd_rn(acc, __fmul_rn(a.sgate[t], ys[pos * 8 + rr]));
+    }
     if (a.residual) acc = __fadd_rn(a.residual[(size_t)t * a.H + r0 + rr], acc);
     a.out[(size_t)t * a.H + r0 + rr] = acc;
   }

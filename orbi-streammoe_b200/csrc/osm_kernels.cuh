@@ -142,6 +142,15 @@ struct GemvArgs {
   const ActEntry* act;
   const int* pair_tok;
   const int* tp_pos;
+  // direct mode (one token, no grouping step): entry p < k is pick p of the
+  // routing, entry k the shared expert
+  int direct;
+  const uint32_t* ids;           // [k]
+  const int* slot_of;            // [E]
+  const uint8_t* slab;
+  uint64_t slab_stride;
+  const uint8_t* shared_ptr;
+  uint32_t* status;
   float* h;                      // [pairs][Imax] SwiGLU output
   const float* weights;          // [B][k]
   const float* sgate;            // [B]

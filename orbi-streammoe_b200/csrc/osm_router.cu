@@ -205,49 +205,67 @@ __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
 }
 
 // Best n (<= number of valid entries) of the lane-strided values v[i]
-// (index i*32 + lane, valid when < E) by (value desc, index asc).  The lane
-// candidates are compared as 64-bit keys (order key of the value, then the
-// complement of the index) with a shuffle butterfly; only the winning lane
-// rescans its values.  Lane 0 writes sel_id / sel_v.
-__device__ __forceinline__ void warp_select(const float (&v)[32], int E, int n, int* sel_id,
-                                            float* sel_v) {
+// (index i*32 + lane, valid when < E) by (value desc, index asc).  Keys are
+// 64-bit: order key of the value, then the complement of the index.  Each lane
+// sorts its NV keys with a bitonic network (independent compare-swaps), then
+// n merge rounds take the warp maximum of the lane heads with a shuffle
+// butterfly; the winning lane shifts its sorted keys by one.  Lane 0 writes
+// sel_id / sel_v.
+template <int NV>
+__device__ __forceinline__ void warp_select_n(const float (&v)[32], int E, int n, int* sel_id,
+                                              float* sel_v) {
   const int lane = threadIdx.x & 31;
-  uint32_t taken = 0;
-  unsigned long long best = 0;
-  auto rescan = [&]() {
-    best = 0;
+  unsigned long long key[NV];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int id = i * 32 + lane;
-      if (id < E && !((taken >> i) & 1u)) {
-        const unsigned long long key =
-            ((unsigned long long)ord_key(v[i]) << 32) | (0xFFFFFFFFu - (uint32_t)id);
-        if (key > best) best = key;
+  for (int i = 0; i < NV; ++i) {
+    const int id = i * 32 + lane;
+    key[i] = id < E ? (((unsigned long long)ord_key(v[i]) << 32) | (0xFFFFFFFFu - (uint32_t)id))
+                    : 0ull;
+  }
+#pragma unroll
+  for (int kk = 2; kk <= NV; kk <<= 1) {
+#pragma unroll
+    for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int l = i ^ jj;
+        if (l > i) {
+          const bool desc = (i & kk) == 0;
+          const unsigned long long a = key[i], b = key[l];
+          const bool sw = desc ? (a < b) : (a > b);
+          key[i] = sw ? b : a;
+          key[l] = sw ? a : b;
+        }
       }
     }
-  };
-  rescan();
+  }
   for (int r = 0; r < n; ++r) {
-    unsigned long long m = best;
+    unsigned long long m = key[0];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, m, o);
       if (other > m) m = other;
     }
     const int win = (int)(0xFFFFFFFFu - (uint32_t)(m & 0xFFFFFFFFull));
-    const uint32_t kk = (uint32_t)(m >> 32);
-    // invert the order key
-    const uint32_t u = (kk & 0x80000000u) ? (kk & 0x7FFFFFFFu) : ~kk;
+    const uint32_t kk32 = (uint32_t)(m >> 32);
+    const uint32_t u = (kk32 & 0x80000000u) ? (kk32 & 0x7FFFFFFFu) : ~kk32;
     if (lane == 0) {
       sel_id[r] = win;
       sel_v[r] = __uint_as_float(u);
     }
     if ((win & 31) == lane) {
-      taken |= 1u << (win >> 5);
-      rescan();
+#pragma unroll
+      for (int i = 0; i + 1 < NV; ++i) key[i] = key[i + 1];
+      key[NV - 1] = 0ull;
     }
   }
   __syncwarp();
+}
+
+__device__ __forceinline__ void warp_select(const float (&v)[32], int E, int n, int* sel_id,
+                                            float* sel_v) {
+  if (E <= 512) warp_select_n<16>(v, E, n, sel_id, sel_v);
+  else warp_select_n<32>(v, E, n, sel_id, sel_v);
 }
 
 // Block-wide exclusive scan of n (<= 4*blockDim) ints in smem `v`, in place;
