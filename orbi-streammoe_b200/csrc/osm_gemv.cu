@@ -25,6 +25,13 @@
 #include "osm_common.cuh"
 #include "osm_kernels.cuh"
 
+#ifdef OSM_PHASE_TIMING
+#include <cstdio>
+#define GV_STAMP(i) do { if (threadIdx.x == 0) gts_[(i)] = clock64(); } while (0)
+#else
+#define GV_STAMP(i) do { } while (0)
+#endif
+
 namespace osm {
 namespace {
 
@@ -150,11 +157,17 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, 
   float* xs = reinterpret_cast<float*>(sm4);             // [B][H/32][36]
   const int nch = a.H >> 5;
   float* xsum = xs + a.B * nch * kChunkPad;              // [B][H/32]
+#ifdef OSM_PHASE_TIMING
+  __shared__ long long gts_[8];
+#endif
+  GV_STAMP(0);
   // x is complete when this kernel starts (the router's predecessor).
   stage_chunks(a.x, a.B, a.H, xs, xsum);
+  GV_STAMP(1);
   pdl_wait();
   pdl_trigger();
   __syncthreads();
+  GV_STAMP(2);
   const int n_items = gemv_entries(a) * tiles;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
@@ -172,6 +185,7 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, 
     const uint16_t* Su = reinterpret_cast<const uint16_t*>(base + a.gu.s2[kind]);
     const uint16_t* Bu = reinterpret_cast<const uint16_t*>(base + a.gu.b2[kind]);
     const int cpr = a.gu.K[kind] >> 5;  // 16-byte chunks per row
+    GV_STAMP(3);
 #pragma unroll
     for (int rr = 0; rr < 2; ++rr) {
       const int r = tile * 2 * kGvWarps + 2 * warp + rr;
@@ -209,8 +223,15 @@ __global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, 
         uacc = warp_sum(uacc);
         if (lane == 0) a.h[(size_t)pos * a.Imax + r] = __fmul_rn(ref_silu(gacc), uacc);
       }
+      if (rr == 0) GV_STAMP(4);
     }
+    GV_STAMP(5);
   }
+#ifdef OSM_PHASE_TIMING
+  if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 200))
+    printf("gateup cta %d: 1:%lld 2:%lld 3:%lld 4:%lld 5:%lld\n", (int)blockIdx.x, gts_[1] - gts_[0],
+           gts_[2] - gts_[0], gts_[3] - gts_[0], gts_[4] - gts_[0], gts_[5] - gts_[0]);
+#endif
 }
 
 // ----------------------------------------------------------------------------
@@ -224,10 +245,16 @@ __global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a)
   float* hs = reinterpret_cast<float*>(sm4);        // [P][Imax/32][36]
   float* hsum = hs + P * nch * kChunkPad;            // [P][Imax/32]
   float* ys = hsum + P * nch;                        // [P][8]
+#ifdef OSM_PHASE_TIMING
+  __shared__ long long gts_[8];
+#endif
+  GV_STAMP(0);
   pdl_wait();
   pdl_trigger();
+  GV_STAMP(1);
   stage_chunks(a.h, P, a.Imax, hs, hsum);
   __syncthreads();
+  GV_STAMP(2);
   const int n_active = gemv_entries(a);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int half = lane >> 4, hl = lane & 15;
@@ -277,6 +304,7 @@ __global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a)
     }
   }
   __syncthreads();
+  GV_STAMP(3);
   // combine in pick order, shared expert last, then the residual
   const int kp1 = a.k + a.has_shared;
   for (int i = threadIdx.x; i < a.B * 8; i += blockDim.x) {
@@ -293,6 +321,12 @@ __global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a)
     if (a.residual) acc = __fadd_rn(a.residual[(size_t)t * a.H + r0 + rr], acc);
     a.out[(size_t)t * a.H + r0 + rr] = acc;
   }
+  GV_STAMP(4);
+#ifdef OSM_PHASE_TIMING
+  if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 200))
+    printf("down cta %d: 1:%lld 2:%lld 3:%lld 4:%lld\n", (int)blockIdx.x, gts_[1] - gts_[0],
+           gts_[2] - gts_[0], gts_[3] - gts_[0], gts_[4] - gts_[0]);
+#endif
 }
 
 template <typename K, typename... Args>

@@ -748,6 +748,13 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
     }
   }
   OSM_STAMP(9);
+#ifdef OSM_PHASE_TIMING
+  if (!a.do_group && tid == 0) {
+    printf("select(nogroup) tok %d:", tok);
+    for (int i = 1; i < 10; ++i) printf(" %d:%lld", i, ts_[i] - ts_[0]);
+    printf("\n");
+  }
+#endif
   if (!a.do_group) return;
   // ---- the last block groups (token, pick) pairs by expert ----
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
