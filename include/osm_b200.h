@@ -81,7 +81,8 @@ int osm_context_reset_stream(osm_context* ctx);
 int osm_context_synchronize(osm_context* ctx);
 /* Device status word accumulated by kernels since the last call (bit 0
  * non-finite router input, bit 1 invalid softmax/mass, bit 2 non-resident
- * expert, bit 3 bad slot); the count of tokens routed on the exact path. */
+ * expert, bit 3 bad slot, bit 4 a bounded wait on an asynchronous weight
+ * copy gave up); the count of tokens routed on the exact path. */
 int osm_context_status(osm_context* ctx, uint32_t* status,
                        uint64_t* exact_tokens);
 

@@ -56,6 +56,7 @@ struct Scratch {
   float* normalized = nullptr;
   uint32_t* status = nullptr;
   unsigned long long* exact_count = nullptr;
+  const uint8_t** pick_ptr = nullptr;
 };
 
 }  // namespace
@@ -90,6 +91,8 @@ struct osm_context {
   uint64_t launches = 0;
   Scratch sc;
   int grid_cap = 148 * 4;       // resident CTAs of the projection kernels
+  int num_sms = 148;
+  int max_smem = 0;             // dynamic shared memory limit of the decode kernels
   bool prof_on = false;
   const float* cur_x = nullptr;  // activations of the call in flight (expert kernels)
   std::vector<cudaEvent_t> ev_pool;
@@ -228,6 +231,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t o_hf = take(P * (I / 8) * 32), o_hs = take(P * (I / 8) * 4);
   const size_t o_part = take(P * H * 4), o_norm = take(T * H * 4);
   const size_t o_status = take(4), o_exact = take(8);
+  const size_t o_pptr = take(T * k * sizeof(void*));
   void* base = nullptr;
   cudaError_t e = cudaMalloc(&base, off);
   if (e != cudaSuccess) return fail(ctx, OSM_ENOMEM, "scratch allocation failed");
@@ -271,6 +275,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.normalized = reinterpret_cast<float*>(b + o_norm);
   s.status = reinterpret_cast<uint32_t*>(b + o_status);
   s.exact_count = reinterpret_cast<unsigned long long*>(b + o_exact);
+  s.pick_ptr = reinterpret_cast<const uint8_t**>(b + o_pptr);
   cudaMemcpy(s.status, &st, 4, cudaMemcpyHostToDevice);
   cudaMemcpy(s.exact_count, &ex, 8, cudaMemcpyHostToDevice);
   return OSM_OK;
@@ -346,6 +351,7 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.cursor = s.cursor;
   a.status = s.status;
   a.exact_count = s.exact_count;
+  a.pick_ptr = L->slab ? s.pick_ptr : nullptr;
   return a;
 }
 
@@ -358,6 +364,29 @@ void launch_router_pair(osm_context* ctx, const osm::RouterArgs& a) {
   osm::launch_router_select(a, ctx->stream, &ctx->launches);
 }
 
+// The decode kernels (osm_gemv.cu) serve calls of 1-2 tokens whose shapes fit
+// their shared-memory plan; fills the call-independent fields of g.
+bool gemv_path(osm_layer* L, uint32_t T, osm::GemvArgs* g, osm::GemvLaunch* gl) {
+  if (T > kGemvMaxTokens || !L->slab) return false;
+  osm_context* ctx = L->ctx;
+  const osm_expert_layout& R = L->slab->layout;
+  const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
+  const int max_active = (int)std::min<size_t>(L->g.E, (size_t)T * L->g.k) + (L->shared_slot ? 1 : 0);
+  *g = osm::GemvArgs{};
+  fill_sections(g->gu, R, S, true);
+  fill_sections(g->dn, R, S, false);
+  g->B = (int)T;
+  g->H = L->g.H;
+  g->Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
+  g->k = L->g.k;
+  g->E = L->g.E;
+  g->has_shared = L->shared_slot ? 1 : 0;
+  g->slab = L->slab->base;
+  g->slab_stride = R.stride;
+  g->shared_ptr = L->shared_slot;
+  return osm::gemv_configure(*g, max_active, ctx->num_sms, ctx->max_smem, gl);
+}
+
 int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
@@ -365,27 +394,19 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
   const int Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
   const int max_active = (int)std::min<size_t>(L->g.E, (size_t)T * L->g.k) + (L->shared_slot ? 1 : 0);
-  if (T <= kGemvMaxTokens) {
-    // 1-2 tokens: CUDA-core latency path, combine fused into the down kernel
-    osm::GemvArgs g{};
-    fill_sections(g.gu, R, S, true);
-    fill_sections(g.dn, R, S, false);
+  osm::GemvArgs g;
+  osm::GemvLaunch gl;
+  if (gemv_path(L, T, &g, &gl)) {
+    // 1-2 tokens: bulk-copy decode kernels, combine fused into the down kernel
     g.x = ctx->cur_x;
-    g.B = (int)T;
-    g.H = L->g.H;
-    g.Imax = Imax;
-    g.k = L->g.k;
-    g.has_shared = L->shared_slot ? 1 : 0;
     g.n_active = s.n_active;
     g.act = s.act;
     g.pair_tok = s.pair_tok;
     g.tp_pos = s.tp_pos;
     g.direct = T == 1 ? 1 : 0;
     g.ids = s.ids;
+    g.pick_ptr = s.pick_ptr;
     g.slot_of = L->slot_of;
-    g.slab = L->slab->base;
-    g.slab_stride = L->slab->layout.stride;
-    g.shared_ptr = L->shared_slot;
     g.status = s.status;
     g.h = s.partial;
     g.weights = s.weights;
@@ -394,13 +415,13 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
     g.out = out;
     {
       Prof p(ctx, kKGateUp);
-      osm::launch_gemv_gateup(g, max_active, ctx->grid_cap, ctx->stream, &ctx->launches);
+      osm::launch_gemv_gateup(g, gl, ctx->stream, &ctx->launches);
     }
     int rc = check_launch(ctx, "gate/up gemv");
     if (rc) return rc;
     {
       Prof p(ctx, kKDown);
-      osm::launch_gemv_down(g, ctx->stream, &ctx->launches);
+      osm::launch_gemv_down(g, gl, ctx->stream, &ctx->launches);
     }
     return check_launch(ctx, "down gemv + combine");
   }
@@ -523,15 +544,19 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   }
   ctx->stream = ctx->own_stream;
   int sms = 0;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) {
     ctx->grid_cap = sms * 4;
-  int max_smem = 0;
-  cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+    ctx->num_sms = sms;
+  }
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
   // dynamic limit = opt-in maximum minus room for each kernel's static smem
-  max_smem = max_smem > 64 * 1024 ? max_smem - 16 * 1024 : 48 * 1024;
+  // (the decode kernels have none)
+  const int max_smem = optin > 64 * 1024 ? optin - 16 * 1024 : 48 * 1024;
+  ctx->max_smem = optin > 64 * 1024 ? optin : 48 * 1024;
   osm::init_router_attributes(max_smem);
   osm::init_expert_attributes(max_smem);
-  osm::init_gemv_attributes(max_smem);
+  osm::init_gemv_attributes(ctx->max_smem);
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {
     cudaStreamDestroy(ctx->own_stream);
@@ -1047,8 +1072,11 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   a.sgate_out = sgate;
   // one token: the expert kernels read the picks directly (no grouping, no
   // tensor-core fragments)
-  a.do_group = T == 1 ? 0 : 1;
-  if (T <= kGemvMaxTokens) a.xfrag = nullptr;
+  osm::GemvArgs g;
+  osm::GemvLaunch gl;
+  const bool dec = gemv_path(L, T, &g, &gl);
+  a.do_group = (T == 1 && dec) ? 0 : 1;
+  if (dec) a.xfrag = nullptr;
   ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");

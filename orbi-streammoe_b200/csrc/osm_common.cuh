@@ -17,6 +17,7 @@ constexpr uint32_t kStatusNonFinite = 1u << 0;
 constexpr uint32_t kStatusBadMass = 1u << 1;
 constexpr uint32_t kStatusNotResident = 1u << 2;
 constexpr uint32_t kStatusBadSlot = 1u << 3;
+constexpr uint32_t kStatusCopyTimeout = 1u << 4;  // a bounded wait on an async copy gave up
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);
@@ -88,9 +89,90 @@ __device__ __forceinline__ float ref_silu(float v) { return __fmul_rn(v, ref_sig
 // stream-serialisation attribute may start before its predecessor ends;
 // pdl_wait() blocks until the predecessor has completed and flushed memory
 // (a no-op for ordinary launches), pdl_trigger() lets the successor start.
+#ifdef OSM_PHASE_TIMING
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t % 100000000ull;
+}
+// kernel timeline (debug builds): slot 4q = first CTA start, 4q+1 = last CTA
+// start, 4q+2 = last return from pdl_wait, 4q+3 = last CTA end
+#define OSM_TL_SLOTS 16
+__device__ __forceinline__ unsigned long long gtime_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+#define TL_START(q) do { if (threadIdx.x == 0) { const unsigned long long t_ = gtime_ns(); \
+  atomicMin(&g_tl[4 * (q)], t_); atomicMax(&g_tl[4 * (q) + 1], t_); } } while (0)
+#define TL_WAITED(q) do { if (threadIdx.x == 0) atomicMax(&g_tl[4 * (q) + 2], gtime_ns()); } while (0)
+#define TL_END(q) do { if (threadIdx.x == 0) atomicMax(&g_tl[4 * (q) + 3], gtime_ns()); } while (0)
+#define TL_MARK(slot) do { if (threadIdx.x == 0) atomicMax(&g_tl[(slot)], gtime_ns()); } while (0)
+#else
+#define TL_MARK(slot) do { } while (0)
+#define TL_START(q) do { } while (0)
+#define TL_WAITED(q) do { } while (0)
+#define TL_END(q) do { } while (0)
+#endif
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- bulk asynchronous copies (global -> shared) tracked by an mbarrier ----
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+// Makes initialised barriers visible to the async proxy (the copy engine).
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+// One arrival that also expects `bytes` of copy completions on the barrier.
+__device__ __forceinline__ void mbar_arrive_expect(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Adds `bytes` of expected copy completions without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Copies `bytes` (a multiple of 16; both addresses 16-byte aligned) and
+// signals their arrival on `bar`.  No multicast.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Polls at most `polls` times (each try_wait may suspend briefly); false when
+// the phase did not complete.
+constexpr uint32_t kCopyPolls = 1u << 21;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kCopyPolls; ++i)
+    if (mbar_test(bar, parity)) return true;
+  return false;
 }
 
 // Monotone map of finite floats (and -inf) to unsigned keys.

@@ -109,7 +109,6 @@ __device__ __forceinline__ void proj_item(const ProjArgs& a, int item, int tiles
   if (early) fetch();
   if (first) {
     pdl_wait();
-    pdl_trigger();
     n_items = *a.n_tg * tiles;
   }
   OSM_PSTAMP(1);
@@ -264,6 +263,7 @@ __global__ void __launch_bounds__(kWarps * 32, PAIRED ? 5 : 4) proj_kernel(ProjA
     proj_item<PAIRED, KSPLIT, MAXG>(a, item, tiles, first, n_items, xs_dyn);
     first = false;
   }
+  pdl_trigger();
 }
 
 __global__ void frag_prep_kernel(const float* __restrict__ x, int rows, int K,

@@ -2,141 +2,160 @@
 // (replaces, for decode, the per-expert q4_gemv / swiglu / weighted_accumulate
 // submits of src/model/routed_moe.cpp:320-404).
 //
-// With one or two tokens a tensor-core tile wastes most of its columns, so the
-// dot products run on CUDA cores in fp32:
-//  * a 16-byte chunk of a Q4 row holds 32 nibbles of one 64-wide group; the
-//    nibbles are turned into floats without shifts: OR-ing the nibble in place
-//    into the mantissa of 2^23 gives 2^23 + q*16^k exactly, and the activation
-//    is stored pre-multiplied by 16^-k (an exact power of two), so
-//    sum (v - 2^23) * x' = sum q * x exactly per product;
-//  * fp32x2 packed FMA/ADD (sm_100) halve the instruction count;
-//  * each group is reduced as s * sum(q x) + b * sum(x) (shaders/
-//    q4_gemv.comp:44-60), then across lanes.
-// gemv_gateup_kernel  one warp per (gate row, up row) pair, lanes over the
-//                     input chunks; SwiGLU in the epilogue; h in fp32.
-// gemv_down_kernel    one CTA per 8 output rows, warps over the active experts,
-//                     half-warps over rows; the CTA then combines every token's
-//                     picks in pick order, the shared expert last, then the
-//                     residual (routed_moe.cpp:13-92, :396-404), so no partial
-//                     buffer or combine kernel is needed.
+// Data movement: every CTA requests all of its weight rows at once with
+// 16-byte cp.async copies into padded shared-memory tiles (one commit group
+// per 16-row tile), so the whole working set is in flight together; the down
+// kernel is launched while gate/up still runs and fetches its rows then.
+//
+// Arithmetic: integer tensor-core MMAs (mma.sync m16n8k32 s8 -> s32).
+//  * A = 16 weight rows x 32 inputs: the nibbles q (0..15) are exact int8;
+//    one 32-bit word of a row (8 nibbles) yields two int8x4 registers with
+//    two LOPs (low nibbles, high nibbles).  The input order inside a 32-wide
+//    slab is permuted; the activation fragments use the same permutation.
+//  * B = activations as block floating point: per token and 64-wide group,
+//    x = s (d0 + d1 2^-7 + d2 2^-14) with s a power of two and int8 digits
+//    (|d| <= 64), exact up to s 2^-15 <= 2^-20 max|x_group|.  Columns 4t..4t+2
+//    of the n=8 tile hold token t's three digit vectors, so one MMA serves
+//    both digits and both tokens; the s32 sums are exact.
+//  * per group: y += s_w s (D0 + D1/128 + D2/16384) + b_w sum(x) (the affine
+//    dequantisation of shaders/q4_gemv.comp:44-60 applied per group), in fp32.
+// dec_gateup_kernel  one CTA per SM over an even split of the (gate row, up
+//                    row) pairs of all active experts, shared expert first
+//                    (its rows are fetched before the routing exists); the
+//                    8 warps split each tile's groups and their partial sums
+//                    are added in a fixed order, then SwiGLU.
+// dec_down_kernel    one CTA per block of <= 16 output rows, every active
+//                    expert; warps take experts; then the CTA combines each
+//                    token's picks in pick order, the shared expert last,
+//                    then the residual (routed_moe.cpp:13-92, :396-404).
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "osm_common.cuh"
 #include "osm_kernels.cuh"
 
-#ifdef OSM_PHASE_TIMING
-#include <cstdio>
-#define GV_STAMP(i) do { if (threadIdx.x == 0) gts_[(i)] = clock64(); } while (0)
-#else
-#define GV_STAMP(i) do { } while (0)
-#endif
-
 namespace osm {
 namespace {
+#ifdef OSM_PHASE_TIMING
+__device__ unsigned long long g_tl[OSM_TL_SLOTS];
+__device__ long long g_cyc[32];
+#define CYC(i) do { if (blockIdx.x == 0 && threadIdx.x == 0) g_cyc[(i)] = clock64(); } while (0)
+#else
+#define CYC(i) do { } while (0)
+#endif
 
-constexpr int kGvWarps = 8;
-constexpr int kChunkPad = 36;  // floats per staged 32-value chunk (bank spread)
-constexpr float kTwo23 = 8388608.0f;
+constexpr int kTileRows = 16;
+constexpr int kDnChunks = 4;  // most group chunks one down entry is split into
 
-// 16^-k for the nibble at word position k; positions 5..7 are read from the
-// word shifted right by 20, so they use 16^-(k-5).
-__device__ __forceinline__ float pos_scale(int k) {
-  const int e = k <= 4 ? 4 * k : 4 * (k - 5);
-  return __uint_as_float((uint32_t)(127 - e) << 23);
+// ---- asynchronous 4/8/16-byte copies global -> shared ----
+__device__ __forceinline__ void cp_async(void* dst, const void* src, int bytes) {
+  if (bytes == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+  else if (bytes == 8)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
-  unsigned long long d;
-  asm("mov.b64 %0, {%1,%2};" : "=l"(d) : "f"(lo), "f"(hi));
-  return d;
-}
-__device__ __forceinline__ void f2unpack(unsigned long long d, float& lo, float& hi) {
-  asm("mov.b64 {%0,%1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// sum over the 32 nibbles of chunk q (4 words) of q_j * x_j, with xp the
-// pre-scaled activations of the chunk (32 floats).
-__device__ __forceinline__ float chunk_dot(uint4 q, const float* xp) {
-  const unsigned long long m23 = f2pack(-kTwo23, -kTwo23);
-  unsigned long long acc = f2pack(0.0f, 0.0f);
-  const uint32_t ws[4] = {q.x, q.y, q.z, q.w};
+// Padded row stride (bytes) for rows of rb bytes: a multiple of 16 that is 32
+// mod 128, so the 8 rows a warp reads at one offset fall in distinct banks.
+__host__ __device__ inline int pad_stride(int rb) { return rb + ((32 - rb % 128) + 128) % 128; }
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+// Scale-row stride (bytes) for rows of rb bytes: a multiple of 16 with an odd
+// quotient, so rows r = 0..7 read at one offset fall in distinct banks.
+__host__ __device__ inline int scale_stride(int rb) {
+  int s = (rb + 15) & ~15;
+  if (((s >> 4) & 1) == 0) s += 16;
+  return s;
+}
+
+// Block-floating-point int8 digits of 8 consecutive activations (physical
+// inputs k0..k0+7 of one group) for the B fragments: b0 takes the even
+// positions, b1 the odd ones.  s = 2^e with 127 s > max|x_group|.
+struct Digits {
+  uint32_t b0[3], b1[3];
+};
+__device__ __forceinline__ int group_exponent(float m) {
+  int E = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+  if (E < -100) E = -100;   // zero / tiny groups: digits are 0 anyway
+  if (E > 120) E = 120;     // keeps 2^-e finite
+  return E - 5;             // |x| < 2^(E+1) = 64 s
+}
+// y = rint(x 2^(14-e)) (|y| < 2^20) split into balanced base-128 digits:
+// y = d0 2^14 + d1 2^7 + d2 with |d| <= 64.
+__device__ __forceinline__ Digits make_digits(const float (&v)[8], int e) {
+  const float sc = __uint_as_float((uint32_t)(127 + 14 - e) << 23);  // 2^(14-e)
+  uint32_t p[3][8];
 #pragma unroll
-  for (int wi = 0; wi < 4; ++wi) {
-    const uint32_t w = ws[wi];
-    const uint32_t w5 = w >> 20;
-    const float4 xa = *reinterpret_cast<const float4*>(xp + 8 * wi);
-    const float4 xb = *reinterpret_cast<const float4*>(xp + 8 * wi + 4);
-    float v[8];
-    v[0] = __uint_as_float(0x4B000000u | (w & 0x0000000Fu));
-    v[1] = __uint_as_float(0x4B000000u | (w & 0x000000F0u));
-    v[2] = __uint_as_float(0x4B000000u | (w & 0x00000F00u));
-    v[3] = __uint_as_float(0x4B000000u | (w & 0x0000F000u));
-    v[4] = __uint_as_float(0x4B000000u | (w & 0x000F0000u));
-    v[5] = __uint_as_float(0x4B000000u | (w5 & 0x0000000Fu));
-    v[6] = __uint_as_float(0x4B000000u | (w5 & 0x000000F0u));
-    v[7] = __uint_as_float(0x4B000000u | (w5 & 0x00000F00u));
-    const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      unsigned long long q2 = f2pack(v[2 * p], v[2 * p + 1]);
-      asm("add.rn.f32x2 %0, %0, %1;" : "+l"(q2) : "l"(m23));
-      asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(q2), "l"(f2pack(xv[2 * p], xv[2 * p + 1])));
-    }
+  for (int m = 0; m < 8; ++m) {
+    const int y = __float2int_rn(v[m] * sc);
+    const int d2 = ((y + 64) & 127) - 64;
+    const int y1 = (y - d2) >> 7;
+    const int d1 = ((y1 + 64) & 127) - 64;
+    const int d0 = (y1 - d1) >> 7;
+    p[0][m] = (uint32_t)d0 & 0xFFu;
+    p[1][m] = (uint32_t)d1 & 0xFFu;
+    p[2][m] = (uint32_t)d2 & 0xFFu;
   }
-  float lo, hi;
-  f2unpack(acc, lo, hi);
-  return lo + hi;
+  Digits D;
+#pragma unroll
+  for (int d = 0; d < 3; ++d) {
+    D.b0[d] = p[d][0] | (p[d][2] << 8) | (p[d][4] << 16) | (p[d][6] << 24);
+    D.b1[d] = p[d][1] | (p[d][3] << 8) | (p[d][5] << 16) | (p[d][7] << 24);
+  }
+  return D;
 }
 
-// Stage activations of length K (token rows of `src`) as pre-scaled chunks:
-// dst[t][c][kChunkPad], and the plain chunk sums sums[t][c].  One thread per
-// 32-value chunk: its 8 float4 loads are all in flight at once.
-__device__ void stage_chunks(const float* __restrict__ src, int rows, int K, float* dst,
-                             float* sums) {
-  const int nch = K >> 5;
-  for (int i = threadIdx.x; i < rows * nch; i += blockDim.x) {
-    const int t = i / nch, c = i - t * nch;
-    const float4* s4 = reinterpret_cast<const float4*>(src + (size_t)t * K + c * 32);
-    float4 v[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) v[u] = s4[u];
-    float acc = 0.0f;
-    float4* d4 = reinterpret_cast<float4*>(dst + (size_t)i * kChunkPad);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      acc += v[u].x;
-      acc += v[u].y;
-      acc += v[u].z;
-      acc += v[u].w;
-      // positions 4u..4u+3 of the chunk: word position (4u + e) & 7
-      const int k0 = (4 * u) & 7;
-      d4[u] = make_float4(v[u].x * pos_scale(k0), v[u].y * pos_scale(k0 + 1),
-                          v[u].z * pos_scale(k0 + 2), v[u].w * pos_scale(k0 + 3));
-    }
-    sums[i] = acc;
-  }
-}
+// MMA rows and tile rows.  Weight rows reach shared memory in blocks of 4
+// consecutive rows (one bulk copy each); the 16 rows of a tile are 4 blocks
+// at a padded stride.  MMA row R reads tile row m = 4 (R & 3) + (R >> 2), so
+// the 4 rows one 16-lane phase reads (R = 0..3 or 4..7, +8) sit in 4
+// different blocks, hence different banks.
+__host__ __device__ inline int mma_to_row(int R) { return 4 * (R & 3) + (R >> 2); }
+__host__ __device__ inline int row_to_mma(int m) { return 4 * (m & 3) + (m >> 2); }
 
 // Active entry j: from the grouping step, or in direct mode pick j of the one
-// token (j == k: the shared expert).
+// token (j == k: the shared expert).  CG: read through L2 only (the routing
+// may be read before this grid's dependency wait; see dec_down_kernel).
+template <bool CG>
 __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
-  if (!a.direct) return a.act[j];
   ActEntry en;
+  if (!a.direct) {
+    if (!CG) return a.act[j];
+    const ActEntry* p = a.act + j;
+    en.ptr = reinterpret_cast<const uint8_t*>(
+        __ldcg(reinterpret_cast<const unsigned long long*>(&p->ptr)));
+    en.off = __ldcg(&p->off);
+    en.cnt = __ldcg(&p->cnt);
+    en.kind = __ldcg(&p->kind);
+    en.tg0 = 0;
+    en.pad0 = en.pad1 = 0;
+    return en;
+  }
   en.off = j;
   en.cnt = 1;
   en.tg0 = 0;
   en.pad0 = en.pad1 = 0;
   if (j < a.k) {
+    // the router wrote the slot base of each pick (null: bad or not resident)
     en.kind = 0;
-    const uint32_t e = a.ids[j];
-    const int slot = a.slot_of[e];
-    if (slot < 0) {
-      if (threadIdx.x == 0) atomicOr(a.status, kStatusNotResident);
-      en.ptr = nullptr;
-    } else {
-      en.ptr = a.slab + (size_t)slot * a.slab_stride;
-    }
+    en.ptr = CG ? reinterpret_cast<const uint8_t*>(__ldcg(
+                      reinterpret_cast<const unsigned long long*>(a.pick_ptr + j)))
+                : a.pick_ptr[j];
   } else {
     en.kind = 1;
     en.ptr = a.shared_ptr;
@@ -144,189 +163,535 @@ __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
   return en;
 }
 
+template <bool CG>
 __device__ __forceinline__ int gemv_entries(const GemvArgs& a) {
-  return a.direct ? a.k + a.has_shared : *a.n_active;
+  if (a.direct) return a.k + a.has_shared;
+  return CG ? __ldcg(a.n_active) : *a.n_active;
 }
 
-// ----------------------------------------------------------------------------
-// gate/up + SwiGLU.  Item = (active expert j, 16 row pairs); warp w owns row
-// pairs r0 + 2w, r0 + 2w + 1.
-// ----------------------------------------------------------------------------
-__global__ void __launch_bounds__(kGvWarps * 32) gemv_gateup_kernel(GemvArgs a, int tiles) {
-  extern __shared__ float4 sm4[];
-  float* xs = reinterpret_cast<float*>(sm4);             // [B][H/32][36]
-  const int nch = a.H >> 5;
-  float* xsum = xs + a.B * nch * kChunkPad;              // [B][H/32]
-#ifdef OSM_PHASE_TIMING
-  __shared__ long long gts_[8];
-#endif
-  GV_STAMP(0);
-  // x is complete when this kernel starts (the router's predecessor).
-  stage_chunks(a.x, a.B, a.H, xs, xsum);
-  GV_STAMP(1);
-  pdl_wait();
-  pdl_trigger();
-  __syncthreads();
-  GV_STAMP(2);
-  const int n_items = gemv_entries(a) * tiles;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-    const int j = item / tiles, tile = item - (item / tiles) * tiles;
-    const ActEntry en = gemv_entry(a, j);
-    if (en.ptr == nullptr) continue;
-    const int kind = en.kind;
-    const int rows = a.gu.rows[kind];
-    const int G = a.gu.K[kind] >> 6;
-    const uint8_t* base = en.ptr;
-    const uint4* Wg = reinterpret_cast<const uint4*>(base + a.gu.w[kind]);
-    const uint4* Wu = reinterpret_cast<const uint4*>(base + a.gu.w2[kind]);
-    const uint16_t* Sg = reinterpret_cast<const uint16_t*>(base + a.gu.s[kind]);
-    const uint16_t* Bg = reinterpret_cast<const uint16_t*>(base + a.gu.b[kind]);
-    const uint16_t* Su = reinterpret_cast<const uint16_t*>(base + a.gu.s2[kind]);
-    const uint16_t* Bu = reinterpret_cast<const uint16_t*>(base + a.gu.b2[kind]);
-    const int cpr = a.gu.K[kind] >> 5;  // 16-byte chunks per row
-    GV_STAMP(3);
-#pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      const int r = tile * 2 * kGvWarps + 2 * warp + rr;
-      if (r >= rows) continue;
-      // chunks c = lane, lane + 32 (K = 2048: one 64-group per two chunks)
-      uint4 qg[2], qu[2];
-      float sg[2], bg[2], su[2], bu[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int c = lane + 32 * u;
-        if (c < cpr) {
-          qg[u] = __ldg(Wg + (size_t)r * cpr + c);
-          qu[u] = __ldg(Wu + (size_t)r * cpr + c);
-          sg[u] = bf16_bits_to_f32(__ldg(Sg + (size_t)r * G + (c >> 1)));
-          bg[u] = bf16_bits_to_f32(__ldg(Bg + (size_t)r * G + (c >> 1)));
-          su[u] = bf16_bits_to_f32(__ldg(Su + (size_t)r * G + (c >> 1)));
-          bu[u] = bf16_bits_to_f32(__ldg(Bu + (size_t)r * G + (c >> 1)));
-        }
-      }
-      for (int i = 0; i < en.cnt; ++i) {
-        const int pos = en.off + i;
-        const int t = a.direct ? 0 : a.pair_tok[pos];
-        float gacc = 0.0f, uacc = 0.0f;
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const int c = lane + 32 * u;
-          if (c < cpr) {
-            const float* xp = xs + (t * nch + c) * kChunkPad;
-            const float xsm = xsum[t * nch + c];
-            gacc = fmaf(bg[u], xsm, fmaf(sg[u], chunk_dot(qg[u], xp), gacc));
-            uacc = fmaf(bu[u], xsm, fmaf(su[u], chunk_dot(qu[u], xp), uacc));
-          }
-        }
-        gacc = warp_sum(gacc);
-        uacc = warp_sum(uacc);
-        if (lane == 0) a.h[(size_t)pos * a.Imax + r] = __fmul_rn(ref_silu(gacc), uacc);
-      }
-      if (rr == 0) GV_STAMP(4);
-    }
-    GV_STAMP(5);
+// What a pair / entry holds.
+struct DecMeta {
+  const uint8_t* ptr;  // slot base (null: nothing to compute)
+  int off, cnt, row, kind;
+};
+
+// ---- shared-memory plans (host and device agree on them) ----
+struct GuLayout {
+  size_t tiles, scales, xfrag, xsx, xsum, part, meta, bars, total;
+  int bs;  // padded stride of a 4-row block
+  int ss;  // padded scale-row stride
+};
+__host__ __device__ inline GuLayout gu_layout(int H, int ntile, int per_cta) {
+  const size_t G = (size_t)H >> 6;
+  GuLayout L;
+  L.bs = pad_stride(4 * (H >> 1));
+  L.ss = scale_stride((int)G * 2);
+  size_t o = 0;
+  L.tiles = o;  o += (size_t)ntile * 2 * 4 * L.bs;               // [tile][gate|up][block]
+  L.scales = o; o += (size_t)ntile * 4 * kTileRows * L.ss;       // [tile][array][mma row]
+  L.xfrag = o;  o += G * 2 * 32 * 8;                             // [g][half][lane] uint2
+  L.xsx = o;    o += G * 2 * 2 * 4;                              // [token][g][even|odd]
+  L.xsum = o;   o += align16(G * 2 * 4);                         // [token][g]
+  L.part = o;   o += (size_t)kDecWarps * kTileRows * 2 * 2 * 4;  // [tile][chunk]: <= kDecWarps items
+  L.meta = o;   o += (size_t)per_cta * sizeof(DecMeta);
+  L.bars = o;   o += (size_t)ntile * 8;
+  L.total = o;
+  return L;
+}
+struct DnLayout {
+  size_t wt, scales, hfrag, hsx, hsum, ys, rw, meta, bars, total;
+  int bs;  // padded stride of a 4-row block
+};
+__host__ __device__ inline DnLayout dn_layout(int ne, int Kmax, int Imax, int P) {
+  const size_t Gd = (size_t)Kmax >> 6, Gh = (size_t)Imax >> 6;
+  DnLayout L;
+  L.bs = pad_stride(4 * (Kmax >> 1));
+  size_t o = 0;
+  L.wt = o;     o += (size_t)ne * 4 * L.bs;                      // [entry][block]
+  L.scales = o; o += align16((size_t)ne * 2 * kTileRows * Gd * 2);  // [entry][s|b][mma row][Gd]
+  L.hfrag = o;  o += (size_t)P * Gh * 2 * 16 * 8;                // [pair][g][half][16 lanes]
+  L.hsx = o;    o += (size_t)P * Gh * 2 * 4;
+  L.hsum = o;   o += align16((size_t)P * Gh * 4);
+  L.ys = o;     o += align16((size_t)kDnChunks * P * kTileRows * 4);  // [chunk][pair][row]
+  L.rw = o;     o += align16((size_t)P * 4 + (size_t)P * 4);     // pick weights, pair of (token, pick)
+  L.meta = o;   o += (size_t)ne * sizeof(DecMeta);
+  L.bars = o;   o += (size_t)ne * 8;
+  L.total = o;
+  return L;
+}
+
+// Pair p of the CTA split: the shared expert's rows first, then the routed
+// entries' rows.  Returns the entry index, or -1 (past the last entry, or a
+// routed pair when shared_only).
+__device__ __forceinline__ int pair_entry(const GemvArgs& a, int p, bool shared_only, int n_ent,
+                                          int& row) {
+  const int rs = a.has_shared ? a.gu.rows[1] : 0;
+  if (p < rs) {
+    row = p;
+    return a.direct ? a.k : 0;
   }
-#ifdef OSM_PHASE_TIMING
-  if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 200))
-    printf("gateup cta %d: 1:%lld 2:%lld 3:%lld 4:%lld 5:%lld\n", (int)blockIdx.x, gts_[1] - gts_[0],
-           gts_[2] - gts_[0], gts_[3] - gts_[0], gts_[4] - gts_[0], gts_[5] - gts_[0]);
-#endif
+  if (shared_only) return -1;
+  const int q = (p - rs) / a.gu.rows[0];
+  row = (p - rs) - q * a.gu.rows[0];
+  const int j = a.direct ? q : a.has_shared + q;
+  return (a.direct ? q < a.k : j < n_ent) ? j : -1;
+}
+
+// int8 A fragment halves of one 32-bit word of 8 nibbles
+__device__ __forceinline__ uint32_t lo_nib(uint32_t w) { return w & 0x0F0F0F0Fu; }
+__device__ __forceinline__ uint32_t hi_nib(uint32_t w) { return (w >> 4) & 0x0F0F0F0Fu; }
+
+// Stages activation digits of `nrow` rows of `src` (row stride ld, K inputs)
+// as B fragments -- cols16: frag[row][g][half][16 lanes] (columns 0..3);
+// else frag[g][half][32 lanes] with row t in columns 4t..4t+3 (nrow <= 2) --
+// digit scales sx[row][g][2] (even lanes s/128, odd lanes s/16384) and
+// sums[row][g].  Items (row, g, half, j) of one (row, g) are 8 consecutive
+// threads.
+__device__ void stage_digits(const float* __restrict__ src, int nrow, int ld, int K, bool cols16,
+                             uint2* frag, float* sx, float* sums) {
+  const int G = K >> 6;
+  const int items = nrow * G * 8;
+  constexpr int U = 2;  // items per thread whose loads are in flight together
+  for (int base = 0; base < items; base += U * blockDim.x) {
+    float v[U][8];
+    int itc[U];
+    bool live[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = base + u * blockDim.x + threadIdx.x;
+      live[u] = it < items;
+      itc[u] = live[u] ? it : items - 1;
+      const int j = itc[u] & 3, h = (itc[u] >> 2) & 1, g = (itc[u] >> 3) % G, t = (itc[u] >> 3) / G;
+      const float* p = src + (size_t)t * ld + 64 * g + 16 * j + 8 * h;
+      const float4 u0 = *reinterpret_cast<const float4*>(p);
+      const float4 u1 = *reinterpret_cast<const float4*>(p + 4);
+      v[u][0] = u0.x; v[u][1] = u0.y; v[u][2] = u0.z; v[u][3] = u0.w;
+      v[u][4] = u1.x; v[u][5] = u1.y; v[u][6] = u1.z; v[u][7] = u1.w;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int j = itc[u] & 3, h = (itc[u] >> 2) & 1, g = (itc[u] >> 3) % G, t = (itc[u] >> 3) / G;
+      float m = 0.0f, sm = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        m = fmaxf(m, fabsf(v[u][q]));
+        sm += v[u][q];
+      }
+      // the 8 items of (t, g) are lanes 8c..8c+7 of this warp
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
+      }
+      if (!live[u]) continue;
+      const int e = group_exponent(m);
+      const Digits D = make_digits(v[u], e);
+      // lane n*4 + j holds column n: digit d of row t is column d (cols16:
+      // one fragment per row) or column 4t + d (two rows share a fragment)
+      uint2* fr = cols16 ? frag + (((size_t)t * G + g) * 2 + h) * 16
+                         : frag + ((size_t)g * 2 + h) * 32 + 16 * t;
+#pragma unroll
+      for (int d = 0; d < 3; ++d) fr[d * 4 + j] = make_uint2(D.b0[d], D.b1[d]);
+      fr[3 * 4 + j] = make_uint2(0u, 0u);
+      if (h == 0 && j == 0) {
+        const float s = __uint_as_float((uint32_t)(127 + e) << 23);
+        sx[((size_t)t * G + g) * 2 + 0] = s * 0.0078125f;
+        sx[((size_t)t * G + g) * 2 + 1] = s * 6.103515625e-05f;
+        sums[(size_t)t * G + g] = sm;
+      }
+    }
+  }
 }
 
 // ----------------------------------------------------------------------------
-// down + combine.  CTA = 8 output rows for every token.
+// gate/up + SwiGLU
 // ----------------------------------------------------------------------------
-template <int CH>  // 16-byte chunks per lane and row: 1 for K <= 512, 2 for K <= 1024
-__global__ void __launch_bounds__(kGvWarps * 32, 2) gemv_down_kernel(GemvArgs a) {
-  extern __shared__ float4 sm4[];
+__global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = a.H, G = H >> 6, rowb = H >> 1;
+  const int c0 = blockIdx.x * a.per_cta;                 // a multiple of 4
+  const int np = min(c0 + a.per_cta, a.total_max) - c0;  // pairs of this CTA
+  const int ntile = (np + kTileRows - 1) / kTileRows;
+  const GuLayout Ly = gu_layout(H, a.nbuf, a.per_cta);
+  unsigned char* tiles = smraw + Ly.tiles;
+  unsigned char* scales = smraw + Ly.scales;
+  uint2* xfrag = reinterpret_cast<uint2*>(smraw + Ly.xfrag);
+  float* xsx = reinterpret_cast<float*>(smraw + Ly.xsx);
+  float* xsum = reinterpret_cast<float*>(smraw + Ly.xsum);
+  float* part = reinterpret_cast<float*>(smraw + Ly.part);
+  DecMeta* meta = reinterpret_cast<DecMeta*>(smraw + Ly.meta);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smraw + Ly.bars);
+  const int bs = Ly.bs, sst = Ly.ss;
+  TL_START(0);
+  CYC(0);
+  if (tid < a.nbuf) mbar_init(&bars[tid], 1);
+  mbar_init_fence();
+  // Copies of the pairs of one pass (the shared expert before the routing
+  // exists, the routed experts after): weights by bulk copies of 4-row blocks
+  // (single rows where a block is not one run of one expert) counted on the
+  // tile's mbarrier; scale rows by 4-16 byte cp.async into MMA-row order.
+  auto issue = [&](bool shared_pass) {
+    auto mine = [&](const DecMeta& m) { return m.ptr != nullptr && (m.kind == 1) == shared_pass; };
+    for (int bb = tid; bb < (np + 3) >> 2; bb += blockDim.x) {
+      const int p0 = bb * 4, tl = p0 / kTileRows, b = (p0 % kTileRows) >> 2;
+      const DecMeta m0 = meta[p0];
+      bool run = p0 + 3 < np && mine(m0);
+      for (int i = 1; i < 4 && run; ++i) {
+        const DecMeta& m = meta[p0 + i];
+        run = mine(m) && m.ptr == m0.ptr && m.kind == m0.kind && m.row == m0.row + i;
+      }
+      uint64_t* bar = &bars[tl];
+      unsigned char* dg = tiles + (size_t)((tl * 2 + 0) * 4 + b) * bs;
+      unsigned char* du = tiles + (size_t)((tl * 2 + 1) * 4 + b) * bs;
+      if (run) {
+        mbar_expect_tx(bar, 8u * rowb);
+        const size_t off = (size_t)m0.row * rowb;
+        bulk_load(dg, m0.ptr + a.gu.w[m0.kind] + off, 4u * rowb, bar);
+        bulk_load(du, m0.ptr + a.gu.w2[m0.kind] + off, 4u * rowb, bar);
+      } else {
+        for (int i = 0; i < 4 && p0 + i < np; ++i) {
+          const DecMeta& m = meta[p0 + i];
+          if (!mine(m)) continue;
+          mbar_expect_tx(bar, 2u * rowb);
+          const size_t off = (size_t)m.row * rowb;
+          bulk_load(dg + (size_t)i * rowb, m.ptr + a.gu.w[m.kind] + off, rowb, bar);
+          bulk_load(du + (size_t)i * rowb, m.ptr + a.gu.w2[m.kind] + off, rowb, bar);
+        }
+      }
+    }
+    const int scb = a.cs_gu, spr = (G * 2) / scb;
+    for (int q = tid; q < np * 4 * spr; q += blockDim.x) {
+      const int p = q / (4 * spr), rem = q - p * 4 * spr, arr = rem / spr, c = rem - arr * spr;
+      const DecMeta& m = meta[p];
+      if (!mine(m)) continue;
+      const int tl = p / kTileRows, R = row_to_mma(p % kTileRows);
+      const uint64_t off = arr == 0 ? a.gu.s[m.kind] : arr == 1 ? a.gu.b[m.kind]
+                         : arr == 2 ? a.gu.s2[m.kind] : a.gu.b2[m.kind];
+      cp_async(scales + (size_t)((tl * 4 + arr) * kTileRows + R) * sst + c * scb,
+               m.ptr + off + (size_t)m.row * G * 2 + c * scb, scb);
+    }
+    cp_commit();
+  };
+  // ---- the shared expert's rows do not depend on the routing ----
+  for (int p = tid; p < np; p += blockDim.x) {
+    int row = 0;
+    DecMeta m;
+    m.ptr = nullptr;
+    m.kind = 0;
+    m.off = m.cnt = 0;
+    if (pair_entry(a, c0 + p, true, 0, row) >= 0) {
+      m.ptr = a.shared_ptr;
+      m.kind = 1;
+      m.off = a.direct ? a.k : 0;
+      m.cnt = a.direct ? 1 : a.B;
+    }
+    m.row = row;
+    meta[p] = m;
+  }
+  __syncthreads();  // meta and barrier initialisation visible
+  issue(true);
+  CYC(1);
+  // activations (complete when this grid starts: they are the router's input)
+  stage_digits(a.x, a.B, H, H, false, xfrag, xsx, xsum);
+  if (a.B == 1) {  // token 1's columns are zero
+    for (int q = tid; q < G * 2 * 4; q += blockDim.x) {
+      const int g = q >> 3, h = (q >> 2) & 1, j = q & 3;
+      uint2* fr = xfrag + ((size_t)g * 2 + h) * 32;
+#pragma unroll
+      for (int d = 0; d < 4; ++d) fr[16 + d * 4 + j] = make_uint2(0u, 0u);
+    }
+  }
+  pdl_wait();
+  TL_WAITED(0);
+  CYC(2);
+  {
+    const int n_ent = gemv_entries<false>(a);
+    for (int p = tid; p < np; p += blockDim.x) {
+      if (meta[p].kind == 1) continue;
+      int row = 0;
+      const int j = pair_entry(a, c0 + p, false, n_ent, row);
+      DecMeta m;
+      m.ptr = nullptr;
+      m.kind = 0;
+      m.row = row;
+      m.off = m.cnt = 0;
+      if (j >= 0) {
+        const ActEntry en = gemv_entry<false>(a, j);
+        m.ptr = en.ptr;
+        m.kind = en.kind;
+        m.off = en.off;
+        m.cnt = en.cnt;
+      }
+      meta[p] = m;
+    }
+  }
+  __syncthreads();
+  CYC(3);
+  issue(false);
+  __syncthreads();  // every expect_tx precedes the arrival
+  if (tid == 0)
+    for (int tl = 0; tl < ntile; ++tl) mbar_arrive(&bars[tl]);
+  // the down kernel may start now: it reads the routing through L2
+  pdl_trigger();
+  TL_MARK(8);
+  CYC(4);
+  cp_wait<0>();
+  __syncthreads();  // scale rows visible
+  CYC(5);
+  // ---- items (tile, chunk of groups) on warps, each waiting only for its
+  //      tile; lanes of a quad hold one MMA row's token columns (j even:
+  //      digits 0,1; j odd: digit 2) ----
+  const int r = lane >> 2, j = lane & 3, t = j >> 1;
+  const int ks = max(1, min(kDecWarps / max(ntile, 1), G));  // chunks per tile
+  const int gpc = (G + ks - 1) / ks;
+  const int ssh = sst >> 1;  // scale-row stride in bf16 elements
+  for (int item = warp; item < ntile * ks; item += kDecWarps) {
+    const int tl = item / ks, q = item - tl * ks;
+    const int g0 = q * gpc, g1 = min(G, g0 + gpc);
+    if (!mbar_wait(&bars[tl], 0)) {
+      if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
+      mbar_wait(&bars[tl], 0);  // the copies may still land: wait once more
+    }
+    if (item == 0) CYC(6);
+    float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};  // [gate|up][mma row r | r+8]
+    // MMA rows r and r+8: block r & 3, rows (r >> 2) and 2 + (r >> 2) in it
+    const unsigned char* rbase = tiles + (size_t)(tl * 2 * 4 + (r & 3)) * bs +
+                                 (size_t)(r >> 2) * rowb + 8 * j;
+    const uint16_t* scb0 = reinterpret_cast<const uint16_t*>(scales) +
+                           ((size_t)(tl * 4) * kTileRows + r) * ssh;
+#pragma unroll 2
+    for (int g = g0; g < g1; ++g) {
+      const uint2 bA = xfrag[((size_t)g * 2 + 0) * 32 + lane];
+      const uint2 bB = xfrag[((size_t)g * 2 + 1) * 32 + lane];
+      const float sxp = xsx[((size_t)t * G + g) * 2 + (j & 1)];
+      const float xsb = (j & 1) ? 0.0f : xsum[(size_t)t * G + g];  // bias term on even lanes
+#pragma unroll
+      for (int mat = 0; mat < 2; ++mat) {
+        const unsigned char* rb0 = rbase + (size_t)mat * 4 * bs + 32 * g;
+        const uint2 w0 = *reinterpret_cast<const uint2*>(rb0);
+        const uint2 w8 = *reinterpret_cast<const uint2*>(rb0 + (size_t)2 * rowb);
+        int d[4] = {0, 0, 0, 0};
+        mma_s8(d, lo_nib(w0.x), lo_nib(w8.x), hi_nib(w0.x), hi_nib(w8.x), bA.x, bA.y);
+        mma_s8(d, lo_nib(w0.y), lo_nib(w8.y), hi_nib(w0.y), hi_nib(w8.y), bB.x, bB.y);
+        // [array][mma row]: scale (2 mat), bias (2 mat + 1)
+        const uint16_t* sc = scb0 + (size_t)(2 * mat) * kTileRows * ssh + g;
+        const uint16_t* bi = sc + (size_t)kTileRows * ssh;
+        const int i0 = (j & 1) ? d[0] : d[0] * 128 + d[1];
+        const int i8 = (j & 1) ? d[2] : d[2] * 128 + d[3];
+        acc[mat][0] = fmaf(bf16_bits_to_f32(sc[0]) * sxp, (float)i0, acc[mat][0]);
+        acc[mat][1] = fmaf(bf16_bits_to_f32(sc[(size_t)8 * ssh]) * sxp, (float)i8, acc[mat][1]);
+        acc[mat][0] = fmaf(bf16_bits_to_f32(bi[0]), xsb, acc[mat][0]);
+        acc[mat][1] = fmaf(bf16_bits_to_f32(bi[(size_t)8 * ssh]), xsb, acc[mat][1]);
+      }
+    }
+#pragma unroll
+    for (int mat = 0; mat < 2; ++mat)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) acc[mat][h] += __shfl_xor_sync(0xFFFFFFFFu, acc[mat][h], 1);
+    if (!(j & 1)) {
+      // part[tile][chunk][mma row][mat][token]
+      float* pw = part + ((size_t)tl * ks + q) * kTileRows * 4;
+#pragma unroll
+      for (int mat = 0; mat < 2; ++mat) {
+        pw[(r * 2 + mat) * 2 + t] = acc[mat][0];
+        pw[((r + 8) * 2 + mat) * 2 + t] = acc[mat][1];
+      }
+    }
+  }
+  __syncthreads();
+  CYC(7);
+  // ---- fixed-order sum over chunks, SwiGLU, store h ----
+  for (int qq = tid; qq < np * a.B; qq += blockDim.x) {
+    const int p = qq / a.B, tk = qq - p * a.B;
+    const DecMeta m = meta[p];
+    if (m.ptr == nullptr) continue;
+    int pos = -1;
+    if (a.direct) {
+      pos = m.off;
+    } else {
+      for (int i = 0; i < m.cnt; ++i)
+        if (a.pair_tok[m.off + i] == tk) pos = m.off + i;
+    }
+    if (pos < 0) continue;
+    const int tl = p / kTileRows, R = row_to_mma(p % kTileRows);
+    float gs = 0.0f, us = 0.0f;
+    for (int q = 0; q < ks; ++q) {
+      const float* pw = part + ((size_t)tl * ks + q) * kTileRows * 4;
+      gs += pw[(R * 2 + 0) * 2 + tk];
+      us += pw[(R * 2 + 1) * 2 + tk];
+    }
+    a.h[(size_t)pos * a.Imax + m.row] = __fmul_rn(ref_silu(gs), us);
+  }
+  CYC(8);
+  TL_END(0);
+}
+
+// ----------------------------------------------------------------------------
+// down + combine.  CTA = output rows [r0, r0 + rpc), rpc <= 16, every entry.
+// ----------------------------------------------------------------------------
+__global__ void __launch_bounds__(kDecWarps * 32, 2) dec_down_kernel(GemvArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
   const int P = a.B * (a.k + a.has_shared);
-  const int nch = a.Imax >> 5;
-  float* hs = reinterpret_cast<float*>(sm4);        // [P][Imax/32][36]
-  float* hsum = hs + P * nch * kChunkPad;            // [P][Imax/32]
-  float* ys = hsum + P * nch;                        // [P][8]
-#ifdef OSM_PHASE_TIMING
-  __shared__ long long gts_[8];
-#endif
-  GV_STAMP(0);
-  pdl_wait();
-  pdl_trigger();
-  GV_STAMP(1);
-  stage_chunks(a.h, P, a.Imax, hs, hsum);
-  __syncthreads();
-  GV_STAMP(2);
-  const int n_active = gemv_entries(a);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int half = lane >> 4, hl = lane & 15;
-  const int r0 = blockIdx.x * 8;
-  for (int j = warp; j < n_active; j += kGvWarps) {
-    const ActEntry en = gemv_entry(a, j);
-    if (en.ptr == nullptr) continue;
-    const int kind = en.kind;
-    const int K = a.dn.K[kind];
-    const int G = K >> 6, cpr = K >> 5;
-    const uint4* W = reinterpret_cast<const uint4*>(en.ptr + a.dn.w[kind]);
-    const uint16_t* S = reinterpret_cast<const uint16_t*>(en.ptr + a.dn.s[kind]);
-    const uint16_t* Bb = reinterpret_cast<const uint16_t*>(en.ptr + a.dn.b[kind]);
-    // rows r0 + 2*step + half, chunks c = hl, hl + 16, ...
-    uint4 q[4][CH];
-    float s[4][CH], b[4][CH];
-#pragma unroll
-    for (int st = 0; st < 4; ++st) {
-      const int r = r0 + 2 * st + half;
-#pragma unroll
-      for (int u = 0; u < CH; ++u) {
-        const int c = hl + 16 * u;
-        if (c < cpr) {
-          q[st][u] = __ldg(W + (size_t)r * cpr + c);
-          s[st][u] = bf16_bits_to_f32(__ldg(S + (size_t)r * G + (c >> 1)));
-          b[st][u] = bf16_bits_to_f32(__ldg(Bb + (size_t)r * G + (c >> 1)));
-        }
-      }
+  const int Kmax = a.dn.K[0] > a.dn.K[1] ? a.dn.K[0] : a.dn.K[1];
+  const int rpc = a.rpc, r0 = blockIdx.x * rpc, nr = min(rpc, a.H - r0);
+  const int GdM = Kmax >> 6, Gh = a.Imax >> 6;
+  const DnLayout Ly = dn_layout(a.max_entries, Kmax, a.Imax, P);
+  unsigned char* wt = smraw + Ly.wt;
+  uint16_t* scales = reinterpret_cast<uint16_t*>(smraw + Ly.scales);
+  uint2* hfrag = reinterpret_cast<uint2*>(smraw + Ly.hfrag);
+  float* hsx = reinterpret_cast<float*>(smraw + Ly.hsx);
+  float* hsum = reinterpret_cast<float*>(smraw + Ly.hsum);
+  float* ys = reinterpret_cast<float*>(smraw + Ly.ys);
+  float* rwt = reinterpret_cast<float*>(smraw + Ly.rw);           // [B*(k+1)] weights, shared gate last
+  int* rpos = reinterpret_cast<int*>(smraw + Ly.rw) + P;          // [B*(k+1)] pair of (token, pick)
+  DecMeta* meta = reinterpret_cast<DecMeta*>(smraw + Ly.meta);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smraw + Ly.bars);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bs = Ly.bs;
+  TL_START(1);
+  CYC(16);
+  // This grid starts once every gate/up CTA has passed its own dependency
+  // wait, so the routing is complete; it is read through L2.
+  const int ne = min(gemv_entries<true>(a), a.max_entries);
+  {
+    // combine inputs: weight and pair position of every (token, pick); the
+    // shared expert is pick k with the sigmoid gate as its weight
+    const int kp1 = a.k + a.has_shared;
+    for (int q = tid; q < a.B * kp1; q += blockDim.x) {
+      const int t = q / kp1, p = q - t * kp1;
+      rwt[q] = p < a.k ? __ldcg(a.weights + t * a.k + p) : __ldcg(a.sgate + t);
+      rpos[q] = a.direct ? p : __ldcg(a.tp_pos + t * kp1 + p);
     }
-    for (int i = 0; i < en.cnt; ++i) {
-      const int pos = en.off + i;
-#pragma unroll
-      for (int st = 0; st < 4; ++st) {
-        float acc = 0.0f;
-#pragma unroll
-        for (int u = 0; u < CH; ++u) {
-          const int c = hl + 16 * u;
-          if (c < cpr) {
-            const float* hp = hs + (pos * nch + c) * kChunkPad;
-            acc = fmaf(b[st][u], hsum[pos * nch + c], fmaf(s[st][u], chunk_dot(q[st][u], hp), acc));
-          }
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-        if (hl == 0) ys[pos * 8 + 2 * st + half] = acc;
+  }
+  for (int jj = tid; jj < ne; jj += blockDim.x) {
+    const ActEntry en = gemv_entry<true>(a, jj);
+    DecMeta m;
+    m.ptr = en.ptr;
+    m.kind = en.kind;
+    m.off = en.off;
+    m.cnt = en.cnt;
+    m.row = 0;
+    meta[jj] = m;
+  }
+  CYC(17);
+  if (tid < ne) mbar_init(&bars[tid], 1);
+  mbar_init_fence();
+  __syncthreads();
+  // rows: one bulk copy per block of <= 4 consecutive output rows
+  for (int q = tid; q < ne * 4; q += blockDim.x) {
+    const int jj = q >> 2, b = q & 3, n = min(4, nr - 4 * b);
+    const DecMeta& m = meta[jj];
+    if (m.ptr == nullptr || n <= 0) continue;
+    const int rb = a.dn.K[m.kind] >> 1;
+    mbar_expect_tx(&bars[jj], (uint32_t)(n * rb));
+    bulk_load(wt + (size_t)(jj * 4 + b) * bs, m.ptr + a.dn.w[m.kind] + (size_t)(r0 + 4 * b) * rb,
+              (uint32_t)(n * rb), &bars[jj]);
+  }
+  CYC(18);
+  // scale rows: cp.async granules, [entry][s|b][row][GdM]
+  {
+    const int scb = a.cs_dn;
+    const int spr = (GdM * 2) / scb;
+    for (int q = tid; q < ne * 2 * nr * spr; q += blockDim.x) {
+      const int jj = q / (2 * nr * spr);
+      int rem = q - jj * 2 * nr * spr;
+      const int arr = rem / (nr * spr);
+      rem -= arr * nr * spr;
+      const int rr = rem / spr, c = rem - rr * spr;
+      const DecMeta& m = meta[jj];
+      const int Gd = a.dn.K[m.kind] >> 6;
+      if (m.ptr == nullptr || c * scb >= Gd * 2) continue;
+      cp_async(reinterpret_cast<unsigned char*>(scales) +
+                   ((size_t)((jj * 2 + arr) * kTileRows + row_to_mma(rr)) * GdM) * 2 + c * scb,
+               m.ptr + (arr ? a.dn.b[m.kind] : a.dn.s[m.kind]) + (size_t)(r0 + rr) * Gd * 2 + c * scb,
+               scb);
+    }
+    cp_commit();
+  }
+  __syncthreads();  // every row issued
+  if (tid < ne) mbar_arrive(&bars[tid]);
+  CYC(19);
+  pdl_wait();
+  TL_WAITED(1);
+  CYC(20);
+  stage_digits(a.h, P, a.Imax, a.Imax, true, hfrag, hsx, hsum);
+  cp_wait<0>();
+  __syncthreads();
+  CYC(21);
+  TL_MARK(12);
+  // ---- items (entry, half of its groups) on warps; each entry's pairs are
+  //      separate MMA columns ----
+  const int r = lane >> 2, j = lane & 3;
+  const float bmask = j == 0 ? 1.0f : 0.0f;  // the bias term on one lane per row
+  const int ksd = max(1, min(kDnChunks, kDecWarps / max(ne, 1)));  // group chunks per entry
+  for (int item = warp; item < ksd * ne; item += kDecWarps) {
+    const int jj = item / ksd, half = item - jj * ksd;
+    const DecMeta m = meta[jj];
+    if (m.ptr == nullptr) continue;
+    if (!mbar_wait(&bars[jj], 0)) {
+      if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
+      mbar_wait(&bars[jj], 0);  // the copies may still land: wait once more
+    }
+    const int Gd = a.dn.K[m.kind] >> 6, gh = (Gd + ksd - 1) / ksd;
+    const int ga = min(Gd, half * gh), gb = min(Gd, ga + gh);
+    const int rbe = a.dn.K[m.kind] >> 1;  // bytes of one of this entry's rows
+    // MMA rows r and r+8: block r & 3, rows (r >> 2) and 2 + (r >> 2) in it
+    const unsigned char* rb0 = wt + (size_t)(jj * 4 + (r & 3)) * bs + (size_t)(r >> 2) * rbe + 8 * j;
+    const uint16_t* sc = scales + ((size_t)(jj * 2) * kTileRows) * GdM;
+    const uint16_t* bi = sc + (size_t)kTileRows * GdM;
+    for (int i = 0; i < m.cnt; ++i) {
+      const int pos = m.off + i;
+      float acc0 = 0.0f, acc8 = 0.0f;
+#pragma unroll 4
+      for (int g = ga; g < gb; ++g) {
+        const uint2 w0 = *reinterpret_cast<const uint2*>(rb0 + 32 * g);
+        const uint2 w8 = *reinterpret_cast<const uint2*>(rb0 + (size_t)2 * rbe + 32 * g);
+        const uint2* fr = hfrag + (((size_t)pos * Gh + g) * 2) * 16;
+        const uint2 bA = lane < 16 ? fr[lane] : make_uint2(0u, 0u);  // columns 4..7 are zero
+        const uint2 bB = lane < 16 ? fr[16 + lane] : make_uint2(0u, 0u);
+        int d[4] = {0, 0, 0, 0};
+        mma_s8(d, lo_nib(w0.x), lo_nib(w8.x), hi_nib(w0.x), hi_nib(w8.x), bA.x, bA.y);
+        mma_s8(d, lo_nib(w0.y), lo_nib(w8.y), hi_nib(w0.y), hi_nib(w8.y), bB.x, bB.y);
+        const float sxp = hsx[((size_t)pos * Gh + g) * 2 + (j & 1)];
+        const float hb = bmask * hsum[(size_t)pos * Gh + g];
+        const int i0 = (j & 1) ? d[0] : d[0] * 128 + d[1];
+        const int i8 = (j & 1) ? d[2] : d[2] * 128 + d[3];
+        acc0 = fmaf(bf16_bits_to_f32(sc[(size_t)r * GdM + g]) * sxp, (float)i0, acc0);
+        acc8 = fmaf(bf16_bits_to_f32(sc[(size_t)(r + 8) * GdM + g]) * sxp, (float)i8, acc8);
+        acc0 = fmaf(bf16_bits_to_f32(bi[(size_t)r * GdM + g]), hb, acc0);
+        acc8 = fmaf(bf16_bits_to_f32(bi[(size_t)(r + 8) * GdM + g]), hb, acc8);
+      }
+      acc0 += __shfl_xor_sync(0xFFFFFFFFu, acc0, 1);
+      acc8 += __shfl_xor_sync(0xFFFFFFFFu, acc8, 1);
+      if (j == 0) {
+        float* yh = ys + ((size_t)half * P + pos) * kTileRows;
+        const int m0 = mma_to_row(r), m8 = mma_to_row(r + 8);
+        if (m0 < nr) yh[m0] = acc0;
+        if (m8 < nr) yh[m8] = acc8;
       }
     }
   }
   __syncthreads();
-  GV_STAMP(3);
+  CYC(22);
+  TL_MARK(13);
+  pdl_trigger();
   // combine in pick order, shared expert last, then the residual
   const int kp1 = a.k + a.has_shared;
-  for (int i = threadIdx.x; i < a.B * 8; i += blockDim.x) {
-    const int t = i >> 3, rr = i & 7;
+  for (int i = tid; i < a.B * nr; i += blockDim.x) {
+    const int t = i / nr, rr = i - t * nr;
     float acc = 0.0f;
-    for (int p = 0; p < a.k; ++p) {
-      const int pos = a.direct ? p : a.tp_pos[t * kp1 + p];
-      acc = __fadd_rn(acc, __fmul_rn(a.weights[t * a.k + p], ys[pos * 8 + rr]));
-    }
-    if (a.has_shared) {
-      const int pos = a.direct ? a.k : a.tp_pos[t * kp1 + a.k];
-      acc = __fadd_rn(acc, __fmul_rn(a.sgate[t], ys[pos * 8 + rr]));
+    for (int p = 0; p < kp1; ++p) {
+      const int pos = rpos[t * kp1 + p];
+      float y = ys[(size_t)pos * kTileRows + rr];
+      for (int c = 1; c < ksd; ++c) y += ys[((size_t)c * P + pos) * kTileRows + rr];
+      acc = __fadd_rn(acc, __fmul_rn(rwt[t * kp1 + p], y));
     }
     if (a.residual) acc = __fadd_rn(a.residual[(size_t)t * a.H + r0 + rr], acc);
     a.out[(size_t)t * a.H + r0 + rr] = acc;
   }
-  GV_STAMP(4);
-#ifdef OSM_PHASE_TIMING
-  if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 200))
-    printf("down cta %d: 1:%lld 2:%lld 3:%lld 4:%lld\n", (int)blockIdx.x, gts_[1] - gts_[0],
-           gts_[2] - gts_[0], gts_[3] - gts_[0], gts_[4] - gts_[0]);
-#endif
+  CYC(23);
+  TL_END(1);
 }
 
 template <typename K, typename... Args>
@@ -344,35 +709,111 @@ void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Ar
   cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
+// Largest copy granule (16, 8 or 4 bytes) dividing every offset and the
+// row length n; 0 when none does.
+int granule(const uint64_t* offs, int count, uint64_t n) {
+  for (int g = 16; g >= 4; g >>= 1) {
+    bool ok = n % g == 0;
+    for (int i = 0; i < count; ++i) ok = ok && offs[i] % g == 0;
+    if (ok) return g;
+  }
+  return 0;
+}
+
 }  // namespace
 
 void init_gemv_attributes(int max_smem) {
-  cudaFuncSetAttribute(gemv_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(gemv_down_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(gemv_down_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(dec_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(dec_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  // the largest shared-memory carveout, so a down CTA fits beside a gate/up CTA
+  cudaFuncSetAttribute(dec_gateup_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  cudaFuncSetAttribute(dec_down_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
 }
 
-void launch_gemv_gateup(const GemvArgs& a, int max_active, int grid_cap, cudaStream_t s,
+bool gemv_configure(GemvArgs& a, int max_active, int num_sms, int max_smem, GemvLaunch* out) {
+  if (a.B < 1 || a.B > 2 || num_sms < 1) return false;
+  const int nk = a.has_shared ? 2 : 1;
+  // the input dims are whole 64-groups in 32-wide MMA slabs; rows copy in
+  // 16-byte chunks
+  if (a.H % 128 || a.Imax % 64) return false;
+  for (int kd = 0; kd < nk; ++kd) {
+    if (a.gu.K[kd] != a.H || a.dn.K[kd] % 64 || a.dn.rows[kd] != a.H) return false;
+    if (a.gu.w[kd] % 16 || a.gu.w2[kd] % 16 || a.dn.w[kd] % 16) return false;
+  }
+  if (a.slab_stride % 16 || reinterpret_cast<uintptr_t>(a.slab) % 16 ||
+      reinterpret_cast<uintptr_t>(a.shared_ptr) % 16)
+    return false;
+  // scale rows: G bf16 per gate/up row, Gd per down row
+  {
+    uint64_t o[9];
+    int n = 0;
+    for (int kd = 0; kd < nk; ++kd) {
+      o[n++] = a.gu.s[kd]; o[n++] = a.gu.b[kd]; o[n++] = a.gu.s2[kd]; o[n++] = a.gu.b2[kd];
+    }
+    o[n++] = a.slab_stride;
+    a.cs_gu = granule(o, n, (uint64_t)(a.H >> 6) * 2);
+    n = 0;
+    for (int kd = 0; kd < nk; ++kd) {
+      o[n++] = a.dn.s[kd]; o[n++] = a.dn.b[kd];
+    }
+    o[n++] = a.slab_stride;
+    int cs = 16;
+    for (int kd = 0; kd < nk; ++kd) {
+      const int c = granule(o, n, (uint64_t)(a.dn.K[kd] >> 6) * 2);
+      if (c < cs) cs = c;
+    }
+    a.cs_dn = cs;
+    if (a.cs_gu == 0 || a.cs_dn == 0) return false;
+  }
+  const int rs = a.has_shared ? a.gu.rows[1] : 0;
+  a.total_max = rs + (max_active - a.has_shared) * a.gu.rows[0];
+  int grid = num_sms;
+  const int need = (a.total_max + kTileRows - 1) / kTileRows;
+  if (need < grid) grid = need < 1 ? 1 : need;
+  a.per_cta = (a.total_max + grid - 1) / grid;
+  a.per_cta = (a.per_cta + 3) & ~3;  // CTA ranges start on 4-row blocks
+  grid = (a.total_max + a.per_cta - 1) / a.per_cta;
+  a.nbuf = (a.per_cta + kTileRows - 1) / kTileRows;  // tiles per CTA
+  if (a.nbuf > 8) return false;
+  const size_t gu_smem = gu_layout(a.H, a.nbuf, a.per_cta).total;
+  a.max_entries = max_active;
+  int rpc = (a.H + num_sms - 1) / num_sms;
+  if (rpc < 1) rpc = 1;
+  if (rpc > kTileRows) return false;
+  a.rpc = rpc;
+  const int Kmax = a.dn.K[0] > a.dn.K[1] ? a.dn.K[0] : a.dn.K[1];
+  if (Kmax > a.Imax) return false;
+  const int P = a.B * (a.k + a.has_shared);
+  const size_t dn_smem = dn_layout(a.max_entries, Kmax, a.Imax, P).total;
+  if (gu_smem > (size_t)max_smem || dn_smem > (size_t)max_smem) return false;
+  out->grid_gu = grid;
+  out->grid_dn = (a.H + rpc - 1) / rpc;
+  out->smem_gu = gu_smem;
+  out->smem_dn = dn_smem;
+  return true;
+}
+
+void launch_gemv_gateup(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s,
                         uint64_t* launches) {
-  const int Imax = a.Imax;
-  const int tiles = (Imax + 2 * kGvWarps - 1) / (2 * kGvWarps);
-  const int nch = a.H >> 5;
-  const size_t smem = (size_t)a.B * nch * (kChunkPad + 1) * sizeof(float);
-  long long items = (long long)tiles * max_active;
-  int grid = (int)(items < grid_cap ? items : grid_cap);
-  if (grid < 1) grid = 1;
-  launch_pdl(gemv_gateup_kernel, dim3(grid), dim3(kGvWarps * 32), smem, s, a, tiles);
+  launch_pdl(dec_gateup_kernel, dim3(l.grid_gu), dim3(kDecWarps * 32), l.smem_gu, s, a);
   if (launches) *launches += 1;
 }
 
-void launch_gemv_down(const GemvArgs& a, cudaStream_t s, uint64_t* launches) {
-  const int P = a.B * (a.k + a.has_shared);
-  const int nch = a.Imax >> 5;
-  const size_t smem = ((size_t)P * nch * (kChunkPad + 1) + (size_t)P * 8) * sizeof(float);
-  const int kmax = a.dn.K[0] > a.dn.K[1] ? a.dn.K[0] : a.dn.K[1];
-  if (kmax <= 512) launch_pdl(gemv_down_kernel<1>, dim3(a.H / 8), dim3(kGvWarps * 32), smem, s, a);
-  else launch_pdl(gemv_down_kernel<2>, dim3(a.H / 8), dim3(kGvWarps * 32), smem, s, a);
+void launch_gemv_down(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s, uint64_t* launches) {
+  launch_pdl(dec_down_kernel, dim3(l.grid_dn), dim3(kDecWarps * 32), l.smem_dn, s, a);
   if (launches) *launches += 1;
 }
 
 }  // namespace osm
+
+#ifdef OSM_PHASE_TIMING
+extern "C" int osm_dbg_timeline_gemv(unsigned long long* out) {
+  unsigned long long init[OSM_TL_SLOTS];
+  for (int i = 0; i < OSM_TL_SLOTS; ++i) init[i] = (i == 0 || i == 4) ? ~0ull : 0ull;
+  cudaMemcpyFromSymbol(out, osm::g_tl, sizeof(init));
+  return (int)cudaMemcpyToSymbol(osm::g_tl, init, sizeof(init));
+}
+extern "C" int osm_dbg_cycles_gemv(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, osm::g_cyc, 32 * sizeof(long long));
+}
+#endif

@@ -71,6 +71,9 @@ struct RouterArgs {
   int* cursor;              // [E+1]
   uint32_t* status;
   unsigned long long* exact_count;
+  // slot base of each pick (null: bad id or not resident), written for the
+  // one-token expert kernels; null pointer: not wanted
+  const uint8_t** pick_ptr;  // [B][k]
 };
 
 // Allow up to max_smem bytes of dynamic shared memory for every kernel that
@@ -146,6 +149,8 @@ struct GemvArgs {
   // routing, entry k the shared expert
   int direct;
   const uint32_t* ids;           // [k]
+  const uint8_t* const* pick_ptr;  // [k] slot base of each pick (router-written)
+  int E;                         // experts (ids >= E are rejected)
   const int* slot_of;            // [E]
   const uint8_t* slab;
   uint64_t slab_stride;
@@ -156,11 +161,27 @@ struct GemvArgs {
   const float* sgate;            // [B]
   const float* residual;         // [B][H] or null
   float* out;                    // [B][H]
+  // set by gemv_configure
+  int total_max;                 // (gate, up) row pairs of all possible entries
+  int per_cta;                   // pairs per gate/up CTA
+  int nbuf;                      // 16-row tiles per gate/up CTA
+  int cs_gu, cs_dn;              // scale-row copy granules (bytes)
+  int rpc;                       // output rows per down CTA
+  int max_entries;               // active entries the down CTA has room for
 };
+struct GemvLaunch {
+  int grid_gu, grid_dn;
+  size_t smem_gu, smem_dn;
+};
+constexpr int kChunkPad = 36;    // floats per staged 32-value chunk (bank spread)
+constexpr int kDecWarps = 16;    // warps per CTA of the decode kernels
 void init_gemv_attributes(int max_smem);
-void launch_gemv_gateup(const GemvArgs& a, int max_active, int grid_cap, cudaStream_t s,
+// false: the shapes or alignment do not suit the decode kernels (the caller
+// uses the tensor-core path instead)
+bool gemv_configure(GemvArgs& a, int max_active, int num_sms, int max_smem, GemvLaunch* out);
+void launch_gemv_gateup(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s,
                         uint64_t* launches);
-void launch_gemv_down(const GemvArgs& a, cudaStream_t s, uint64_t* launches);
+void launch_gemv_down(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s, uint64_t* launches);
 
 struct CombineArgs {
   const float* partial;          // [B][k+1][H]

@@ -31,13 +31,16 @@
 
 #ifdef OSM_PHASE_TIMING
 #include <cstdio>
-#define OSM_STAMP(i) do { if (threadIdx.x == 0 || threadIdx.x == 32) ts_[(i)] = clock64(); } while (0)
+#define OSM_STAMP(i) do { if (threadIdx.x == 0 || threadIdx.x == 32) { ts_[(i)] = clock64(); if ((i) == 0) gt0_ = gtime(); } } while (0)
 #else
 #define OSM_STAMP(i) do { } while (0)
 #endif
 
 namespace osm {
 namespace {
+#ifdef OSM_PHASE_TIMING
+__device__ unsigned long long g_tl[OSM_TL_SLOTS];
+#endif
 
 constexpr float kU = 5.9604644775390625e-8f;  // 2^-24
 constexpr int kLogitWarps = 4;
@@ -77,6 +80,10 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(RouterA
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = (blockIdx.x * kLogitWarps + warp) * EXP;
   const bool reg_path = !g.f32w && g.nvec <= kMaxVec;
+#ifdef OSM_PHASE_TIMING
+  const unsigned long long lg0 = gtime();
+#endif
+  TL_START(0);
   // The weights are immutable: fetch them before waiting on the predecessor.
   uint4 wv[EXP][kMaxVec];
 #pragma unroll
@@ -88,6 +95,7 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(RouterA
         wv[q][m] = __ldg(a.wp + ((size_t)(e0 + q) * g.nvec + m) * 32 + lane);
     }
   pdl_wait();
+  TL_WAITED(0);
   const int t0 = blockIdx.y * TOKS;
   const int nv4 = g.Hp >> 2;
   const bool vec_ok = (g.H & 3) == 0;
@@ -111,7 +119,10 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(RouterA
   }
   __syncthreads();
   pdl_trigger();
-  if (e0 >= g.E) return;
+  if (e0 >= g.E) {
+    TL_END(0);
+    return;
+  }
   float tacc[EXP][TOKS], aacc[EXP][TOKS], sacc[EXP][TOKS];
 #pragma unroll
   for (int q = 0; q < EXP; ++q)
@@ -195,6 +206,11 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(RouterA
       }
     }
   }
+  TL_END(0);
+#ifdef OSM_PHASE_PRINT
+  if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 7) && blockIdx.y == 0)
+    printf("logits cta %d: g %llu..%llu\n", (int)blockIdx.x, lg0, gtime());
+#endif
 }
 
 // ----------------------------------------------------------------------------
@@ -424,25 +440,70 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
 
 // Softmax weights of the picks from logits lsel[0..k) (lsel[0] the largest)
 // with the sum over the fast logits v[] (lane-strided); lane j handles pick j.
-__device__ __forceinline__ void write_weights(const RouterArgs& a, int tok, const float (&v)[32],
+// Slot base of expert id (null, with a status bit, when the id is out of
+// range or the expert is not resident).
+__device__ __forceinline__ const uint8_t* slot_base(const RouterArgs& a, uint32_t id) {
+  if (id >= (uint32_t)a.g.E) {
+    atomicOr(a.status, kStatusBadSlot);
+    return nullptr;
+  }
+  const int slot = a.slot_of[id];
+  if (slot < 0) {
+    atomicOr(a.status, kStatusNotResident);
+    return nullptr;
+  }
+  return a.slab + (size_t)slot * a.slab_stride;
+}
+
+// Weights of the k picks (warp 0): p_j = exp(l_j - mx) / s, where s is the sum
+// of exp(l_e - mx) over every expert, then renormalised over the picks.
+__device__ __forceinline__ void write_weights(const RouterArgs& a, int tok, float s, float mx,
                                               const int* sid, const float* lsel) {
   const int lane = threadIdx.x & 31;
   const int k = a.g.k;
-  const float mx = lsel[0];
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 32; ++i)
-    if (i * 32 + lane < a.g.E) s += expf(__fsub_rn(v[i], mx));
-  s = warp_sum(s);
-  const float p = lane < k ? __fdiv_rn(expf(__fsub_rn(lsel[lane], mx)), s) : 0.0f;
+  const float p = lane < k ? __fdiv_rn(__expf(__fsub_rn(lsel[lane], mx)), s) : 0.0f;
   const float mass = warp_sum(p);
   if (lane == 0 && (!(mass > 0.0f) || !isfinite(mass) || !(s > 0.0f) || !isfinite(s)))
     atomicOr(a.status, kStatusBadMass);
   if (lane < k) {
+    const float wv = a.norm ? __fdiv_rn(p, mass) : p;
     a.ids[(size_t)tok * k + lane] = (uint32_t)sid[lane];
-    a.weights[(size_t)tok * k + lane] = a.norm ? __fdiv_rn(p, mass) : p;
+    a.weights[(size_t)tok * k + lane] = wv;
+    if (a.ids_out) a.ids_out[(size_t)tok * k + lane] = (uint32_t)sid[lane];
+    if (a.weights_out) a.weights_out[(size_t)tok * k + lane] = wv;
+    if (a.pick_ptr) a.pick_ptr[(size_t)tok * k + lane] = slot_base(a, (uint32_t)sid[lane]);
   }
-  if (lane == 0) a.mass[tok] = mass;
+  if (lane == 0) {
+    a.mass[tok] = mass;
+    if (a.mass_out) a.mass_out[tok] = mass;
+  }
+}
+
+// Sorts one key per lane across the warp, largest first (bitonic network).
+__device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long key) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, key, stride);
+      const bool lower = (lane & stride) == 0;
+      const bool take_max = lower == ((lane & size) == 0 || size == 32);
+      key = take_max ? (other > key ? other : key) : (other < key ? other : key);
+    }
+  }
+  return key;
+}
+
+__device__ __forceinline__ unsigned long long sel_key(float v, int id) {
+  return ((unsigned long long)ord_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)id);
+}
+__device__ __forceinline__ int key_id(unsigned long long key) {
+  return (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+}
+__device__ __forceinline__ float key_value(unsigned long long key) {
+  const uint32_t kk32 = (uint32_t)(key >> 32);
+  return __uint_as_float((kk32 & 0x80000000u) ? (kk32 & 0x7FFFFFFFu) : ~kk32);
 }
 
 // True when consecutive (exact) logits are far enough apart that their
@@ -461,20 +522,48 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   __shared__ int cand_id[kMaxCand];
   __shared__ float cand_l[kMaxCand];
   __shared__ int s_flag, s_ncand;
-  __shared__ float s_bm, s_bcast;
+  __shared__ float s_bm, s_bcast, s_sum, s_mx;
   __shared__ float sg_part[kSelThreads / 32];
+  __shared__ float s_red2[kSelThreads / 32];
+  __shared__ unsigned long long s_heads[32 * (kMaxTopK + 1)];
   const RouterGeom g = a.g;
   const int tok = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int k = g.k;
 #ifdef OSM_PHASE_TIMING
   __shared__ long long ts_[16];
+  __shared__ unsigned long long gt0_;
 #endif
   OSM_STAMP(0);
+  TL_START(1);
+  // the shared gate row is immutable: fetch it before waiting
+  constexpr int kSgRegs = 4;
+  float sgw[kSgRegs];
+#pragma unroll
+  for (int j = 0; j < kSgRegs; ++j) {
+    const int h = tid + j * kSelThreads;
+    sgw[j] = (a.sgate_w != nullptr && h < g.H) ? a.sgate_w[h] : 0.0f;
+  }
   pdl_wait();
+  // the expert kernels may launch now: they stage their inputs and prefetch
+  // the shared expert while this grid selects, then wait for it
   pdl_trigger();
   OSM_STAMP(1);
+  TL_WAITED(1);
   const float* x = a.x + (size_t)tok * g.H;
+  // this thread's experts: tid and tid + kSelThreads (E <= 2 * kSelThreads)
+  float lv[2] = {-INFINITY, -INFINITY};
+  float bmax = 0.0f;
+  if (!a.skip_route) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int e = tid + r * kSelThreads;
+      if (e < g.E) {
+        lv[r] = a.logits[(size_t)tok * g.E + e];
+        bmax = fmaxf(bmax, a.bounds[(size_t)tok * g.E + e]);
+      }
+    }
+  }
   int nonfinite = 0;
   if ((g.H & 3) == 0) {
     for (int i = tid; i < (g.H >> 2); i += blockDim.x) {
@@ -496,66 +585,125 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   nonfinite = __syncthreads_or(nonfinite);
   OSM_STAMP(2);
   if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
-  const bool route = !nonfinite && !a.skip_route;
-  // ---- warps 1..: activation fragments and the shared-gate dot, while
-  //      warp 0 selects ----
-  if (warp != 0) {
-    const int nt = blockDim.x - 32, me = tid - 32;
-    if (a.xfrag != nullptr) {
-      const int nch = g.H >> 3;
-      for (int c = me; c < nch; c += nt) {
-        const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
-        const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
-        const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
-        uint32_t hi[8], lo[8];
+  const bool route = !nonfinite && !a.skip_route;  // block-uniform
+  const int nsel = k + 1 <= g.E ? k + 1 : k;
+  const int nl = (g.E + 31) >> 5;  // lists of 32 experts
+  // ---- 1. fast path: certified top-k over the fast logits.  Each warp sorts
+  //      its lists of 32 and keeps nsel heads; every head is then ranked
+  //      against all heads. ----
+  if (route) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
-        float fs = xc[0];
-#pragma unroll
-        for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
-        uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
-        dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
-                            pack2(hi[3], hi[7]));
-        dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
-                            pack2(lo[3], lo[7]));
-        a.xfsum8[(size_t)tok * nch + c] = fs;
+    for (int r = 0; r < 2; ++r) {
+      const int L = warp + r * (kSelThreads / 32);
+      if (L < nl) {
+        const int e = L * 32 + lane;
+        const unsigned long long key = warp_sort_desc(e < g.E ? sel_key(lv[r], e) : 0ull);
+        if (lane < nsel) s_heads[L * nsel + lane] = key;
       }
     }
-    if (a.sgate_w != nullptr) {
-      float d = 0.0f;
-      for (int h = me; h < g.H; h += nt) d = fmaf(a.sgate_w[h], xs[h], d);
-      d = warp_sum(d);
-      if (lane == 0) sg_part[warp] = d;
+    bmax = warp_max(bmax);
+    if (lane == 0) s_red2[warp] = bmax;
+  }
+  // activation fragments of the tensor-core path
+  if (a.xfrag != nullptr) {
+    const int nch = g.H >> 3;
+    for (int c = tid; c < nch; c += blockDim.x) {
+      const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
+      const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
+      const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+      uint32_t hi[8], lo[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
+      float fs = xc[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
+      uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
+      dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
+                          pack2(hi[3], hi[7]));
+      dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
+                          pack2(lo[3], lo[7]));
+      a.xfsum8[(size_t)tok * nch + c] = fs;
     }
   }
-  // ---- 1. fast path: certified top-k over the fast logits ----
-  float v[32];
-  if (warp == 0 && route) {
-    OSM_STAMP(3);
-    float bm = 0.0f;
+  if (a.sgate_w != nullptr) {
+    float d = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int id = i * 32 + lane;
-      v[i] = id < g.E ? a.logits[(size_t)tok * g.E + id] : -INFINITY;
-      if (id < g.E) bm = fmaxf(bm, a.bounds[(size_t)tok * g.E + id]);
+    for (int j = 0; j < kSgRegs; ++j) {
+      const int h = tid + j * kSelThreads;
+      if (h < g.H) d = fmaf(sgw[j], xs[h], d);
     }
-    bm = warp_max(bm);
-    OSM_STAMP(4);
-    const int nsel = k + 1 <= g.E ? k + 1 : k;
-    warp_select(v, g.E, nsel, sel_id, sel_v);
-    OSM_STAMP(5);
-    bool ok = !a.force_exact && isfinite(sel_v[0]);
-    const float mx0 = sel_v[0];
-    for (int j = 0; j + 1 < nsel; ++j) {
+    for (int h = tid + kSgRegs * kSelThreads; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
+    d = warp_sum(d);
+    if (lane == 0) sg_part[warp] = d;
+  }
+  __syncthreads();
+  OSM_STAMP(3);
+  if (route) {
+    // warp w ranks heads w, w + nw, ...: lanes count the heads above it
+    const int nc = nl * nsel;
+    const int nw = blockDim.x >> 5;
+    unsigned long long hk[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hk[j] = lane + 32 * j < nc ? s_heads[lane + 32 * j] : 0ull;
+#pragma unroll 2
+    for (int c = warp; c < nc; c += nw) {
+      const unsigned long long mine = s_heads[c];
+      unsigned int cnt = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cnt += hk[j] > mine ? 1u : 0u;
+      for (int i = lane + 256; i < nc; i += 32) cnt += s_heads[i] > mine ? 1u : 0u;
+      const unsigned int rank = __reduce_add_sync(0xFFFFFFFFu, cnt);
+      if (lane == 0 && rank < (unsigned int)nsel) {
+        sel_id[rank] = key_id(mine);
+        sel_v[rank] = key_value(mine);
+      }
+    }
+  }
+  // ---- shared expert scalar gate ----
+  if (tid == blockDim.x - 32) {
+    if (a.sgate_w != nullptr) {
+      float dot = 0.0f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) dot += sg_part[w];
+      const float sgv = ref_sigmoid(dot);
+      a.sgate[tok] = sgv;
+      if (a.sgate_out) a.sgate_out[tok] = sgv;
+    } else {
+      if (a.sgate) a.sgate[tok] = 0.0f;
+      if (a.sgate_out) a.sgate_out[tok] = 0.0f;
+    }
+  }
+  __syncthreads();
+  OSM_STAMP(4);
+  float mx = 0.0f;
+  if (route) {
+    mx = sel_v[0];
+    float es = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+      if (tid + r * kSelThreads < g.E) es += __expf(__fsub_rn(lv[r], mx));
+    es = warp_sum(es);
+    if (lane == 0) red[warp] = es;
+  }
+  __syncthreads();
+  OSM_STAMP(5);
+  if (warp == 0 && route) {
+    const int nw = blockDim.x >> 5;
+    const float ssum = warp_sum(lane < nw ? red[lane] : 0.0f);
+    const float bm = warp_max(lane < nw ? s_red2[lane] : 0.0f);
+    bool ok_j = true;
+    if (lane + 1 < nsel) {
       const float need = 2.0f * bm * 1.0001f + 1e-6f +
-                         3e-7f * (fabsf(sel_v[j] - mx0) + fabsf(sel_v[j + 1] - mx0));
-      if (!(__fsub_rd(sel_v[j], sel_v[j + 1]) > need)) ok = false;
+                         3e-7f * (fabsf(sel_v[lane] - mx) + fabsf(sel_v[lane + 1] - mx));
+      ok_j = __fsub_rd(sel_v[lane], sel_v[lane + 1]) > need;
     }
+    const bool ok = __all_sync(0xFFFFFFFFu, ok_j) && !a.force_exact && isfinite(mx);
     if (ok) {
-      write_weights(a, tok, v, sel_id, sel_v);
+      write_weights(a, tok, ssum, mx, sel_id, sel_v);
     } else if (lane == 0) {
       s_flag = a.force_exact ? 2 : 1;
       s_bm = bm;
+      s_sum = ssum;
+      s_mx = mx;
     }
     OSM_STAMP(6);
   }
@@ -630,7 +778,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
         const int npair = k < nc ? k : nc - 1;  // pairs (r, r+1) that decide ids/order
         for (int r = 0; r < npair; ++r)
           if (!distinct_p(sel_v[r], sel_v[r + 1], sel_v[0])) ok = false;
-        if (ok) write_weights(a, tok, v, sel_id, sel_v);
+        if (ok) write_weights(a, tok, s_sum, s_mx, sel_id, sel_v);
         else if (lane == 0) s_flag = 2;
       }
     }
@@ -714,6 +862,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
         for (int j = 0; j < k; ++j) {
           a.ids[(size_t)tok * k + j] = (uint32_t)sel_id[j];
           a.weights[(size_t)tok * k + j] = a.norm ? __fdiv_rn(sel_v[j], mass) : sel_v[j];
+          if (a.pick_ptr) a.pick_ptr[(size_t)tok * k + j] = slot_base(a, (uint32_t)sel_id[j]);
         }
         a.mass[tok] = mass;
       }
@@ -725,32 +874,24 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
     for (int j = 0; j < k; ++j) {
       a.ids[(size_t)tok * k + j] = 0;
       a.weights[(size_t)tok * k + j] = 0.0f;
+      if (a.pick_ptr) a.pick_ptr[(size_t)tok * k + j] = nullptr;
     }
     a.mass[tok] = 0.0f;
   }
   __syncthreads();
-  if (tid < k && !a.skip_route) {
+  if ((s_flag == 2 || nonfinite) && tid < k && !a.skip_route) {
     if (a.ids_out) a.ids_out[(size_t)tok * k + tid] = a.ids[(size_t)tok * k + tid];
     if (a.weights_out) a.weights_out[(size_t)tok * k + tid] = a.weights[(size_t)tok * k + tid];
   }
-  if (tid == 0 && a.mass_out && !a.skip_route) a.mass_out[tok] = a.mass[tok];
-  // ---- shared expert scalar gate (partials of warps 1.. summed here) ----
-  if (tid == 0) {
-    if (a.sgate_w != nullptr) {
-      float dot = 0.0f;
-      for (int w = 1; w < (int)(blockDim.x >> 5); ++w) dot += sg_part[w];
-      const float sgv = ref_sigmoid(dot);
-      a.sgate[tok] = sgv;
-      if (a.sgate_out) a.sgate_out[tok] = sgv;
-    } else {
-      if (a.sgate) a.sgate[tok] = 0.0f;
-      if (a.sgate_out) a.sgate_out[tok] = 0.0f;
-    }
-  }
+  if ((s_flag == 2 || nonfinite) && tid == 0 && a.mass_out && !a.skip_route) a.mass_out[tok] = a.mass[tok];
+  // given routing (osm_moe_experts): slot bases of the caller's picks
+  if (a.skip_route && a.pick_ptr && tid < k)
+    a.pick_ptr[(size_t)tok * k + tid] = slot_base(a, a.ids[(size_t)tok * k + tid]);
   OSM_STAMP(9);
-#ifdef OSM_PHASE_TIMING
+  if (!a.do_group) TL_END(1);
+#ifdef OSM_PHASE_PRINT
   if (!a.do_group && tid == 0) {
-    printf("select(nogroup) tok %d:", tok);
+    printf("select(nogroup) tok %d: g %llu..%llu", tok, gt0_, gtime());
     for (int i = 1; i < 10; ++i) printf(" %d:%lld", i, ts_[i] - ts_[0]);
     printf("\n");
   }
@@ -773,7 +914,8 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   if (tid == 0) *a.ticket = 0u;
   __syncthreads();
   OSM_STAMP(13);
-#ifdef OSM_PHASE_TIMING
+  TL_END(1);
+#ifdef OSM_PHASE_PRINT
   if (tid == 0) {
     printf("select tok %d:", tok);
     for (int i = 1; i < 14; ++i) printf(" %d:%lld", i, ts_[i] - ts_[0]);
@@ -852,3 +994,12 @@ void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
 }
 
 }  // namespace osm
+
+#ifdef OSM_PHASE_TIMING
+extern "C" int osm_dbg_timeline_router(unsigned long long* out) {
+  unsigned long long init[OSM_TL_SLOTS];
+  for (int i = 0; i < OSM_TL_SLOTS; ++i) init[i] = (i == 0 || i == 4) ? ~0ull : 0ull;
+  cudaMemcpyFromSymbol(out, osm::g_tl, sizeof(init));
+  return (int)cudaMemcpyToSymbol(osm::g_tl, init, sizeof(init));
+}
+#endif

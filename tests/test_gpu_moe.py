@@ -190,7 +190,7 @@ def test_moe_hash_fixture(torch, golden_dir):
     assert normwise_rel(out[0], z["out"]) <= 1e-4
 
 
-@pytest.mark.parametrize("B", [1, 8, 33])
+@pytest.mark.parametrize("B", [1, 2, 8, 33])
 def test_moe_q3n_decode(torch, B):
     """Qwen3-Next shape (H 2048, E 512, k 10, I 512, shared 512), Zipf bias."""
     H, E, I, K = 2048, 512, 512, 10
@@ -242,10 +242,11 @@ def _q3n_fixture(torch):
     return fx
 
 
-def test_moe_split_route_then_experts_matches_forward(torch):
+@pytest.mark.parametrize("B", [1, 2, 5])
+def test_moe_split_route_then_experts_matches_forward(torch, B):
     """osm_moe_route + osm_moe_experts (host cache between) == osm_moe_forward."""
     fx = _q3n_fixture(torch)
-    B, H, K = 5, fx.H, fx.K
+    H, K = fx.H, fx.K
     x = fx.port.gen_normal(9, 7, 1.0, B * H).reshape(B, H)
     out, ids, w, m, sg = fx.run(torch, x)
     xd = torch.from_numpy(x).cuda()
@@ -257,6 +258,21 @@ def test_moe_split_route_then_experts_matches_forward(torch):
     torch.cuda.synchronize()
     assert np.array_equal(ids2.cpu().numpy().astype(np.uint32), ids)
     assert np.array_equal(out2.cpu().numpy().view(np.uint32), out.view(np.uint32))
+
+
+@pytest.mark.parametrize("shared,B", [(True, 1), (True, 2), (False, 1), (False, 2)])
+def test_moe_decode_small_shapes(torch, shared, B):
+    """The 1-2 token kernels at a small shape (H 256, I 128), with and without
+    a shared expert, against the oracle."""
+    H, E, I, K = 256, 16, 128, 4
+    fx = MoeFixture(torch, H, E, I, K, seed=57, shared=shared)
+    x = fx.port.gen_normal(57, 3 + B, 1.0, B * H).reshape(B, H)
+    out, ids, w, m, sg = fx.run(torch, x)
+    assert fx.ctx.status()[0] == 0
+    for b in range(B):
+        ref, rids, rw, rm, rs = fx.oracle_token(x[b])
+        assert np.array_equal(ids[b], rids)
+        assert normwise_rel(out[b], ref) <= 1e-4, normwise_rel(out[b], ref)
 
 
 def test_moe_nonresident_expert_reported(torch):
