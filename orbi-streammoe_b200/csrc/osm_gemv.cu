@@ -38,8 +38,9 @@ namespace osm {
 namespace {
 #ifdef OSM_PHASE_TIMING
 __device__ unsigned long long g_tl[OSM_TL_SLOTS];
-__device__ long long g_cyc[32];
-#define CYC(i) do { if (blockIdx.x == 0 && threadIdx.x == 0) g_cyc[(i)] = clock64(); } while (0)
+__device__ long long g_cyc[64];
+#define CYC(i) do { if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 70)) \
+  g_cyc[(i) + (blockIdx.x == 70 ? 32 : 0)] = clock64(); } while (0)
 #else
 #define CYC(i) do { } while (0)
 #endif
@@ -325,8 +326,10 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
   const int bs = Ly.bs, sst = Ly.ss;
   TL_START(0);
   CYC(0);
-  if (tid < a.nbuf) mbar_init(&bars[tid], 1);
-  mbar_init_fence();
+  if (tid < a.nbuf) {
+    mbar_init(&bars[tid], 1);
+    mbar_init_fence();
+  }
   // Copies of the pairs of one pass (the shared expert before the routing
   // exists, the routed experts after): weights by bulk copies of 4-row blocks
   // (single rows where a block is not one run of one expert) counted on the
@@ -360,6 +363,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
         }
       }
     }
+    CYC(shared_pass ? 11 : 9);
     const int scb = a.cs_gu, spr = (G * 2) / scb;
     for (int q = tid; q < np * 4 * spr; q += blockDim.x) {
       const int p = q / (4 * spr), rem = q - p * 4 * spr, arr = rem / spr, c = rem - arr * spr;
@@ -371,6 +375,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
       cp_async(scales + (size_t)((tl * 4 + arr) * kTileRows + R) * sst + c * scb,
                m.ptr + off + (size_t)m.row * G * 2 + c * scb, scb);
     }
+    CYC(shared_pass ? 12 : 10);
     cp_commit();
   };
   // ---- the shared expert's rows do not depend on the routing ----
@@ -575,8 +580,10 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_down_kernel(GemvArgs a)
     meta[jj] = m;
   }
   CYC(17);
-  if (tid < ne) mbar_init(&bars[tid], 1);
-  mbar_init_fence();
+  if (tid < ne) {
+    mbar_init(&bars[tid], 1);
+    mbar_init_fence();
+  }
   __syncthreads();
   // rows: one bulk copy per block of <= 4 consecutive output rows
   for (int q = tid; q < ne * 4; q += blockDim.x) {
@@ -814,6 +821,6 @@ extern "C" int osm_dbg_timeline_gemv(unsigned long long* out) {
   return (int)cudaMemcpyToSymbol(osm::g_tl, init, sizeof(init));
 }
 extern "C" int osm_dbg_cycles_gemv(long long* out) {
-  return (int)cudaMemcpyFromSymbol(out, osm::g_cyc, 32 * sizeof(long long));
+  return (int)cudaMemcpyFromSymbol(out, osm::g_cyc, 64 * sizeof(long long));
 }
 #endif

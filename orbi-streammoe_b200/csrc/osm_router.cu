@@ -40,6 +40,7 @@ namespace osm {
 namespace {
 #ifdef OSM_PHASE_TIMING
 __device__ unsigned long long g_tl[OSM_TL_SLOTS];
+__device__ long long g_rcyc[16];
 #endif
 
 constexpr float kU = 5.9604644775390625e-8f;  // 2^-24
@@ -495,6 +496,22 @@ __device__ __forceinline__ unsigned long long warp_sort_desc(unsigned long long 
   return key;
 }
 
+// Top 32 of two descending lists held one key per lane: a, and b read in
+// reverse (b_rev[lane] = b[31 - lane]).  max(a, b_rev) holds the 32 largest
+// keys as a bitonic sequence; a half-cleaner cascade sorts it descending.
+__device__ __forceinline__ unsigned long long merge_top(unsigned long long a,
+                                                        unsigned long long b_rev) {
+  const int lane = threadIdx.x & 31;
+  unsigned long long c = a > b_rev ? a : b_rev;
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) {
+    const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, c, stride);
+    const bool lower = (lane & stride) == 0;
+    c = lower ? (o > c ? o : c) : (o < c ? o : c);
+  }
+  return c;
+}
+
 __device__ __forceinline__ unsigned long long sel_key(float v, int id) {
   return ((unsigned long long)ord_key(v) << 32) | (0xFFFFFFFFu - (uint32_t)id);
 }
@@ -525,7 +542,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   __shared__ float s_bm, s_bcast, s_sum, s_mx;
   __shared__ float sg_part[kSelThreads / 32];
   __shared__ float s_red2[kSelThreads / 32];
-  __shared__ unsigned long long s_heads[32 * (kMaxTopK + 1)];
+  __shared__ unsigned long long s_top[kSelThreads];
   const RouterGeom g = a.g;
   const int tok = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -589,19 +606,19 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   const int nsel = k + 1 <= g.E ? k + 1 : k;
   const int nl = (g.E + 31) >> 5;  // lists of 32 experts
   // ---- 1. fast path: certified top-k over the fast logits.  Each warp sorts
-  //      its lists of 32 and keeps nsel heads; every head is then ranked
-  //      against all heads. ----
+  //      its 32 (or 2 x 32) keys; a tree of bitonic merges through shared
+  //      memory leaves the top 32 of all experts in warp 0. ----
+  unsigned long long top = 0ull;
   if (route) {
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int L = warp + r * (kSelThreads / 32);
-      if (L < nl) {
-        const int e = L * 32 + lane;
-        const unsigned long long key = warp_sort_desc(e < g.E ? sel_key(lv[r], e) : 0ull);
-        if (lane < nsel) s_heads[L * nsel + lane] = key;
-      }
+    const int e0 = warp * 32 + lane;
+    top = warp_sort_desc(e0 < g.E ? sel_key(lv[0], e0) : 0ull);
+    if (nl > kSelThreads / 32) {  // E > 512: fold in the second list
+      const int e1 = e0 + kSelThreads;
+      const unsigned long long k1 = warp_sort_desc(e1 < g.E ? sel_key(lv[1], e1) : 0ull);
+      top = merge_top(top, __shfl_sync(0xFFFFFFFFu, k1, 31 - lane));
     }
-    bmax = warp_max(bmax);
+    s_top[warp * 32 + lane] = top;
+  bmax = warp_max(bmax);
     if (lane == 0) s_red2[warp] = bmax;
   }
   // activation fragments of the tensor-core path
@@ -638,26 +655,16 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   }
   __syncthreads();
   OSM_STAMP(3);
-  if (route) {
-    // warp w ranks heads w, w + nw, ...: lanes count the heads above it
-    const int nc = nl * nsel;
-    const int nw = blockDim.x >> 5;
-    unsigned long long hk[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) hk[j] = lane + 32 * j < nc ? s_heads[lane + 32 * j] : 0ull;
-#pragma unroll 2
-    for (int c = warp; c < nc; c += nw) {
-      const unsigned long long mine = s_heads[c];
-      unsigned int cnt = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cnt += hk[j] > mine ? 1u : 0u;
-      for (int i = lane + 256; i < nc; i += 32) cnt += s_heads[i] > mine ? 1u : 0u;
-      const unsigned int rank = __reduce_add_sync(0xFFFFFFFFu, cnt);
-      if (lane == 0 && rank < (unsigned int)nsel) {
-        sel_id[rank] = key_id(mine);
-        sel_v[rank] = key_value(mine);
-      }
+  for (int step = 1; step < kSelThreads / 32; step <<= 1) {
+    if (route && (warp & (2 * step - 1)) == 0) {
+      top = merge_top(top, s_top[(warp + step) * 32 + 31 - lane]);
+      s_top[warp * 32 + lane] = top;
     }
+    __syncthreads();
+  }
+  if (route && warp == 0 && lane < nsel && nsel <= 32) {
+    sel_id[lane] = key_id(top);
+    sel_v[lane] = key_value(top);
   }
   // ---- shared expert scalar gate ----
   if (tid == blockDim.x - 32) {
@@ -696,7 +703,7 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
                          3e-7f * (fabsf(sel_v[lane] - mx) + fabsf(sel_v[lane + 1] - mx));
       ok_j = __fsub_rd(sel_v[lane], sel_v[lane + 1]) > need;
     }
-    const bool ok = __all_sync(0xFFFFFFFFu, ok_j) && !a.force_exact && isfinite(mx);
+    const bool ok = __all_sync(0xFFFFFFFFu, ok_j) && !a.force_exact && isfinite(mx) && nsel <= 32;
     if (ok) {
       write_weights(a, tok, ssum, mx, sel_id, sel_v);
     } else if (lane == 0) {
@@ -889,6 +896,10 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
     a.pick_ptr[(size_t)tok * k + tid] = slot_base(a, a.ids[(size_t)tok * k + tid]);
   OSM_STAMP(9);
   if (!a.do_group) TL_END(1);
+#ifdef OSM_PHASE_TIMING
+  if (blockIdx.x == 0 && tid == 0)
+    for (int i = 0; i < 10; ++i) g_rcyc[i] = ts_[i] - ts_[0];
+#endif
 #ifdef OSM_PHASE_PRINT
   if (!a.do_group && tid == 0) {
     printf("select(nogroup) tok %d: g %llu..%llu", tok, gt0_, gtime());
@@ -996,6 +1007,9 @@ void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
 }  // namespace osm
 
 #ifdef OSM_PHASE_TIMING
+extern "C" int osm_dbg_cycles_router(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, osm::g_rcyc, 16 * sizeof(long long));
+}
 extern "C" int osm_dbg_timeline_router(unsigned long long* out) {
   unsigned long long init[OSM_TL_SLOTS];
   for (int i = 0; i < OSM_TL_SLOTS; ++i) init[i] = (i == 0 || i == 4) ? ~0ull : 0ull;
