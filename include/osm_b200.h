@@ -139,6 +139,27 @@ int osm_expert_forward(osm_context* ctx, const void* slot_dev,
                        const osm_expert_layout* layout, const float* x_dev,
                        uint32_t tokens, float* out_dev);
 
+/* Allocation-free variant of osm_expert_forward.  It has no counterpart in
+ * the reference: it is for hosts that cannot call cudaMalloc where experts
+ * run (a server whose device memory belongs to a pool allocator that forbids
+ * driver allocations after warm-up, or a plugin that only borrows a CUDA
+ * context it did not create).  No context is needed and nothing is
+ * allocated: the intermediates live in one fixed device array of this
+ * library (254 KB, held on every GPU that loads it until the process
+ * exits), on the device current at the call, launched on `cuda_stream`
+ * (NULL: the legacy default stream).  Limits: tokens 1..16, hidden <= 2048,
+ * inter <= 768; anything larger, or an unsupported layout, returns
+ * OSM_EINVAL before any GPU work.  The first call on a device sets it up
+ * (looks up the array's device address and sets kernel attributes); make
+ * that first call before any stream capture.  Each call clears the array
+ * before use.  All calls on a device share the one array: calls that can
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller.  Returns OSM_OK, OSM_EINVAL or OSM_ECUDA. */
+int osm_expert_forward_noalloc(const void* slot_dev,
+                               const osm_expert_layout* layout,
+                               const float* x_dev, uint32_t tokens,
+                               float* out_dev, void* cuda_stream);
+
 /* ---- expert slab: the HBM side of VulkanResidentExpertCache
  *      (include/orbi/streammoe/backend/vulkan_resident_expert_cache.hpp:
  *      27-83); the policy lives in the host layer ---- */

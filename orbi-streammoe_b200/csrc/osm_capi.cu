@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <thread>
@@ -1259,3 +1260,155 @@ int osm_gen_expert_slots(osm_slab* s, uint64_t seed, uint64_t tensor_base, float
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Allocation-free single-expert forward.
+//
+// Some hosts cannot call cudaMalloc on the path that runs an expert: an
+// inference server whose memory is owned by a pool allocator that forbids
+// driver allocations after warm-up, a process that only borrows a device
+// context it did not create, or code that runs where an allocation would
+// synchronise the device.  osm_expert_forward_noalloc serves them: it takes
+// no context and keeps its intermediates (activation and SwiGLU fragments,
+// the one-expert work list) in a file-scope device array of fixed size that
+// every GPU loading this library holds until the process exits.
+// ----------------------------------------------------------------------------
+namespace {
+
+constexpr uint32_t kNaMaxTokens = 16;
+constexpr uint32_t kNaMaxHidden = 2048;
+constexpr uint32_t kNaMaxInter = 768;
+constexpr size_t na_up(size_t v) { return (v + 255) / 256 * 256; }
+// pairs of the one-expert work list: one per token (two per token reserved,
+// as the context scratch sizes it)
+constexpr size_t kNaPairs = 2 * kNaMaxTokens;
+constexpr size_t kNaMaxTg = kNaPairs / osm::kTokGroup + 3;
+constexpr size_t kNaXfrag = 0;
+constexpr size_t kNaXsum = kNaXfrag + na_up(kNaMaxTokens * (kNaMaxHidden / 8) * 32);
+constexpr size_t kNaNact = kNaXsum + na_up(kNaMaxTokens * (kNaMaxHidden / 8) * 4);
+constexpr size_t kNaAct = kNaNact + na_up(4);
+constexpr size_t kNaNtg = kNaAct + na_up(2 * sizeof(osm::ActEntry));
+constexpr size_t kNaTge = kNaNtg + na_up(4);
+constexpr size_t kNaTgb = kNaTge + na_up(kNaMaxTg * 4);
+constexpr size_t kNaPtok = kNaTgb + na_up(kNaMaxTg * 4);
+constexpr size_t kNaPpick = kNaPtok + na_up(kNaPairs * 4);
+constexpr size_t kNaOrow = kNaPpick + na_up(kNaPairs * 4);
+constexpr size_t kNaHfrag = kNaOrow + na_up(kNaPairs * 4);
+constexpr size_t kNaHsum = kNaHfrag + na_up(kNaPairs * (kNaMaxInter / 8) * 32);
+constexpr size_t kNaBytes = kNaHsum + na_up(kNaPairs * (kNaMaxInter / 8) * 4);
+
+// The scratch of every call on this GPU.  Host code must not pass this name
+// to a kernel: on the host it is a stand-in, not the device address.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNaBytes];
+
+struct NaDevice {
+  bool ready = false;
+  uint8_t* base = nullptr;  // device address of g_noalloc_scratch
+  int grid_cap = 0;
+};
+constexpr int kNaMaxDevices = 64;
+std::mutex g_na_mu;
+NaDevice g_na[kNaMaxDevices];
+
+// Set-up of the current device, once: the scratch's device address and the
+// kernel attributes the context creation would otherwise set.
+int na_device(int dev, NaDevice** out) {
+  if (dev < 0 || dev >= kNaMaxDevices) return OSM_EINVAL;
+  std::lock_guard<std::mutex> lock(g_na_mu);
+  NaDevice& d = g_na[dev];
+  if (!d.ready) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return OSM_ECUDA;
+    }
+    int sms = 0, optin = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
+      cudaGetLastError();
+      return OSM_ECUDA;
+    }
+    osm::init_expert_attributes(optin > 64 * 1024 ? optin - 16 * 1024 : 48 * 1024);
+    if (cudaGetLastError() != cudaSuccess) return OSM_ECUDA;
+    d.base = static_cast<uint8_t*>(p);
+    d.grid_cap = (sms > 0 ? sms : 148) * 4;
+    d.ready = true;
+  }
+  *out = &d;
+  return OSM_OK;
+}
+
+}  // namespace
+
+extern "C" int osm_expert_forward_noalloc(const void* slot_dev, const osm_expert_layout* layout,
+                                          const float* x_dev, uint32_t tokens, float* out_dev,
+                                          void* cuda_stream) {
+  if (!slot_dev || !x_dev || !out_dev || !layout_ok(layout)) return OSM_EINVAL;
+  if (tokens == 0 || tokens > kNaMaxTokens || layout->hidden > kNaMaxHidden ||
+      layout->inter > kNaMaxInter)
+    return OSM_EINVAL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return OSM_ECUDA;
+  }
+  NaDevice* d = nullptr;
+  int rc = na_device(dev, &d);
+  if (rc) return rc;
+  const cudaStream_t st = static_cast<cudaStream_t>(cuda_stream);
+  const osm_expert_layout& L = *layout;
+  uint8_t* b = d->base;
+  auto at = [&](size_t off) { return b + off; };
+  // every intermediate of the call starts cleared: the previous call's
+  // contents stay in the array
+  if (cudaMemsetAsync(b, 0, kNaBytes, st) != cudaSuccess) {
+    cudaGetLastError();
+    return OSM_ECUDA;
+  }
+  uint4* xfrag = reinterpret_cast<uint4*>(at(kNaXfrag));
+  float* xfsum = reinterpret_cast<float*>(at(kNaXsum));
+  int* n_active = reinterpret_cast<int*>(at(kNaNact));
+  osm::ActEntry* act = reinterpret_cast<osm::ActEntry*>(at(kNaAct));
+  int* n_tg = reinterpret_cast<int*>(at(kNaNtg));
+  int* tg_expert = reinterpret_cast<int*>(at(kNaTge));
+  int* tg_begin = reinterpret_cast<int*>(at(kNaTgb));
+  int* pair_tok = reinterpret_cast<int*>(at(kNaPtok));
+  int* pair_pick = reinterpret_cast<int*>(at(kNaPpick));
+  int* out_row = reinterpret_cast<int*>(at(kNaOrow));
+  uint4* hfrag = reinterpret_cast<uint4*>(at(kNaHfrag));
+  float* hfsum = reinterpret_cast<float*>(at(kNaHsum));
+  osm::launch_frag_prep(x_dev, (int)tokens, (int)L.hidden, xfrag, xfsum, st, nullptr);
+  osm::launch_setup_single((int)tokens, static_cast<const uint8_t*>(slot_dev), n_active, act, n_tg,
+                           tg_expert, tg_begin, pair_tok, pair_pick, out_row, st, nullptr);
+  osm::ProjArgs gu{};
+  fill_sections(gu.sec, L, L, true);
+  gu.n_tg = n_tg;
+  gu.act = act;
+  gu.tg_expert = tg_expert;
+  gu.tg_begin = tg_begin;
+  gu.pair_tok = pair_tok;
+  gu.frag_stride = (int)L.hidden / 8;
+  gu.frag = xfrag;
+  gu.fsum8 = xfsum;
+  gu.hfrag = hfrag;
+  gu.hfsum8 = hfsum;
+  gu.hK = (int)L.inter;
+  const int ntg = (int)((tokens + osm::kTokGroup - 1) / osm::kTokGroup);
+  const int tch = (int)std::min<uint32_t>(tokens, 8);
+  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, ntg, d->grid_cap, tch, st, nullptr);
+  osm::ProjArgs dn = gu;
+  fill_sections(dn.sec, L, L, false);
+  dn.frag_by_pair = 1;
+  dn.frag_stride = (int)L.inter / 8;
+  dn.frag = hfrag;
+  dn.fsum8 = hfsum;
+  dn.out = out_dev;
+  dn.out_row = out_row;
+  dn.pair_pick = pair_pick;
+  dn.kp1 = 1;
+  dn.ostride = (int)L.hidden;
+  osm::launch_proj(dn, L.inter <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12,
+                   (int)L.hidden, ntg, d->grid_cap, tch, st, nullptr);
+  if (cudaGetLastError() != cudaSuccess) return OSM_ECUDA;
+  return OSM_OK;
+}

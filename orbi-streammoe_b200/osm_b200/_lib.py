@@ -79,6 +79,7 @@ _SIGS = {
     "osm_weighted_accumulate": (C.c_int, [_P, _P, C.c_float, _P, C.c_size_t]),
     "osm_rms_norm": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_float, C.c_uint32]),
     "osm_expert_forward": (C.c_int, [_P, _P, C.POINTER(ExpertLayout), _P, C.c_uint32, _P]),
+    "osm_expert_forward_noalloc": (C.c_int, [_P, C.POINTER(ExpertLayout), _P, C.c_uint32, _P, _P]),
     "osm_slab_create": (C.c_int, [_P, C.POINTER(ExpertLayout), C.c_uint32, C.POINTER(_P)]),
     "osm_slab_destroy": (C.c_int, [_P]),
     "osm_slab_slots": (C.c_uint32, [_P]),
