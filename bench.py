@@ -431,6 +431,28 @@ def run_reference(args, rank, world):
     }
 
 
+def run_single(B: int, reps: int):
+    """A few calls of one batch size on the bench sublayer: the small case
+    for ncu captures of one kernel."""
+    import torch
+
+    import osm_b200 as osm
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx = osm.Context(0, max_tokens=max(SWEEP + (B,)))
+    ctx.set_stream(stream.cuda_stream)
+    layer = build_sublayer(torch, ctx, osm)[0]
+    x = torch.empty(B, H, device="cuda")
+    ctx.gen_normal(SEED, 5000 + B, 1.0, x)
+    out = torch.empty(B, H, device="cuda")
+    for _ in range(reps):
+        layer.run_qwen_sparse_moe(x, B, out)
+    torch.cuda.synchronize()
+    print(json.dumps({"single": B, "reps": reps, "status": list(ctx.status())}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -438,7 +460,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--single", type=int, default=0,
+                    help="profiling driver: run REPS calls of this many tokens and exit")
+    ap.add_argument("--reps", type=int, default=3)
     args = ap.parse_args()
+    if args.single:
+        run_single(args.single, args.reps)
+        return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
