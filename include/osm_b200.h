@@ -177,6 +177,43 @@ int osm_slab_fill_wait(osm_slab* slab, uint32_t timeout_ms);
 /* Bytes copied host->device by fills since creation. */
 uint64_t osm_slab_h2d_bytes(const osm_slab* slab);
 
+/* ---- HBM expert cache: the residency policy of VulkanResidentExpertCache
+ *      (include/orbi/streammoe/backend/vulkan_resident_expert_cache.hpp:
+ *      27-83, src/backend/vulkan_resident_expert_cache.cpp:40-200) over slab
+ *      slots.  Each get() counts a use of (layer, expert); a miss evicts the
+ *      resident entry with the smallest (use count, last use, key) -- use
+ *      counts survive evictions -- until the newcomer's accounted bytes fit
+ *      the budget and a slot is free, then copies the expert from the host
+ *      source into the freed slot and rebinds the layers registered with
+ *      osm_cache_bind_layer.  slab NULL: the policy alone (no copies). ---- */
+typedef struct osm_cache osm_cache;
+typedef struct osm_cache_counts {
+  uint64_t hits, misses, loads, evictions;
+  uint64_t resident_entries, resident_bytes, budget_bytes;
+} osm_cache_counts;
+/* Host level of the cache (ExpertCache::fetch, src/cache/expert_cache.cpp):
+ * sets *src to the expert's slot bytes in (ideally pinned) host memory, which
+ * must stay valid until the copy has landed; returns 0 on success. */
+typedef int (*osm_cache_source_fn)(void* user, uint32_t layer, uint32_t expert,
+                                   const void** src);
+/* accounted_bytes 0: the slab's slot stride. */
+int osm_cache_create(osm_slab* slab, uint64_t budget_bytes,
+                     uint64_t accounted_bytes, osm_cache_source_fn source,
+                     void* user, osm_cache** out);
+int osm_cache_destroy(osm_cache* cache);
+const char* osm_cache_last_error(const osm_cache* cache);
+int osm_cache_bind_layer(osm_cache* cache, uint32_t layer_id, osm_layer* layer);
+/* VulkanResidentExpertCache::get for one expert; *slot_out may be NULL. */
+int osm_cache_get(osm_cache* cache, uint32_t layer_id, uint32_t expert,
+                  int32_t* slot_out);
+/* get() for each of n experts in order (the picks of a call); entries used by
+ * this acquire are not evicted by it (OSM_ENOMEM when they cannot all fit). */
+int osm_cache_acquire(osm_cache* cache, uint32_t layer_id,
+                      const uint32_t* experts, uint32_t n);
+int osm_cache_contains(const osm_cache* cache, uint32_t layer_id,
+                       uint32_t expert);
+int osm_cache_stats(const osm_cache* cache, osm_cache_counts* out);
+
 /* ---- one MoE layer: the dense state QwenCheckpointSparseMoeLayer keeps
  *      (src/model/checkpoint_sparse_moe.cpp:112-220): router, shared expert
  *      and its scalar gate, plus the table expert -> slab slot ---- */

@@ -12,6 +12,7 @@
 #include <new>
 #include <string>
 #include <thread>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/osm_b200.h"
@@ -46,6 +47,8 @@ struct Scratch {
   int* n_tg = nullptr;
   int* tg_expert = nullptr;
   int* tg_begin = nullptr;
+  int* n_ch = nullptr;
+  int2* chunks = nullptr;
   int* pair_tok = nullptr;
   int* pair_pick = nullptr;
   int* tp_pos = nullptr;
@@ -226,6 +229,8 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t o_act = take((E + 1) * sizeof(osm::ActEntry)), o_ntg = take(4);
   const size_t max_tg = P / osm::kTokGroup + E + 2;
   const size_t o_tge = take(max_tg * 4), o_tgb = take(max_tg * 4);
+  const size_t max_ch = P / 8 + E + 2;
+  const size_t o_nch = take(4), o_ch = take(max_ch * 8);
   const size_t o_ptok = take(P * 4), o_ppick = take(P * 4), o_cursor = take((E + 1) * 4);
   const size_t o_tpp = take(P * 4);
   const size_t o_orow = take(P * 4);
@@ -265,6 +270,8 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.n_tg = reinterpret_cast<int*>(b + o_ntg);
   s.tg_expert = reinterpret_cast<int*>(b + o_tge);
   s.tg_begin = reinterpret_cast<int*>(b + o_tgb);
+  s.n_ch = reinterpret_cast<int*>(b + o_nch);
+  s.chunks = reinterpret_cast<int2*>(b + o_ch);
   s.pair_tok = reinterpret_cast<int*>(b + o_ptok);
   s.pair_pick = reinterpret_cast<int*>(b + o_ppick);
   s.tp_pos = reinterpret_cast<int*>(b + o_tpp);
@@ -349,6 +356,8 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.pair_tok = s.pair_tok;
   a.pair_pick = s.pair_pick;
   a.tp_pos = s.tp_pos;
+  a.n_ch = s.n_ch;
+  a.chunks = s.chunks;
   a.cursor = s.cursor;
   a.status = s.status;
   a.exact_count = s.exact_count;
@@ -388,6 +397,24 @@ bool gemv_path(osm_layer* L, uint32_t T, osm::GemvArgs* g, osm::GemvLaunch* gl) 
   return osm::gemv_configure(*g, max_active, ctx->num_sms, ctx->max_smem, gl);
 }
 
+// The grouped kernels (osm_gemv.cu) serve calls of 3+ tokens whose layouts
+// suit them; fills the call-independent fields of a.
+bool grouped_path(osm_layer* L, osm::GrpArgs* a, size_t* smem_gu, size_t* smem_dn) {
+  if (!L->slab) return false;
+  osm_context* ctx = L->ctx;
+  const osm_expert_layout& R = L->slab->layout;
+  const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
+  *a = osm::GrpArgs{};
+  fill_sections(a->gu, R, S, true);
+  fill_sections(a->dn, R, S, false);
+  a->H = L->g.H;
+  a->Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
+  a->kp1 = (int)L->g.k + 1;
+  a->has_shared = L->shared_slot ? 1 : 0;
+  a->slab_stride = R.stride;
+  return osm::grouped_configure(*a, ctx->max_smem, smem_gu, smem_dn);
+}
+
 int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
@@ -425,6 +452,48 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
       osm::launch_gemv_down(g, gl, ctx->stream, &ctx->launches);
     }
     return check_launch(ctx, "down gemv + combine");
+  }
+  {
+    // 3+ tokens: grouped projections over 8-token chunks of each expert
+    osm::GrpArgs ga;
+    size_t smem_gu = 0, smem_dn = 0;
+    if (grouped_path(L, &ga, &smem_gu, &smem_dn)) {
+      ga.x = ctx->cur_x;
+      ga.n_ch = s.n_ch;
+      ga.chunks = s.chunks;
+      ga.act = s.act;
+      ga.pair_tok = s.pair_tok;
+      ga.pair_pick = s.pair_pick;
+      ga.h = reinterpret_cast<float*>(s.hfrag);
+      ga.partial = s.partial;
+      ga.status = s.status;
+      {
+        Prof p(ctx, kKGateUp);
+        osm::launch_grouped_gateup(ga, ctx->num_sms, smem_gu, ctx->stream, &ctx->launches);
+      }
+      int rc = check_launch(ctx, "grouped gate/up");
+      if (rc) return rc;
+      {
+        Prof p(ctx, kKDown);
+        osm::launch_grouped_down(ga, ctx->num_sms, smem_dn, ctx->stream, &ctx->launches);
+      }
+      rc = check_launch(ctx, "grouped down");
+      if (rc) return rc;
+      osm::CombineArgs c{};
+      c.partial = s.partial;
+      c.weights = s.weights;
+      c.sgate = L->shared_slot ? s.sgate : nullptr;
+      c.residual = residual;
+      c.out = out;
+      c.B = (int)T;
+      c.H = L->g.H;
+      c.k = L->g.k;
+      {
+        Prof p(ctx, kKCombine);
+        osm::launch_combine(c, ctx->stream, &ctx->launches);
+      }
+      return check_launch(ctx, "combine");
+    }
   }
   const int max_tg = (int)((size_t)T * (L->g.k + 1) / osm::kTokGroup) + max_active + 1;
   const int tchunk = (int)std::min<uint32_t>(T, 8);
@@ -558,6 +627,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   osm::init_router_attributes(max_smem);
   osm::init_expert_attributes(max_smem);
   osm::init_gemv_attributes(ctx->max_smem);
+  osm::init_grouped_attributes(ctx->max_smem);
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {
     cudaStreamDestroy(ctx->own_stream);
@@ -1053,6 +1123,7 @@ int osm_moe_route(osm_layer* L, const float* x, uint32_t T, uint32_t* ids, float
   a.do_group = 0;
   a.xfrag = nullptr;
   a.sgate_w = nullptr;
+  a.pick_ptr = nullptr;  // routing only: residency is the caller's next step
   launch_router_pair(ctx, a);
   return check_launch(ctx, "router");
 }
@@ -1077,7 +1148,9 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   osm::GemvLaunch gl;
   const bool dec = gemv_path(L, T, &g, &gl);
   a.do_group = (T == 1 && dec) ? 0 : 1;
-  if (dec) a.xfrag = nullptr;
+  osm::GrpArgs ga;
+  size_t sgu = 0, sdn = 0;
+  if (dec || grouped_path(L, &ga, &sgu, &sdn)) a.xfrag = nullptr;  // only the older kernels read it
   ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");
@@ -1257,6 +1330,199 @@ int osm_gen_expert_slots(osm_slab* s, uint64_t seed, uint64_t tensor_base, float
                           reinterpret_cast<uint16_t*>(b + L.down_b), ctx->stream, &ctx->launches);
   }
   return check_launch(ctx, "gen expert slots");
+}
+
+}  // extern "C"
+
+
+// ----------------------------------------------------------------------------
+// HBM expert cache: the residency policy of VulkanResidentExpertCache
+// (src/backend/vulkan_resident_expert_cache.cpp:40-200) over slab slots.
+// ----------------------------------------------------------------------------
+struct osm_cache {
+  osm_slab* slab = nullptr;             // null: policy only (no copies)
+  uint64_t budget = 0, accounted = 0;
+  osm_cache_source_fn source = nullptr;
+  void* user = nullptr;
+  struct Node {
+    int32_t slot = -1;
+    uint64_t frequency = 0, last_use = 0, epoch = 0;
+  };
+  std::unordered_map<uint64_t, Node> entries;
+  std::unordered_map<uint64_t, uint64_t> frequency_history;  // survives evictions
+  std::unordered_map<uint32_t, osm_layer*> layers;
+  std::vector<int32_t> free_slots;
+  uint64_t tick = 0, epoch = 0, resident_bytes = 0;
+  uint64_t hits = 0, misses = 0, loads = 0, evictions = 0;
+  std::string err;
+};
+
+namespace {
+
+uint64_t cache_key(uint32_t layer, uint32_t expert) { return ((uint64_t)layer << 32) | expert; }
+
+int cache_fail(osm_cache* c, int code, const char* msg) {
+  c->err = msg;
+  return code;
+}
+
+// One get() of the reference: a hit refreshes frequency and recency; a miss
+// evicts the entry with the smallest (frequency, last use, key) until the
+// newcomer fits, then copies the expert into a free slot.  Entries touched
+// in the current acquire (epoch) are not evicted.
+int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) {
+  ++c->tick;
+  const uint64_t key = cache_key(layer, expert);
+  const uint64_t freq = ++c->frequency_history[key];
+  auto it = c->entries.find(key);
+  if (it != c->entries.end()) {
+    ++c->hits;
+    it->second.frequency = freq;
+    it->second.last_use = c->tick;
+    it->second.epoch = c->epoch;
+    if (slot_out) *slot_out = it->second.slot;
+    return OSM_OK;
+  }
+  ++c->misses;
+  if (c->accounted > c->budget) return cache_fail(c, OSM_EINVAL, "cache: one expert exceeds the budget");
+  while (!c->entries.empty() &&
+         (c->resident_bytes + c->accounted > c->budget || (c->slab && c->free_slots.empty()))) {
+    auto victim = c->entries.end();
+    for (auto e = c->entries.begin(); e != c->entries.end(); ++e) {
+      if (e->second.epoch == c->epoch) continue;
+      if (victim == c->entries.end() ||
+          std::make_tuple(e->second.frequency, e->second.last_use, e->first) <
+              std::make_tuple(victim->second.frequency, victim->second.last_use, victim->first))
+        victim = e;
+    }
+    if (victim == c->entries.end())
+      return cache_fail(c, OSM_ENOMEM, "cache: the experts of one call do not fit in the budget");
+    const uint32_t vl = (uint32_t)(victim->first >> 32), ve = (uint32_t)(victim->first & 0xFFFFFFFFu);
+    auto lit = c->layers.find(vl);
+    if (lit != c->layers.end()) {
+      const int rc = osm_layer_set_slot(lit->second, ve, -1);
+      if (rc) return cache_fail(c, rc, "cache: unbinding an evicted expert failed");
+    }
+    if (victim->second.slot >= 0) c->free_slots.push_back(victim->second.slot);
+    c->resident_bytes -= c->accounted;
+    c->entries.erase(victim);
+    ++c->evictions;
+  }
+  int32_t slot = -1;
+  if (c->slab) {
+    if (c->free_slots.empty()) return cache_fail(c, OSM_ENOMEM, "cache: no free slot");
+    const void* src = nullptr;
+    if (!c->source || c->source(c->user, layer, expert, &src) != 0 || !src)
+      return cache_fail(c, OSM_ERUNTIME, "cache: the host source could not provide the expert");
+    slot = c->free_slots.back();
+    c->free_slots.pop_back();
+    const int rc = osm_slab_fill_async(c->slab, (uint32_t)slot, src);
+    if (rc) {
+      c->free_slots.push_back(slot);
+      return cache_fail(c, rc, "cache: slot fill failed");
+    }
+    auto lit = c->layers.find(layer);
+    if (lit != c->layers.end()) {
+      const int rc2 = osm_layer_set_slot(lit->second, expert, slot);
+      if (rc2) return cache_fail(c, rc2, "cache: binding the loaded expert failed");
+    }
+  } else if (c->source) {
+    const void* src = nullptr;
+    if (c->source(c->user, layer, expert, &src) != 0)
+      return cache_fail(c, OSM_ERUNTIME, "cache: the host source could not provide the expert");
+  }
+  osm_cache::Node n;
+  n.slot = slot;
+  n.frequency = freq;
+  n.last_use = c->tick;
+  n.epoch = c->epoch;
+  c->entries.emplace(key, n);
+  c->resident_bytes += c->accounted;
+  ++c->loads;
+  if (slot_out) *slot_out = slot;
+  return OSM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int osm_cache_create(osm_slab* slab, uint64_t budget_bytes, uint64_t accounted_bytes,
+                     osm_cache_source_fn source, void* user, osm_cache** out) {
+  if (!out) return OSM_EINVAL;
+  *out = nullptr;
+  if (budget_bytes == 0) return OSM_EINVAL;
+  if (accounted_bytes == 0) {
+    if (!slab) return OSM_EINVAL;
+    accounted_bytes = slab->layout.stride;
+  }
+  if (slab && !source) return OSM_EINVAL;
+  osm_cache* c = new (std::nothrow) osm_cache;
+  if (!c) return OSM_ENOMEM;
+  c->slab = slab;
+  c->budget = budget_bytes;
+  c->accounted = accounted_bytes;
+  c->source = source;
+  c->user = user;
+  if (slab)
+    for (uint32_t s = slab->slots; s > 0; --s) c->free_slots.push_back((int32_t)(s - 1));
+  *out = c;
+  return OSM_OK;
+}
+
+int osm_cache_destroy(osm_cache* c) {
+  delete c;
+  return OSM_OK;
+}
+
+const char* osm_cache_last_error(const osm_cache* c) { return c ? c->err.c_str() : "null cache"; }
+
+int osm_cache_bind_layer(osm_cache* c, uint32_t layer_id, osm_layer* layer) {
+  if (!c || !layer) return OSM_EINVAL;
+  if (c->slab && layer->slab != c->slab)
+    return cache_fail(c, OSM_EINVAL, "cache: the layer must be bound to the cache's slab");
+  c->layers[layer_id] = layer;
+  // experts of this layer already resident keep their slots; all others are
+  // marked not resident
+  for (uint32_t e = 0; e < (uint32_t)layer->g.E; ++e) {
+    auto it = c->entries.find(cache_key(layer_id, e));
+    const int rc = osm_layer_set_slot(layer, e, it != c->entries.end() ? it->second.slot : -1);
+    if (rc) return cache_fail(c, rc, "cache: binding the layer failed");
+  }
+  return OSM_OK;
+}
+
+int osm_cache_get(osm_cache* c, uint32_t layer_id, uint32_t expert, int32_t* slot_out) {
+  if (!c) return OSM_EINVAL;
+  ++c->epoch;
+  return cache_get(c, layer_id, expert, slot_out);
+}
+
+int osm_cache_acquire(osm_cache* c, uint32_t layer_id, const uint32_t* experts, uint32_t n) {
+  if (!c || (n && !experts)) return OSM_EINVAL;
+  ++c->epoch;
+  for (uint32_t i = 0; i < n; ++i) {
+    const int rc = cache_get(c, layer_id, experts[i], nullptr);
+    if (rc) return rc;
+  }
+  return OSM_OK;
+}
+
+int osm_cache_contains(const osm_cache* c, uint32_t layer_id, uint32_t expert) {
+  if (!c) return 0;
+  return c->entries.count(cache_key(layer_id, expert)) ? 1 : 0;
+}
+
+int osm_cache_stats(const osm_cache* c, osm_cache_counts* out) {
+  if (!c || !out) return OSM_EINVAL;
+  out->hits = c->hits;
+  out->misses = c->misses;
+  out->loads = c->loads;
+  out->evictions = c->evictions;
+  out->resident_entries = c->entries.size();
+  out->resident_bytes = c->resident_bytes;
+  out->budget_bytes = c->budget;
+  return OSM_OK;
 }
 
 }  // extern "C"

@@ -39,10 +39,13 @@ namespace {
 #ifdef OSM_PHASE_TIMING
 __device__ unsigned long long g_tl[OSM_TL_SLOTS];
 __device__ long long g_cyc[64];
+__device__ long long g_gcyc[2][64];  // grouped kernels: [gate/up | down][stamp]
+#define GCYC(k, i) do { if (blockIdx.x == 0 && threadIdx.x == 0 && (i) < 64) g_gcyc[(k)][(i)] = clock64(); } while (0)
 #define CYC(i) do { if (threadIdx.x == 0 && (blockIdx.x == 0 || blockIdx.x == 70)) \
   g_cyc[(i) + (blockIdx.x == 70 ? 32 : 0)] = clock64(); } while (0)
 #else
 #define CYC(i) do { } while (0)
+#define GCYC(k, i) do { } while (0)
 #endif
 
 constexpr int kTileRows = 16;
@@ -246,10 +249,10 @@ __device__ __forceinline__ uint32_t hi_nib(uint32_t w) { return (w >> 4) & 0x0F0
 // as B fragments -- cols16: frag[row][g][half][16 lanes] (columns 0..3);
 // else frag[g][half][32 lanes] with row t in columns 4t..4t+3 (nrow <= 2) --
 // digit scales sx[row][g][2] (even lanes s/128, odd lanes s/16384) and
-// sums[row][g].  Items (row, g, half, j) of one (row, g) are 8 consecutive
-// threads.
+// sums[row][g].  Row t reads src row rowmap[t] when rowmap is given.  Items
+// (row, g, half, j) of one (row, g) are 8 consecutive threads.
 __device__ void stage_digits(const float* __restrict__ src, int nrow, int ld, int K, bool cols16,
-                             uint2* frag, float* sx, float* sums) {
+                             uint2* frag, float* sx, float* sums, const int* rowmap = nullptr) {
   const int G = K >> 6;
   const int items = nrow * G * 8;
   constexpr int U = 2;  // items per thread whose loads are in flight together
@@ -263,7 +266,7 @@ __device__ void stage_digits(const float* __restrict__ src, int nrow, int ld, in
       live[u] = it < items;
       itc[u] = live[u] ? it : items - 1;
       const int j = itc[u] & 3, h = (itc[u] >> 2) & 1, g = (itc[u] >> 3) % G, t = (itc[u] >> 3) / G;
-      const float* p = src + (size_t)t * ld + 64 * g + 16 * j + 8 * h;
+      const float* p = src + (size_t)(rowmap ? rowmap[t] : t) * ld + 64 * g + 16 * j + 8 * h;
       const float4 u0 = *reinterpret_cast<const float4*>(p);
       const float4 u1 = *reinterpret_cast<const float4*>(p + 4);
       v[u][0] = u0.x; v[u][1] = u0.y; v[u][2] = u0.z; v[u][3] = u0.w;
@@ -701,6 +704,564 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_down_kernel(GemvArgs a)
   TL_END(1);
 }
 
+// ============================================================================
+// Three or more tokens: grouped projections.
+//
+// Work items are (chunk of up to 8 pairs of one active expert, block of
+// rows), numbered chunk-major so that a CTA's contiguous run of items mostly
+// shares its chunk, whose activation digits are staged once.  One producer
+// thread streams each item's weight rows and scale rows into a ring of
+// stages with bulk copies (full barrier: copies landed; empty barrier: all 8
+// consumer warps are done with the stage), writing the item's descriptor at
+// the head of the stage.  The MMA tile's 8 columns are the chunk's 8 tokens
+// and its three digit planes are three MMAs (digit-major), so one A fragment
+// serves every token; the consumer warps split the input groups and their
+// partial sums are added in a fixed order.
+// ============================================================================
+constexpr int kChunk = 8;       // pairs per chunk = MMA columns
+constexpr int kGuBlk = 32;      // gate/up rows per item (2 MMA row tiles)
+constexpr int kDnBlk = 64;      // down output rows per item (4 MMA row tiles)
+constexpr int kCons = 8;        // consumer warps
+constexpr int kGrpThreads = (kCons + 1) * 32;
+constexpr int kMaxStages = 8;
+constexpr int kStageHdr = 128;  // item descriptor at the head of each stage
+
+struct GrpDesc {
+  const uint8_t* ptr;
+  int kind, rb, pos0, ntok, chunk, end;
+};
+
+struct GrpLayout {
+  size_t dig, q, stage, stage_bytes, wts, scales, part, part_bytes, crow, bars, total;
+  int bs, nst;
+};
+__host__ __device__ inline size_t align128(size_t v) { return (v + 127) & ~(size_t)127; }
+
+// gate/up stage: [descriptor][gate: 8 blocks of 4 rows][up: 8 blocks][scales:
+// gate_s, gate_b, up_s, up_b, 32 rows of G bf16 each]
+__host__ __device__ inline GrpLayout grp_gu_layout(int H, int nst) {
+  const size_t G = (size_t)H >> 6;
+  GrpLayout L;
+  L.nst = nst;
+  L.bs = pad_stride(4 * (H >> 1));
+  size_t o = 0;
+  L.dig = o;   o += G * 2 * 3 * 32 * 8;
+  L.q = o;     o += G * kChunk * 16;
+  L.wts = kStageHdr;
+  L.scales = kStageHdr + (size_t)2 * (kGuBlk / 4) * L.bs;
+  L.stage_bytes = align128(L.scales + (size_t)4 * kGuBlk * G * 2);
+  o = align128(o);
+  L.stage = o; o += (size_t)nst * L.stage_bytes;
+  L.part_bytes = (size_t)kCons * 32 * 8 * 4;
+  L.part = o;  o += 2 * L.part_bytes;
+  L.crow = o;  o += 64;
+  L.bars = o;  o += 2 * kMaxStages * 8;
+  L.total = o;
+  return L;
+}
+
+// down stage: [descriptor][16 blocks of 4 rows][scales: down_s, down_b, 64
+// rows of K/64 bf16 each]
+__host__ __device__ inline GrpLayout grp_dn_layout(int Kmax, int Imax, int nst) {
+  const size_t Gh = (size_t)Imax >> 6, Gk = (size_t)Kmax >> 6;
+  GrpLayout L;
+  L.nst = nst;
+  L.bs = pad_stride(4 * (Kmax >> 1));
+  size_t o = 0;
+  L.dig = o;   o += Gh * 2 * 3 * 32 * 8;
+  L.q = o;     o += Gh * kChunk * 16;
+  L.wts = kStageHdr;
+  L.scales = kStageHdr + (size_t)(kDnBlk / 4) * L.bs;
+  L.stage_bytes = align128(L.scales + (size_t)2 * kDnBlk * Gk * 2);
+  o = align128(o);
+  L.stage = o; o += (size_t)nst * L.stage_bytes;
+  L.part_bytes = (size_t)kCons * 32 * 4 * 4;
+  L.part = o;  o += 2 * L.part_bytes;
+  L.crow = o;  o += 64;
+  L.bars = o;  o += 2 * kMaxStages * 8;
+  L.total = o;
+  return L;
+}
+
+// Digit-major activation fragments of a chunk (consumer threads only):
+// dig[g][half][digit][t*4 + j] (uint2) for slots t < 8 (slots >= nrow are
+// zero) and q[g][t] = {s/128, s/16384, sum(x), 0}.  The 8 items of (t, g) are
+// consecutive lanes of one warp; a thread's loads are issued ahead of its
+// conversions.
+__device__ void stage_digits_dm(const float* __restrict__ src, const int* rowmap, int nrow,
+                                int ld, int K, uint2* dig, float4* q, int tid) {
+  constexpr int U = 4;
+  const int G = K >> 6;
+  const int items = kChunk * G * 8;  // a multiple of 64: warps are all live or all idle
+  for (int base = 0; base < items; base += U * kCons * 32) {
+    float v[U][8];
+    int itc[U];
+    bool live[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int it = base + u * kCons * 32 + tid;
+      live[u] = it < items;
+      itc[u] = live[u] ? it : items - 1;
+      const int j = itc[u] & 3, h = (itc[u] >> 2) & 1, g = (itc[u] >> 3) % G, t = (itc[u] >> 3) / G;
+      if (t < nrow) {
+        const float* p = src + (size_t)rowmap[t] * ld + 64 * g + 16 * j + 8 * h;
+        const float4 u0 = __ldcg(reinterpret_cast<const float4*>(p));
+        const float4 u1 = __ldcg(reinterpret_cast<const float4*>(p + 4));
+        v[u][0] = u0.x; v[u][1] = u0.y; v[u][2] = u0.z; v[u][3] = u0.w;
+        v[u][4] = u1.x; v[u][5] = u1.y; v[u][6] = u1.z; v[u][7] = u1.w;
+      } else {
+#pragma unroll
+        for (int m = 0; m < 8; ++m) v[u][m] = 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      if (base + u * kCons * 32 + (tid & ~31) >= items) break;  // the whole warp is idle
+      const int j = itc[u] & 3, h = (itc[u] >> 2) & 1, g = (itc[u] >> 3) % G, t = (itc[u] >> 3) / G;
+      float mx = 0.0f, sm = 0.0f;
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        mx = fmaxf(mx, fabsf(v[u][m]));
+        sm += v[u][m];
+      }
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, o));
+        sm += __shfl_xor_sync(0xFFFFFFFFu, sm, o);
+      }
+      if (!live[u]) continue;
+      const int e = group_exponent(mx);
+      const Digits D = make_digits(v[u], e);
+#pragma unroll
+      for (int d = 0; d < 3; ++d)
+        dig[(((size_t)g * 2 + h) * 3 + d) * 32 + t * 4 + j] = make_uint2(D.b0[d], D.b1[d]);
+      if (h == 0 && j == 0) {
+        const float s = __uint_as_float((uint32_t)(127 + e) << 23);
+        q[(size_t)g * kChunk + t] =
+            t < nrow ? make_float4(s * 0.0078125f, s * 6.103515625e-05f, sm, 0.0f)
+                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    }
+  }
+}
+
+// One group of one 16-row tile against the chunk's 8 tokens: the three
+// digit-plane sums D[d][4] (s32, exact).
+__device__ __forceinline__ void mma_group_dm(int (&D)[3][4], uint2 w0, uint2 w8, const uint2* dig,
+                                             int g, int lane) {
+  const uint32_t a0 = lo_nib(w0.x), a1 = lo_nib(w8.x), a2 = hi_nib(w0.x), a3 = hi_nib(w8.x);
+  const uint32_t c0 = lo_nib(w0.y), c1 = lo_nib(w8.y), c2 = hi_nib(w0.y), c3 = hi_nib(w8.y);
+#pragma unroll
+  for (int d = 0; d < 3; ++d) {
+    D[d][0] = D[d][1] = D[d][2] = D[d][3] = 0;
+    const uint2 b0 = dig[(((size_t)g * 2 + 0) * 3 + d) * 32 + lane];
+    const uint2 b1 = dig[(((size_t)g * 2 + 1) * 3 + d) * 32 + lane];
+    mma_s8(D[d], a0, a1, a2, a3, b0.x, b0.y);
+    mma_s8(D[d], c0, c1, c2, c3, b1.x, b1.y);
+  }
+}
+
+// acc[hh][tt] += s_w * q.s (D0*128 + D1 + D2/128) + b_w * sum(x), for MMA rows
+// r (hh 0) and r+8 (hh 1) and this lane's tokens 2j, 2j+1 (tt); sb packs the
+// row's bf16 scale (low half) and bias (high half).
+__device__ __forceinline__ void epilogue_dm(float (&acc)[2][2], const int (&D)[3][4], uint32_t sb0,
+                                            uint32_t sb8, float4 q0, float4 q1) {
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    const uint32_t sb = hh ? sb8 : sb0;
+    const float sw = __uint_as_float(sb << 16), bw = __uint_as_float(sb & 0xFFFF0000u);
+#pragma unroll
+    for (int tt = 0; tt < 2; ++tt) {
+      const int c = 2 * hh + tt;
+      const float4 q = tt ? q1 : q0;
+      const float inner = fmaf(q.y, (float)D[2][c], q.x * (float)(D[0][c] * 128 + D[1][c]));
+      acc[hh][tt] = fmaf(bw, q.z, fmaf(sw, inner, acc[hh][tt]));
+    }
+  }
+}
+
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kCons * 32) : "memory");
+}
+// Named barrier of the consumer warps that also ORs a flag across them.
+__device__ __forceinline__ bool consumer_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 2, %2, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kCons * 32)
+      : "memory");
+  return r != 0;
+}
+
+// Item -> descriptor; false when the item has no work (a chunk's rows beyond
+// a smaller expert kind, or an expert without a slot).
+__device__ __forceinline__ bool grp_decode(const GrpArgs& a, int item, int nrb, bool down,
+                                           int& last_ch, ActEntry& en, int2& cj, GrpDesc& d) {
+  const int rb = item % nrb, ch = item / nrb;
+  if (ch != last_ch) {
+    cj = a.chunks[ch];
+    en = a.act[cj.x];
+    last_ch = ch;
+  }
+  const int ntok = min(kChunk, en.cnt - cj.y);
+  const int rows = down ? a.dn.rows[en.kind] : a.gu.rows[en.kind];
+  d.ptr = en.ptr;
+  d.kind = en.kind;
+  d.rb = rb;
+  d.pos0 = en.off + cj.y;
+  d.ntok = ntok;
+  d.chunk = ch;
+  d.end = 0;
+  return ntok > 0 && en.ptr != nullptr && rb * (down ? kDnBlk : kGuBlk) < rows;
+}
+
+// Producer thread: items [i0, i1) into the stage ring, then an end marker;
+// finally waits (bounded) for its copies still in flight.
+template <bool DOWN>
+__device__ void grp_produce(const GrpArgs& a, const GrpLayout& Ly, unsigned char* smraw,
+                            uint64_t* full, uint64_t* empty, int i0, int i1, int nrb) {
+  const int nst = Ly.nst;
+  uint32_t n = 0;
+  bool ok = true;
+  int last_ch = -1;
+  ActEntry en{};
+  int2 cj = make_int2(0, 0);
+  for (int item = i0; item < i1; ++item) {
+    GrpDesc d;
+    if (!grp_decode(a, item, nrb, DOWN, last_ch, en, cj, d)) continue;
+    const int s = (int)(n % nst);
+    const uint32_t k = n / nst;
+    if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1)) {
+      atomicOr(a.status, kStatusCopyTimeout);
+      ok = false;
+      break;
+    }
+    unsigned char* base = smraw + Ly.stage + (size_t)s * Ly.stage_bytes;
+    *reinterpret_cast<GrpDesc*>(base) = d;
+    if (!DOWN) {
+      const int H = a.H, G = H >> 6, rowb = H >> 1;
+      const int nrow = min(kGuBlk, a.gu.rows[d.kind] - d.rb * kGuBlk);  // a multiple of 4
+      const uint32_t sbytes = (uint32_t)(nrow * G * 2);
+      mbar_arrive_expect(&full[s], (uint32_t)(2 * nrow * rowb) + 4u * sbytes);
+      const size_t r0 = (size_t)d.rb * kGuBlk;
+      for (int b = 0; b < nrow / 4; ++b) {
+        const size_t off = (r0 + 4 * b) * rowb;
+        bulk_load(base + Ly.wts + (size_t)b * Ly.bs, d.ptr + a.gu.w[d.kind] + off, 4u * rowb, &full[s]);
+        bulk_load(base + Ly.wts + (size_t)(kGuBlk / 4 + b) * Ly.bs, d.ptr + a.gu.w2[d.kind] + off,
+                  4u * rowb, &full[s]);
+      }
+      const uint64_t so[4] = {a.gu.s[d.kind], a.gu.b[d.kind], a.gu.s2[d.kind], a.gu.b2[d.kind]};
+      for (int arr = 0; arr < 4; ++arr)
+        bulk_load(base + Ly.scales + (size_t)arr * kGuBlk * G * 2, d.ptr + so[arr] + r0 * G * 2, sbytes,
+                  &full[s]);
+    } else {
+      const int K = a.dn.K[d.kind], rbe = K >> 1, Gd = K >> 6;
+      const int r0 = d.rb * kDnBlk;
+      const int nrow = min(kDnBlk, a.dn.rows[d.kind] - r0);  // a multiple of 64
+      const uint32_t sbytes = (uint32_t)(nrow * Gd * 2);
+      mbar_arrive_expect(&full[s], (uint32_t)(nrow * rbe) + 2u * sbytes);
+      for (int b = 0; b < nrow / 4; ++b)
+        bulk_load(base + Ly.wts + (size_t)b * Ly.bs, d.ptr + a.dn.w[d.kind] + (size_t)(r0 + 4 * b) * rbe,
+                  4u * rbe, &full[s]);
+      bulk_load(base + Ly.scales, d.ptr + a.dn.s[d.kind] + (size_t)r0 * Gd * 2, sbytes, &full[s]);
+      bulk_load(base + Ly.scales + (size_t)kDnBlk * Gd * 2, d.ptr + a.dn.b[d.kind] + (size_t)r0 * Gd * 2,
+                sbytes, &full[s]);
+    }
+    ++n;
+  }
+  if (ok) {
+    const int s = (int)(n % nst);
+    const uint32_t k = n / nst;
+    if (k > 0 && !mbar_wait(&empty[s], (k - 1) & 1)) {
+      atomicOr(a.status, kStatusCopyTimeout);
+    } else {
+      GrpDesc d{};
+      d.end = 1;
+      *reinterpret_cast<GrpDesc*>(smraw + Ly.stage + (size_t)s * Ly.stage_bytes) = d;
+      mbar_arrive(&full[s]);
+    }
+  }
+  // copies of the last uses of the other stages may still be landing
+  for (uint32_t m = n + 1 > (uint32_t)nst ? n + 1 - nst : 0; m < n; ++m)
+    mbar_wait(&full[m % nst], (m / nst) & 1);
+}
+
+__global__ void __launch_bounds__(kGrpThreads, 1) grp_gateup_kernel(GrpArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int H = a.H, G = H >> 6, rowb = H >> 1;
+  const GrpLayout Ly = grp_gu_layout(H, a.st_gu);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smraw + Ly.bars);
+  uint64_t* empty = full + kMaxStages;
+  GCYC(0, 0);
+  TL_START(2);
+  if (tid == 0) {
+    for (int s = 0; s < Ly.nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCons);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  GCYC(0, 1);
+  TL_WAITED(2);
+  const int nrb = a.rb_gu;
+  const int n_items = *a.n_ch * nrb;
+  const int per = (n_items + gridDim.x - 1) / gridDim.x;
+  const int i0 = min(n_items, (int)blockIdx.x * per), i1 = min(n_items, i0 + per);
+  if (warp == kCons) {
+    if (lane == 0) grp_produce<false>(a, Ly, smraw, full, empty, i0, i1, nrb);
+    return;
+  }
+  uint2* dig = reinterpret_cast<uint2*>(smraw + Ly.dig);
+  float4* xq = reinterpret_cast<float4*>(smraw + Ly.q);
+  int* crow = reinterpret_cast<int*>(smraw + Ly.crow);
+  const int r = lane >> 2, j = lane & 3;
+  const int rt = warp & 1, kq = warp >> 1;  // row tile, input quarter
+  const int gq = (G + 3) / 4, ga = min(G, kq * gq), gb = min(G, ga + gq);
+  const int m0 = rt * 16 + mma_to_row(r);   // tile rows of MMA rows r and r+8 (m0 + 2)
+  uint32_t n = 0;
+  int cur_chunk = -1, pb = 0;
+  for (;; ++n) {
+    const int s = (int)(n % Ly.nst);
+    bool bad = false;
+    if (!mbar_wait(&full[s], (n / Ly.nst) & 1)) {
+      if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
+      bad = !mbar_wait(&full[s], (n / Ly.nst) & 1);
+    }
+    if (consumer_sync_or(bad)) break;
+    const unsigned char* base = smraw + Ly.stage + (size_t)s * Ly.stage_bytes;
+    const GrpDesc cur = *reinterpret_cast<const GrpDesc*>(base);
+    if (cur.end) break;
+    GCYC(0, 2 + 3 * (n & 15));
+    if (cur.chunk != cur_chunk) {
+      if (tid < kChunk) crow[tid] = tid < cur.ntok ? a.pair_tok[cur.pos0 + tid] : 0;
+      consumer_sync();
+      stage_digits_dm(a.x, crow, cur.ntok, H, H, dig, xq, tid);
+      consumer_sync();
+      cur_chunk = cur.chunk;
+    }
+    GCYC(0, 3 + 3 * (n & 15));
+    // scale/bias pairs of this lane's two rows over its input groups
+    const uint16_t* scr = reinterpret_cast<const uint16_t*>(base + Ly.scales);
+    uint32_t sb[2][2][8];
+#pragma unroll
+    for (int mat = 0; mat < 2; ++mat)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint16_t* sr = scr + ((size_t)(2 * mat) * kGuBlk + m0 + 2 * hh) * G + ga;
+        const uint16_t* br = sr + (size_t)kGuBlk * G;
+        if (G == 32) {
+          const uint4 sv = *reinterpret_cast<const uint4*>(sr), bv = *reinterpret_cast<const uint4*>(br);
+          const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            sb[mat][hh][2 * u] = __byte_perm(sw[u], bw[u], 0x5410);
+            sb[mat][hh][2 * u + 1] = __byte_perm(sw[u], bw[u], 0x7632);
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            sb[mat][hh][u] = ga + u < gb ? (uint32_t)sr[u] | ((uint32_t)br[u] << 16) : 0u;
+        }
+      }
+    const unsigned char* rbase = base + Ly.wts + (size_t)(rt * 4 + (r & 3)) * Ly.bs + (size_t)(r >> 2) * rowb + 8 * j;
+    float acc[2][2][2] = {};  // [gate|up][row r | r+8][token 2j | 2j+1]
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int g = ga + u;
+      if (g < gb) {
+        const float4 q0 = xq[(size_t)g * kChunk + 2 * j], q1 = xq[(size_t)g * kChunk + 2 * j + 1];
+#pragma unroll
+        for (int mat = 0; mat < 2; ++mat) {
+          const unsigned char* rb0 = rbase + (size_t)mat * (kGuBlk / 4) * Ly.bs + 32 * g;
+          const uint2 w0 = *reinterpret_cast<const uint2*>(rb0);
+          const uint2 w8 = *reinterpret_cast<const uint2*>(rb0 + (size_t)2 * rowb);
+          int D[3][4];
+          mma_group_dm(D, w0, w8, dig, g, lane);
+          epilogue_dm(acc[mat], D, sb[mat][0][u], sb[mat][1][u], q0, q1);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage
+    float* part = reinterpret_cast<float*>(smraw + Ly.part + (size_t)pb * Ly.part_bytes);
+    float* pw = part + ((size_t)warp * 32 + lane) * 8;
+#pragma unroll
+    for (int mat = 0; mat < 2; ++mat)
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) pw[(mat * 2 + hh) * 2 + tt] = acc[mat][hh][tt];
+    consumer_sync();
+    GCYC(0, 4 + 3 * (n & 15));
+    // fixed-order sum of the four input quarters, SwiGLU, store h
+    if (tid < 64) {
+      const int ort = tid >> 5, ol = tid & 31, orr = ol >> 2, oj = ol & 3;
+      float s8[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) s8[v] = 0.0f;
+      for (int qq = 0; qq < 4; ++qq) {
+        const float* pp = part + ((size_t)(qq * 2 + ort) * 32 + ol) * 8;
+#pragma unroll
+        for (int v = 0; v < 8; ++v) s8[v] += pp[v];
+      }
+      const int rows = a.gu.rows[cur.kind];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = cur.rb * kGuBlk + ort * 16 + mma_to_row(orr + 8 * hh);
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const int t = 2 * oj + tt;
+          if (t < cur.ntok && row < rows)
+            a.h[(size_t)(cur.pos0 + t) * a.Imax + row] =
+                __fmul_rn(ref_silu(s8[(0 * 2 + hh) * 2 + tt]), s8[(1 * 2 + hh) * 2 + tt]);
+        }
+      }
+    }
+    pb ^= 1;
+  }
+  GCYC(0, 63);
+  TL_END(2);
+  pdl_trigger();
+}
+
+__global__ void __launch_bounds__(kGrpThreads, 1) grp_down_kernel(GrpArgs a) {
+  extern __shared__ __align__(128) unsigned char smraw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Kmax = a.dn.K[0] > a.dn.K[1] ? a.dn.K[0] : a.dn.K[1];
+  const GrpLayout Ly = grp_dn_layout(Kmax, a.Imax, a.st_dn);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smraw + Ly.bars);
+  uint64_t* empty = full + kMaxStages;
+  GCYC(1, 0);
+  TL_START(3);
+  if (tid == 0) {
+    for (int s = 0; s < Ly.nst; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kCons);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  pdl_wait();
+  GCYC(1, 1);
+  TL_WAITED(3);
+  const int nrb = a.ob_dn;
+  const int n_items = *a.n_ch * nrb;
+  const int per = (n_items + gridDim.x - 1) / gridDim.x;
+  const int i0 = min(n_items, (int)blockIdx.x * per), i1 = min(n_items, i0 + per);
+  if (warp == kCons) {
+    if (lane == 0) grp_produce<true>(a, Ly, smraw, full, empty, i0, i1, nrb);
+    return;
+  }
+  uint2* dig = reinterpret_cast<uint2*>(smraw + Ly.dig);
+  float4* hq = reinterpret_cast<float4*>(smraw + Ly.q);
+  int* crow = reinterpret_cast<int*>(smraw + Ly.crow);
+  const int r = lane >> 2, j = lane & 3;
+  const int rt = warp & 3, kh = warp >> 2;  // row tile, input half
+  const int m0 = rt * 16 + mma_to_row(r);
+  int orow[2] = {0, 0};                      // reducers: partial rows of tokens 2j, 2j+1
+  uint32_t n = 0;
+  int cur_chunk = -1, pb = 0;
+  for (;; ++n) {
+    const int s = (int)(n % Ly.nst);
+    bool bad = false;
+    if (!mbar_wait(&full[s], (n / Ly.nst) & 1)) {
+      if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
+      bad = !mbar_wait(&full[s], (n / Ly.nst) & 1);
+    }
+    if (consumer_sync_or(bad)) break;
+    const unsigned char* base = smraw + Ly.stage + (size_t)s * Ly.stage_bytes;
+    const GrpDesc cur = *reinterpret_cast<const GrpDesc*>(base);
+    if (cur.end) break;
+    GCYC(1, 2 + 3 * (n & 15));
+    if (cur.chunk != cur_chunk) {
+      if (tid < kChunk) crow[tid] = tid < cur.ntok ? cur.pos0 + tid : cur.pos0;
+      if (tid < 128) {
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const int t = 2 * j + tt, pos = cur.pos0 + t;
+          orow[tt] = t < cur.ntok ? a.pair_tok[pos] * a.kp1 + a.pair_pick[pos] : 0;
+        }
+      }
+      consumer_sync();
+      stage_digits_dm(a.h, crow, cur.ntok, a.Imax, a.Imax, dig, hq, tid);
+      consumer_sync();
+      cur_chunk = cur.chunk;
+    }
+    GCYC(1, 3 + 3 * (n & 15));
+    const int rbe = a.dn.K[cur.kind] >> 1, Gd = a.dn.K[cur.kind] >> 6;
+    const int gh = (Gd + 1) >> 1, ga = min(Gd, kh * gh), gb = min(Gd, ga + gh);
+    const uint16_t* sr0 = reinterpret_cast<const uint16_t*>(base + Ly.scales) + (size_t)m0 * Gd + ga;
+    uint32_t sb[2][6];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const uint16_t* sr = sr0 + (size_t)(2 * hh) * Gd;
+      const uint16_t* br = sr + (size_t)kDnBlk * Gd;
+      if (Gd == 8) {
+        const uint2 sv = *reinterpret_cast<const uint2*>(sr), bv = *reinterpret_cast<const uint2*>(br);
+        sb[hh][0] = __byte_perm(sv.x, bv.x, 0x5410);
+        sb[hh][1] = __byte_perm(sv.x, bv.x, 0x7632);
+        sb[hh][2] = __byte_perm(sv.y, bv.y, 0x5410);
+        sb[hh][3] = __byte_perm(sv.y, bv.y, 0x7632);
+        sb[hh][4] = sb[hh][5] = 0u;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 6; ++u)
+          sb[hh][u] = ga + u < gb ? (uint32_t)sr[u] | ((uint32_t)br[u] << 16) : 0u;
+      }
+    }
+    const unsigned char* rbase = base + Ly.wts + (size_t)(rt * 4 + (r & 3)) * Ly.bs + (size_t)(r >> 2) * rbe + 8 * j;
+    float acc[2][2] = {};  // [row r | r+8][pair 2j | 2j+1]
+#pragma unroll
+    for (int u = 0; u < 6; ++u) {
+      const int g = ga + u;
+      if (g < gb) {
+        const float4 q0 = hq[(size_t)g * kChunk + 2 * j], q1 = hq[(size_t)g * kChunk + 2 * j + 1];
+        const uint2 w0 = *reinterpret_cast<const uint2*>(rbase + 32 * g);
+        const uint2 w8 = *reinterpret_cast<const uint2*>(rbase + (size_t)2 * rbe + 32 * g);
+        int D[3][4];
+        mma_group_dm(D, w0, w8, dig, g, lane);
+        epilogue_dm(acc, D, sb[0][u], sb[1][u], q0, q1);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    float* part = reinterpret_cast<float*>(smraw + Ly.part + (size_t)pb * Ly.part_bytes);
+    float* pw = part + ((size_t)warp * 32 + lane) * 4;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+      for (int tt = 0; tt < 2; ++tt) pw[hh * 2 + tt] = acc[hh][tt];
+    consumer_sync();
+    GCYC(1, 4 + 3 * (n & 15));
+    // fixed-order sum of the two input halves, store partial rows
+    if (tid < 128) {
+      const int ort = tid >> 5, orr = lane >> 2;
+      const float* p0 = part + ((size_t)ort * 32 + lane) * 4;
+      const float* p1 = part + ((size_t)(4 + ort) * 32 + lane) * 4;
+      const int rows = a.dn.rows[cur.kind];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int row = cur.rb * kDnBlk + ort * 16 + mma_to_row(orr + 8 * hh);
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt) {
+          const int t = 2 * j + tt;
+          if (t < cur.ntok && row < rows)
+            a.partial[(size_t)orow[tt] * a.H + row] = p0[hh * 2 + tt] + p1[hh * 2 + tt];
+        }
+      }
+    }
+    pb ^= 1;
+  }
+  GCYC(1, 63);
+  TL_END(3);
+  pdl_trigger();
+}
+
 template <typename K, typename... Args>
 void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg{};
@@ -811,14 +1372,66 @@ void launch_gemv_down(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s, ui
   if (launches) *launches += 1;
 }
 
+
+void init_grouped_attributes(int max_smem) {
+  cudaFuncSetAttribute(grp_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(grp_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+}
+
+bool grouped_configure(GrpArgs& a, int max_smem, size_t* smem_gu, size_t* smem_dn) {
+  const int nk = a.has_shared ? 2 : 1;
+  if (a.H % 128 || a.Imax % 128 || a.H > 2048) return false;
+  for (int kd = 0; kd < nk; ++kd) {
+    if (a.gu.K[kd] != a.H || a.dn.rows[kd] != a.H || a.dn.K[kd] % 128 || a.dn.K[kd] > 768)
+      return false;
+    if (a.gu.rows[kd] % 4) return false;  // whole 4-row copy blocks
+    // bulk copies: 16-byte aligned sources
+    const uint64_t o[9] = {a.gu.w[kd], a.gu.w2[kd], a.dn.w[kd], a.gu.s[kd], a.gu.b[kd],
+                           a.gu.s2[kd], a.gu.b2[kd], a.dn.s[kd], a.dn.b[kd]};
+    for (uint64_t v : o)
+      if (v % 16) return false;
+  }
+  if (a.slab_stride % 16) return false;
+  const int rmax = a.gu.rows[0] > a.gu.rows[1] ? a.gu.rows[0] : a.gu.rows[1];
+  a.rb_gu = (rmax + kGuBlk - 1) / kGuBlk;
+  a.ob_dn = (a.H + kDnBlk - 1) / kDnBlk;
+  const int Kmax = a.dn.K[0] > a.dn.K[1] ? a.dn.K[0] : a.dn.K[1];
+  if (Kmax > a.Imax) return false;
+  // as many stages as fit, up to kMaxStages; at least two
+  int st = kMaxStages;
+  while (st >= 2 && grp_gu_layout(a.H, st).total > (size_t)max_smem) --st;
+  a.st_gu = st;
+  st = kMaxStages;
+  while (st >= 2 && grp_dn_layout(Kmax, a.Imax, st).total > (size_t)max_smem) --st;
+  a.st_dn = st;
+  if (a.st_gu < 2 || a.st_dn < 2) return false;
+  *smem_gu = grp_gu_layout(a.H, a.st_gu).total;
+  *smem_dn = grp_dn_layout(Kmax, a.Imax, a.st_dn).total;
+  return true;
+}
+
+void launch_grouped_gateup(const GrpArgs& a, int grid, size_t smem, cudaStream_t s,
+                           uint64_t* launches) {
+  launch_pdl(grp_gateup_kernel, dim3(grid), dim3(kGrpThreads), smem, s, a);
+  if (launches) *launches += 1;
+}
+
+void launch_grouped_down(const GrpArgs& a, int grid, size_t smem, cudaStream_t s,
+                         uint64_t* launches) {
+  launch_pdl(grp_down_kernel, dim3(grid), dim3(kGrpThreads), smem, s, a);
+  if (launches) *launches += 1;
+}
 }  // namespace osm
 
 #ifdef OSM_PHASE_TIMING
 extern "C" int osm_dbg_timeline_gemv(unsigned long long* out) {
   unsigned long long init[OSM_TL_SLOTS];
-  for (int i = 0; i < OSM_TL_SLOTS; ++i) init[i] = (i == 0 || i == 4) ? ~0ull : 0ull;
+  for (int i = 0; i < OSM_TL_SLOTS; ++i) init[i] = (i % 4 == 0) ? ~0ull : 0ull;
   cudaMemcpyFromSymbol(out, osm::g_tl, sizeof(init));
   return (int)cudaMemcpyToSymbol(osm::g_tl, init, sizeof(init));
+}
+extern "C" int osm_dbg_cycles_grouped(long long* out) {
+  return (int)cudaMemcpyFromSymbol(out, osm::g_gcyc, 128 * sizeof(long long));
 }
 extern "C" int osm_dbg_cycles_gemv(long long* out) {
   return (int)cudaMemcpyFromSymbol(out, osm::g_cyc, 64 * sizeof(long long));

@@ -68,6 +68,8 @@ struct RouterArgs {
   int* pair_tok;            // [B*(k+1)]
   int* pair_pick;
   int* tp_pos;              // (token, pick) -> pair position
+  int* n_ch;                // 8-token chunks of the call (null: not built)
+  int2* chunks;             // chunk -> {active entry, first token within it}
   int* cursor;              // [E+1]
   uint32_t* status;
   unsigned long long* exact_count;
@@ -182,6 +184,32 @@ bool gemv_configure(GemvArgs& a, int max_active, int num_sms, int max_smem, Gemv
 void launch_gemv_gateup(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s,
                         uint64_t* launches);
 void launch_gemv_down(const GemvArgs& a, const GemvLaunch& l, cudaStream_t s, uint64_t* launches);
+
+// Three or more tokens (osm_gemv.cu): grouped projections over 8-token
+// chunks of each active expert; down writes partial [token][k+1][H] rows for
+// the combine kernel.
+struct GrpArgs {
+  ProjSections gu, dn;
+  const float* x;                // [T][H]
+  int H, Imax, kp1, has_shared;
+  uint64_t slab_stride;
+  const int* n_ch;               // chunks of up to 8 pairs of one active entry
+  const int2* chunks;            // {active entry, first pair within it}
+  const ActEntry* act;
+  const int* pair_tok;
+  const int* pair_pick;
+  float* h;                      // [pairs][Imax] SwiGLU output
+  float* partial;                // [T][kp1][H]
+  uint32_t* status;
+  // set by grouped_configure
+  int rb_gu, ob_dn, st_gu, st_dn;  // row blocks; ring stages
+};
+void init_grouped_attributes(int max_smem);
+bool grouped_configure(GrpArgs& a, int max_smem, size_t* smem_gu, size_t* smem_dn);
+void launch_grouped_gateup(const GrpArgs& a, int grid, size_t smem, cudaStream_t s,
+                           uint64_t* launches);
+void launch_grouped_down(const GrpArgs& a, int grid, size_t smem, cudaStream_t s,
+                         uint64_t* launches);
 
 struct CombineArgs {
   const float* partial;          // [B][k+1][H]

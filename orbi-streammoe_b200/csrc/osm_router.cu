@@ -417,6 +417,19 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     }
   }
   __syncthreads();
+  if (a.chunks) {
+    // 8-token chunks of each active entry, in entry order
+    for (int j = threadIdx.x; j < n_active; j += blockDim.x)
+      cur[j] = (cnt[expert_of[j]] + 7) / 8;
+    __syncthreads();
+    const int n_ch = small_or_block_scan(cur, n_active, red);
+    for (int j = threadIdx.x; j < n_active; j += blockDim.x) {
+      const int nc = (cnt[expert_of[j]] + 7) / 8;
+      for (int q = 0; q < nc; ++q) a.chunks[cur[j] + q] = make_int2(j, 8 * q);
+    }
+    if (threadIdx.x == 0) *a.n_ch = n_ch;
+    __syncthreads();
+  }
   for (int i = threadIdx.x; i < NE; i += blockDim.x) cur[i] = 0;
   __syncthreads();
   for (int p = threadIdx.x; p < B * k; p += blockDim.x) {

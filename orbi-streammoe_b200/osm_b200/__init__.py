@@ -293,3 +293,57 @@ class Plan:
             self.close()
         except Exception:
             pass
+
+
+class ExpertCache:
+    """HBM expert residency with the reference's LFU + recency policy
+    (VulkanResidentExpertCache).  ``source(layer, expert)`` returns the
+    address of the expert's slot bytes in (pinned) host memory; with
+    ``slab=None`` only the policy runs (no copies)."""
+
+    def __init__(self, slab, budget_bytes: int, accounted_bytes: int = 0, source=None):
+        self._source = source
+
+        def _cb(user, layer, expert, out):
+            try:
+                out[0] = int(self._source(layer, expert)) if self._source else 0
+                return 0
+            except Exception:  # the C side reports the failure
+                return -1
+
+        self._cb = _lib.CACHE_SOURCE_FN(_cb)
+        self.h = C.c_void_p()
+        rc = lib().osm_cache_create(slab.h if slab is not None else None, budget_bytes,
+                                    accounted_bytes, self._cb, None, C.byref(self.h))
+        if rc:
+            raise OsmError(rc, "cache creation failed")
+
+    def _check(self, rc, what):
+        if rc:
+            raise OsmError(rc, f"{what}: {lib().osm_cache_last_error(self.h).decode()}")
+
+    def bind_layer(self, layer_id: int, layer: "Layer"):
+        self._check(lib().osm_cache_bind_layer(self.h, layer_id, layer.h), "bind_layer")
+
+    def get(self, layer_id: int, expert: int) -> int:
+        slot = C.c_int32()
+        self._check(lib().osm_cache_get(self.h, layer_id, expert, C.byref(slot)), "get")
+        return slot.value
+
+    def acquire(self, layer_id: int, experts) -> None:
+        arr = (C.c_uint32 * len(experts))(*[int(e) for e in experts])
+        self._check(lib().osm_cache_acquire(self.h, layer_id, arr, len(experts)), "acquire")
+
+    def contains(self, layer_id: int, expert: int) -> bool:
+        return bool(lib().osm_cache_contains(self.h, layer_id, expert))
+
+    def stats(self) -> dict:
+        c = _lib.CacheCounts()
+        self._check(lib().osm_cache_stats(self.h, C.byref(c)), "stats")
+        return {f: getattr(c, f) for f, _ in c._fields_}
+
+    def close(self):
+        if self.h:
+            lib().osm_cache_destroy(self.h)
+            self.h = C.c_void_p()
+

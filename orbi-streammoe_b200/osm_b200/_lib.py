@@ -50,6 +50,15 @@ class LayerDesc(C.Structure):
                 ("norm_eps", C.c_float)]
 
 
+class CacheCounts(C.Structure):
+    _fields_ = [("hits", C.c_uint64), ("misses", C.c_uint64), ("loads", C.c_uint64),
+                ("evictions", C.c_uint64), ("resident_entries", C.c_uint64),
+                ("resident_bytes", C.c_uint64), ("budget_bytes", C.c_uint64)]
+
+
+# int source(void* user, uint32_t layer, uint32_t expert, const void** src)
+CACHE_SOURCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_void_p))
+
 # name -> (restype, argtypes)
 _P = C.c_void_p
 _SIGS = {
@@ -102,6 +111,14 @@ _SIGS = {
     "osm_plan_kernels": (C.c_uint32, [_P]),
     "osm_gen_normal": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_float, _P, C.c_size_t, C.c_size_t]),
     "osm_gen_expert_slots": (C.c_int, [_P, C.c_uint64, C.c_uint64, C.c_float, C.c_uint32, C.c_uint32]),
+    "osm_cache_create": (C.c_int, [_P, C.c_uint64, C.c_uint64, CACHE_SOURCE_FN, _P, C.POINTER(_P)]),
+    "osm_cache_destroy": (C.c_int, [_P]),
+    "osm_cache_last_error": (C.c_char_p, [_P]),
+    "osm_cache_bind_layer": (C.c_int, [_P, C.c_uint32, _P]),
+    "osm_cache_get": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.POINTER(C.c_int32)]),
+    "osm_cache_acquire": (C.c_int, [_P, C.c_uint32, _P, C.c_uint32]),
+    "osm_cache_contains": (C.c_int, [_P, C.c_uint32, C.c_uint32]),
+    "osm_cache_stats": (C.c_int, [_P, C.POINTER(CacheCounts)]),
 }
 
 _lib = None

@@ -1,0 +1,116 @@
+"""Residency policy of the HBM expert cache, on the CPU (no slab: the policy
+alone).  Restates tests/vulkan_resident_expert_cache_test.cpp:314-382 of the
+reference (E0, E1, E0, E2 with room for two: E1 is evicted) and compares random
+access streams with a Python model of
+src/backend/vulkan_resident_expert_cache.cpp:40-200 (victim = smallest
+(use count, last use, key); use counts survive evictions)."""
+import random
+
+import pytest
+
+ACCOUNTED = 17152  # the reference fixture's accounted bytes per expert
+
+
+@pytest.fixture(scope="module")
+def osm():
+    from osm_b200 import build
+
+    build.build()
+    import osm_b200
+
+    return osm_b200
+
+
+class Model:
+    def __init__(self, budget, accounted):
+        self.budget, self.acc = budget, accounted
+        self.entries = {}          # key -> [freq, last_use]
+        self.hist = {}
+        self.tick = 0
+        self.hits = self.misses = self.loads = self.evictions = 0
+        self.protect = set()
+
+    def acquire(self, layer, experts):
+        """get() of each pick of one call; entries used by this call are not
+        evicted by it (they must stay resident until the call runs)."""
+        self.protect = set()
+        for e in experts:
+            self.get(layer, e)
+            self.protect.add((layer << 32) | e)
+        self.protect = set()
+
+    def get(self, layer, expert):
+        self.tick += 1
+        key = (layer << 32) | expert
+        f = self.hist.get(key, 0) + 1
+        self.hist[key] = f
+        if key in self.entries:
+            self.hits += 1
+            self.entries[key] = [f, self.tick]
+            return
+        self.misses += 1
+        while self.entries and (len(self.entries) + 1) * self.acc > self.budget:
+            cand = [k for k in self.entries if k not in self.protect]
+            victim = min(cand, key=lambda k: (self.entries[k][0], self.entries[k][1], k))
+            del self.entries[victim]
+            self.evictions += 1
+        self.entries[key] = [f, self.tick]
+        self.loads += 1
+
+    def stats(self):
+        return {"hits": self.hits, "misses": self.misses, "loads": self.loads,
+                "evictions": self.evictions, "resident_entries": len(self.entries),
+                "resident_bytes": len(self.entries) * self.acc, "budget_bytes": self.budget}
+
+
+def test_reference_eviction_kat(osm):
+    c = osm.ExpertCache(None, 2 * ACCOUNTED, ACCOUNTED)
+    c.get(0, 0)
+    c.get(0, 1)
+    s = c.stats()
+    assert (s["hits"], s["misses"], s["loads"], s["evictions"]) == (0, 2, 2, 0)
+    assert s["resident_entries"] == 2 and s["resident_bytes"] == 2 * ACCOUNTED
+    c.get(0, 0)
+    c.get(0, 2)
+    s = c.stats()
+    assert (s["hits"], s["misses"], s["loads"], s["evictions"]) == (1, 3, 3, 1)
+    assert s["resident_entries"] == 2 and s["resident_bytes"] <= s["budget_bytes"]
+    assert c.contains(0, 0) and not c.contains(0, 1) and c.contains(0, 2)
+    c.get(0, 0)
+    c.get(0, 2)
+    s = c.stats()
+    assert (s["hits"], s["misses"], s["loads"], s["evictions"]) == (3, 3, 3, 1)
+    c.close()
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_random_streams_match_the_policy_model(osm, seed):
+    rng = random.Random(seed)
+    slots = rng.choice([3, 5, 8])
+    c = osm.ExpertCache(None, slots * ACCOUNTED, ACCOUNTED)
+    m = Model(slots * ACCOUNTED, ACCOUNTED)
+    # Zipf-skewed experts over two layers
+    weights = [1.0 / (r + 1) ** 1.1 for r in range(24)]
+    for _ in range(600):
+        layer = rng.randrange(2)
+        expert = rng.choices(range(24), weights)[0]
+        c.get(layer, expert)
+        m.get(layer, expert)
+    assert c.stats() == m.stats()
+    for layer in range(2):
+        for e in range(24):
+            assert c.contains(layer, e) == (((layer << 32) | e) in m.entries)
+    c.close()
+
+
+def test_one_call_larger_than_the_budget_is_refused(osm):
+    from osm_b200 import OsmError
+
+    c = osm.ExpertCache(None, 3 * ACCOUNTED, ACCOUNTED)
+    c.acquire(0, [1, 2, 3])
+    with pytest.raises(OsmError) as e:
+        c.acquire(0, [4, 5, 6, 7])  # four experts of one call, room for three
+    assert e.value.code == -4  # OSM_ENOMEM
+    c.close()
+    with pytest.raises(OsmError):
+        osm.ExpertCache(None, ACCOUNTED - 1, ACCOUNTED).get(0, 0)
