@@ -125,6 +125,7 @@ struct osm_layer {
   osm::RouterGeom g{};
   uint32_t norm = 0;
   void* wp = nullptr;          // permuted router
+  void* wx = nullptr;          // router tiles of the exact logits
   float* bias = nullptr;
   float* sgate_w = nullptr;
   uint8_t* shared_slot = nullptr;
@@ -329,6 +330,7 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   osm::RouterArgs a{};
   a.g = L->g;
   a.wp = static_cast<const uint4*>(L->wp);
+  a.wx = L->wx;
   a.bias = L->bias;
   a.x = x;
   a.B = (int)T;
@@ -1028,10 +1030,12 @@ int osm_layer_create(osm_context* ctx, const osm_layer_desc* d, osm_layer** out)
   };
   float* tmp = nullptr;
   if (cudaMalloc(&L->wp, (size_t)g.E * g.Hp * (g.f32w ? 4 : 2)) != cudaSuccess ||
+      cudaMalloc(&L->wx, osm::router_tile_bytes(g)) != cudaSuccess ||
       cudaMalloc(&tmp, EH * 4) != cudaSuccess)
     return cleanup(OSM_ENOMEM, "layer: router allocation failed");
   cudaMemcpyAsync(tmp, d->router_weight_host, EH * 4, cudaMemcpyHostToDevice, ctx->stream);
   osm::launch_router_pack(tmp, g, L->wp, ctx->stream, &ctx->launches);
+  osm::launch_router_tile(tmp, g, L->wx, ctx->stream, &ctx->launches);
   cudaStreamSynchronize(ctx->stream);
   cudaFree(tmp);
   if (d->logit_bias_host) {
@@ -1069,6 +1073,7 @@ int osm_layer_destroy(osm_layer* L) {
   DeviceGuard dg(L->ctx->device);
   cudaStreamSynchronize(L->ctx->stream);
   cudaFree(L->wp);
+  cudaFree(L->wx);
   cudaFree(L->bias);
   cudaFree(L->sgate_w);
   cudaFree(L->shared_slot);

@@ -68,8 +68,8 @@ __device__ __forceinline__ void cp_wait() {
 
 __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                        uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+  // not volatile: a pure function of its registers, free to interleave
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -845,26 +845,37 @@ __device__ void stage_digits_dm(const float* __restrict__ src, const int* rowmap
   }
 }
 
-// One group of one 16-row tile against the chunk's 8 tokens: the three
-// digit-plane sums D[d][4] (s32, exact).
-__device__ __forceinline__ void mma_group_dm(int (&D)[3][4], uint2 w0, uint2 w8, const uint2* dig,
-                                             int g, int lane) {
+// B fragments of group g: b[digit][half].
+__device__ __forceinline__ void load_b_dm(uint2 (&b)[3][2], const uint2* dig, int g, int lane) {
+#pragma unroll
+  for (int d = 0; d < 3; ++d)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) b[d][h] = dig[(((size_t)g * 2 + h) * 3 + d) * 32 + lane];
+}
+
+// One group of one 16-row tile against the chunk's 8 tokens.  Each digit
+// plane has its own s32 tile (two dependent MMAs each, so the three planes
+// overlap in the pipe); V = D0 2^14 + D1 2^7 + D2 exactly
+// (|V| < 64*15*64*16384*1.01 < 2^31).
+__device__ __forceinline__ void mma_group_dm(int (&V)[4], uint2 w0, uint2 w8, const uint2 (&b)[3][2]) {
   const uint32_t a0 = lo_nib(w0.x), a1 = lo_nib(w8.x), a2 = hi_nib(w0.x), a3 = hi_nib(w8.x);
   const uint32_t c0 = lo_nib(w0.y), c1 = lo_nib(w8.y), c2 = hi_nib(w0.y), c3 = hi_nib(w8.y);
+  int D[3][4];
 #pragma unroll
   for (int d = 0; d < 3; ++d) {
     D[d][0] = D[d][1] = D[d][2] = D[d][3] = 0;
-    const uint2 b0 = dig[(((size_t)g * 2 + 0) * 3 + d) * 32 + lane];
-    const uint2 b1 = dig[(((size_t)g * 2 + 1) * 3 + d) * 32 + lane];
-    mma_s8(D[d], a0, a1, a2, a3, b0.x, b0.y);
-    mma_s8(D[d], c0, c1, c2, c3, b1.x, b1.y);
+    mma_s8(D[d], a0, a1, a2, a3, b[d][0].x, b[d][0].y);
   }
+#pragma unroll
+  for (int d = 0; d < 3; ++d) mma_s8(D[d], c0, c1, c2, c3, b[d][1].x, b[d][1].y);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) V[i] = D[0][i] * 16384 + D[1][i] * 128 + D[2][i];
 }
 
-// acc[hh][tt] += s_w * q.s (D0*128 + D1 + D2/128) + b_w * sum(x), for MMA rows
-// r (hh 0) and r+8 (hh 1) and this lane's tokens 2j, 2j+1 (tt); sb packs the
-// row's bf16 scale (low half) and bias (high half).
-__device__ __forceinline__ void epilogue_dm(float (&acc)[2][2], const int (&D)[3][4], uint32_t sb0,
+// acc[hh][tt] += s_w * (s / 2^14) V + b_w * sum(x), for MMA rows r (hh 0) and
+// r+8 (hh 1) and this lane's tokens 2j, 2j+1 (tt); sb packs the row's bf16
+// scale (low half) and bias (high half).
+__device__ __forceinline__ void epilogue_dm(float (&acc)[2][2], const int (&V)[4], uint32_t sb0,
                                             uint32_t sb8, float4 q0, float4 q1) {
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
@@ -872,10 +883,8 @@ __device__ __forceinline__ void epilogue_dm(float (&acc)[2][2], const int (&D)[3
     const float sw = __uint_as_float(sb << 16), bw = __uint_as_float(sb & 0xFFFF0000u);
 #pragma unroll
     for (int tt = 0; tt < 2; ++tt) {
-      const int c = 2 * hh + tt;
       const float4 q = tt ? q1 : q0;
-      const float inner = fmaf(q.y, (float)D[2][c], q.x * (float)(D[0][c] * 128 + D[1][c]));
-      acc[hh][tt] = fmaf(bw, q.z, fmaf(sw, inner, acc[hh][tt]));
+      acc[hh][tt] = fmaf(bw, q.z, fmaf(sw, q.y * (float)V[2 * hh + tt], acc[hh][tt]));
     }
   }
 }
@@ -1075,14 +1084,16 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_gateup_kernel(GrpArgs a) {
       const int g = ga + u;
       if (g < gb) {
         const float4 q0 = xq[(size_t)g * kChunk + 2 * j], q1 = xq[(size_t)g * kChunk + 2 * j + 1];
+        uint2 bf[3][2];
+        load_b_dm(bf, dig, g, lane);
 #pragma unroll
         for (int mat = 0; mat < 2; ++mat) {
           const unsigned char* rb0 = rbase + (size_t)mat * (kGuBlk / 4) * Ly.bs + 32 * g;
           const uint2 w0 = *reinterpret_cast<const uint2*>(rb0);
           const uint2 w8 = *reinterpret_cast<const uint2*>(rb0 + (size_t)2 * rowb);
-          int D[3][4];
-          mma_group_dm(D, w0, w8, dig, g, lane);
-          epilogue_dm(acc[mat], D, sb[mat][0][u], sb[mat][1][u], q0, q1);
+          int V[4];
+          mma_group_dm(V, w0, w8, bf);
+          epilogue_dm(acc[mat], V, sb[mat][0][u], sb[mat][1][u], q0, q1);
         }
       }
     }
@@ -1098,29 +1109,21 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_gateup_kernel(GrpArgs a) {
         for (int tt = 0; tt < 2; ++tt) pw[(mat * 2 + hh) * 2 + tt] = acc[mat][hh][tt];
     consumer_sync();
     GCYC(0, 4 + 3 * (n & 15));
-    // fixed-order sum of the four input quarters, SwiGLU, store h
-    if (tid < 64) {
-      const int ort = tid >> 5, ol = tid & 31, orr = ol >> 2, oj = ol & 3;
-      float s8[8];
+    // fixed-order sum of the four input quarters, SwiGLU, store h: one
+    // (row, token) per consumer thread
+    {
+      const int ort = tid >> 7, ol = (tid >> 2) & 31, ohh = (tid >> 1) & 1, ott = tid & 1;
+      float gs = 0.0f, us = 0.0f;
 #pragma unroll
-      for (int v = 0; v < 8; ++v) s8[v] = 0.0f;
       for (int qq = 0; qq < 4; ++qq) {
         const float* pp = part + ((size_t)(qq * 2 + ort) * 32 + ol) * 8;
-#pragma unroll
-        for (int v = 0; v < 8; ++v) s8[v] += pp[v];
+        gs += pp[(0 * 2 + ohh) * 2 + ott];
+        us += pp[(1 * 2 + ohh) * 2 + ott];
       }
-      const int rows = a.gu.rows[cur.kind];
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int row = cur.rb * kGuBlk + ort * 16 + mma_to_row(orr + 8 * hh);
-#pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
-          const int t = 2 * oj + tt;
-          if (t < cur.ntok && row < rows)
-            a.h[(size_t)(cur.pos0 + t) * a.Imax + row] =
-                __fmul_rn(ref_silu(s8[(0 * 2 + hh) * 2 + tt]), s8[(1 * 2 + hh) * 2 + tt]);
-        }
-      }
+      const int row = cur.rb * kGuBlk + ort * 16 + mma_to_row((ol >> 2) + 8 * ohh);
+      const int t = 2 * (ol & 3) + ott;
+      if (t < cur.ntok && row < a.gu.rows[cur.kind])
+        a.h[(size_t)(cur.pos0 + t) * a.Imax + row] = __fmul_rn(ref_silu(gs), us);
     }
     pb ^= 1;
   }
@@ -1163,7 +1166,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_down_kernel(GrpArgs a) {
   const int r = lane >> 2, j = lane & 3;
   const int rt = warp & 3, kh = warp >> 2;  // row tile, input half
   const int m0 = rt * 16 + mma_to_row(r);
-  int orow[2] = {0, 0};                      // reducers: partial rows of tokens 2j, 2j+1
+  int* corow = crow + kChunk;                // partial row of each pair of the chunk
   uint32_t n = 0;
   int cur_chunk = -1, pb = 0;
   for (;; ++n) {
@@ -1179,13 +1182,10 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_down_kernel(GrpArgs a) {
     if (cur.end) break;
     GCYC(1, 2 + 3 * (n & 15));
     if (cur.chunk != cur_chunk) {
-      if (tid < kChunk) crow[tid] = tid < cur.ntok ? cur.pos0 + tid : cur.pos0;
-      if (tid < 128) {
-#pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
-          const int t = 2 * j + tt, pos = cur.pos0 + t;
-          orow[tt] = t < cur.ntok ? a.pair_tok[pos] * a.kp1 + a.pair_pick[pos] : 0;
-        }
+      if (tid < kChunk) {
+        const int pos = cur.pos0 + tid;
+        crow[tid] = tid < cur.ntok ? pos : cur.pos0;
+        corow[tid] = tid < cur.ntok ? a.pair_tok[pos] * a.kp1 + a.pair_pick[pos] : 0;
       }
       consumer_sync();
       stage_digits_dm(a.h, crow, cur.ntok, a.Imax, a.Imax, dig, hq, tid);
@@ -1223,9 +1223,11 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_down_kernel(GrpArgs a) {
         const float4 q0 = hq[(size_t)g * kChunk + 2 * j], q1 = hq[(size_t)g * kChunk + 2 * j + 1];
         const uint2 w0 = *reinterpret_cast<const uint2*>(rbase + 32 * g);
         const uint2 w8 = *reinterpret_cast<const uint2*>(rbase + (size_t)2 * rbe + 32 * g);
-        int D[3][4];
-        mma_group_dm(D, w0, w8, dig, g, lane);
-        epilogue_dm(acc, D, sb[0][u], sb[1][u], q0, q1);
+        uint2 bf[3][2];
+        load_b_dm(bf, dig, g, lane);
+        int V[4];
+        mma_group_dm(V, w0, w8, bf);
+        epilogue_dm(acc, V, sb[0][u], sb[1][u], q0, q1);
       }
     }
     __syncwarp();
@@ -1238,22 +1240,17 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_down_kernel(GrpArgs a) {
       for (int tt = 0; tt < 2; ++tt) pw[hh * 2 + tt] = acc[hh][tt];
     consumer_sync();
     GCYC(1, 4 + 3 * (n & 15));
-    // fixed-order sum of the two input halves, store partial rows
-    if (tid < 128) {
-      const int ort = tid >> 5, orr = lane >> 2;
-      const float* p0 = part + ((size_t)ort * 32 + lane) * 4;
-      const float* p1 = part + ((size_t)(4 + ort) * 32 + lane) * 4;
-      const int rows = a.dn.rows[cur.kind];
+    // fixed-order sum of the two input halves, store partial rows: two
+    // (row, pair) outputs per consumer thread
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int row = cur.rb * kDnBlk + ort * 16 + mma_to_row(orr + 8 * hh);
-#pragma unroll
-        for (int tt = 0; tt < 2; ++tt) {
-          const int t = 2 * j + tt;
-          if (t < cur.ntok && row < rows)
-            a.partial[(size_t)orow[tt] * a.H + row] = p0[hh * 2 + tt] + p1[hh * 2 + tt];
-        }
-      }
+    for (int half = 0; half < 2; ++half) {
+      const int o = tid + half * kCons * 32;
+      const int ort = o >> 7, ol = (o >> 2) & 31, ohh = (o >> 1) & 1, ott = o & 1;
+      const int c = ohh * 2 + ott;
+      const float v = part[((size_t)ort * 32 + ol) * 4 + c] + part[((size_t)(4 + ort) * 32 + ol) * 4 + c];
+      const int row = cur.rb * kDnBlk + ort * 16 + mma_to_row((ol >> 2) + 8 * ohh);
+      const int t = 2 * (ol & 3) + ott;
+      if (t < cur.ntok && row < a.dn.rows[cur.kind]) a.partial[(size_t)corow[t] * a.H + row] = v;
     }
     pb ^= 1;
   }

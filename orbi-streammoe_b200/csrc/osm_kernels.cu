@@ -172,6 +172,24 @@ __global__ void router_pack_kernel(const float* __restrict__ w, RouterGeom g,
   }
 }
 
+__global__ void router_tile_kernel(const float* __restrict__ w, RouterGeom g,
+                                   unsigned char* __restrict__ wx) {
+  const int esz = g.f32w ? 4 : 2, hpt = 128 / esz, epc = 16 / esz;
+  const int nht = g.H / hpt;
+  const int Ep = (g.E + 127) & ~127;
+  const size_t total = (size_t)Ep * g.H;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int e = (int)(i / g.H), h = (int)(i - (size_t)e * g.H);
+    const float v = e < g.E ? w[(size_t)e * g.H + h] : 0.0f;
+    const int eb = e >> 7, r = e & 127, ht = h / hpt, hh = h - ht * hpt;
+    const int c = hh / epc, p = hh - c * epc;
+    const size_t off = (((size_t)eb * nht + ht) * 128 + r) * 128 + (size_t)((c ^ (r & 7)) * 16) + (size_t)p * esz;
+    if (g.f32w) *reinterpret_cast<float*>(wx + off) = v;
+    else *reinterpret_cast<uint16_t*>(wx + off) = (uint16_t)f32_to_bf16_rne(v);
+  }
+}
+
 inline int grid_for(size_t n, int threads) {
   size_t b = (n + threads - 1) / threads;
   if (b > 148 * 64) b = 148 * 64;
@@ -234,6 +252,17 @@ void launch_gen_quant(uint64_t seed, uint64_t tensor, float sigma, int rows, int
   const size_t n = (size_t)rows * (cols >> 6);
   gen_quant_kernel<<<grid_for(n, 128), 128, 0, s>>>(stream_base(seed, tensor), sigma, rows, cols,
                                                      packed, sc, bi);
+  if (launches) *launches += 1;
+}
+
+size_t router_tile_bytes(const RouterGeom& g) {
+  return (size_t)((g.E + 127) & ~127) * g.H * (g.f32w ? 4 : 2);
+}
+
+void launch_router_tile(const float* w, const RouterGeom& g, void* wx, cudaStream_t s,
+                        uint64_t* launches) {
+  router_tile_kernel<<<grid_for((size_t)((g.E + 127) & ~127) * g.H, 256), 256, 0, s>>>(
+      w, g, static_cast<unsigned char*>(wx));
   if (launches) *launches += 1;
 }
 

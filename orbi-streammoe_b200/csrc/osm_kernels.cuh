@@ -31,6 +31,7 @@ struct RouterGeom {
 struct RouterArgs {
   RouterGeom g;
   const uint4* wp;          // permuted router rows (bf16 or fp32)
+  const void* wx;           // router in 16 KB tiles (router_tile_kernel)
   const float* bias;        // [E] or null
   const float* x;           // [B][H]
   int B;
@@ -237,6 +238,12 @@ void launch_gen_quant(uint64_t seed, uint64_t tensor, float sigma, int rows, int
                       uint32_t* packed, uint16_t* sc, uint16_t* bi, cudaStream_t s,
                       uint64_t* launches);
 // Permute fp32 [E][H] router rows (bf16-representable) into the router layout.
+// Router tiles: 128 experts x 128 bytes of one row each (64 bf16 or 32 fp32
+// weights), tiles of one 128-expert block consecutive along h; in each
+// 128-byte row the 16-byte chunk c sits at c ^ (row & 7).
+size_t router_tile_bytes(const RouterGeom& g);
+void launch_router_tile(const float* w, const RouterGeom& g, void* wx, cudaStream_t s,
+                        uint64_t* launches);
 void launch_router_pack(const float* w, const RouterGeom& g, void* wp, cudaStream_t s,
                         uint64_t* launches);
 void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,

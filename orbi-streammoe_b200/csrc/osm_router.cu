@@ -70,6 +70,141 @@ __device__ __forceinline__ void load8(const RouterArgs& a, int e, int m, int lan
 }
 
 // ----------------------------------------------------------------------------
+// exact logits (3+ tokens)
+//
+// router_exact_kernel<TT, F32>: every (token, expert) logit by the
+// reference's own arithmetic -- a sequential fp32 sum over h = 0..H-1 of
+// separately rounded products (matvec_row_major, reference_ops.cpp:85-91),
+// then the bias -- so the selection needs no error bound (bounds are 0).  A
+// block owns 128 experts (one per thread) and TT tokens.  The experts' router
+// rows stream through a ring of 16 KB tiles (128 rows x 128 bytes, one bulk
+// copy each, started before the wait on the predecessor since the weights
+// never change); the row-swizzled chunks make each thread's 16-byte row reads
+// conflict-free.  The tokens' x[h] come from shared memory, and the TT sums
+// advance two at a time with packed f32x2 multiplies and adds (each lane
+// rounded like a scalar mul.rn / add.rn).
+// ----------------------------------------------------------------------------
+constexpr int kExThreads = 128;
+constexpr int kExStages = 4;
+constexpr int kExTile = 16384;
+
+__device__ __forceinline__ float2 fmul2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
+  float2 r;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+
+template <int TT, bool F32>
+__global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) {
+  constexpr int EPC = F32 ? 4 : 8;  // weights per 16-byte chunk
+  constexpr int HPT = 8 * EPC;      // h per tile
+  extern __shared__ __align__(128) unsigned char exsm[];
+  __shared__ __align__(8) uint64_t full[kExStages];
+  unsigned char* ring = exsm;
+  float* xs = reinterpret_cast<float*>(exsm + kExStages * kExTile);  // [H][TT]
+  const int E = a.g.E, H = a.g.H, nht = H / HPT;
+  const int tid = threadIdx.x, e = blockIdx.x * kExThreads + tid, t0 = blockIdx.y * TT;
+  const unsigned char* src = static_cast<const unsigned char*>(a.wx) + (size_t)blockIdx.x * nht * kExTile;
+  TL_START(0);
+  if (tid == 0) {
+    for (int s = 0; s < kExStages; ++s) mbar_init(&full[s], 1);
+    mbar_init_fence();
+    for (int s = 0; s < kExStages && s < nht; ++s) {
+      mbar_arrive_expect(&full[s], kExTile);
+      bulk_load(ring + s * kExTile, src + (size_t)s * kExTile, kExTile, &full[s]);
+    }
+  }
+  pdl_wait();
+  TL_WAITED(0);
+  for (int i = tid; i < TT * H; i += kExThreads) {
+    const int t = i / H, h = i - t * H;
+    xs[h * TT + t] = t0 + t < a.B ? a.x[(size_t)(t0 + t) * H + h] : 0.0f;
+  }
+  __syncthreads();
+  pdl_trigger();
+  float acc[TT];
+#pragma unroll
+  for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
+  const int sw = tid & 7;
+  for (int j = 0; j < nht; ++j) {
+    const int s = j % kExStages;
+    const uint32_t par = (uint32_t)(j / kExStages) & 1u;
+    if (!mbar_wait(&full[s], par)) {
+      if (tid == 0) atomicOr(a.status, kStatusCopyTimeout);
+      mbar_wait(&full[s], par);  // the copy may still land: wait once more
+    }
+    const uint4* row = reinterpret_cast<const uint4*>(ring + s * kExTile + tid * 128);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 q = row[c ^ sw];
+      const int h0 = j * HPT + c * EPC;
+      float w[EPC];
+      if constexpr (F32) {
+        w[0] = __uint_as_float(q.x); w[1] = __uint_as_float(q.y);
+        w[2] = __uint_as_float(q.z); w[EPC - 1] = __uint_as_float(q.w);
+      } else {
+        const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          w[2 * jj] = __uint_as_float(qq[jj] << 16);
+          w[2 * jj + 1] = __uint_as_float(qq[jj] & 0xFFFF0000u);
+        }
+      }
+      if constexpr (TT == 1) {
+        float xv[EPC];
+#pragma unroll
+        for (int u = 0; u < EPC; u += 4) {
+          const float4 x4 = reinterpret_cast<const float4*>(xs + h0)[u >> 2];
+          xv[u] = x4.x; xv[u + 1] = x4.y; xv[u + 2] = x4.z; xv[u + 3] = x4.w;
+        }
+#pragma unroll
+        for (int jj = 0; jj < EPC; ++jj) acc[0] = __fadd_rn(acc[0], __fmul_rn(w[jj], xv[jj]));
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < EPC; ++jj) {
+          const float2* xp = reinterpret_cast<const float2*>(xs + (size_t)(h0 + jj) * TT);
+#pragma unroll
+          for (int t = 0; t < TT; t += 2) {
+            const float2 p2 = fmul2_rn(make_float2(w[jj], w[jj]), xp[t >> 1]);
+            const float2 s2 = fadd2_rn(make_float2(acc[t], acc[t + 1]), p2);
+            acc[t] = s2.x;
+            acc[t + 1] = s2.y;
+          }
+        }
+      }
+    }
+    __syncthreads();  // every thread is done with stage s
+    if (tid == 0 && j + kExStages < nht) {
+      mbar_arrive_expect(&full[s], kExTile);
+      bulk_load(ring + s * kExTile, src + (size_t)(j + kExStages) * kExTile, kExTile, &full[s]);
+    }
+  }
+  if (e < E) {
+    const float bias = a.bias != nullptr ? a.bias[e] : 0.0f;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      if (t0 + t < a.B) {
+        const float v = a.bias != nullptr ? __fadd_rn(acc[t], bias) : acc[t];
+        a.logits[(size_t)(t0 + t) * E + e] = v;
+        a.bounds[(size_t)(t0 + t) * E + e] = 0.0f;
+      }
+    }
+  }
+  TL_END(0);
+}
+
+// ----------------------------------------------------------------------------
 // logits
 // ----------------------------------------------------------------------------
 template <int EXP, int TOKS>
@@ -990,11 +1125,34 @@ size_t select_smem(const RouterGeom& g) {
   return xs + u;
 }
 
+template <int TT, bool F32>
+void launch_exact_t(const RouterArgs& a, cudaStream_t s) {
+  const dim3 grid((a.g.E + kExThreads - 1) / kExThreads, (a.B + TT - 1) / TT);
+  const size_t sm = (size_t)kExStages * kExTile + (size_t)TT * a.g.H * sizeof(float);
+  launch_pdl(router_exact_kernel<TT, F32>, grid, dim3(kExThreads), sm, s, a);
+}
+
+template <bool F32>
+void launch_exact(const RouterArgs& a, cudaStream_t s) {
+  // tokens per thread grow with the batch; the sequential sum's latency
+  // (H dependent adds) bounds small batches
+  if (a.B <= 16) launch_exact_t<1, F32>(a, s);
+  else if (a.B <= 64) launch_exact_t<2, F32>(a, s);
+  else launch_exact_t<4, F32>(a, s);
+}
+
 }  // namespace
 
+// 1-2 tokens: certified fast logits (the selection checks their bounds);
+// 3+ tokens: exact logits, one thread per (expert, token group).
 void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
-  if (a.B <= 2) launch_logits_t<1, 1>(a, s);
-  else launch_logits_t<2, 4>(a, s);
+  if (a.B <= 2) {
+    launch_logits_t<1, 1>(a, s);
+  } else if (a.g.f32w) {
+    launch_exact<true>(a, s);
+  } else {
+    launch_exact<false>(a, s);
+  }
   if (launches) *launches += 1;
 }
 
@@ -1007,6 +1165,12 @@ void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launche
 void init_router_attributes(int max_smem) {
   cudaFuncSetAttribute(router_logits_kernel<1, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_logits_kernel<2, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
