@@ -42,6 +42,9 @@ extern "C" {
 #define OSM_ROUTE_EXACT 0x1u      /* route every token on the exact path */
 #define OSM_RMSNORM_EXACT 0x2u    /* sequential RMSNorm sum (bit-exact)   */
 #define OSM_ADD_RESIDUAL 0x4u     /* out = residual + MoE(...)            */
+#define OSM_PREFILL_BF16 0x8u     /* experts as a 16-bit tensor-core grouped GEMM (tcgen05, fp16
+                                     operands, fp32 accumulation) for prefill-sized batches; outputs
+                                     within 2e-3 of the fp32 path; |x|, h < 65504 (status bit 5) */
 
 typedef struct osm_context osm_context;
 typedef struct osm_layer osm_layer;
@@ -82,7 +85,9 @@ int osm_context_synchronize(osm_context* ctx);
 /* Device status word accumulated by kernels since the last call (bit 0
  * non-finite router input, bit 1 invalid softmax/mass, bit 2 non-resident
  * expert, bit 3 bad slot, bit 4 a bounded wait on an asynchronous weight
- * copy gave up); the count of tokens routed on the exact path. */
+ * copy gave up, bit 5 an activation left the fp16 range on the
+ * OSM_PREFILL_BF16 path, whose outputs are then invalid); the count of tokens
+ * routed on the exact path. */
 int osm_context_status(osm_context* ctx, uint32_t* status,
                        uint64_t* exact_tokens);
 

@@ -40,6 +40,7 @@ struct Scratch {
   float* sgate = nullptr;
   uint4* xfrag = nullptr;
   float* xfsum8 = nullptr;
+  uint16_t* xbf = nullptr;      // bf16 copy of x (prefill path)
   unsigned int* ticket = nullptr;
   int* counts = nullptr;
   int* n_active = nullptr;
@@ -226,6 +227,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t o_ids = take(T * k * 4), o_w = take(T * k * 4), o_mass = take(T * 4);
   const size_t o_sg = take(T * 4);
   const size_t o_xf = take(T * (Kx / 8) * 32), o_xs = take(T * (Kx / 8) * 4);
+  const size_t o_xbf = take(T * H * 2);
   const size_t o_ticket = take(4), o_counts = take((E + 1) * 4), o_nact = take(4);
   const size_t o_act = take((E + 1) * sizeof(osm::ActEntry)), o_ntg = take(4);
   const size_t max_tg = P / osm::kTokGroup + E + 2;
@@ -264,6 +266,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.sgate = reinterpret_cast<float*>(b + o_sg);
   s.xfrag = reinterpret_cast<uint4*>(b + o_xf);
   s.xfsum8 = reinterpret_cast<float*>(b + o_xs);
+  s.xbf = reinterpret_cast<uint16_t*>(b + o_xbf);
   s.ticket = reinterpret_cast<unsigned int*>(b + o_ticket);
   s.counts = reinterpret_cast<int*>(b + o_counts);
   s.n_active = reinterpret_cast<int*>(b + o_nact);
@@ -344,6 +347,8 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.sgate = s.sgate;
   a.xfrag = s.xfrag;
   a.xfsum8 = s.xfsum8;
+  a.xbf = nullptr;
+  a.chunk_pairs = 8;
   a.slot_of = L->slot_of;
   a.slab = L->slab ? L->slab->base : nullptr;
   a.slab_stride = L->slab ? L->slab->layout.stride : 0;
@@ -559,6 +564,56 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
   return check_launch(ctx, "combine");
 }
 
+// The bf16 tensor-core path (osm_prefill.cu) for prefill-sized batches; fills
+// the call-independent fields of pa.
+bool prefill_path(osm_layer* L, osm::PfArgs* pa, size_t* smem) {
+  if (!L->slab) return false;
+  osm_context* ctx = L->ctx;
+  const osm_expert_layout& R = L->slab->layout;
+  const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
+  *pa = osm::PfArgs{};
+  fill_sections(pa->gu, R, S, true);
+  fill_sections(pa->dn, R, S, false);
+  pa->H = L->g.H;
+  pa->Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
+  const int rmax = std::max(pa->gu.rows[0], L->shared_slot ? pa->gu.rows[1] : 0);
+  pa->nmt_gu = (rmax + 127) / 128;
+  pa->nmt_dn = (L->g.H + 127) / 128;
+  return osm::prefill_configure(*pa, L->shared_slot ? 1 : 0, ctx->max_smem, smem);
+}
+
+int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm::PfArgs pa,
+                size_t smem) {
+  osm_context* ctx = L->ctx;
+  Scratch& s = ctx->sc;
+  pa.xb = s.xbf;
+  pa.hb = reinterpret_cast<uint16_t*>(s.hfrag);
+  pa.pb = reinterpret_cast<uint16_t*>(s.partial);
+  pa.n_ch = s.n_ch;
+  pa.chunks = s.chunks;
+  pa.act = s.act;
+  pa.pair_tok = s.pair_tok;
+  pa.status = s.status;
+  {
+    Prof p(ctx, kKGateUp);
+    osm::launch_prefill_gateup(pa, ctx->num_sms, smem, ctx->stream, &ctx->launches);
+  }
+  int rc = check_launch(ctx, "prefill gate/up");
+  if (rc) return rc;
+  {
+    Prof p(ctx, kKDown);
+    osm::launch_prefill_down(pa, ctx->num_sms, smem, ctx->stream, &ctx->launches);
+  }
+  rc = check_launch(ctx, "prefill down");
+  if (rc) return rc;
+  {
+    Prof p(ctx, kKCombine);
+    osm::launch_combine_bf16(pa.pb, s.tp_pos, s.weights, L->shared_slot ? s.sgate : nullptr, residual,
+                             out, (int)T, L->g.H, L->g.k, ctx->stream, &ctx->launches);
+  }
+  return check_launch(ctx, "prefill combine");
+}
+
 int layer_ready(osm_layer* L, uint32_t T, bool need_slab) {
   if (!L || !L->ctx) return OSM_EINVAL;
   osm_context* ctx = L->ctx;
@@ -630,6 +685,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   osm::init_expert_attributes(max_smem);
   osm::init_gemv_attributes(ctx->max_smem);
   osm::init_grouped_attributes(ctx->max_smem);
+  osm::init_prefill_attributes(ctx->max_smem);
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {
     cudaStreamDestroy(ctx->own_stream);
@@ -1147,6 +1203,20 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   a.weights_out = w;
   a.mass_out = mass;
   a.sgate_out = sgate;
+  if (flags & OSM_PREFILL_BF16) {
+    osm::PfArgs pa;
+    size_t psm = 0;
+    if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
+    a.do_group = 1;
+    a.xfrag = nullptr;
+    a.xbf = ctx->sc.xbf;
+    a.chunk_pairs = 128;
+    ctx->cur_x = x;
+    launch_router_pair(ctx, a);
+    rc = check_launch(ctx, "router");
+    if (rc) return rc;
+    return run_prefill(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr, pa, psm);
+  }
   // one token: the expert kernels read the picks directly (no grouping, no
   // tensor-core fragments)
   osm::GemvArgs g;

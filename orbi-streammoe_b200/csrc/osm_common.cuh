@@ -18,6 +18,7 @@ constexpr uint32_t kStatusBadMass = 1u << 1;
 constexpr uint32_t kStatusNotResident = 1u << 2;
 constexpr uint32_t kStatusBadSlot = 1u << 3;
 constexpr uint32_t kStatusCopyTimeout = 1u << 4;  // a bounded wait on an async copy gave up
+constexpr uint32_t kStatusF16Range = 1u << 5;     // prefill: a value left the fp16 range
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);

@@ -52,6 +52,8 @@ struct RouterArgs {
   float* sgate_out;         // optional
   // fragments of x for the expert kernels
   uint4* xfrag;             // [B][H/8][2]
+  uint16_t* xbf;            // optional [B][H] fp16 copy of x (prefill)
+  int chunk_pairs;          // pairs per chunk of the chunk list (8, or 128 for prefill)
   float* xfsum8;            // [B][H/8]
   // grouping (done by the last block)
   int do_group;
@@ -221,6 +223,29 @@ struct CombineArgs {
   int B, H, k;
 };
 void launch_combine(const CombineArgs& a, cudaStream_t s, uint64_t* launches);
+
+// ---- prefill: 16-bit tensor-core (tcgen05, fp16 operands) grouped GEMM over 128-pair chunks ----
+struct PfArgs {
+  ProjSections gu, dn;
+  const uint16_t* xb;            // [T][H] fp16 activations (gate/up B operand)
+  uint16_t* hb;                  // [pairs][Imax] fp16 SwiGLU output (down B operand)
+  uint16_t* pb;                  // [pairs][H] fp16 expert outputs
+  const int* n_ch;               // chunks of up to 128 pairs of one active entry
+  const int2* chunks;
+  const ActEntry* act;
+  const int* pair_tok;
+  int H, Imax, nmt_gu, nmt_dn;   // M tiles (128 rows) per chunk
+  uint32_t* status;
+};
+bool prefill_configure(const PfArgs& a, int has_shared, int max_smem, size_t* smem);
+void init_prefill_attributes(int max_smem);
+void launch_prefill_gateup(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches);
+void launch_prefill_down(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches);
+// out[b] = sum over picks of w * pb[tp_pos[b][j]] in pick order, then sgate * the
+// shared row, then the residual
+void launch_combine_bf16(const uint16_t* pb, const int* tp_pos, const float* weights,
+                         const float* sgate, const float* residual, float* out, int B, int H,
+                         int k, cudaStream_t s, uint64_t* launches);
 
 void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float* w,
                     float eps, bool exact, cudaStream_t s, uint64_t* launches);

@@ -22,6 +22,7 @@
 //      sequential sum, stable top-k (reference_ops.cpp:130-212).
 //   Then the shared-expert scalar gate, the activation fragments and, in the
 //   last block, the grouping of (token, pick) pairs by expert.
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -553,14 +554,15 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
   }
   __syncthreads();
   if (a.chunks) {
-    // 8-token chunks of each active entry, in entry order
+    // chunks of chunk_pairs pairs of each active entry, in entry order
+    const int cp = a.chunk_pairs > 0 ? a.chunk_pairs : 8;
     for (int j = threadIdx.x; j < n_active; j += blockDim.x)
-      cur[j] = (cnt[expert_of[j]] + 7) / 8;
+      cur[j] = (cnt[expert_of[j]] + cp - 1) / cp;
     __syncthreads();
     const int n_ch = small_or_block_scan(cur, n_active, red);
     for (int j = threadIdx.x; j < n_active; j += blockDim.x) {
-      const int nc = (cnt[expert_of[j]] + 7) / 8;
-      for (int q = 0; q < nc; ++q) a.chunks[cur[j] + q] = make_int2(j, 8 * q);
+      const int nc = (cnt[expert_of[j]] + cp - 1) / cp;
+      for (int q = 0; q < nc; ++q) a.chunks[cur[j] + q] = make_int2(j, cp * q);
     }
     if (threadIdx.x == 0) *a.n_ch = n_ch;
     __syncthreads();
@@ -749,6 +751,15 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   }
   nonfinite = __syncthreads_or(nonfinite);
   OSM_STAMP(2);
+  if (a.xbf != nullptr) {  // fp16 copy of x for the prefill tensor-core path
+    bool over = false;
+    for (int h = tid; h < g.H; h += blockDim.x) {
+      const float v = xs[h];
+      over |= fabsf(v) >= 65504.0f;
+      a.xbf[(size_t)tok * g.H + h] = __half_as_ushort(__float2half_rn(v));
+    }
+    if (over) atomicOr(a.status, kStatusF16Range);
+  }
   if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
   const bool route = !nonfinite && !a.skip_route;  // block-uniform
   const int nsel = k + 1 <= g.E ? k + 1 : k;

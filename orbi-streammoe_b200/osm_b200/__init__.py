@@ -12,7 +12,7 @@ from __future__ import annotations
 import ctypes as C
 
 from . import _lib
-from ._lib import (OSM_ADD_RESIDUAL, OSM_RMSNORM_EXACT, OSM_ROUTE_EXACT,  # noqa: F401
+from ._lib import (OSM_ADD_RESIDUAL, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT, OSM_ROUTE_EXACT,  # noqa: F401
                    ExpertLayout, LayerDesc)
 
 
@@ -235,8 +235,11 @@ class Layer:
                                            _ptr(mass), OSM_ROUTE_EXACT if exact else 0), "route")
 
     def run_qwen_sparse_moe(self, x, tokens, out, ids=None, weights=None, mass=None,
-                            shared_gate=None, residual=None, exact_route=False):
-        flags = (OSM_ROUTE_EXACT if exact_route else 0) | (OSM_ADD_RESIDUAL if residual is not None else 0)
+                            shared_gate=None, residual=None, exact_route=False, prefill=False):
+        """prefill=True: experts as the bf16 tcgen05 grouped GEMM (outputs within
+        bf16 rounding of the fp32 path; for prefill-sized batches)."""
+        flags = ((OSM_ROUTE_EXACT if exact_route else 0) | (OSM_ADD_RESIDUAL if residual is not None else 0)
+                 | (OSM_PREFILL_BF16 if prefill else 0))
         self.ctx.check(lib().osm_moe_forward(self.h, _ptr(x), tokens, _ptr(out), _ptr(ids),
                                              _ptr(weights), _ptr(mass), _ptr(shared_gate),
                                              _ptr(residual), flags), "moe_forward")
@@ -248,8 +251,10 @@ class Layer:
                        "moe_experts")
 
     def run_sublayer(self, residual, tokens, out, normalized=None, ids=None, weights=None,
-                     mass=None, shared_gate=None, exact_route=False, exact_rmsnorm=False):
-        flags = (OSM_ROUTE_EXACT if exact_route else 0) | (OSM_RMSNORM_EXACT if exact_rmsnorm else 0)
+                     mass=None, shared_gate=None, exact_route=False, exact_rmsnorm=False,
+                     prefill=False):
+        flags = ((OSM_ROUTE_EXACT if exact_route else 0) | (OSM_RMSNORM_EXACT if exact_rmsnorm else 0)
+                 | (OSM_PREFILL_BF16 if prefill else 0))
         self.ctx.check(lib().osm_moe_sublayer_forward(self.h, _ptr(residual), tokens, _ptr(out),
                                                       _ptr(normalized), _ptr(ids), _ptr(weights),
                                                       _ptr(mass), _ptr(shared_gate), flags),

@@ -1,0 +1,65 @@
+"""Prefill path (OSM_PREFILL_BF16): the experts run as a 16-bit tcgen05 grouped
+GEMM (fp16 operands, fp32 accumulation) over 128-pair chunks.  Routing stays
+exact (ids bit-equal to the oracle's route_qwen_top_k); outputs are within
+16-bit rounding of the fp32 oracle: the 2e-3 bound for tensor-core prefill, as
+max|a - b| / max|b| per token.  Cases cover partial chunks and partial 128-row
+tiles, a shared expert spanning several chunks, no shared expert, and the Q3N
+hidden/intermediate sizes with top-10."""
+import numpy as np
+import pytest
+
+from gpu_util import MoeFixture, normwise_rel, require_cuda
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def torch():
+    return require_cuda()
+
+
+@pytest.mark.parametrize("H,E,I,K,T,shared,seed", [
+    (256, 16, 256, 4, 300, True, 91),
+    (512, 8, 256, 2, 200, False, 92),
+    (2048, 24, 512, 10, 96, True, 93),
+])
+def test_prefill_matches_oracle(torch, H, E, I, K, T, shared, seed):
+    f = MoeFixture(torch, H, E, I, K, seed=seed, shared=shared, max_tokens=T)
+    x = f.port.gen_normal(seed, 1, 1.0, T * H).reshape(T, H)
+    xd = torch.from_numpy(x).cuda()
+    out = torch.empty(T, H, device="cuda")
+    ids = torch.empty(T, K, dtype=torch.int32, device="cuda")
+    w = torch.empty(T, K, device="cuda")
+    f.layer.run_qwen_sparse_moe(xd, T, out, ids=ids, weights=w, prefill=True)
+    torch.cuda.synchronize()
+    o, ih = out.cpu().numpy(), ids.cpu().numpy().astype(np.uint32)
+    worst = 0.0
+    for t in range(T):
+        ref, rids, _, _, _ = f.oracle_token(x[t])
+        assert np.array_equal(ih[t], rids), t
+        worst = max(worst, normwise_rel(o[t], ref))
+    assert worst <= TOL, worst
+    assert f.ctx.status()[0] == 0
+
+
+def test_prefill_agrees_with_the_fp32_path(torch):
+    """The same call without the flag (fp32 grouped path) and with it agree to
+    16-bit rounding; routing and the shared gate are identical."""
+    H, E, I, K, T = 256, 12, 256, 3, 150
+    f = MoeFixture(torch, H, E, I, K, seed=94, max_tokens=T)
+    x = torch.from_numpy(f.port.gen_normal(94, 2, 1.0, T * H).reshape(T, H)).cuda()
+    outs, idss, sgs = [], [], []
+    for prefill in (False, True):
+        out = torch.empty(T, H, device="cuda")
+        ids = torch.empty(T, K, dtype=torch.int32, device="cuda")
+        sg = torch.empty(T, device="cuda")
+        f.layer.run_qwen_sparse_moe(x, T, out, ids=ids, shared_gate=sg, prefill=prefill)
+        outs.append(out.cpu().numpy())
+        idss.append(ids.cpu().numpy())
+        sgs.append(sg.cpu().numpy())
+    assert np.array_equal(idss[0], idss[1])
+    assert np.array_equal(sgs[0], sgs[1])
+    for t in range(T):
+        assert normwise_rel(outs[1][t], outs[0][t]) <= TOL
