@@ -70,8 +70,9 @@ def load_peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d.get("bf16_tflops", 1590.0),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 class ClockSampler:
@@ -136,7 +137,9 @@ class ClockSampler:
 # ----------------------------------------------------------------------------
 # our arm
 # ----------------------------------------------------------------------------
-def build_sublayer(torch, ctx, osm):
+def build_sublayer(torch, ctx, osm, zipf=True):
+    """The Q3N sublayer of configs 0-2 (config 1 adds the Zipf router bias;
+    config 2 routes without it)."""
     lay = osm.expert_layout(H, I, GROUP)
     slab = osm.Slab(ctx, lay, E)
     slab.generate(SEED, 1000, 0.02, 0, E)
@@ -155,7 +158,7 @@ def build_sublayer(torch, ctx, osm):
     ctx.check(osm.lib().osm_download(ctx.h, ctypes.c_void_p(shared.ctypes.data),
                                      ctypes.c_void_p(sh_slab.slot_ptr(0)), lay.stride))
     sh_slab.close()
-    bias = zipf_bias(E, ZIPF_S, SEED)
+    bias = zipf_bias(E, ZIPF_S, SEED) if zipf else None
     layer = osm.Layer(ctx, W, K, True, logit_bias=bias, shared_slot=shared, shared_layout=lay,
                       shared_gate=sg)
     layer.bind_slab(slab, np.arange(E, dtype=np.int32))
@@ -349,6 +352,135 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+# ----------------------------------------------------------------------------
+# 4096-token prefill on the tensor-core path (--workload prefill)
+# ----------------------------------------------------------------------------
+PF_T = 4096
+# expert GEMM flops per token: top-k routed gate/up/down + the shared expert
+PF_FLOP_PER_TOKEN = K * 3 * 2 * H * I + 3 * 2 * H * SHI
+
+
+def run_prefill(args, rank, world, local_rank):
+    import torch
+
+    import osm_b200 as osm
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    ctx = osm.Context(local_rank, max_tokens=PF_T)
+    ctx.set_stream(stream.cuda_stream)
+    layer = build_sublayer(torch, ctx, osm, zipf=False)[0]
+    x = torch.empty(PF_T, H, device=dev)
+    ctx.gen_normal(SEED, 7000 + rank, 1.0, x)
+    out = torch.empty(PF_T, H, device=dev)
+    hx = x.cpu().pin_memory()
+    hout = torch.empty(PF_T, H).pin_memory()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def call(e2e):
+        if e2e:
+            x.copy_(hx, non_blocking=True)
+        layer.run_qwen_sparse_moe(x, PF_T, out, prefill=True)
+        if e2e:
+            hout.copy_(out, non_blocking=True)
+
+    def timed_pass(steps, e2e):
+        ms = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            call(e2e)
+            b.record(stream)
+            b.synchronize()
+            ms += a.elapsed_time(b)
+        return ms
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    gpu_uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local_rank))
+    if gpu_uuid and not gpu_uuid.startswith("GPU-") and len(gpu_uuid) > 8:
+        gpu_uuid = "GPU-" + gpu_uuid
+    clocks = ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else str(local_rank))
+    timed_pass(args.warmup, False)
+    timed_pass(max(1, args.warmup // 2), True)
+    ctx.status()
+    clocks.start()
+    barrier()
+    torch.cuda.synchronize()
+    l0 = ctx.launches
+    total_ms = timed_pass(args.steps, False)
+    barrier()
+    launches = ctx.launches - l0
+    total_ms_e2e = timed_pass(args.steps, True)
+    barrier()
+    ctx.profile_read()
+    ctx.profile(True)
+    prof_steps = max(1, min(args.steps, 10))
+    for _ in range(prof_steps):
+        flush.zero_()
+        call(False)
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    clk = clocks.stop()
+    status, exact_tokens = ctx.status()
+    if status:
+        raise RuntimeError(f"device status {status} during the prefill benchmark")
+    total_ms = max_over_ranks(total_ms)
+    total_ms_e2e = max_over_ranks(total_ms_e2e)
+    value = world * PF_T * args.steps / (total_ms / 1e3)
+    e2e_value = world * PF_T * args.steps / (total_ms_e2e / 1e3)
+    peaks = load_peaks()
+    gemm_ms = (prof.get("proj_gate_up", (0.0, 0))[0] + prof.get("proj_down", (0.0, 0))[0]) / prof_steps
+    tflops = PF_T * PF_FLOP_PER_TOKEN / (gemm_ms / 1e3) / 1e12
+    kernels = {k: {"ms_per_call": round(v[0] / prof_steps, 4), "launches": int(v[1]),
+                   "share": round(v[0] / sum(x[0] for x in prof.values()), 3)} for k, v in prof.items()}
+    return {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 operands, fp32 accumulation (experts); fp32 exact routing",
+        "data": "synthetic (seeded N(0,0.02) weights, reference quantiser, bf16 scale/bias; x~N(0,1))",
+        "config": {"workload": "configs[2]: Qwen3-Next-80B-A3B routed-MoE sublayer, 4096-token prefill, "
+                               "uniform routing (no router bias), tcgen05 grouped GEMM",
+                   "tokens_per_step": PF_T, "hidden": H, "experts": E, "top_k": K,
+                   "moe_inter": I, "shared_inter": SHI,
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
+                   "timing": "sum of per-call CUDA-event intervals on the launching stream",
+                   "exact_route_tokens": int(exact_tokens), "kernels": kernels},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": PF_T * H * 4, "d2h_bytes_per_step": PF_T * H * 4},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": "pf_gemm (gate/up + down)",
+                     "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops"], 3), "traffic": None,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, burst)"},
+        "clocks": clk,
+    }
+
+
 def cpu_baseline_leg(torch, ctx, slab, W, sg, bias, shared, xs, osm):
     """The reference CPU path on the host cores on a bounded sample (the B=32
     batch of the sweep), token-parallel over all threads."""
@@ -431,9 +563,10 @@ def run_reference(args, rank, world):
     }
 
 
-def run_single(B: int, reps: int):
+def run_single(B: int, reps: int, prefill: bool = False):
     """A few calls of one batch size on the bench sublayer: the small case
-    for ncu captures of one kernel."""
+    for ncu captures of one kernel (prefill: the config-2 sublayer, no router
+    bias, on the tensor-core prefill path)."""
     import torch
 
     import osm_b200 as osm
@@ -443,12 +576,12 @@ def run_single(B: int, reps: int):
     torch.cuda.set_stream(stream)
     ctx = osm.Context(0, max_tokens=max(SWEEP + (B,)))
     ctx.set_stream(stream.cuda_stream)
-    layer = build_sublayer(torch, ctx, osm)[0]
+    layer = build_sublayer(torch, ctx, osm, zipf=not prefill)[0]
     x = torch.empty(B, H, device="cuda")
     ctx.gen_normal(SEED, 5000 + B, 1.0, x)
     out = torch.empty(B, H, device="cuda")
     for _ in range(reps):
-        layer.run_qwen_sparse_moe(x, B, out)
+        layer.run_qwen_sparse_moe(x, B, out, prefill=prefill)
     torch.cuda.synchronize()
     print(json.dumps({"single": B, "reps": reps, "status": list(ctx.status())}))
 
@@ -462,10 +595,14 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--single", type=int, default=0,
                     help="profiling driver: run REPS calls of this many tokens and exit")
+    ap.add_argument("--prefill", action="store_true",
+                    help="with --single: the config-2 sublayer on the tensor-core prefill path")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
+                    help="decode: configs[1] sweep (the headline line); prefill: configs[2]")
     args = ap.parse_args()
     if args.single:
-        run_single(args.single, args.reps)
+        run_single(args.single, args.reps, args.prefill)
         return
     args.warmup = max(3, args.warmup)
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -485,7 +622,10 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        if args.workload == "prefill":
+            line = run_prefill(args, rank, world, local_rank)
+        else:
+            line = run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch

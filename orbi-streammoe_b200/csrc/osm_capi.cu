@@ -366,6 +366,7 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.n_ch = s.n_ch;
   a.chunks = s.chunks;
   a.cursor = s.cursor;
+  a.defer_scatter = (size_t)T * (L->g.k + 1) > 8192 ? 1 : 0;  // grid-wide pair scatter
   a.status = s.status;
   a.exact_count = s.exact_count;
   a.pick_ptr = L->slab ? s.pick_ptr : nullptr;

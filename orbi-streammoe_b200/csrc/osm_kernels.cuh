@@ -62,7 +62,7 @@ struct RouterArgs {
   uint64_t slab_stride;
   const uint8_t* shared_slot;  // null without shared expert
   unsigned int* ticket;
-  int* counts;              // [E+1] scratch (zeroed by the last block)
+  int* counts;              // [E+1] first pair position of each expert (deferred scatter)
   int* n_active;
   ActEntry* act;            // [E+1]
   int* n_tg;                // token groups of the call
@@ -73,7 +73,8 @@ struct RouterArgs {
   int* tp_pos;              // (token, pick) -> pair position
   int* n_ch;                // 8-token chunks of the call (null: not built)
   int2* chunks;             // chunk -> {active entry, first token within it}
-  int* cursor;              // [E+1]
+  int* cursor;              // [E+1] pairs placed so far per expert (deferred scatter)
+  int defer_scatter;        // pairs placed by scatter_pairs_kernel, not the last select block
   uint32_t* status;
   unsigned long long* exact_count;
   // slot base of each pick (null: bad id or not resident), written for the

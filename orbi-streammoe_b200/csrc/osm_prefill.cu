@@ -5,7 +5,8 @@
 // SwiGLU -> down GEMV, weighted sum in pick order, plus the sigmoid-gated
 // shared expert) runs as a token-sorted grouped GEMM.  Pairs (token, pick) are
 // grouped by expert into chunks of up to 128; an item is (chunk, 128 weight
-// rows).  Per 64-wide K tile, 128 worker threads (one per weight row):
+// rows).  Per 64-wide K tile, 256 worker threads (two per weight row, each
+// with half of the tile's K range):
 //   * copy the tile's Q4 rows (MLX affine, eight nibbles per u32, LSB first:
 //     reference_ops.cpp:47-63) and the chunk's fp16 activation rows into a
 //     6-stage ring (cp.async, four tiles ahead);
@@ -37,7 +38,7 @@
 namespace osm {
 namespace {
 
-constexpr int kPfThreads = 128;            // one thread per weight row of the item
+constexpr int kPfThreads = 256;            // two threads per weight row of the item
 constexpr int kPfM = 128;                  // weight rows per item (MMA M)
 constexpr int kPfN = 128;                  // pairs per chunk (MMA N <= 128)
 constexpr int kPfStages = 6;               // copy ring depth (K tiles)
@@ -204,12 +205,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
   // ---- copy side: walks the same K tiles kPfAhead tiles ahead ----
   PfItem li;
   int litem = pf_next<DOWN>(a, i0, i1, li), lkt = 0;
-  int tok[8];
+  const int row = t & (kPfM - 1), kh = t >> 7;  // weight row, half of the K tile
+  int tok[4];
   auto load_tok = [&]() {
     if (DOWN || litem >= i1) return;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int n = (t >> 3) + 16 * j;
+    for (int j = 0; j < 4; ++j) {
+      const int n = (t >> 3) + 32 * j;
       tok[j] = n < li.ntok ? a.pair_tok[li.pos0 + n] : 0;
     }
   };
@@ -217,22 +219,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
   auto issue_load = [&](uint32_t step) {
     if (litem < i1) {
       const int st = (int)(step % kPfStages);
-      unsigned char* qdst = Qbuf + (size_t)st * 2 * kPfQTile + t * 32;
+      // this thread's 16 bytes (32 nibbles) of its row: it dequantises them itself
+      unsigned char* qdst = Qbuf + (size_t)st * 2 * kPfQTile + row * 32 + kh * 16;
       unsigned char* bdst = Bbuf + (size_t)st * kPfBTile;
-      if (t < li.nrows) {
+      if (row < li.nrows) {
         const size_t rowb = DOWN ? (size_t)(a.dn.K[li.kind] >> 1) : (size_t)(a.H >> 1);
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
           const uint64_t off = DOWN ? a.dn.w[li.kind] : (m ? a.gu.w2[li.kind] : a.gu.w[li.kind]);
-          const uint8_t* src = li.ptr + off + (size_t)(li.r0 + t) * rowb + (size_t)lkt * 32;
-          cp16(qdst + m * kPfQTile, src);
-          cp16(qdst + m * kPfQTile + 16, src + 16);
+          cp16(qdst + m * kPfQTile, li.ptr + off + (size_t)(li.r0 + row) * rowb + (size_t)lkt * 32 + kh * 16);
         }
       }
       const int c = t & 7;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int n = (t >> 3) + 16 * j;
+      for (int j = 0; j < 4; ++j) {
+        const int n = (t >> 3) + 32 * j;
         if (n < li.ntok) {
           const uint16_t* src = DOWN ? a.hb + (size_t)(li.pos0 + n) * a.Imax + lkt * 64 + c * 8
                                      : a.xb + (size_t)tok[j] * a.H + lkt * 64 + c * 8;
@@ -262,7 +263,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
       off = arr == 0 ? a.gu.s[it.kind] : arr == 1 ? a.gu.b[it.kind] : arr == 2 ? a.gu.s2[it.kind] : a.gu.b2[it.kind];
       G = a.H >> 6;
     }
-    return it.ptr + off + (size_t)(it.r0 + t) * G * 2 + (size_t)kb * 2;
+    return it.ptr + off + (size_t)(it.r0 + row) * G * 2 + (size_t)kb * 2;
   };
   uint2 sc_cur[NARR], sc_nxt[NARR];
 #pragma unroll
@@ -270,7 +271,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
     sc_cur[r] = make_uint2(0u, 0u);
     sc_nxt[r] = make_uint2(0u, 0u);
   }
-  if (citem < i1 && t < ci.nrows)
+  if (citem < i1 && row < ci.nrows)
 #pragma unroll
     for (int r = 0; r < NARR; ++r) sc_cur[r] = ld_nc_u2(scale_ptr(ci, r, 0));
   uint32_t s = 0, nacc = 0;
@@ -282,10 +283,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
     for (int kb = 0; kb < ci.nk; kb += 4) {
       // the next four groups' scales, one block ahead
       if (kb + 4 < ci.nk) {
-        if (t < ci.nrows)
+        if (row < ci.nrows)
 #pragma unroll
           for (int r = 0; r < NARR; ++r) sc_nxt[r] = ld_nc_u2(scale_ptr(ci, r, kb + 4));
-      } else if (nitem < i1 && t < ni.nrows) {
+      } else if (nitem < i1 && row < ni.nrows) {
 #pragma unroll
         for (int r = 0; r < NARR; ++r) sc_nxt[r] = ld_nc_u2(scale_ptr(ni, r, 0));
       }
@@ -303,9 +304,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
         }
         issue_load(s + kPfAhead);
         cp_wait_pf<kPfAhead>();  // this thread's copies of step s have landed
-        __syncthreads();         // everyone's
-        // dequantise this row's 64 weights of each matrix
-        const unsigned char* qrow = Qbuf + (size_t)st * 2 * kPfQTile + t * 32;
+        // dequantise this thread's 32 weights of its row in each matrix (the
+        // Q4 bytes it copied itself; the activation rows are covered by the
+        // barrier before the MMAs)
+        const unsigned char* qrow = Qbuf + (size_t)st * 2 * kPfQTile + row * 32 + kh * 16;
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
           const uint2 sv = sc_cur[2 * m], bv = sc_cur[2 * m + 1];
@@ -313,12 +315,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
           const uint32_t b16 = ((kk < 2 ? bv.x : bv.y) >> ((kk & 1) * 16)) & 0xFFFFu;
           const __half2 s2 = bf16_to_h2(s16), b2 = bf16_to_h2(b16);
           const uint4 w0 = *reinterpret_cast<const uint4*>(qrow + m * kPfQTile);
-          const uint4 w1 = *reinterpret_cast<const uint4*>(qrow + m * kPfQTile + 16);
-          const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-          unsigned char* arow = Abuf + (size_t)((s & 1) * 2 + m) * kPfATile + t * 128;
+          const uint32_t wd[4] = {w0.x, w0.y, w0.z, w0.w};
+          unsigned char* arow = Abuf + (size_t)((s & 1) * 2 + m) * kPfATile + row * 128;
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<uint4*>(arow + ((c ^ (t & 7)) << 4)) = dequant8(wd[c], s2, b2);
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(arow + (((4 * kh + c) ^ (row & 7)) << 4)) = dequant8(wd[c], s2, b2);
         }
         // generic-proxy writes (cp.async, stores) -> the tensor core's async proxy
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -347,15 +348,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
     }
     ++nacc;
     tc_fence_after();
-    const int row = warp * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    // warp w reads tensor-memory lanes 32 (w % 4) .. +31; warps w and w + 4
+    // take alternate 16-column blocks
+    const int erow = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     bool over = false;
-    for (int c0 = 0; c0 < npad; c0 += 16) {
+    for (int c0 = 16 * (warp >> 2); c0 < npad; c0 += 32) {
       uint32_t g[16], u[16];
       tc_ld16(lane_base + (uint32_t)c0, g);
       if (!DOWN) tc_ld16(lane_base + 128u + (uint32_t)c0, u);
       tc_wait_ld();
-      if (row < ci.nrows) {
+      if (erow < ci.nrows) {
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           const int n = c0 + j;
@@ -364,8 +367,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
                                  : __fmul_rn(ref_silu(__uint_as_float(g[j])), __uint_as_float(u[j]));
             over |= !(fabsf(v) < 65504.0f);
             const uint16_t hv = __half_as_ushort(__float2half_rn(v));
-            if (DOWN) a.pb[(size_t)(ci.pos0 + n) * a.H + ci.r0 + row] = hv;
-            else a.hb[(size_t)(ci.pos0 + n) * a.Imax + ci.r0 + row] = hv;
+            if (DOWN) a.pb[(size_t)(ci.pos0 + n) * a.H + ci.r0 + erow] = hv;
+            else a.hb[(size_t)(ci.pos0 + n) * a.Imax + ci.r0 + erow] = hv;
           }
         }
       }

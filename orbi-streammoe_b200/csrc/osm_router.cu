@@ -504,13 +504,24 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     actidx[E] = 0;
     cnt[E] = B;
   }
-  for (int p = threadIdx.x; p < B * k; p += blockDim.x) {
-    const uint32_t e = __ldcg(a.ids + p);
-    if (e >= (uint32_t)E) {
-      atomicOr(a.status, kStatusBadSlot);
-      continue;
+  // picks are read eight per thread ahead of their atomics
+  for (int p0 = threadIdx.x; p0 < B * k; p0 += 8 * blockDim.x) {
+    uint32_t ev[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int p = p0 + u * blockDim.x;
+      ev[u] = p < B * k ? __ldcg(a.ids + p) : 0xFFFFFFFFu;
     }
-    if (atomicAdd(&cnt[e], 1) == 0) actidx[e] = atomicAdd(&s_nact, 1);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (p0 + u * (int)blockDim.x >= B * k) break;
+      const uint32_t e = ev[u];
+      if (e >= (uint32_t)E) {
+        atomicOr(a.status, kStatusBadSlot);
+        continue;
+      }
+      if (atomicAdd(&cnt[e], 1) == 0) actidx[e] = atomicAdd(&s_nact, 1);
+    }
   }
   __syncthreads();
   const int n_active = s_nact;
@@ -567,22 +578,42 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     if (threadIdx.x == 0) *a.n_ch = n_ch;
     __syncthreads();
   }
-  for (int i = threadIdx.x; i < NE; i += blockDim.x) cur[i] = 0;
-  __syncthreads();
-  for (int p = threadIdx.x; p < B * k; p += blockDim.x) {
-    const uint32_t e = __ldcg(a.ids + p);
-    if (e >= (uint32_t)E) continue;
-    const int pos = off[actidx[e]] + atomicAdd(&cur[e], 1);
-    a.pair_tok[pos] = p / k;
-    a.pair_pick[pos] = p % k;
-    if (a.tp_pos) a.tp_pos[(p / k) * (k + has_sh) + p % k] = pos;
-  }
-  if (has_sh)
-    for (int t = threadIdx.x; t < B; t += blockDim.x) {
-      a.pair_tok[off[0] + t] = t;
-      a.pair_pick[off[0] + t] = k;
-      if (a.tp_pos) a.tp_pos[t * (k + 1) + k] = off[0] + t;
+  if (a.defer_scatter) {
+    // many pairs: each expert's first position and a zero cursor for
+    // scatter_pairs_kernel, which places the pairs across the whole GPU
+    for (int e = threadIdx.x; e < NE; e += blockDim.x) {
+      a.counts[e] = actidx[e] >= 0 ? off[actidx[e]] : 0;
+      a.cursor[e] = 0;
     }
+  } else {
+    for (int i = threadIdx.x; i < NE; i += blockDim.x) cur[i] = 0;
+    __syncthreads();
+    for (int p0 = threadIdx.x; p0 < B * k; p0 += 8 * blockDim.x) {
+      uint32_t ev[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int p = p0 + u * blockDim.x;
+        ev[u] = p < B * k ? __ldcg(a.ids + p) : 0xFFFFFFFFu;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int p = p0 + u * blockDim.x;
+        if (p >= B * k) break;
+        const uint32_t e = ev[u];
+        if (e >= (uint32_t)E) continue;
+        const int pos = off[actidx[e]] + atomicAdd(&cur[e], 1);
+        a.pair_tok[pos] = p / k;
+        a.pair_pick[pos] = p % k;
+        if (a.tp_pos) a.tp_pos[(p / k) * (k + has_sh) + p % k] = pos;
+      }
+    }
+    if (has_sh)
+      for (int t = threadIdx.x; t < B; t += blockDim.x) {
+        a.pair_tok[off[0] + t] = t;
+        a.pair_pick[off[0] + t] = k;
+        if (a.tp_pos) a.tp_pos[t * (k + 1) + k] = off[0] + t;
+      }
+  }
   if (threadIdx.x == 0) {
     *a.n_active = n_active;
     *a.n_tg = n_tg;
@@ -679,7 +710,7 @@ __device__ __forceinline__ bool distinct_p(float hi, float lo, float mx) {
   return __fsub_rd(hi, lo) > 1e-6f + 3e-7f * (fabsf(hi - mx) + fabsf(lo - mx));
 }
 
-__global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a) {
+__global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArgs a) {
   extern __shared__ float4 smem4[];
   float* xs = reinterpret_cast<float*>(smem4);  // [H]
   char* uni = reinterpret_cast<char*>(xs + ((a.g.H + 3) & ~3));
@@ -1080,10 +1111,12 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
   if (s_flag != 3) return;
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
   OSM_STAMP(12);
+  TL_MARK(8);
   group_pairs(a, reinterpret_cast<int*>(uni), reinterpret_cast<int*>(red));
   if (tid == 0) *a.ticket = 0u;
   __syncthreads();
   OSM_STAMP(13);
+  TL_MARK(9);
   TL_END(1);
 #ifdef OSM_PHASE_PRINT
   if (tid == 0) {
@@ -1092,6 +1125,31 @@ __global__ void __launch_bounds__(kSelThreads) router_select_kernel(RouterArgs a
     printf("\n");
   }
 #endif
+}
+
+// Places (token, pick) pairs at their expert's next position (positions
+// inside an expert are arbitrary: every pair's result is independent of its
+// place), then the shared expert's pairs in token order.  One thread per pair.
+__global__ void __launch_bounds__(256) scatter_pairs_kernel(RouterArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int E = a.g.E, k = a.g.k, B = a.B;
+  const int has_sh = a.shared_slot != nullptr;
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p < B * k) {
+    const uint32_t e = __ldcg(a.ids + p);
+    if (e >= (uint32_t)E) return;
+    const int pos = __ldcg(a.counts + e) + atomicAdd(a.cursor + e, 1);
+    a.pair_tok[pos] = p / k;
+    a.pair_pick[pos] = p % k;
+    if (a.tp_pos) a.tp_pos[(p / k) * (k + has_sh) + p % k] = pos;
+  } else if (has_sh && p < B * k + B) {
+    const int t = p - B * k;
+    const int pos = __ldcg(a.counts + E) + t;
+    a.pair_tok[pos] = t;
+    a.pair_pick[pos] = k;
+    if (a.tp_pos) a.tp_pos[t * (k + 1) + k] = pos;
+  }
 }
 
 __global__ void __launch_bounds__(kSelThreads) group_kernel(RouterArgs a) {
@@ -1171,6 +1229,11 @@ void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launche
   const size_t sm = select_smem(a.g);
   launch_pdl(router_select_kernel, dim3(a.B), dim3(kSelThreads), sm, s, a);
   if (launches) *launches += 1;
+  if (a.defer_scatter && a.do_group) {
+    const int n = a.B * (a.g.k + 1);
+    launch_pdl(scatter_pairs_kernel, dim3((n + 255) / 256), dim3(256), 0, s, a);
+    if (launches) *launches += 1;
+  }
 }
 
 void init_router_attributes(int max_smem) {
@@ -1190,6 +1253,11 @@ void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
   const size_t sm = (size_t)5 * (a.g.E + 1) * sizeof(int);
   launch_pdl(group_kernel, dim3(1), dim3(kSelThreads), sm, s, a);
   if (launches) *launches += 1;
+  if (a.defer_scatter) {
+    const int n = a.B * (a.g.k + 1);
+    launch_pdl(scatter_pairs_kernel, dim3((n + 255) / 256), dim3(256), 0, s, a);
+    if (launches) *launches += 1;
+  }
 }
 
 }  // namespace osm
