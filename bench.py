@@ -46,9 +46,10 @@ S_GATEUP = 1179648   # gate + up sections
 S_DOWN = 589824
 S_ROUTER = E * H * 2
 S_SGATE = H * 2
-# Per-launch DRAM traffic of proj_gate_up, B=1 launch (ncu, see profiles/);
-# None until a capture exists for the current kernel.
-NCU_GATEUP_TRAFFIC_B1 = None
+# DRAM traffic (read + write) of one grouped gate/up launch at B = 256, from
+# the ncu capture summarised in profiles/grp_gateup_q3n_b256.md (algorithmic
+# bytes of that launch: 105.8 MB).
+NCU_GATEUP_TRAFFIC_B256 = 107_173_888 + 4_133_632
 
 
 def bf16_round(v: np.ndarray) -> np.ndarray:
@@ -313,9 +314,11 @@ def run_ours(args, rank, world, local_rank):
                          "frac_hbm": round(byt / us / 1e3 / peaks["hbm_gbs"], 3)}
     kernels = {k: {"ms": round(v[0], 3), "launches": int(v[1]),
                    "share": round(v[0] / sum(x[0] for x in prof.values()), 3)} for k, v in prof.items()}
-    traffic = None
-    if NCU_GATEUP_TRAFFIC_B1 is not None and dom_kind == "proj_gate_up":
-        traffic = NCU_GATEUP_TRAFFIC_B1
+    traffic, traffic_note = None, None
+    if dom_kind == "proj_gate_up":
+        traffic = NCU_GATEUP_TRAFFIC_B256
+        traffic_note = ("bytes of one B=256 launch (ncu); that launch's algorithmic bytes: "
+                        f"{kernel_bytes('proj_gate_up', 256, uniq[256])}")
     h2d = sum(B * H * 4 for B in SWEEP)
     line = {
         "metric": METRIC,
@@ -344,6 +347,7 @@ def run_ours(args, rank, world, local_rank):
         "roofline": {"bound": "hbm", "kernel": dom_kind, "achieved": round(achieved, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 3), "traffic": traffic,
+                     "traffic_note": traffic_note,
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
         "clocks": clk,
     }
