@@ -138,12 +138,10 @@ class ClockSampler:
 # ----------------------------------------------------------------------------
 # our arm
 # ----------------------------------------------------------------------------
-def build_sublayer(torch, ctx, osm, zipf=True):
-    """The Q3N sublayer of configs 0-2 (config 1 adds the Zipf router bias;
-    config 2 routes without it)."""
+def replicated_weights(torch, ctx, osm):
+    """Router weight, shared-expert gate row and shared-expert slot bytes (the
+    parts every rank holds), from the bench seeds."""
     lay = osm.expert_layout(H, I, GROUP)
-    slab = osm.Slab(ctx, lay, E)
-    slab.generate(SEED, 1000, 0.02, 0, E)
     sh_slab = osm.Slab(ctx, lay, 1)
     sh_slab.generate(SEED, 1000 + 3 * E, 0.02, 0, 1)
     buf = torch.empty(E * H, device="cuda")
@@ -159,6 +157,16 @@ def build_sublayer(torch, ctx, osm, zipf=True):
     ctx.check(osm.lib().osm_download(ctx.h, ctypes.c_void_p(shared.ctypes.data),
                                      ctypes.c_void_p(sh_slab.slot_ptr(0)), lay.stride))
     sh_slab.close()
+    return W, sg, shared
+
+
+def build_sublayer(torch, ctx, osm, zipf=True):
+    """The Q3N sublayer of configs 0-2 (config 1 adds the Zipf router bias;
+    config 2 routes without it)."""
+    lay = osm.expert_layout(H, I, GROUP)
+    slab = osm.Slab(ctx, lay, E)
+    slab.generate(SEED, 1000, 0.02, 0, E)
+    W, sg, shared = replicated_weights(torch, ctx, osm)
     bias = zipf_bias(E, ZIPF_S, SEED) if zipf else None
     layer = osm.Layer(ctx, W, K, True, logit_bias=bias, shared_slot=shared, shared_layout=lay,
                       shared_gate=sg)
@@ -373,21 +381,40 @@ def run_prefill(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.Stream(device=dev)
     torch.cuda.set_stream(stream)
-    ctx = osm.Context(local_rank, max_tokens=PF_T)
+    # N > 1: expert parallelism over the ranks (E/N experts each) on the same
+    # 4096 tokens, T/N routed per rank (strong scaling)
+    t_local = PF_T // world
+    ctx = osm.Context(local_rank, max_tokens=t_local * K * world if world > 1 else PF_T)
     ctx.set_stream(stream.cuda_stream)
-    layer = build_sublayer(torch, ctx, osm, zipf=False)[0]
-    x = torch.empty(PF_T, H, device=dev)
-    ctx.gen_normal(SEED, 7000 + rank, 1.0, x)
-    out = torch.empty(PF_T, H, device=dev)
+    x_all = torch.empty(PF_T, H, device=dev)
+    ctx.gen_normal(SEED, 7000, 1.0, x_all)
+    x = x_all[rank * t_local:(rank + 1) * t_local].contiguous()
+    del x_all
+    out = torch.empty(t_local, H, device=dev)
+    if world > 1:
+        from osm_b200 import ep as osm_ep
+
+        e_count = E // world
+        e0 = rank * e_count
+        lay = osm.expert_layout(H, I, GROUP)
+        slab = osm.Slab(ctx, lay, e_count)
+        slab.generate(SEED, 1000 + 3 * e0, 0.02, 0, e_count)
+        W, sg, shared = replicated_weights(torch, ctx, osm)
+        moe = osm_ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg)
+    else:
+        layer = build_sublayer(torch, ctx, osm, zipf=False)[0]
     hx = x.cpu().pin_memory()
-    hout = torch.empty(PF_T, H).pin_memory()
+    hout = torch.empty(t_local, H).pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
 
     def call(e2e):
         if e2e:
             x.copy_(hx, non_blocking=True)
-        layer.run_qwen_sparse_moe(x, PF_T, out, prefill=True)
+        if world > 1:
+            moe.forward(x, out)
+        else:
+            layer.run_qwen_sparse_moe(x, PF_T, out, prefill=True)
         if e2e:
             hout.copy_(out, non_blocking=True)
 
@@ -446,11 +473,13 @@ def run_prefill(args, rank, world, local_rank):
         raise RuntimeError(f"device status {status} during the prefill benchmark")
     total_ms = max_over_ranks(total_ms)
     total_ms_e2e = max_over_ranks(total_ms_e2e)
-    value = world * PF_T * args.steps / (total_ms / 1e3)
-    e2e_value = world * PF_T * args.steps / (total_ms_e2e / 1e3)
+    value = PF_T * args.steps / (total_ms / 1e3)
+    e2e_value = PF_T * args.steps / (total_ms_e2e / 1e3)
     peaks = load_peaks()
     gemm_ms = (prof.get("proj_gate_up", (0.0, 0))[0] + prof.get("proj_down", (0.0, 0))[0]) / prof_steps
-    tflops = PF_T * PF_FLOP_PER_TOKEN / (gemm_ms / 1e3) / 1e12
+    # this rank's expert GEMM work: its share of the routed pairs and the
+    # shared expert for its own tokens
+    tflops = t_local * PF_FLOP_PER_TOKEN / (gemm_ms / 1e3) / 1e12
     kernels = {k: {"ms_per_call": round(v[0] / prof_steps, 4), "launches": int(v[1]),
                    "share": round(v[0] / sum(x[0] for x in prof.values()), 3)} for k, v in prof.items()}
     return {
@@ -462,7 +491,7 @@ def run_prefill(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "fp16 operands, fp32 accumulation (experts); fp32 exact routing",
         "data": "synthetic (seeded N(0,0.02) weights, reference quantiser, bf16 scale/bias; x~N(0,1))",
@@ -470,12 +499,14 @@ def run_prefill(args, rank, world, local_rank):
                                "uniform routing (no router bias), tcgen05 grouped GEMM",
                    "tokens_per_step": PF_T, "hidden": H, "experts": E, "top_k": K,
                    "moe_inter": I, "shared_inter": SHI,
-                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "parallelism": (f"expert parallel x{world} ({E // world} experts and "
+                                   f"{t_local} tokens per rank, NCCL all-to-all dispatch/combine)"
+                                   if world > 1 else "single GPU"),
                    "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
                    "timing": "sum of per-call CUDA-event intervals on the launching stream",
                    "exact_route_tokens": int(exact_tokens), "kernels": kernels},
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": PF_T * H * 4, "d2h_bytes_per_step": PF_T * H * 4},
+                "h2d_bytes_per_step": t_local * H * 4, "d2h_bytes_per_step": t_local * H * 4},
         "gpu_launches": int(launches),
         "roofline": {"bound": "tensor", "kernel": "pf_gemm (gate/up + down)",
                      "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

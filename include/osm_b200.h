@@ -266,7 +266,8 @@ int osm_moe_forward(osm_layer* layer, const float* x_dev, uint32_t tokens,
                     const float* residual_dev, uint32_t flags);
 
 /* Expert half of osm_moe_forward for a routing already in device memory
- * (after osm_moe_route and host-side cache fills). */
+ * (after osm_moe_route and host-side cache fills).  OSM_PREFILL_BF16 selects
+ * the tensor-core prefill path as for osm_moe_forward. */
 int osm_moe_experts(osm_layer* layer, const float* x_dev, uint32_t tokens,
                     const uint32_t* ids_dev, const float* weights_dev,
                     float* out_dev, float* shared_gate_dev,

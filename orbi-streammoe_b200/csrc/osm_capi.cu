@@ -1250,10 +1250,20 @@ int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* id
   a.skip_route = 1;
   a.sgate_out = sgate;
   a.do_group = 1;
+  osm::PfArgs pa;
+  size_t psm = 0;
+  const bool prefill = (flags & OSM_PREFILL_BF16) != 0;
+  if (prefill) {
+    if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
+    a.xfrag = nullptr;
+    a.xbf = s.xbf;
+    a.chunk_pairs = 128;
+  }
   ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "expert grouping");
   if (rc) return rc;
+  if (prefill) return run_prefill(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr, pa, psm);
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
 }
 

@@ -244,8 +244,9 @@ class Layer:
                                              _ptr(weights), _ptr(mass), _ptr(shared_gate),
                                              _ptr(residual), flags), "moe_forward")
 
-    def run_experts(self, x, tokens, ids, weights, out, shared_gate=None, residual=None):
-        flags = OSM_ADD_RESIDUAL if residual is not None else 0
+    def run_experts(self, x, tokens, ids, weights, out, shared_gate=None, residual=None,
+                    prefill=False):
+        flags = (OSM_ADD_RESIDUAL if residual is not None else 0) | (OSM_PREFILL_BF16 if prefill else 0)
         self.ctx.check(lib().osm_moe_experts(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
                                              _ptr(out), _ptr(shared_gate), _ptr(residual), flags),
                        "moe_experts")

@@ -1,0 +1,132 @@
+"""Expert parallelism for prefill-sized batches (configs 2 and 3): one process
+per GPU, rank r owning experts [r E/N, (r+1) E/N) in its slab.
+
+Each rank routes its own tokens with the replicated router (ids exact as the
+single-GPU path), then:
+  1. sorts its (token, pick) pairs by the rank that owns the picked expert;
+  2. exchanges pair counts, then the pairs' activation rows (fp16) with the
+     owner-local expert id and routing weight, in one all-to-all each;
+  3. runs the owned experts on the rows it received (the tensor-core prefill
+     path, one pick per row, scaled by the routing weight);
+  4. sends the weighted rows back with the reverse all-to-all;
+  5. adds each token's rows in pick order, then the shared expert (replicated,
+     computed locally for the rank's own tokens) scaled by its sigmoid gate --
+     the accumulation order of run_qwen_sparse_moe_vulkan_accum
+     (src/model/routed_moe.cpp:396-404).
+
+The exchange steps are plain functions of tensors and a process group, so the
+index arithmetic runs unchanged on gloo ranks on the CPU; ExpertParallelMoE
+binds them to the library's kernels on CUDA ranks (NCCL over NVLink)."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def dispatch_plan(ids: torch.Tensor, e_local: int, world: int):
+    """Send order of the flattened (token, pick) pairs grouped by owner rank
+    (stable: token-major, then pick, inside each destination), pairs per
+    destination, and each pair's expert id local to its owner."""
+    flat = ids.reshape(-1).long()
+    owner = flat // e_local
+    if flat.numel() and int(owner.max()) >= world:
+        raise ValueError("expert id beyond the last rank's range")
+    order = torch.sort(owner, stable=True).indices
+    counts = torch.bincount(owner, minlength=world)
+    return order, counts, (flat % e_local)
+
+
+def exchange_counts(send_counts: torch.Tensor, group=None) -> torch.Tensor:
+    recv = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv, send_counts, group=group)
+    return recv
+
+
+def dispatch_rows(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, e_local: int, world: int,
+                  group=None, row_dtype=torch.float16):
+    """Steps 1-2: returns (received rows, their local expert ids, their routing
+    weights, state for combine_rows)."""
+    T, k = ids.shape
+    order, send_counts, local = dispatch_plan(ids, e_local, world)
+    recv_counts = exchange_counts(send_counts.to(x.device), group).cpu()
+    send_counts = send_counts.cpu()
+    ss, rs = send_counts.tolist(), recv_counts.tolist()
+    n_recv = int(sum(rs))
+    tok = torch.div(order, k, rounding_mode="floor")
+    send_x = x.index_select(0, tok).to(row_dtype).contiguous()
+    meta = torch.stack([local.index_select(0, order).to(torch.float32),
+                        w.reshape(-1).index_select(0, order).to(torch.float32)], dim=1).contiguous()
+    recv_x = torch.empty(n_recv, x.shape[1], dtype=row_dtype, device=x.device)
+    recv_meta = torch.empty(n_recv, 2, dtype=torch.float32, device=x.device)
+    dist.all_to_all_single(recv_x, send_x, rs, ss, group=group)
+    dist.all_to_all_single(recv_meta, meta, rs, ss, group=group)
+    state = (order, ss, rs, T, k)
+    return recv_x, recv_meta[:, 0].to(torch.int32), recv_meta[:, 1].contiguous(), state
+
+
+def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float16):
+    """Steps 4-5 (routed part): the weighted rows back to their tokens, summed
+    in pick order in fp32.  Returns [T, H]."""
+    order, ss, rs, T, k = state
+    H = y_recv.shape[1]
+    back = torch.empty(len(order), H, dtype=row_dtype, device=y_recv.device)
+    dist.all_to_all_single(back, y_recv.to(row_dtype).contiguous(), ss, rs, group=group)
+    y = torch.empty(T * k, H, dtype=torch.float32, device=y_recv.device)
+    y.index_copy_(0, order, back.to(torch.float32))
+    y = y.view(T, k, H)
+    acc = y[:, 0].clone()
+    for p in range(1, k):
+        acc.add_(y[:, p])
+    return acc
+
+
+class ExpertParallelMoE:
+    """The Q4 routed-MoE sublayer with its experts spread over the ranks of a
+    process group (NCCL, one GPU per rank).  `slab` holds this rank's experts
+    [e_first, e_first + e_count) in slots 0..e_count-1; the router weight, the
+    shared expert and its gate row are replicated."""
+
+    def __init__(self, ctx, W: np.ndarray, k: int, norm: bool, layout, slab, e_first: int,
+                 e_count: int, shared_slot: np.ndarray, shared_gate: np.ndarray, bias=None,
+                 group=None):
+        import osm_b200 as osm
+
+        self.ctx, self.k, self.group = ctx, k, group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.e_first, self.e_count = e_first, e_count
+        H = W.shape[1]
+        self.router = osm.Layer(ctx, W, k, norm, logit_bias=bias)
+        self.experts = osm.Layer(ctx, np.zeros((e_count, H), np.float32), 1, False)
+        self.experts.bind_slab(slab, np.arange(e_count, dtype=np.int32))
+        self.sh_slab = osm.Slab(ctx, layout, 1)
+        self._sh_host = torch.from_numpy(np.ascontiguousarray(shared_slot).reshape(-1)).pin_memory()
+        self.sh_slab.fill_async(0, self._sh_host.data_ptr())
+        self.sh_slab.fill_wait()
+        self.shared = osm.Layer(ctx, np.zeros((1, H), np.float32), 1, False)
+        self.shared.bind_slab(self.sh_slab, np.zeros(1, np.int32))
+        self.gate = torch.from_numpy(np.asarray(shared_gate, np.float32)).cuda()
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor, ids: torch.Tensor | None = None,
+                weights: torch.Tensor | None = None):
+        T, H = x.shape
+        dev = x.device
+        ids = ids if ids is not None else torch.empty(T, self.k, dtype=torch.int32, device=dev)
+        w = weights if weights is not None else torch.empty(T, self.k, device=dev)
+        self.router.route_qwen_top_k(x, T, ids, w)
+        recv_x, recv_ids, recv_w, state = dispatch_rows(x, ids, w, self.e_count, self.world, self.group)
+        n = recv_x.shape[0]
+        y_recv = torch.empty(n, H, device=dev)
+        if n:
+            self.experts.run_experts(recv_x.to(torch.float32).contiguous(), n,
+                                     recv_ids.view(n, 1).contiguous(), recv_w.view(n, 1), y_recv,
+                                     prefill=True)
+        routed = combine_rows(y_recv, state, self.group)
+        # shared expert, scaled by sigmoid(g . x), added last
+        sg = torch.sigmoid(x @ self.gate).view(T, 1).contiguous()
+        sh = torch.empty(T, H, device=dev)
+        self.shared.run_experts(x, T, torch.zeros(T, 1, dtype=torch.int32, device=dev), sg, sh,
+                                prefill=True)
+        torch.add(routed, sh, out=out)
+        return ids, w

@@ -1,0 +1,97 @@
+"""Expert parallelism over two GPUs (osm_b200.ep, NCCL): each rank owns half
+of the experts and routes half of the tokens; ids match the oracle exactly and
+outputs agree with the fp32 oracle within the prefill bound (2e-3, max|a-b| /
+max|b| per token).  Needs two visible GPUs (skipped otherwise)."""
+import os
+import sys
+
+import numpy as np
+import pytest
+
+from gpu_util import require_cuda
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+H, E, I, K, T, SEED = 256, 16, 256, 4, 160, 61
+
+
+def _worker(rank, world, port, q):
+    sys.path[:0] = [HERE, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "orbi-streammoe_b200")]
+    import torch
+    import torch.distributed as dist
+
+    import osm_b200 as osm
+    import pyoracle
+    from osm_b200 import ep
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        port_o = pyoracle.Oracle("port")
+        slots = np.stack([port_o.gen_expert_slot(SEED, 100 + 3 * e, 0.02, H, I) for e in range(E)])
+        shared = port_o.gen_expert_slot(SEED, 90, 0.02, H, I)
+        W = pyoracle.bf16_widen(port_o.bf16_round(port_o.gen_normal(SEED, 6, 0.02, E * H))).reshape(E, H)
+        sg = pyoracle.bf16_widen(port_o.bf16_round(port_o.gen_normal(SEED, 7, 0.02, H)))
+        x_all = port_o.gen_normal(SEED, 1, 1.0, T * H).reshape(T, H)
+        e_count, t_count = E // world, T // world
+        e0, t0 = rank * e_count, rank * t_count
+        ctx = osm.Context(rank, max_tokens=T * K)
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        lay = osm.expert_layout(H, I)
+        slab = osm.Slab(ctx, lay, e_count)
+        pinned = torch.from_numpy(np.ascontiguousarray(slots[e0:e0 + e_count]).reshape(-1)).pin_memory()
+        for e in range(e_count):
+            slab.fill_async(e, pinned.data_ptr() + e * lay.stride)
+        slab.fill_wait()
+        moe = ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg)
+        x = torch.from_numpy(x_all[t0:t0 + t_count]).cuda()
+        out = torch.empty(t_count, H, device="cuda")
+        ids, _ = moe.forward(x, out)
+        torch.cuda.synchronize()
+        o, ih = out.cpu().numpy(), ids.cpu().numpy().astype(np.uint32)
+        deq = {}
+        sh = port_o.dequant_slot(shared, H, I)
+        worst, ids_ok = 0.0, True
+        for t in range(t_count):
+            xt = x_all[t0 + t]
+            _, rids, _, _ = port_o.route_qwen_top_k(xt, W, K, True)
+            ids_ok &= bool(np.array_equal(ih[t], rids))
+            for e in rids:
+                if int(e) not in deq:
+                    deq[int(e)] = port_o.dequant_slot(slots[int(e)], H, I)
+            ref = port_o.moe_token(xt, W, K, True, {int(e): deq[int(e)] for e in rids}, shared=sh,
+                                   scalar_gate=sg)[0]
+            worst = max(worst, float(np.abs(o[t] - ref).max()) / float(np.abs(ref).max()))
+        q.put((rank, ids_ok, worst, ctx.status()[0]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ep_two_ranks_match_oracle():
+    torch = require_cuda()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = 29800 + os.getpid() % 100
+    procs = [mpc.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=5) for _ in range(2))
+    for rank, ids_ok, worst, status in res:
+        assert ids_ok, rank
+        assert worst <= 2e-3, (rank, worst)
+        assert status == 0, (rank, status)
