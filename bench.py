@@ -384,7 +384,7 @@ def run_prefill(args, rank, world, local_rank):
     # N > 1: expert parallelism over the ranks (E/N experts each) on the same
     # 4096 tokens, T/N routed per rank (strong scaling)
     t_local = PF_T // world
-    ctx = osm.Context(local_rank, max_tokens=t_local * K * world if world > 1 else PF_T)
+    ctx = osm.Context(local_rank, max_tokens=t_local * (K * world + 1) if world > 1 else PF_T)
     ctx.set_stream(stream.cuda_stream)
     x_all = torch.empty(PF_T, H, device=dev)
     ctx.gen_normal(SEED, 7000, 1.0, x_all)
@@ -397,7 +397,7 @@ def run_prefill(args, rank, world, local_rank):
         e_count = E // world
         e0 = rank * e_count
         lay = osm.expert_layout(H, I, GROUP)
-        slab = osm.Slab(ctx, lay, e_count)
+        slab = osm.Slab(ctx, lay, e_count + 1)  # + the shared expert's slot
         slab.generate(SEED, 1000 + 3 * e0, 0.02, 0, e_count)
         W, sg, shared = replicated_weights(torch, ctx, osm)
         moe = osm_ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg)

@@ -45,6 +45,8 @@ extern "C" {
 #define OSM_PREFILL_BF16 0x8u     /* experts as a 16-bit tensor-core grouped GEMM (tcgen05, fp16
                                      operands, fp32 accumulation) for prefill-sized batches; outputs
                                      within 2e-3 of the fp32 path; |x|, h < 65504 (status bit 5) */
+#define OSM_INPUT_F16 0x10u       /* osm_moe_experts with OSM_PREFILL_BF16: x_dev holds fp16 rows
+                                     [tokens][hidden] (layers without a shared expert) */
 
 typedef struct osm_context osm_context;
 typedef struct osm_layer osm_layer;
@@ -267,7 +269,8 @@ int osm_moe_forward(osm_layer* layer, const float* x_dev, uint32_t tokens,
 
 /* Expert half of osm_moe_forward for a routing already in device memory
  * (after osm_moe_route and host-side cache fills).  OSM_PREFILL_BF16 selects
- * the tensor-core prefill path as for osm_moe_forward. */
+ * the tensor-core prefill path as for osm_moe_forward; with OSM_INPUT_F16 the
+ * rows are already fp16 (as an expert-parallel exchange delivers them). */
 int osm_moe_experts(osm_layer* layer, const float* x_dev, uint32_t tokens,
                     const uint32_t* ids_dev, const float* weights_dev,
                     float* out_dev, float* shared_gate_dev,

@@ -584,10 +584,10 @@ bool prefill_path(osm_layer* L, osm::PfArgs* pa, size_t* smem) {
 }
 
 int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm::PfArgs pa,
-                size_t smem) {
+                size_t smem, bool x_given = false) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
-  pa.xb = s.xbf;
+  if (!x_given) pa.xb = s.xbf;
   pa.hb = reinterpret_cast<uint16_t*>(s.hfrag);
   pa.pb = reinterpret_cast<uint16_t*>(s.partial);
   pa.n_ch = s.n_ch;
@@ -1253,6 +1253,9 @@ int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* id
   osm::PfArgs pa;
   size_t psm = 0;
   const bool prefill = (flags & OSM_PREFILL_BF16) != 0;
+  const bool f16 = (flags & OSM_INPUT_F16) != 0;
+  if (f16 && (!prefill || L->shared_slot))
+    return fail(ctx, OSM_EINVAL, "experts: fp16 rows need OSM_PREFILL_BF16 and no shared expert");
   if (prefill) {
     if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
     a.xfrag = nullptr;
@@ -1260,10 +1263,24 @@ int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* id
     a.chunk_pairs = 128;
   }
   ctx->cur_x = x;
-  launch_router_pair(ctx, a);
+  if (f16) {
+    // the rows are the GEMM's operand already: only the grouping runs first
+    Prof p(ctx, kKRouterSelect);
+    osm::launch_group(a, ctx->stream, &ctx->launches);
+  } else {
+    launch_router_pair(ctx, a);
+  }
   rc = check_launch(ctx, "expert grouping");
   if (rc) return rc;
-  if (prefill) return run_prefill(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr, pa, psm);
+  if (prefill) {
+    const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
+    if (f16) {
+      osm::PfArgs pf = pa;
+      pf.xb = reinterpret_cast<const uint16_t*>(x);
+      return run_prefill(L, T, out, res, pf, psm, true);
+    }
+    return run_prefill(L, T, out, res, pa, psm);
+  }
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
 }
 

@@ -12,8 +12,8 @@ from __future__ import annotations
 import ctypes as C
 
 from . import _lib
-from ._lib import (OSM_ADD_RESIDUAL, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT, OSM_ROUTE_EXACT,  # noqa: F401
-                   ExpertLayout, LayerDesc)
+from ._lib import (OSM_ADD_RESIDUAL, OSM_INPUT_F16, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT,  # noqa: F401
+                   OSM_ROUTE_EXACT, ExpertLayout, LayerDesc)
 
 
 class OsmError(RuntimeError):
@@ -246,7 +246,11 @@ class Layer:
 
     def run_experts(self, x, tokens, ids, weights, out, shared_gate=None, residual=None,
                     prefill=False):
-        flags = (OSM_ADD_RESIDUAL if residual is not None else 0) | (OSM_PREFILL_BF16 if prefill else 0)
+        """prefill=True: tensor-core path; an fp16 x (torch.float16) is passed
+        as is (OSM_INPUT_F16, layers without a shared expert)."""
+        f16 = str(getattr(x, "dtype", "")) == "torch.float16"
+        flags = ((OSM_ADD_RESIDUAL if residual is not None else 0) | (OSM_PREFILL_BF16 if prefill else 0)
+                 | (OSM_INPUT_F16 if f16 else 0))
         self.ctx.check(lib().osm_moe_experts(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
                                              _ptr(out), _ptr(shared_gate), _ptr(residual), flags),
                        "moe_experts")

@@ -22,6 +22,7 @@ OSM_ROUTE_EXACT = 0x1
 OSM_RMSNORM_EXACT = 0x2
 OSM_ADD_RESIDUAL = 0x4
 OSM_PREFILL_BF16 = 0x8
+OSM_INPUT_F16 = 0x10
 OSM_PLAN_SUBLAYER = 0x100
 OSM_PLAN_PROFILE = 0x200
 

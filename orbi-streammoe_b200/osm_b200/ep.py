@@ -6,8 +6,10 @@ single-GPU path), then:
   1. sorts its (token, pick) pairs by the rank that owns the picked expert;
   2. exchanges pair counts, then the pairs' activation rows (fp16) with the
      owner-local expert id and routing weight, in one all-to-all each;
-  3. runs the owned experts on the rows it received (the tensor-core prefill
-     path, one pick per row, scaled by the routing weight);
+  3. runs the owned experts on the rows it received, together with its own
+     tokens routed to the shared expert (held in the slab's spare last slot,
+     weighted by its sigmoid gate): one tensor-core prefill call on the fp16
+     rows, one pick per row, each row scaled by its weight;
   4. sends the weighted rows back with the reverse all-to-all;
   5. adds each token's rows in pick order, then the shared expert (replicated,
      computed locally for the rank's own tokens) scaled by its sigmoid gate --
@@ -84,8 +86,10 @@ def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float1
 class ExpertParallelMoE:
     """The Q4 routed-MoE sublayer with its experts spread over the ranks of a
     process group (NCCL, one GPU per rank).  `slab` holds this rank's experts
-    [e_first, e_first + e_count) in slots 0..e_count-1; the router weight, the
-    shared expert and its gate row are replicated."""
+    [e_first, e_first + e_count) in slots 0..e_count-1 and has one more slot,
+    which receives the shared expert; the router weight, the shared expert and
+    its gate row are replicated.  The context's max_tokens must cover the rows
+    a rank can receive plus its own tokens."""
 
     def __init__(self, ctx, W: np.ndarray, k: int, norm: bool, layout, slab, e_first: int,
                  e_count: int, shared_slot: np.ndarray, shared_gate: np.ndarray, bias=None,
@@ -97,15 +101,15 @@ class ExpertParallelMoE:
         self.rank = dist.get_rank(group)
         self.e_first, self.e_count = e_first, e_count
         H = W.shape[1]
+        if slab.slots < e_count + 1:
+            raise ValueError("the slab needs one slot beyond the rank's experts (shared expert)")
         self.router = osm.Layer(ctx, W, k, norm, logit_bias=bias)
-        self.experts = osm.Layer(ctx, np.zeros((e_count, H), np.float32), 1, False)
-        self.experts.bind_slab(slab, np.arange(e_count, dtype=np.int32))
-        self.sh_slab = osm.Slab(ctx, layout, 1)
         self._sh_host = torch.from_numpy(np.ascontiguousarray(shared_slot).reshape(-1)).pin_memory()
-        self.sh_slab.fill_async(0, self._sh_host.data_ptr())
-        self.sh_slab.fill_wait()
-        self.shared = osm.Layer(ctx, np.zeros((1, H), np.float32), 1, False)
-        self.shared.bind_slab(self.sh_slab, np.zeros(1, np.int32))
+        slab.fill_async(e_count, self._sh_host.data_ptr())
+        slab.fill_wait()
+        # local experts 0..e_count-1, then the shared expert as local id e_count
+        self.experts = osm.Layer(ctx, np.zeros((e_count + 1, H), np.float32), 1, False)
+        self.experts.bind_slab(slab, np.arange(e_count + 1, dtype=np.int32))
         self.gate = torch.from_numpy(np.asarray(shared_gate, np.float32)).cuda()
 
     def forward(self, x: torch.Tensor, out: torch.Tensor, ids: torch.Tensor | None = None,
@@ -117,16 +121,14 @@ class ExpertParallelMoE:
         self.router.route_qwen_top_k(x, T, ids, w)
         recv_x, recv_ids, recv_w, state = dispatch_rows(x, ids, w, self.e_count, self.world, self.group)
         n = recv_x.shape[0]
-        y_recv = torch.empty(n, H, device=dev)
-        if n:
-            self.experts.run_experts(recv_x.to(torch.float32).contiguous(), n,
-                                     recv_ids.view(n, 1).contiguous(), recv_w.view(n, 1), y_recv,
-                                     prefill=True)
-        routed = combine_rows(y_recv, state, self.group)
-        # shared expert, scaled by sigmoid(g . x), added last
-        sg = torch.sigmoid(x @ self.gate).view(T, 1).contiguous()
-        sh = torch.empty(T, H, device=dev)
-        self.shared.run_experts(x, T, torch.zeros(T, 1, dtype=torch.int32, device=dev), sg, sh,
-                                prefill=True)
-        torch.add(routed, sh, out=out)
+        # received rows, then this rank's own tokens for the shared expert
+        rows = torch.cat([recv_x, x.to(recv_x.dtype)], dim=0).contiguous()
+        rid = torch.cat([recv_ids, torch.full((T,), self.e_count, dtype=torch.int32, device=dev)])
+        sg = torch.sigmoid(x @ self.gate)
+        rw = torch.cat([recv_w, sg]).contiguous()
+        y = torch.empty(n + T, H, device=dev)
+        self.experts.run_experts(rows, n + T, rid.view(-1, 1).contiguous(), rw.view(-1, 1), y,
+                                 prefill=True)
+        routed = combine_rows(y[:n], state, self.group)
+        torch.add(routed, y[n:], out=out)  # the shared expert last
         return ids, w

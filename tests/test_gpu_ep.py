@@ -43,10 +43,10 @@ def _worker(rank, world, port, q):
         x_all = port_o.gen_normal(SEED, 1, 1.0, T * H).reshape(T, H)
         e_count, t_count = E // world, T // world
         e0, t0 = rank * e_count, rank * t_count
-        ctx = osm.Context(rank, max_tokens=T * K)
+        ctx = osm.Context(rank, max_tokens=T * K + T)
         ctx.set_stream(torch.cuda.current_stream().cuda_stream)
         lay = osm.expert_layout(H, I)
-        slab = osm.Slab(ctx, lay, e_count)
+        slab = osm.Slab(ctx, lay, e_count + 1)
         pinned = torch.from_numpy(np.ascontiguousarray(slots[e0:e0 + e_count]).reshape(-1)).pin_memory()
         for e in range(e_count):
             slab.fill_async(e, pinned.data_ptr() + e * lay.stride)

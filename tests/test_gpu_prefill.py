@@ -63,3 +63,22 @@ def test_prefill_agrees_with_the_fp32_path(torch):
     assert np.array_equal(sgs[0], sgs[1])
     for t in range(T):
         assert normwise_rel(outs[1][t], outs[0][t]) <= TOL
+
+
+def test_prefill_experts_take_fp16_rows(torch):
+    """osm_moe_experts with fp16 rows (OSM_INPUT_F16, as an expert-parallel
+    exchange delivers them) equals the same call on fp32 rows, which the
+    library rounds to fp16 itself."""
+    H, E, I, K, T = 256, 8, 256, 2, 140
+    f = MoeFixture(torch, H, E, I, K, seed=95, shared=False, max_tokens=T)
+    x = torch.from_numpy(f.port.gen_normal(95, 3, 1.0, T * H).reshape(T, H)).cuda()
+    rs = np.random.RandomState(3)
+    ids = torch.from_numpy(np.stack([rs.permutation(E)[:K] for _ in range(T)]).astype(np.int32)).cuda()
+    w = torch.from_numpy(rs.rand(T, K).astype(np.float32)).cuda()
+    o32 = torch.empty(T, H, device="cuda")
+    o16 = torch.empty(T, H, device="cuda")
+    f.layer.run_experts(x, T, ids, w, o32, prefill=True)
+    f.layer.run_experts(x.half(), T, ids, w, o16, prefill=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o32, o16)
+    assert f.ctx.status()[0] == 0
