@@ -516,6 +516,147 @@ def run_prefill(args, rank, world, local_rank):
     }
 
 
+# ----------------------------------------------------------------------------
+# 48-layer batch-1 decode streaming experts from pinned host memory
+# into an 8 GB HBM cache (--workload stream)
+# ----------------------------------------------------------------------------
+STREAM_CACHE_BYTES = 8_000_000_000
+
+
+def run_stream(args, rank, world, local_rank):
+    import ctypes
+
+    import torch
+
+    import osm_b200 as osm
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    L = args.stream_layers
+    ctx = osm.Context(local_rank, max_tokens=1)
+    ctx.set_stream(stream.cuda_stream)
+    lay = osm.expert_layout(H, I, GROUP)
+    stride = lay.stride
+    # every layer's experts in pinned host memory, generated on the GPU layer by layer
+    host = torch.empty(L * E * stride, dtype=torch.uint8, pin_memory=True)
+    stage = osm.Slab(ctx, lay, E)
+    layers = []
+    for l in range(L):
+        seed = SEED + 7919 * (l + 1)
+        stage.generate(seed, 1000, 0.02, 0, E)
+        ctx.synchronize()
+        ctx.check(osm.lib().osm_download(ctx.h, ctypes.c_void_p(host.data_ptr() + l * E * stride),
+                                         ctypes.c_void_p(stage.slot_ptr(0)), E * stride))
+        sh = osm.Slab(ctx, lay, 1)
+        sh.generate(seed, 1000 + 3 * E, 0.02, 0, 1)
+        buf = torch.empty(E * H, device=dev)
+        ctx.gen_normal(seed, 1, 0.02, buf)
+        W = bf16_round(buf.cpu().numpy()).reshape(E, H)
+        g = torch.empty(H, device=dev)
+        ctx.gen_normal(seed, 2, 0.02, g)
+        sg = bf16_round(g.cpu().numpy())
+        ctx.synchronize()
+        shared = np.zeros(stride, np.uint8)
+        ctx.check(osm.lib().osm_download(ctx.h, ctypes.c_void_p(shared.ctypes.data),
+                                         ctypes.c_void_p(sh.slot_ptr(0)), stride))
+        sh.close()
+        layers.append(osm.Layer(ctx, W, K, True, logit_bias=zipf_bias(E, ZIPF_S, seed),
+                                shared_slot=shared, shared_layout=lay, shared_gate=sg))
+    stage.close()
+    slots = STREAM_CACHE_BYTES // stride
+    slab = osm.Slab(ctx, lay, slots)
+    for layer in layers:
+        layer.bind_slab(slab, np.full(E, -1, np.int32))
+    base = host.data_ptr()
+    cache = osm.ExpertCache(slab, slots * stride,
+                            source=lambda l, e: base + (l * E + e) * stride)
+    for l, layer in enumerate(layers):
+        cache.bind_layer(l, layer)
+    ones = torch.ones(H, device=dev)
+    bufs = [torch.empty(1, H, device=dev), torch.empty(1, H, device=dev)]
+    ctx.gen_normal(SEED, 9000, 1.0, bufs[0])
+
+    def token():
+        """One decode token through the stack: per layer one cached call
+        (route, picks to the host, residency, experts), then the output
+        RMS-normalised in place as the next layer's input.  Returns (ms,
+        exposed H2D ms)."""
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for l, layer in enumerate(layers):
+            x, out = bufs[l & 1], bufs[(l + 1) & 1]
+            layer.run_cached(cache, l, x, 1, out)
+            ctx.rms_norm(out, 1, H, ones, 1e-6)
+        if L & 1:
+            bufs.reverse()
+        t1.record(stream)
+        t1.synchronize()
+        return t0.elapsed_time(t1), cache.exposed_read()[0]
+
+    cache.time_copies(True)
+    for _ in range(args.warmup):
+        token()
+    s0 = cache.stats()
+    h2d0 = osm.lib().osm_slab_h2d_bytes(slab.h)
+    gpu_uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local_rank))
+    if gpu_uuid and not gpu_uuid.startswith("GPU-") and len(gpu_uuid) > 8:
+        gpu_uuid = "GPU-" + gpu_uuid
+    clocks = ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else str(local_rank))
+    clocks.start()
+    l0 = ctx.launches
+    tot_ms = exp_ms = 0.0
+    for _ in range(args.steps):
+        a, b = token()
+        tot_ms += a
+        exp_ms += b
+    launches = ctx.launches - l0
+    clk = clocks.stop()
+    s1 = cache.stats()
+    h2d = osm.lib().osm_slab_h2d_bytes(slab.h) - h2d0
+    status, _ = ctx.status()
+    if status:
+        raise RuntimeError(f"device status {status} during the streaming benchmark")
+    hits, misses = s1["hits"] - s0["hits"], s1["misses"] - s0["misses"]
+    value = args.steps / (tot_ms / 1e3)
+    peaks = load_peaks()
+    alg = L * sublayer_bytes(1, K)
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (independently seeded layers, reference quantiser, bf16 scale/bias)",
+        "config": {"workload": f"configs[4]: {L}-layer stack of Q3N sublayers, batch-1 decode, "
+                               "output RMS-normalised and fed back, per-layer Zipf(1.1) bias, experts "
+                               "in pinned host memory streamed into an HBM cache (LFU + recency)",
+                   "layers": L, "host_expert_bytes": L * E * stride, "cache_bytes": slots * stride,
+                   "cache_slots": int(slots),
+                   "timing": "per-token CUDA events on the launching stream (the host's wait "
+                             "for each layer's picks included); inputs: each token streams its "
+                             "layers' weights (>1 GB) through HBM",
+                   "cache_hit_rate": round(hits / max(1, hits + misses), 4),
+                   "cache_loads": int(s1["loads"] - s0["loads"]),
+                   "cache_evictions": int(s1["evictions"] - s0["evictions"]),
+                   "h2d_bytes_per_token": int(h2d // args.steps),
+                   "exposed_h2d_ms_per_token": round(exp_ms / args.steps, 4),
+                   "exposed_h2d_note": "compute-stream time from an acquire's copies being "
+                                       "issued to the stream's wait for them ending, summed "
+                                       "over layers (osm_cache_exposed_read)"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d // args.steps),
+                "d2h_bytes_per_step": L * K * 4},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "hbm", "kernel": "whole token (all layers)",
+                     "achieved": round(alg / (tot_ms / args.steps / 1e3) / 1e9, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(alg / (tot_ms / args.steps / 1e3) / 1e9 / peaks["hbm_gbs"], 4),
+                     "traffic": None,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
+        "clocks": clk,
+    }
+
+
 def cpu_baseline_leg(torch, ctx, slab, W, sg, bias, shared, xs, osm):
     """The reference CPU path on the host cores on a bounded sample (the B=32
     batch of the sweep), token-parallel over all threads."""
@@ -633,8 +774,11 @@ def main():
     ap.add_argument("--prefill", action="store_true",
                     help="with --single: the config-2 sublayer on the tensor-core prefill path")
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--workload", choices=("decode", "prefill"), default="decode",
-                    help="decode: configs[1] sweep (the headline line); prefill: configs[2]")
+    ap.add_argument("--workload", choices=("decode", "prefill", "stream"), default="decode",
+                    help="decode: configs[1] sweep (the headline line); prefill: configs[2]; "
+                         "stream: configs[4]")
+    ap.add_argument("--stream-layers", type=int, default=48,
+                    help="with --workload stream: layers in the stack")
     args = ap.parse_args()
     if args.single:
         run_single(args.single, args.reps, args.prefill)
@@ -659,6 +803,8 @@ def main():
     try:
         if args.workload == "prefill":
             line = run_prefill(args, rank, world, local_rank)
+        elif args.workload == "stream":
+            line = run_stream(args, rank, world, local_rank)
         else:
             line = run_ours(args, rank, world, local_rank)
     finally:

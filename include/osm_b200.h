@@ -220,6 +220,13 @@ int osm_cache_acquire(osm_cache* cache, uint32_t layer_id,
 int osm_cache_contains(const osm_cache* cache, uint32_t layer_id,
                        uint32_t expert);
 int osm_cache_stats(const osm_cache* cache, osm_cache_counts* out);
+/* Exposed-copy timing (the reference's config-4 "exposed H2D time"): with
+ * enable set, every acquire that copies brackets its copies with a pair of
+ * events on the compute stream, from their issue to the compute stream's
+ * wait for them ending.  osm_cache_exposed_read waits for the recorded pairs
+ * and returns their summed time in ms and their count, then starts over. */
+int osm_cache_time_copies(osm_cache* cache, int enable);
+int osm_cache_exposed_read(osm_cache* cache, double* ms, uint64_t* waits);
 
 /* ---- one MoE layer: the dense state QwenCheckpointSparseMoeLayer keeps
  *      (src/model/checkpoint_sparse_moe.cpp:112-220): router, shared expert
@@ -275,6 +282,22 @@ int osm_moe_experts(osm_layer* layer, const float* x_dev, uint32_t tokens,
                     const uint32_t* ids_dev, const float* weights_dev,
                     float* out_dev, float* shared_gate_dev,
                     const float* residual_dev, uint32_t flags);
+
+/* run_qwen_sparse_moe_vulkan_accum with its VulkanResidentExpertCache and
+ * layer index (include/orbi/streammoe/model/routed_moe.hpp:58-65): route,
+ * read the picks back to the host, make them resident through `cache` (one
+ * osm_cache_acquire in token-major pick order; misses are copied from the
+ * cache's host source on the slab's side stream), then run the experts and
+ * the shared expert.  `layer` must be bound to `cache` as `layer_id`.  The
+ * call returns once the picks are known and the copies and kernels are
+ * queued; outputs as for osm_moe_forward (ids_dev, weights_dev,
+ * shared_gate_dev may be NULL).  Flags: OSM_ROUTE_EXACT, OSM_PREFILL_BF16,
+ * OSM_ADD_RESIDUAL. */
+int osm_moe_forward_cached(osm_layer* layer, osm_cache* cache, uint32_t layer_id,
+                           const float* x_dev, uint32_t tokens, float* out_dev,
+                           uint32_t* ids_dev, float* weights_dev,
+                           float* shared_gate_dev, const float* residual_dev,
+                           uint32_t flags);
 
 /* QwenCheckpointMoeSublayer::run (include/orbi/streammoe/model/
  * checkpoint_moe_sublayer.hpp:55-58): normalized = RMSNorm(residual),

@@ -9,9 +9,11 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <set>
 #include <new>
 #include <string>
 #include <thread>
+#include <tuple>
 #include <unordered_map>
 #include <vector>
 
@@ -102,6 +104,9 @@ struct osm_context {
   const float* cur_x = nullptr;  // activations of the call in flight (expert kernels)
   std::vector<cudaEvent_t> ev_pool;
   std::vector<ProfRec> recs;
+  uint32_t* picks_host = nullptr;   // pinned: the picks a cached call reads back
+  size_t picks_cap = 0;
+  cudaEvent_t picks_ev = nullptr;
 };
 
 struct osm_slab {
@@ -112,6 +117,37 @@ struct osm_slab {
   cudaStream_t side = nullptr;
   cudaEvent_t ev = nullptr;
   uint64_t h2d_bytes = 0;
+};
+
+// Expert residency over one slab: LFU + recency entries keyed (layer, expert).
+struct osm_cache {
+  osm_slab* slab = nullptr;             // null: policy only (no copies)
+  uint64_t budget = 0, accounted = 0;
+  osm_cache_source_fn source = nullptr;
+  void* user = nullptr;
+  struct Node {
+    int32_t slot = -1;
+    uint64_t frequency = 0, last_use = 0, epoch = 0;
+  };
+  using Rank = std::tuple<uint64_t, uint64_t, uint64_t>;  // (frequency, last use, key)
+  std::unordered_map<uint64_t, Node> entries;
+  std::set<Rank> order;                 // eviction order of the resident entries
+  std::unordered_map<uint64_t, uint64_t> frequency_history;  // survives evictions
+  std::unordered_map<uint32_t, osm_layer*> layers;
+  std::vector<int32_t> free_slots;
+  // one acquire's copies (slot, host source) and slot-table writes, issued
+  // together when the acquire ends
+  std::vector<std::pair<uint32_t, const void*>> fills;
+  std::vector<std::pair<int32_t*, int32_t>> table_writes;
+  uint64_t tick = 0, epoch = 0, resident_bytes = 0;
+  uint64_t hits = 0, misses = 0, loads = 0, evictions = 0;
+  // exposed-copy timing: event pairs on the compute stream around each
+  // acquire's copies (issue to landing), read and released by
+  // osm_cache_exposed_read
+  bool time_copies = false;
+  int device = 0;                       // the slab's device
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> copy_waits, spare_events;
+  std::string err;
 };
 
 struct osm_plan {
@@ -707,6 +743,8 @@ int osm_context_destroy(osm_context* ctx) {
     cudaEventDestroy(r.b);
   }
   for (cudaEvent_t e : ctx->ev_pool) cudaEventDestroy(e);
+  if (ctx->picks_host) cudaFreeHost(ctx->picks_host);
+  if (ctx->picks_ev) cudaEventDestroy(ctx->picks_ev);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
   return OSM_OK;
@@ -1234,18 +1272,24 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
 }
 
-int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, const float* w,
-                    float* out, float* sgate, const float* residual, uint32_t flags) {
-  int rc = layer_ready(L, T, true);
-  if (rc) return rc;
+}  // extern "C"
+
+namespace {
+
+// The expert half of a call whose routing is in device memory: `ids`/`w`
+// are copied into the context's routing scratch first, or, with both null,
+// are already there (a cached call routed into it).
+int experts_impl(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, const float* w,
+                 float* out, float* sgate, const float* residual, uint32_t flags) {
   osm_context* ctx = L->ctx;
-  if (!x || !out || !ids || !w) return fail(ctx, OSM_EINVAL, "experts: null argument");
-  if ((flags & OSM_ADD_RESIDUAL) && !residual) return fail(ctx, OSM_EINVAL, "experts: residual missing");
   DeviceGuard dg(ctx->device);
   Scratch& s = ctx->sc;
+  int rc = OSM_OK;
   const size_t nk = (size_t)T * L->g.k;
-  OSM_CUDA(ctx, cudaMemcpyAsync(s.ids, ids, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
-  OSM_CUDA(ctx, cudaMemcpyAsync(s.weights, w, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  if (ids) {
+    OSM_CUDA(ctx, cudaMemcpyAsync(s.ids, ids, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+    OSM_CUDA(ctx, cudaMemcpyAsync(s.weights, w, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  }
   osm::RouterArgs a = router_args(L, x, T);
   a.skip_route = 1;
   a.sgate_out = sgate;
@@ -1282,6 +1326,69 @@ int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* id
     return run_prefill(L, T, out, res, pa, psm);
   }
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
+}
+
+}  // namespace
+
+extern "C" {
+
+int osm_moe_experts(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, const float* w,
+                    float* out, float* sgate, const float* residual, uint32_t flags) {
+  int rc = layer_ready(L, T, true);
+  if (rc) return rc;
+  osm_context* ctx = L->ctx;
+  if (!x || !out || !ids || !w) return fail(ctx, OSM_EINVAL, "experts: null argument");
+  if ((flags & OSM_ADD_RESIDUAL) && !residual) return fail(ctx, OSM_EINVAL, "experts: residual missing");
+  return experts_impl(L, x, T, ids, w, out, sgate, residual, flags);
+}
+
+int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, const float* x,
+                           uint32_t T, float* out, uint32_t* ids, float* w, float* sgate,
+                           const float* residual, uint32_t flags) {
+  int rc = layer_ready(L, T, true);
+  if (rc) return rc;
+  osm_context* ctx = L->ctx;
+  if (!cache || !x || !out) return fail(ctx, OSM_EINVAL, "cached forward: null argument");
+  if ((flags & OSM_ADD_RESIDUAL) && !residual)
+    return fail(ctx, OSM_EINVAL, "cached forward: residual missing");
+  if (flags & OSM_INPUT_F16) return fail(ctx, OSM_EINVAL, "cached forward: fp32 rows only");
+  if (cache->slab != L->slab) return fail(ctx, OSM_EINVAL, "cached forward: the layer is not on the cache's slab");
+  auto lit = cache->layers.find(layer_id);
+  if (lit == cache->layers.end() || lit->second != L)
+    return fail(ctx, OSM_EINVAL, "cached forward: layer_id is not bound to this layer");
+  DeviceGuard dg(ctx->device);
+  Scratch& s = ctx->sc;
+  const size_t nk = (size_t)T * L->g.k;
+  if (ctx->picks_cap < nk) {
+    if (ctx->picks_host) cudaFreeHost(ctx->picks_host);
+    ctx->picks_host = nullptr;
+    ctx->picks_cap = 0;
+    OSM_CUDA(ctx, cudaHostAlloc(&ctx->picks_host, nk * 4, cudaHostAllocDefault));
+    ctx->picks_cap = nk;
+  }
+  if (!ctx->picks_ev) OSM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->picks_ev, cudaEventDisableTiming));
+  // 1. route into the context's scratch (and the caller's buffers)
+  osm::RouterArgs a = router_args(L, x, T);
+  a.force_exact = (flags & OSM_ROUTE_EXACT) ? 1 : 0;
+  a.ids_out = ids;
+  a.weights_out = w;
+  a.do_group = 0;
+  a.xfrag = nullptr;
+  a.sgate_w = nullptr;
+  a.pick_ptr = nullptr;
+  launch_router_pair(ctx, a);
+  rc = check_launch(ctx, "router");
+  if (rc) return rc;
+  // 2. the host needs the picks to make them resident
+  OSM_CUDA(ctx, cudaMemcpyAsync(ctx->picks_host, s.ids, nk * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  OSM_CUDA(ctx, cudaEventRecord(ctx->picks_ev, ctx->stream));
+  OSM_CUDA(ctx, cudaEventSynchronize(ctx->picks_ev));
+  // 3. one acquire over the picks in token-major pick order (the order of
+  //    the reference's expert_cache.get calls, routed_moe.cpp:319-327)
+  rc = osm_cache_acquire(cache, layer_id, ctx->picks_host, (uint32_t)nk);
+  if (rc) return fail(ctx, rc, std::string("cached forward: ") + cache->err);
+  // 4. the experts on the routing left in scratch
+  return experts_impl(L, x, T, nullptr, nullptr, out, sgate, residual, flags);
 }
 
 int osm_moe_sublayer_forward(osm_layer* L, const float* residual, uint32_t T, float* out,
@@ -1442,23 +1549,6 @@ int osm_gen_expert_slots(osm_slab* s, uint64_t seed, uint64_t tensor_base, float
 // HBM expert cache: the residency policy of VulkanResidentExpertCache
 // (src/backend/vulkan_resident_expert_cache.cpp:40-200) over slab slots.
 // ----------------------------------------------------------------------------
-struct osm_cache {
-  osm_slab* slab = nullptr;             // null: policy only (no copies)
-  uint64_t budget = 0, accounted = 0;
-  osm_cache_source_fn source = nullptr;
-  void* user = nullptr;
-  struct Node {
-    int32_t slot = -1;
-    uint64_t frequency = 0, last_use = 0, epoch = 0;
-  };
-  std::unordered_map<uint64_t, Node> entries;
-  std::unordered_map<uint64_t, uint64_t> frequency_history;  // survives evictions
-  std::unordered_map<uint32_t, osm_layer*> layers;
-  std::vector<int32_t> free_slots;
-  uint64_t tick = 0, epoch = 0, resident_bytes = 0;
-  uint64_t hits = 0, misses = 0, loads = 0, evictions = 0;
-  std::string err;
-};
 
 namespace {
 
@@ -1469,10 +1559,24 @@ int cache_fail(osm_cache* c, int code, const char* msg) {
   return code;
 }
 
+osm_cache::Rank cache_rank(uint64_t key, const osm_cache::Node& n) {
+  return {n.frequency, n.last_use, key};
+}
+
+// Records expert -> slot in the layer's host mirror now and queues the device
+// table write for the end of the acquire.
+void cache_bind_slot(osm_cache* c, osm_layer* L, uint32_t expert, int32_t slot) {
+  L->slot_host[expert] = slot;
+  // without a slab every entry of a bound layer stays -1 on the device
+  if (c->slab) c->table_writes.emplace_back(L->slot_of + expert, slot);
+}
+
 // One get() of the reference: a hit refreshes frequency and recency; a miss
 // evicts the entry with the smallest (frequency, last use, key) until the
-// newcomer fits, then copies the expert into a free slot.  Entries touched
-// in the current acquire (epoch) are not evicted.
+// newcomer fits, then queues the expert's copy into a free slot.  Entries
+// touched in the current acquire (epoch) are not evicted.  The victim is the
+// first unprotected entry of an ordered index, the same entry as the
+// reference's linear scan (vulkan_resident_expert_cache.cpp:58-69) picks.
 int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) {
   ++c->tick;
   const uint64_t key = cache_key(layer, expert);
@@ -1480,9 +1584,11 @@ int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) 
   auto it = c->entries.find(key);
   if (it != c->entries.end()) {
     ++c->hits;
+    c->order.erase(cache_rank(key, it->second));
     it->second.frequency = freq;
     it->second.last_use = c->tick;
     it->second.epoch = c->epoch;
+    c->order.insert(cache_rank(key, it->second));
     if (slot_out) *slot_out = it->second.slot;
     return OSM_OK;
   }
@@ -1491,23 +1597,22 @@ int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) 
   while (!c->entries.empty() &&
          (c->resident_bytes + c->accounted > c->budget || (c->slab && c->free_slots.empty()))) {
     auto victim = c->entries.end();
-    for (auto e = c->entries.begin(); e != c->entries.end(); ++e) {
-      if (e->second.epoch == c->epoch) continue;
-      if (victim == c->entries.end() ||
-          std::make_tuple(e->second.frequency, e->second.last_use, e->first) <
-              std::make_tuple(victim->second.frequency, victim->second.last_use, victim->first))
+    auto rank = c->order.begin();
+    for (; rank != c->order.end(); ++rank) {
+      auto e = c->entries.find(std::get<2>(*rank));
+      if (e->second.epoch != c->epoch) {
         victim = e;
+        break;
+      }
     }
     if (victim == c->entries.end())
       return cache_fail(c, OSM_ENOMEM, "cache: the experts of one call do not fit in the budget");
     const uint32_t vl = (uint32_t)(victim->first >> 32), ve = (uint32_t)(victim->first & 0xFFFFFFFFu);
     auto lit = c->layers.find(vl);
-    if (lit != c->layers.end()) {
-      const int rc = osm_layer_set_slot(lit->second, ve, -1);
-      if (rc) return cache_fail(c, rc, "cache: unbinding an evicted expert failed");
-    }
+    if (lit != c->layers.end()) cache_bind_slot(c, lit->second, ve, -1);
     if (victim->second.slot >= 0) c->free_slots.push_back(victim->second.slot);
     c->resident_bytes -= c->accounted;
+    c->order.erase(rank);
     c->entries.erase(victim);
     ++c->evictions;
   }
@@ -1519,16 +1624,9 @@ int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) 
       return cache_fail(c, OSM_ERUNTIME, "cache: the host source could not provide the expert");
     slot = c->free_slots.back();
     c->free_slots.pop_back();
-    const int rc = osm_slab_fill_async(c->slab, (uint32_t)slot, src);
-    if (rc) {
-      c->free_slots.push_back(slot);
-      return cache_fail(c, rc, "cache: slot fill failed");
-    }
+    c->fills.emplace_back((uint32_t)slot, src);
     auto lit = c->layers.find(layer);
-    if (lit != c->layers.end()) {
-      const int rc2 = osm_layer_set_slot(lit->second, expert, slot);
-      if (rc2) return cache_fail(c, rc2, "cache: binding the loaded expert failed");
-    }
+    if (lit != c->layers.end()) cache_bind_slot(c, lit->second, expert, slot);
   } else if (c->source) {
     const void* src = nullptr;
     if (c->source(c->user, layer, expert, &src) != 0)
@@ -1540,10 +1638,73 @@ int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) 
   n.last_use = c->tick;
   n.epoch = c->epoch;
   c->entries.emplace(key, n);
+  c->order.insert(cache_rank(key, n));
   c->resident_bytes += c->accounted;
   ++c->loads;
   if (slot_out) *slot_out = slot;
   return OSM_OK;
+}
+
+// Issues the acquire's queued copies and slot-table writes.  The copies run
+// back to back on the slab's side stream after the work already queued on
+// the compute stream (which may still read the slots being overwritten); the
+// compute stream waits once for all of them, then the table writes follow in
+// its order, ahead of the caller's next kernel.
+int cache_flush(osm_cache* c) {
+  int rc = OSM_OK;
+  if (c->slab && !c->fills.empty()) {
+    osm_slab* s = c->slab;
+    osm_context* ctx = s->ctx;
+    DeviceGuard dg(ctx->device);
+    cudaError_t e = cudaSuccess;
+    std::pair<cudaEvent_t, cudaEvent_t> tw{nullptr, nullptr};
+    if (c->time_copies) {
+      if (!c->spare_events.empty()) {
+        tw = c->spare_events.back();
+        c->spare_events.pop_back();
+      } else {
+        e = cudaEventCreate(&tw.first);
+        if (e == cudaSuccess) e = cudaEventCreate(&tw.second);
+      }
+      if (e == cudaSuccess) e = cudaEventRecord(tw.first, ctx->stream);
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(s->ev, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s->side, s->ev, 0);
+    for (size_t i = 0; e == cudaSuccess && i < c->fills.size(); ++i) {
+      e = cudaMemcpyAsync(s->base + (size_t)c->fills[i].first * s->layout.stride, c->fills[i].second,
+                          s->layout.stride, cudaMemcpyHostToDevice, s->side);
+      if (e == cudaSuccess) s->h2d_bytes += s->layout.stride;
+    }
+    if (e == cudaSuccess) e = cudaEventRecord(s->ev, s->side);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ctx->stream, s->ev, 0);
+    if (e == cudaSuccess && tw.second) {
+      e = cudaEventRecord(tw.second, ctx->stream);
+      if (e == cudaSuccess) c->copy_waits.push_back(tw);
+    }
+    if (e != cudaSuccess) {
+      if (tw.first) cudaEventDestroy(tw.first);
+      if (tw.second) cudaEventDestroy(tw.second);
+      rc = cache_fail(c, OSM_ECUDA, cudaGetErrorString(e));
+    }
+  }
+  c->fills.clear();
+  if (rc == OSM_OK && !c->table_writes.empty()) {
+    osm_context* ctx = c->slab->ctx;
+    DeviceGuard dg(ctx->device);
+    osm::SlotUpdates u{};
+    for (size_t i = 0; i < c->table_writes.size(); i += osm::SlotUpdates::kMax) {
+      u.n = (int)std::min<size_t>(osm::SlotUpdates::kMax, c->table_writes.size() - i);
+      for (int j = 0; j < u.n; ++j) {
+        u.ptr[j] = c->table_writes[i + j].first;
+        u.val[j] = c->table_writes[i + j].second;
+      }
+      osm::launch_slot_updates(u, ctx->stream, &ctx->launches);
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cache_fail(c, OSM_ECUDA, cudaGetErrorString(e));
+  }
+  c->table_writes.clear();
+  return rc;
 }
 
 }  // namespace
@@ -1563,6 +1724,7 @@ int osm_cache_create(osm_slab* slab, uint64_t budget_bytes, uint64_t accounted_b
   osm_cache* c = new (std::nothrow) osm_cache;
   if (!c) return OSM_ENOMEM;
   c->slab = slab;
+  if (slab) c->device = slab->ctx->device;
   c->budget = budget_bytes;
   c->accounted = accounted_bytes;
   c->source = source;
@@ -1574,7 +1736,47 @@ int osm_cache_create(osm_slab* slab, uint64_t budget_bytes, uint64_t accounted_b
 }
 
 int osm_cache_destroy(osm_cache* c) {
+  if (!c) return OSM_EINVAL;
+  if (!c->copy_waits.empty() || !c->spare_events.empty()) {
+    // events still pending are released by the driver once they complete
+    DeviceGuard dg(c->device);
+    for (auto& p : c->copy_waits) {
+      cudaEventDestroy(p.first);
+      cudaEventDestroy(p.second);
+    }
+    for (auto& p : c->spare_events) {
+      cudaEventDestroy(p.first);
+      cudaEventDestroy(p.second);
+    }
+  }
   delete c;
+  return OSM_OK;
+}
+
+int osm_cache_time_copies(osm_cache* c, int enable) {
+  if (!c) return OSM_EINVAL;
+  if (enable && !c->slab) return cache_fail(c, OSM_EINVAL, "cache: copy timing needs a slab");
+  c->time_copies = enable != 0;
+  return OSM_OK;
+}
+
+int osm_cache_exposed_read(osm_cache* c, double* ms, uint64_t* waits) {
+  if (!c || !ms) return OSM_EINVAL;
+  double sum = 0.0;
+  const uint64_t n = c->copy_waits.size();
+  if (n) {
+    DeviceGuard dg(c->slab->ctx->device);
+    const cudaError_t e = cudaEventSynchronize(c->copy_waits.back().second);
+    if (e != cudaSuccess) return cache_fail(c, OSM_ECUDA, cudaGetErrorString(e));
+    for (auto& p : c->copy_waits) {
+      float t = 0.f;
+      if (cudaEventElapsedTime(&t, p.first, p.second) == cudaSuccess) sum += t;
+      c->spare_events.push_back(p);
+    }
+    c->copy_waits.clear();
+  }
+  *ms = sum;
+  if (waits) *waits = n;
   return OSM_OK;
 }
 
@@ -1589,26 +1791,33 @@ int osm_cache_bind_layer(osm_cache* c, uint32_t layer_id, osm_layer* layer) {
   // marked not resident
   for (uint32_t e = 0; e < (uint32_t)layer->g.E; ++e) {
     auto it = c->entries.find(cache_key(layer_id, e));
-    const int rc = osm_layer_set_slot(layer, e, it != c->entries.end() ? it->second.slot : -1);
-    if (rc) return cache_fail(c, rc, "cache: binding the layer failed");
+    layer->slot_host[e] = it != c->entries.end() ? it->second.slot : -1;
   }
+  osm_context* ctx = layer->ctx;
+  DeviceGuard dg(ctx->device);
+  // pageable source: staged before the call returns
+  const cudaError_t e = cudaMemcpyAsync(layer->slot_of, layer->slot_host.data(), layer->g.E * 4,
+                                        cudaMemcpyHostToDevice, ctx->stream);
+  if (e != cudaSuccess) return cache_fail(c, OSM_ECUDA, "cache: binding the layer failed");
   return OSM_OK;
 }
 
 int osm_cache_get(osm_cache* c, uint32_t layer_id, uint32_t expert, int32_t* slot_out) {
   if (!c) return OSM_EINVAL;
   ++c->epoch;
-  return cache_get(c, layer_id, expert, slot_out);
+  const int rc = cache_get(c, layer_id, expert, slot_out);
+  const int rc2 = cache_flush(c);
+  return rc ? rc : rc2;
 }
 
 int osm_cache_acquire(osm_cache* c, uint32_t layer_id, const uint32_t* experts, uint32_t n) {
   if (!c || (n && !experts)) return OSM_EINVAL;
   ++c->epoch;
-  for (uint32_t i = 0; i < n; ++i) {
-    const int rc = cache_get(c, layer_id, experts[i], nullptr);
-    if (rc) return rc;
-  }
-  return OSM_OK;
+  int rc = OSM_OK;
+  for (uint32_t i = 0; i < n && rc == OSM_OK; ++i) rc = cache_get(c, layer_id, experts[i], nullptr);
+  // what this call already changed is issued even when a later pick failed
+  const int rc2 = cache_flush(c);
+  return rc ? rc : rc2;
 }
 
 int osm_cache_contains(const osm_cache* c, uint32_t layer_id, uint32_t expert) {

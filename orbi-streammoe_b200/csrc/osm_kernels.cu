@@ -199,6 +199,18 @@ inline int grid_for(size_t n, int threads) {
 
 }  // namespace
 
+__global__ void slot_updates_kernel(const SlotUpdates u) {
+  // in order: a later write to the same entry wins
+  if (threadIdx.x == 0)
+    for (int i = 0; i < u.n; ++i) *u.ptr[i] = u.val[i];
+}
+
+void launch_slot_updates(const SlotUpdates& u, cudaStream_t s, uint64_t* launches) {
+  if (u.n <= 0) return;
+  slot_updates_kernel<<<1, 32, 0, s>>>(u);
+  if (launches) *launches += 1;
+}
+
 void launch_combine(const CombineArgs& a, cudaStream_t s, uint64_t* launches) {
   const dim3 grid((a.H + 255) / 256, a.B);
   combine_kernel<<<grid, 256, 0, s>>>(a);

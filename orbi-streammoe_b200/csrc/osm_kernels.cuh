@@ -272,6 +272,16 @@ void launch_router_tile(const float* w, const RouterGeom& g, void* wx, cudaStrea
                         uint64_t* launches);
 void launch_router_pack(const float* w, const RouterGeom& g, void* wp, cudaStream_t s,
                         uint64_t* launches);
+// Slot-table writes (expert -> slab slot) passed by value, so that the host
+// batches a cache acquire's table changes into one launch without a staging
+// buffer that a later acquire could overwrite before the copy ran.
+struct SlotUpdates {
+  static constexpr int kMax = 48;
+  int n;
+  int32_t val[kMax];
+  int32_t* ptr[kMax];
+};
+void launch_slot_updates(const SlotUpdates& u, cudaStream_t s, uint64_t* launches);
 void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
                          int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
                          int* out_row, cudaStream_t s, uint64_t* launches);

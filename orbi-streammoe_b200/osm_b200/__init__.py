@@ -255,6 +255,19 @@ class Layer:
                                              _ptr(out), _ptr(shared_gate), _ptr(residual), flags),
                        "moe_experts")
 
+    def run_cached(self, cache: "ExpertCache", layer_id: int, x, tokens, out, ids=None,
+                   weights=None, shared_gate=None, residual=None, exact_route=False,
+                   prefill=False):
+        """run_qwen_sparse_moe_vulkan_accum with its expert cache: route, make
+        the picks resident through ``cache`` (this layer bound as
+        ``layer_id``), run the experts."""
+        flags = ((OSM_ROUTE_EXACT if exact_route else 0) | (OSM_ADD_RESIDUAL if residual is not None else 0)
+                 | (OSM_PREFILL_BF16 if prefill else 0))
+        rc = lib().osm_moe_forward_cached(self.h, cache.h, layer_id, _ptr(x), tokens, _ptr(out),
+                                          _ptr(ids), _ptr(weights), _ptr(shared_gate),
+                                          _ptr(residual), flags)
+        self.ctx.check(rc, "moe_forward_cached")
+
     def run_sublayer(self, residual, tokens, out, normalized=None, ids=None, weights=None,
                      mass=None, shared_gate=None, exact_route=False, exact_rmsnorm=False,
                      prefill=False):
@@ -351,6 +364,18 @@ class ExpertCache:
         c = _lib.CacheCounts()
         self._check(lib().osm_cache_stats(self.h, C.byref(c)), "stats")
         return {f: getattr(c, f) for f, _ in c._fields_}
+
+    def time_copies(self, enable: bool):
+        """Bracket each acquire's copies with compute-stream events."""
+        self._check(lib().osm_cache_time_copies(self.h, int(bool(enable))), "time_copies")
+
+    def exposed_read(self):
+        """(ms the compute stream spent waiting on copies, number of waits)
+        since the last read."""
+        ms = C.c_double()
+        n = C.c_uint64()
+        self._check(lib().osm_cache_exposed_read(self.h, C.byref(ms), C.byref(n)), "exposed_read")
+        return ms.value, n.value
 
     def close(self):
         if self.h:

@@ -105,6 +105,8 @@ _SIGS = {
     "osm_moe_route": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, C.c_uint32]),
     "osm_moe_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_experts": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, C.c_uint32]),
+    "osm_moe_forward_cached": (C.c_int, [_P, _P, C.c_uint32, _P, C.c_uint32, _P, _P, _P, _P, _P,
+                                         C.c_uint32]),
     "osm_moe_sublayer_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_plan_create": (C.c_int, [_P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32, C.POINTER(_P)]),
     "osm_plan_launch": (C.c_int, [_P]),
@@ -121,6 +123,8 @@ _SIGS = {
     "osm_cache_acquire": (C.c_int, [_P, C.c_uint32, _P, C.c_uint32]),
     "osm_cache_contains": (C.c_int, [_P, C.c_uint32, C.c_uint32]),
     "osm_cache_stats": (C.c_int, [_P, C.POINTER(CacheCounts)]),
+    "osm_cache_time_copies": (C.c_int, [_P, C.c_int]),
+    "osm_cache_exposed_read": (C.c_int, [_P, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
 }
 
 _lib = None

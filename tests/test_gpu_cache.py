@@ -60,3 +60,76 @@ def test_cache_streams_experts_into_a_small_slab(torch):
     assert osm.lib().osm_slab_h2d_bytes(slab.h) == s["loads"] * lay.stride
     assert ctx.status()[0] == 0
     cache.close()
+
+
+@pytest.mark.parametrize("E,SLOTS,B", [(16, 6, 1), (24, 13, 3)])
+def test_cached_forward_matches_oracle_and_policy(torch, E, SLOTS, B):
+    """osm_moe_forward_cached (run_qwen_sparse_moe_vulkan_accum with its cache)
+    in one call per layer: routing, the picks' residency and the experts.
+    Outputs and ids match the oracle; the cache counts match the policy model
+    acquiring each call's picks in token-major order; each load moved one
+    slot of bytes."""
+    import osm_b200 as osm
+
+    H, I, K = 256, 128, 4
+    fx = [MoeFixture(torch, H, E, I, K, seed=170 + l, max_tokens=B) for l in range(2)]
+    lay = osm.expert_layout(H, I)
+    ctx = osm.Context(0, max_tokens=B)
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    slab = osm.Slab(ctx, lay, SLOTS)
+    pinned = [torch.from_numpy(np.ascontiguousarray(f.slots).reshape(-1)).pin_memory() for f in fx]
+    layers = []
+    for f in fx:
+        L = osm.Layer(ctx, f.W, K, True, shared_slot=f.shared_slot, shared_layout=lay,
+                      shared_gate=f.sg)
+        L.bind_slab(slab, np.full(E, -1, np.int32))
+        layers.append(L)
+    cache = osm.ExpertCache(slab, SLOTS * lay.stride,
+                            source=lambda l, e: pinned[l].data_ptr() + e * lay.stride)
+    for l, L in enumerate(layers):
+        cache.bind_layer(l, L)
+    model = Model(SLOTS * lay.stride, lay.stride)
+    for step in range(8):
+        for l, (f, L) in enumerate(zip(fx, layers)):
+            x = f.port.gen_normal(180 + l, step, 1.0, B * H).reshape(B, H)
+            xd = torch.from_numpy(x).cuda()
+            ids = torch.empty(B, K, dtype=torch.int32, device="cuda")
+            out = torch.empty(B, H, device="cuda")
+            L.run_cached(cache, l, xd, B, out, ids=ids)
+            torch.cuda.synchronize()
+            got_ids = ids.cpu().numpy().astype(np.uint32)
+            model.acquire(l, [int(e) for e in got_ids.reshape(-1)])
+            o = out.cpu().numpy()
+            for t in range(B):
+                ref, rids, _, _, _ = f.oracle_token(x[t])
+                assert np.array_equal(got_ids[t], rids)
+                assert normwise_rel(o[t], ref) <= 1e-4
+    s = cache.stats()
+    assert s == model.stats()
+    assert s["evictions"] > 0 and s["hits"] > 0
+    assert osm.lib().osm_slab_h2d_bytes(slab.h) == s["loads"] * lay.stride
+    assert ctx.status()[0] == 0
+    cache.close()
+
+
+def test_cached_forward_rejects_an_unbound_layer(torch):
+    import osm_b200 as osm
+
+    H, E, I, K = 256, 8, 128, 2
+    f = MoeFixture(torch, H, E, I, K, seed=190, max_tokens=1)
+    lay = osm.expert_layout(H, I)
+    slab = osm.Slab(f.ctx, lay, 4)
+    L = osm.Layer(f.ctx, f.W, K, True)
+    L.bind_slab(slab, np.full(E, -1, np.int32))
+    cache = osm.ExpertCache(slab, 4 * lay.stride, source=lambda l, e: f.pinned.data_ptr())
+    x = torch.zeros(1, H, device="cuda")
+    out = torch.empty(1, H, device="cuda")
+    with pytest.raises(osm.OsmError):
+        L.run_cached(cache, 0, x, 1, out)   # layer 0 was never bound to the cache
+    cache.bind_layer(0, L)
+    with pytest.raises(osm.OsmError):
+        L.run_cached(cache, 1, x, 1, out)   # bound as 0, called as 1
+    L.run_cached(cache, 0, x, 1, out)
+    torch.cuda.synchronize()
+    assert cache.stats()["loads"] == K
+    cache.close()
