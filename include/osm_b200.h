@@ -47,6 +47,8 @@ extern "C" {
                                      within 2e-3 of the fp32 path; |x|, h < 65504 (status bit 5) */
 #define OSM_INPUT_F16 0x10u       /* osm_moe_experts with OSM_PREFILL_BF16: x_dev holds fp16 rows
                                      [tokens][hidden] (layers without a shared expert) */
+#define OSM_OUTPUT_F16 0x20u      /* osm_moe_experts with OSM_PREFILL_BF16: out_dev receives fp16
+                                     rows [tokens][hidden] (each fp32 sum rounded once) */
 
 typedef struct osm_context osm_context;
 typedef struct osm_layer osm_layer;
@@ -277,7 +279,9 @@ int osm_moe_forward(osm_layer* layer, const float* x_dev, uint32_t tokens,
 /* Expert half of osm_moe_forward for a routing already in device memory
  * (after osm_moe_route and host-side cache fills).  OSM_PREFILL_BF16 selects
  * the tensor-core prefill path as for osm_moe_forward; with OSM_INPUT_F16 the
- * rows are already fp16 (as an expert-parallel exchange delivers them). */
+ * rows are already fp16 (as an expert-parallel exchange delivers them), with
+ * OSM_OUTPUT_F16 the output rows are fp16 (as the exchange returns them).  On
+ * the prefill path out_dev and residual_dev are 16-byte aligned. */
 int osm_moe_experts(osm_layer* layer, const float* x_dev, uint32_t tokens,
                     const uint32_t* ids_dev, const float* weights_dev,
                     float* out_dev, float* shared_gate_dev,

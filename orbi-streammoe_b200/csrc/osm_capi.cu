@@ -104,7 +104,8 @@ struct osm_context {
   const float* cur_x = nullptr;  // activations of the call in flight (expert kernels)
   std::vector<cudaEvent_t> ev_pool;
   std::vector<ProfRec> recs;
-  uint32_t* picks_host = nullptr;   // pinned: the picks a cached call reads back
+  uint32_t* picks_host = nullptr;   // mapped pinned: the picks a cached call reads back
+  uint32_t* picks_dev = nullptr;    // the same memory as the kernels address it
   size_t picks_cap = 0;
   cudaEvent_t picks_ev = nullptr;
 };
@@ -620,9 +621,11 @@ bool prefill_path(osm_layer* L, osm::PfArgs* pa, size_t* smem) {
 }
 
 int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm::PfArgs pa,
-                size_t smem, bool x_given = false) {
+                size_t smem, bool x_given = false, bool f16_out = false) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
+    return fail(ctx, OSM_EINVAL, "prefill: out and residual must be 16-byte aligned");
   if (!x_given) pa.xb = s.xbf;
   pa.hb = reinterpret_cast<uint16_t*>(s.hfrag);
   pa.pb = reinterpret_cast<uint16_t*>(s.partial);
@@ -646,7 +649,8 @@ int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm
   {
     Prof p(ctx, kKCombine);
     osm::launch_combine_bf16(pa.pb, s.tp_pos, s.weights, L->shared_slot ? s.sgate : nullptr, residual,
-                             out, (int)T, L->g.H, L->g.k, ctx->stream, &ctx->launches);
+                             out, f16_out, s.status, (int)T, L->g.H, L->g.k, ctx->stream,
+                             &ctx->launches);
   }
   return check_launch(ctx, "prefill combine");
 }
@@ -1298,8 +1302,10 @@ int experts_impl(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, 
   size_t psm = 0;
   const bool prefill = (flags & OSM_PREFILL_BF16) != 0;
   const bool f16 = (flags & OSM_INPUT_F16) != 0;
+  const bool f16_out = (flags & OSM_OUTPUT_F16) != 0;
   if (f16 && (!prefill || L->shared_slot))
     return fail(ctx, OSM_EINVAL, "experts: fp16 rows need OSM_PREFILL_BF16 and no shared expert");
+  if (f16_out && !prefill) return fail(ctx, OSM_EINVAL, "experts: fp16 output needs OSM_PREFILL_BF16");
   if (prefill) {
     if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
     a.xfrag = nullptr;
@@ -1310,6 +1316,7 @@ int experts_impl(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, 
   if (f16) {
     // the rows are the GEMM's operand already: only the grouping runs first
     Prof p(ctx, kKRouterSelect);
+    a.pick_ptr = nullptr;  // the grouped entries carry the slot bases
     osm::launch_group(a, ctx->stream, &ctx->launches);
   } else {
     launch_router_pair(ctx, a);
@@ -1321,9 +1328,9 @@ int experts_impl(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, 
     if (f16) {
       osm::PfArgs pf = pa;
       pf.xb = reinterpret_cast<const uint16_t*>(x);
-      return run_prefill(L, T, out, res, pf, psm, true);
+      return run_prefill(L, T, out, res, pf, psm, true, f16_out);
     }
-    return run_prefill(L, T, out, res, pa, psm);
+    return run_prefill(L, T, out, res, pa, psm, false, f16_out);
   }
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
 }
@@ -1362,33 +1369,67 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   if (ctx->picks_cap < nk) {
     if (ctx->picks_host) cudaFreeHost(ctx->picks_host);
     ctx->picks_host = nullptr;
+    ctx->picks_dev = nullptr;
     ctx->picks_cap = 0;
-    OSM_CUDA(ctx, cudaHostAlloc(&ctx->picks_host, nk * 4, cudaHostAllocDefault));
+    OSM_CUDA(ctx, cudaHostAlloc(&ctx->picks_host, nk * 4, cudaHostAllocMapped));
+    OSM_CUDA(ctx, cudaHostGetDevicePointer(reinterpret_cast<void**>(&ctx->picks_dev), ctx->picks_host, 0));
     ctx->picks_cap = nk;
   }
   if (!ctx->picks_ev) OSM_CUDA(ctx, cudaEventCreateWithFlags(&ctx->picks_ev, cudaEventDisableTiming));
-  // 1. route into the context's scratch (and the caller's buffers)
+  const bool prefill = (flags & OSM_PREFILL_BF16) != 0;
+  osm::PfArgs pa;
+  size_t psm = 0;
+  osm::GemvArgs g;
+  osm::GemvLaunch gl;
+  osm::GrpArgs ga;
+  size_t sgu = 0, sdn = 0;
+  bool dec = false;
   osm::RouterArgs a = router_args(L, x, T);
+  if (prefill) {
+    if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
+    a.xfrag = nullptr;
+    a.xbf = s.xbf;
+    a.chunk_pairs = 128;
+  } else {
+    dec = gemv_path(L, T, &g, &gl);
+    if (dec || grouped_path(L, &ga, &sgu, &sdn)) a.xfrag = nullptr;  // only the older kernels read it
+  }
+  // 1. route, with the shared gate and the activation operands; the picks go
+  //    straight to mapped host memory
   a.force_exact = (flags & OSM_ROUTE_EXACT) ? 1 : 0;
-  a.ids_out = ids;
+  a.ids_out = ctx->picks_dev;
   a.weights_out = w;
+  a.sgate_out = sgate;
   a.do_group = 0;
-  a.xfrag = nullptr;
-  a.sgate_w = nullptr;
   a.pick_ptr = nullptr;
+  ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");
   if (rc) return rc;
-  // 2. the host needs the picks to make them resident
-  OSM_CUDA(ctx, cudaMemcpyAsync(ctx->picks_host, s.ids, nk * 4, cudaMemcpyDeviceToHost, ctx->stream));
   OSM_CUDA(ctx, cudaEventRecord(ctx->picks_ev, ctx->stream));
+  if (ids) OSM_CUDA(ctx, cudaMemcpyAsync(ids, s.ids, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  // 2. the host needs the picks to make them resident
   OSM_CUDA(ctx, cudaEventSynchronize(ctx->picks_ev));
   // 3. one acquire over the picks in token-major pick order (the order of
   //    the reference's expert_cache.get calls, routed_moe.cpp:319-327)
   rc = osm_cache_acquire(cache, layer_id, ctx->picks_host, (uint32_t)nk);
   if (rc) return fail(ctx, rc, std::string("cached forward: ") + cache->err);
-  // 4. the experts on the routing left in scratch
-  return experts_impl(L, x, T, nullptr, nullptr, out, sgate, residual, flags);
+  // 4. bind the picks to their slots (and group them), then the experts
+  a.skip_route = 1;
+  a.ids_out = nullptr;
+  a.weights_out = nullptr;
+  a.sgate_out = nullptr;
+  a.pick_ptr = s.pick_ptr;
+  a.do_group = (!prefill && T == 1 && dec) ? 0 : 1;
+  {
+    Prof p(ctx, kKRouterSelect);
+    osm::launch_group(a, ctx->stream, &ctx->launches);
+  }
+  rc = check_launch(ctx, "pick binding");
+  if (rc) return rc;
+  const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
+  if (prefill) return run_prefill(L, T, out, res, pa, psm);
+  return run_experts(L, T, out, res);
 }
 
 int osm_moe_sublayer_forward(osm_layer* L, const float* residual, uint32_t T, float* out,

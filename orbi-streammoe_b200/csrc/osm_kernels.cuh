@@ -243,10 +243,12 @@ void init_prefill_attributes(int max_smem);
 void launch_prefill_gateup(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches);
 void launch_prefill_down(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches);
 // out[b] = sum over picks of w * pb[tp_pos[b][j]] in pick order, then sgate * the
-// shared row, then the residual
+// shared row, then the residual; H % 8 == 0, out and residual 16-byte aligned;
+// f16_out: out holds fp16 rows
 void launch_combine_bf16(const uint16_t* pb, const int* tp_pos, const float* weights,
-                         const float* sgate, const float* residual, float* out, int B, int H,
-                         int k, cudaStream_t s, uint64_t* launches);
+                         const float* sgate, const float* residual, void* out, bool f16_out,
+                         unsigned int* status, int B, int H, int k, cudaStream_t s,
+                         uint64_t* launches);
 
 void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float* w,
                     float eps, bool exact, cudaStream_t s, uint64_t* launches);

@@ -386,27 +386,58 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPfTmemCols));
 }
 
-__global__ void combine_bf16_kernel(const uint16_t* __restrict__ pb, const int* __restrict__ tp_pos,
-                                    const float* __restrict__ w, const float* __restrict__ sg,
-                                    const float* __restrict__ res, float* __restrict__ out, int H,
-                                    int k) {
+// out[b] = sum over picks j in order of w[b][j] * row(tp_pos[b][j]), then the
+// shared expert's row scaled by sg[b], then the residual; each element in
+// fp32 with one rounding per operation.  Eight consecutive elements per
+// thread (H % 8 == 0): 16-byte row loads.  F16OUT: out holds fp16 rows
+// (values beyond the fp16 range set kStatusF16Range).
+template <bool F16OUT>
+__global__ void __launch_bounds__(256) combine_bf16_kernel(
+    const uint16_t* __restrict__ pb, const int* __restrict__ tp_pos, const float* __restrict__ w,
+    const float* __restrict__ sg, const float* __restrict__ res, void* __restrict__ out, int H, int k,
+    unsigned int* status) {
   pdl_wait();
   const int b = blockIdx.y;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (i >= H) return;
   const int kp = k + (sg != nullptr ? 1 : 0);
   const int* tp = tp_pos + (size_t)b * kp;
-  float acc = 0.0f;
-  for (int j = 0; j < k; ++j) {
-    const float v = __half2float(__ushort_as_half(pb[(size_t)tp[j] * H + i]));
-    acc = __fadd_rn(acc, __fmul_rn(w[(size_t)b * k + j], v));
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int j = 0; j < kp; ++j) {
+    const float wj = j < k ? w[(size_t)b * k + j] : sg[b];
+    const uint4 q = *reinterpret_cast<const uint4*>(pb + (size_t)tp[j] * H + i);
+    const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&qq[u]));
+      acc[2 * u] = __fadd_rn(acc[2 * u], __fmul_rn(wj, v.x));
+      acc[2 * u + 1] = __fadd_rn(acc[2 * u + 1], __fmul_rn(wj, v.y));
+    }
   }
-  if (sg) {
-    const float v = __half2float(__ushort_as_half(pb[(size_t)tp[k] * H + i]));
-    acc = __fadd_rn(acc, __fmul_rn(sg[b], v));
+  if (res) {
+    const float4 r0 = *reinterpret_cast<const float4*>(res + (size_t)b * H + i);
+    const float4 r1 = *reinterpret_cast<const float4*>(res + (size_t)b * H + i + 4);
+    const float rr[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc[u] = __fadd_rn(rr[u], acc[u]);
   }
-  if (res) acc = __fadd_rn(res[(size_t)b * H + i], acc);
-  out[(size_t)b * H + i] = acc;
+  if (F16OUT) {
+    bool over = false;
+    uint32_t o[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      over |= fabsf(acc[2 * u]) >= 65504.0f || fabsf(acc[2 * u + 1]) >= 65504.0f;
+      const __half2 hv = __floats2half2_rn(acc[2 * u], acc[2 * u + 1]);
+      o[u] = *reinterpret_cast<const uint32_t*>(&hv);
+    }
+    if (over) atomicOr(status, kStatusF16Range);
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out) + (size_t)b * H + i) =
+        make_uint4(o[0], o[1], o[2], o[3]);
+  } else {
+    float* op = static_cast<float*>(out) + (size_t)b * H + i;
+    *reinterpret_cast<float4*>(op) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(op + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
 }
 
 template <typename Kern, typename... Args>
@@ -461,10 +492,16 @@ void launch_prefill_down(const PfArgs& a, int grid, size_t smem, cudaStream_t s,
 }
 
 void launch_combine_bf16(const uint16_t* pb, const int* tp_pos, const float* weights,
-                         const float* sgate, const float* residual, float* out, int B, int H,
-                         int k, cudaStream_t s, uint64_t* launches) {
-  launch_pdl_pf(combine_bf16_kernel, dim3((H + 255) / 256, B), dim3(256), 0, s, pb, tp_pos, weights,
-                sgate, residual, out, H, k);
+                         const float* sgate, const float* residual, void* out, bool f16_out,
+                         unsigned int* status, int B, int H, int k, cudaStream_t s,
+                         uint64_t* launches) {
+  const dim3 grid((H / 8 + 255) / 256, B);
+  if (f16_out)
+    launch_pdl_pf(combine_bf16_kernel<true>, grid, dim3(256), 0, s, pb, tp_pos, weights, sgate,
+                  residual, out, H, k, status);
+  else
+    launch_pdl_pf(combine_bf16_kernel<false>, grid, dim3(256), 0, s, pb, tp_pos, weights, sgate,
+                  residual, out, H, k, status);
   if (launches) *launches += 1;
 }
 

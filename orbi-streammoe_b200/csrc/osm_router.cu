@@ -1152,12 +1152,19 @@ __global__ void __launch_bounds__(256) scatter_pairs_kernel(RouterArgs a) {
   }
 }
 
+// Binds a routing that the select kernel left in a.ids / a.mass to the slab
+// (pick_ptr, when requested: null for a token the select refused, whose
+// mass it set to 0, as the select itself does) and, with a.do_group, groups
+// the (token, pick) pairs by expert.
 __global__ void __launch_bounds__(kSelThreads) group_kernel(RouterArgs a) {
   extern __shared__ float4 smem4[];
   __shared__ int red[32];
   pdl_wait();
   pdl_trigger();
-  group_pairs(a, reinterpret_cast<int*>(smem4), red);
+  if (a.pick_ptr)
+    for (int p = threadIdx.x; p < a.B * a.g.k; p += blockDim.x)
+      a.pick_ptr[p] = __ldcg(a.mass + p / a.g.k) > 0.0f ? slot_base(a, __ldcg(a.ids + p)) : nullptr;
+  if (a.do_group) group_pairs(a, reinterpret_cast<int*>(smem4), red);
 }
 
 template <typename K, typename... Args>
@@ -1253,7 +1260,7 @@ void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
   const size_t sm = (size_t)5 * (a.g.E + 1) * sizeof(int);
   launch_pdl(group_kernel, dim3(1), dim3(kSelThreads), sm, s, a);
   if (launches) *launches += 1;
-  if (a.defer_scatter) {
+  if (a.defer_scatter && a.do_group) {
     const int n = a.B * (a.g.k + 1);
     launch_pdl(scatter_pairs_kernel, dim3((n + 255) / 256), dim3(256), 0, s, a);
     if (launches) *launches += 1;

@@ -12,7 +12,7 @@ from __future__ import annotations
 import ctypes as C
 
 from . import _lib
-from ._lib import (OSM_ADD_RESIDUAL, OSM_INPUT_F16, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT,  # noqa: F401
+from ._lib import (OSM_ADD_RESIDUAL, OSM_INPUT_F16, OSM_OUTPUT_F16, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT,  # noqa: F401
                    OSM_ROUTE_EXACT, ExpertLayout, LayerDesc)
 
 
@@ -247,10 +247,12 @@ class Layer:
     def run_experts(self, x, tokens, ids, weights, out, shared_gate=None, residual=None,
                     prefill=False):
         """prefill=True: tensor-core path; an fp16 x (torch.float16) is passed
-        as is (OSM_INPUT_F16, layers without a shared expert)."""
+        as is (OSM_INPUT_F16, layers without a shared expert), and an fp16
+        `out` receives fp16 rows (OSM_OUTPUT_F16)."""
         f16 = str(getattr(x, "dtype", "")) == "torch.float16"
+        f16_out = str(getattr(out, "dtype", "")) == "torch.float16"
         flags = ((OSM_ADD_RESIDUAL if residual is not None else 0) | (OSM_PREFILL_BF16 if prefill else 0)
-                 | (OSM_INPUT_F16 if f16 else 0))
+                 | (OSM_INPUT_F16 if f16 else 0) | (OSM_OUTPUT_F16 if f16_out else 0))
         self.ctx.check(lib().osm_moe_experts(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
                                              _ptr(out), _ptr(shared_gate), _ptr(residual), flags),
                        "moe_experts")

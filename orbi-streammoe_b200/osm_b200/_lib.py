@@ -23,6 +23,7 @@ OSM_RMSNORM_EXACT = 0x2
 OSM_ADD_RESIDUAL = 0x4
 OSM_PREFILL_BF16 = 0x8
 OSM_INPUT_F16 = 0x10
+OSM_OUTPUT_F16 = 0x20
 OSM_PLAN_SUBLAYER = 0x100
 OSM_PLAN_PROFILE = 0x200
 

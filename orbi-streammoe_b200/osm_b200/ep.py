@@ -9,8 +9,8 @@ single-GPU path), then:
   3. runs the owned experts on the rows it received, together with its own
      tokens routed to the shared expert (held in the slab's spare last slot,
      weighted by its sigmoid gate): one tensor-core prefill call on the fp16
-     rows, one pick per row, each row scaled by its weight;
-  4. sends the weighted rows back with the reverse all-to-all;
+     rows, one pick per row, each row scaled by its weight, fp16 rows out;
+  4. sends the weighted fp16 rows back with the reverse all-to-all;
   5. adds each token's rows in pick order, then the shared expert (replicated,
      computed locally for the rank's own tokens) scaled by its sigmoid gate --
      the accumulation order of run_qwen_sparse_moe_vulkan_accum
@@ -46,9 +46,12 @@ def exchange_counts(send_counts: torch.Tensor, group=None) -> torch.Tensor:
 
 
 def dispatch_rows(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, e_local: int, world: int,
-                  group=None, row_dtype=torch.float16):
+                  group=None, row_dtype=torch.float16, extra_rows: int = 0):
     """Steps 1-2: returns (received rows, their local expert ids, their routing
-    weights, state for combine_rows)."""
+    weights, state for combine_rows).  The rows are gathered after one
+    conversion of x to `row_dtype` (none when x has it already); the returned
+    row buffer has `extra_rows` more rows after the received ones, left for
+    the caller to fill."""
     T, k = ids.shape
     order, send_counts, local = dispatch_plan(ids, e_local, world)
     recv_counts = exchange_counts(send_counts.to(x.device), group).cpu()
@@ -56,28 +59,31 @@ def dispatch_rows(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, e_local: 
     ss, rs = send_counts.tolist(), recv_counts.tolist()
     n_recv = int(sum(rs))
     tok = torch.div(order, k, rounding_mode="floor")
-    send_x = x.index_select(0, tok).to(row_dtype).contiguous()
+    xr = x if x.dtype == row_dtype else x.to(row_dtype)
+    send_x = xr.index_select(0, tok)
     meta = torch.stack([local.index_select(0, order).to(torch.float32),
                         w.reshape(-1).index_select(0, order).to(torch.float32)], dim=1).contiguous()
-    recv_x = torch.empty(n_recv, x.shape[1], dtype=row_dtype, device=x.device)
+    recv_x = torch.empty(n_recv + extra_rows, x.shape[1], dtype=row_dtype, device=x.device)
     recv_meta = torch.empty(n_recv, 2, dtype=torch.float32, device=x.device)
-    dist.all_to_all_single(recv_x, send_x, rs, ss, group=group)
+    dist.all_to_all_single(recv_x[:n_recv], send_x, rs, ss, group=group)
     dist.all_to_all_single(recv_meta, meta, rs, ss, group=group)
     state = (order, ss, rs, T, k)
     return recv_x, recv_meta[:, 0].to(torch.int32), recv_meta[:, 1].contiguous(), state
 
 
 def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float16):
-    """Steps 4-5 (routed part): the weighted rows back to their tokens, summed
-    in pick order in fp32.  Returns [T, H]."""
+    """Steps 4-5 (routed part): the weighted rows back to their tokens (sent as
+    `row_dtype`), put in (token, pick) order by the inverse of the dispatch
+    permutation and summed in pick order in fp32.  Returns [T, H] fp32."""
     order, ss, rs, T, k = state
     H = y_recv.shape[1]
     back = torch.empty(len(order), H, dtype=row_dtype, device=y_recv.device)
-    dist.all_to_all_single(back, y_recv.to(row_dtype).contiguous(), ss, rs, group=group)
-    y = torch.empty(T * k, H, dtype=torch.float32, device=y_recv.device)
-    y.index_copy_(0, order, back.to(torch.float32))
-    y = y.view(T, k, H)
-    acc = y[:, 0].clone()
+    send = y_recv if y_recv.dtype == row_dtype else y_recv.to(row_dtype)
+    dist.all_to_all_single(back, send.contiguous(), ss, rs, group=group)
+    inv = torch.empty_like(order)
+    inv[order] = torch.arange(len(order), device=order.device, dtype=order.dtype)
+    y = back.index_select(0, inv).view(T, k, H)
+    acc = y[:, 0].to(torch.float32, copy=True)
     for p in range(1, k):
         acc.add_(y[:, p])
     return acc
@@ -119,14 +125,16 @@ class ExpertParallelMoE:
         ids = ids if ids is not None else torch.empty(T, self.k, dtype=torch.int32, device=dev)
         w = weights if weights is not None else torch.empty(T, self.k, device=dev)
         self.router.route_qwen_top_k(x, T, ids, w)
-        recv_x, recv_ids, recv_w, state = dispatch_rows(x, ids, w, self.e_count, self.world, self.group)
-        n = recv_x.shape[0]
+        x16 = x.to(torch.float16)
         # received rows, then this rank's own tokens for the shared expert
-        rows = torch.cat([recv_x, x.to(recv_x.dtype)], dim=0).contiguous()
+        rows, recv_ids, recv_w, state = dispatch_rows(x16, ids, w, self.e_count, self.world,
+                                                      self.group, extra_rows=T)
+        n = rows.shape[0] - T
+        rows[n:].copy_(x16)
         rid = torch.cat([recv_ids, torch.full((T,), self.e_count, dtype=torch.int32, device=dev)])
         sg = torch.sigmoid(x @ self.gate)
         rw = torch.cat([recv_w, sg]).contiguous()
-        y = torch.empty(n + T, H, device=dev)
+        y = torch.empty(n + T, H, dtype=torch.float16, device=dev)   # fp16 rows out
         self.experts.run_experts(rows, n + T, rid.view(-1, 1).contiguous(), rw.view(-1, 1), y,
                                  prefill=True)
         routed = combine_rows(y[:n], state, self.group)

@@ -82,3 +82,21 @@ def test_prefill_experts_take_fp16_rows(torch):
     torch.cuda.synchronize()
     assert torch.equal(o32, o16)
     assert f.ctx.status()[0] == 0
+
+
+def test_prefill_experts_write_fp16_rows(torch):
+    """With an fp16 output (OSM_OUTPUT_F16) each output element is the fp32
+    result of the same call rounded to fp16 once."""
+    H, E, I, K, T = 256, 8, 256, 2, 130
+    f = MoeFixture(torch, H, E, I, K, seed=96, shared=False, max_tokens=T)
+    x = torch.from_numpy(f.port.gen_normal(96, 4, 1.0, T * H).reshape(T, H)).cuda()
+    rs = np.random.RandomState(4)
+    ids = torch.from_numpy(np.stack([rs.permutation(E)[:K] for _ in range(T)]).astype(np.int32)).cuda()
+    w = torch.from_numpy(rs.rand(T, K).astype(np.float32)).cuda()
+    o32 = torch.empty(T, H, device="cuda")
+    o16 = torch.empty(T, H, dtype=torch.float16, device="cuda")
+    f.layer.run_experts(x, T, ids, w, o32, prefill=True)
+    f.layer.run_experts(x.half(), T, ids, w, o16, prefill=True)
+    torch.cuda.synchronize()
+    assert torch.equal(o32.half(), o16)
+    assert f.ctx.status()[0] == 0
