@@ -218,15 +218,25 @@ def run_ours(args, rank, world, local_rank):
         hout[B] = torch.empty(B, H).pin_memory()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     torch.cuda.synchronize()
+    # one CUDA-graph plan per batch size (osm_plan_create), the e2e ones with the
+    # pinned-host copy of x in and of out back inside the graph
+    # (largest batch first: the context's scratch is sized once)
+    order = sorted(SWEEP, reverse=True)
+    plans = {B: osm.Plan(layer, B, xs[B], outs[B], ids=ids_d[B]) for B in order} if args.graphs else {}
+    plans_e2e = ({B: osm.Plan(layer, B, xs[B], outs[B], ids=ids_d[B], x_host=hx[B], out_host=hout[B])
+                  for B in order} if args.graphs else {})
 
-    def call(B, e2e):
+    def call(B, e2e, eager=False):
+        if args.graphs and not eager:
+            (plans_e2e if e2e else plans)[B].launch()
+            return
         if e2e:
             xs[B].copy_(hx[B], non_blocking=True)
         layer.run_qwen_sparse_moe(xs[B], B, outs[B], ids=ids_d[B])
         if e2e:
             hout[B].copy_(outs[B], non_blocking=True)
 
-    def timed_pass(steps, e2e):
+    def timed_pass(steps, e2e, eager=False):
         evs = []
         for _ in range(steps):
             for B in SWEEP:
@@ -234,7 +244,7 @@ def run_ours(args, rank, world, local_rank):
                 a = torch.cuda.Event(enable_timing=True)
                 b = torch.cuda.Event(enable_timing=True)
                 a.record(stream)
-                call(B, e2e)
+                call(B, e2e, eager)
                 b.record(stream)
                 evs.append((B, a, b))
         return evs
@@ -257,6 +267,7 @@ def run_ours(args, rank, world, local_rank):
 
     timed_pass(args.warmup, False)
     timed_pass(max(1, args.warmup // 2), True)
+    timed_pass(max(1, args.warmup // 2), False, eager=True)
     torch.cuda.synchronize()
     ctx.status()
     clocks.start()
@@ -281,6 +292,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     total_ms_e2e = sum(a.elapsed_time(b) for _, a, b in evs2)
+    # ---- the same calls launched one by one (no graph), for comparison ----
+    eager_b = {B: 0.0 for B in SWEEP}
+    if args.graphs:
+        evs3 = timed_pass(args.steps, False, eager=True)
+        torch.cuda.synchronize()
+        for B, a, b in evs3:
+            eager_b[B] += a.elapsed_time(b)
+    for p in list(plans.values()) + list(plans_e2e.values()):
+        p.close()
     # ---- per-kernel profile pass (roofline) ----
     uniq = {}
     for B in SWEEP:
@@ -320,6 +340,8 @@ def run_ours(args, rank, world, local_rank):
         sweep[str(B)] = {"us_per_call": round(us, 2), "distinct_experts": uniq[B],
                          "alg_bytes": byt, "gbs": round(byt / us / 1e3, 1),
                          "frac_hbm": round(byt / us / 1e3 / peaks["hbm_gbs"], 3)}
+        if args.graphs:
+            sweep[str(B)]["eager_us_per_call"] = round(eager_b[B] / args.steps * 1e3, 2)
     kernels = {k: {"ms": round(v[0], 3), "launches": int(v[1]),
                    "share": round(v[0] / sum(x[0] for x in prof.values()), 3)} for k, v in prof.items()}
     traffic, traffic_note = None, None
@@ -346,6 +368,10 @@ def run_ours(args, rank, world, local_rank):
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                    "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
                    "timing": "sum of per-call CUDA-event intervals on the launching stream",
+                   "calls": ("one CUDA-graph plan launch per call (osm_plan_launch; e2e plans hold "
+                             "the pinned-host copies); eager_us_per_call: the same call through "
+                             "osm_moe_forward, kernels launched one by one") if args.graphs
+                            else "osm_moe_forward, kernels launched one by one",
                    "bracket_wall_s": round(bracket_s, 3),
                    "exact_route_tokens": int(exact_tokens),
                    "per_batch": sweep, "kernels": kernels},
@@ -777,6 +803,9 @@ def main():
     ap.add_argument("--workload", choices=("decode", "prefill", "stream"), default="decode",
                     help="decode: configs[1] sweep (the headline line); prefill: configs[2]; "
                          "stream: configs[4]")
+    ap.add_argument("--eager", dest="graphs", action="store_false",
+                    help="decode sweep: launch each call's kernels one by one instead of "
+                         "replaying a CUDA-graph plan")
     ap.add_argument("--stream-layers", type=int, default=48,
                     help="with --workload stream: layers in the stack")
     args = ap.parse_args()

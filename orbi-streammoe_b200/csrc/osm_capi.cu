@@ -104,6 +104,9 @@ struct osm_context {
   const float* cur_x = nullptr;  // activations of the call in flight (expert kernels)
   std::vector<cudaEvent_t> ev_pool;
   std::vector<ProfRec> recs;
+  void* status_blk = nullptr;       // status word + exact-route counter: never moves
+  int plans_alive = 0;              // captured graphs hold scratch pointers
+  std::vector<void*> retired;       // scratch blocks a live plan may still use
   uint32_t* picks_host = nullptr;   // mapped pinned: the picks a cached call reads back
   uint32_t* picks_dev = nullptr;    // the same memory as the kernels address it
   size_t picks_cap = 0;
@@ -276,19 +279,19 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t o_orow = take(P * 4);
   const size_t o_hf = take(P * (I / 8) * 32), o_hs = take(P * (I / 8) * 4);
   const size_t o_part = take(P * H * 4), o_norm = take(T * H * 4);
-  const size_t o_status = take(4), o_exact = take(8);
   const size_t o_pptr = take(T * k * sizeof(void*));
   void* base = nullptr;
   cudaError_t e = cudaMalloc(&base, off);
   if (e != cudaSuccess) return fail(ctx, OSM_ENOMEM, "scratch allocation failed");
-  // Keep status / exact counters across growth.
-  uint32_t st = 0;
-  unsigned long long ex = 0;
   if (s.base) {
-    cudaStreamSynchronize(ctx->stream);
-    cudaMemcpy(&st, s.status, 4, cudaMemcpyDeviceToHost);
-    cudaMemcpy(&ex, s.exact_count, 8, cudaMemcpyDeviceToHost);
-    cudaFree(s.base);
+    // a captured plan replays on the block it was captured with: keep it
+    // until the context goes; otherwise free it once queued work is done
+    if (ctx->plans_alive > 0) {
+      ctx->retired.push_back(s.base);
+    } else {
+      cudaStreamSynchronize(ctx->stream);
+      cudaFree(s.base);
+    }
   }
   cudaMemset(base, 0, off);
   char* b = static_cast<char*>(base);
@@ -322,11 +325,7 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.hfsum8 = reinterpret_cast<float*>(b + o_hs);
   s.partial = reinterpret_cast<float*>(b + o_part);
   s.normalized = reinterpret_cast<float*>(b + o_norm);
-  s.status = reinterpret_cast<uint32_t*>(b + o_status);
-  s.exact_count = reinterpret_cast<unsigned long long*>(b + o_exact);
   s.pick_ptr = reinterpret_cast<const uint8_t**>(b + o_pptr);
-  cudaMemcpy(s.status, &st, 4, cudaMemcpyHostToDevice);
-  cudaMemcpy(s.exact_count, &ex, 8, cudaMemcpyHostToDevice);
   return OSM_OK;
 }
 
@@ -711,6 +710,14 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
     return OSM_ECUDA;
   }
   ctx->stream = ctx->own_stream;
+  if (cudaMalloc(&ctx->status_blk, 16) != cudaSuccess || cudaMemset(ctx->status_blk, 0, 16) != cudaSuccess) {
+    if (ctx->status_blk) cudaFree(ctx->status_blk);
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+    return OSM_ENOMEM;
+  }
+  ctx->sc.status = static_cast<uint32_t*>(ctx->status_blk);
+  ctx->sc.exact_count = reinterpret_cast<unsigned long long*>(static_cast<char*>(ctx->status_blk) + 8);
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) {
     ctx->grid_cap = sms * 4;
@@ -729,6 +736,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   osm::init_prefill_attributes(ctx->max_smem);
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {
+    cudaFree(ctx->status_blk);
     cudaStreamDestroy(ctx->own_stream);
     delete ctx;
     return OSM_ECUDA;
@@ -742,6 +750,8 @@ int osm_context_destroy(osm_context* ctx) {
   DeviceGuard dg(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   if (ctx->sc.base) cudaFree(ctx->sc.base);
+  for (void* p : ctx->retired) cudaFree(p);
+  if (ctx->status_blk) cudaFree(ctx->status_blk);
   for (const ProfRec& r : ctx->recs) {
     cudaEventDestroy(r.a);
     cudaEventDestroy(r.b);
@@ -813,13 +823,11 @@ int osm_context_status(osm_context* ctx, uint32_t* status, uint64_t* exact_token
   DeviceGuard dg(ctx->device);
   uint32_t st = 0;
   unsigned long long ex = 0;
-  if (ctx->sc.base) {
-    OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-    OSM_CUDA(ctx, cudaMemcpy(&st, ctx->sc.status, 4, cudaMemcpyDeviceToHost));
-    OSM_CUDA(ctx, cudaMemcpy(&ex, ctx->sc.exact_count, 8, cudaMemcpyDeviceToHost));
-    OSM_CUDA(ctx, cudaMemset(ctx->sc.status, 0, 4));
-    OSM_CUDA(ctx, cudaMemset(ctx->sc.exact_count, 0, 8));
-  }
+  OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  OSM_CUDA(ctx, cudaMemcpy(&st, ctx->sc.status, 4, cudaMemcpyDeviceToHost));
+  OSM_CUDA(ctx, cudaMemcpy(&ex, ctx->sc.exact_count, 8, cudaMemcpyDeviceToHost));
+  OSM_CUDA(ctx, cudaMemset(ctx->sc.status, 0, 4));
+  OSM_CUDA(ctx, cudaMemset(ctx->sc.exact_count, 0, 8));
   if (status) *status = st;
   if (exact_tokens) *exact_tokens = ex;
   return OSM_OK;
@@ -1499,6 +1507,7 @@ int osm_plan_create(osm_layer* L, uint32_t T, const float* x, float* out, uint32
     e = cudaGraphInstantiate(&plan->exec, graph, 0);
     if (e != cudaSuccess) rc = cuda_fail(ctx, e, "plan: instantiate");
   }
+  if (rc == OSM_OK) ++ctx->plans_alive;
   if (graph) cudaGraphDestroy(graph);
   if (rc != OSM_OK) {
     osm_plan_destroy(plan);
@@ -1522,7 +1531,10 @@ int osm_plan_destroy(osm_plan* plan) {
   osm_context* ctx = plan->layer->ctx;
   DeviceGuard dg(ctx->device);
   cudaStreamSynchronize(ctx->stream);
-  if (plan->exec) cudaGraphExecDestroy(plan->exec);
+  if (plan->exec) {
+    cudaGraphExecDestroy(plan->exec);
+    --ctx->plans_alive;
+  }
   for (const ProfRec& r : plan->recs) {
     cudaEventDestroy(r.a);
     cudaEventDestroy(r.b);

@@ -355,3 +355,41 @@ def test_plan_replay_matches_direct_call(torch):
                 plan2.close()
         finally:
             fx.ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+
+
+def test_plans_keep_their_scratch_when_a_larger_call_grows_it(torch):
+    """Plans captured for growing batch sizes on one context (each capture
+    grows the context's scratch) and all replayed afterwards: every plan still
+    gives the direct call's bits, and the status word stays clean."""
+    import osm_b200 as osm
+
+    fx = _q3n_fixture(torch)
+    ctx = osm.Context(0, max_tokens=64)       # fresh context: scratch not sized yet
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    slab = osm.Slab(ctx, fx.layout, fx.E)
+    for e in range(fx.E):
+        slab.fill_async(e, fx.pinned.data_ptr() + e * fx.layout.stride)
+    slab.fill_wait()
+    layer = osm.Layer(ctx, fx.W, fx.K, True, logit_bias=fx.bias, shared_slot=fx.shared_slot,
+                      shared_layout=fx.layout, shared_gate=fx.sg)
+    layer.bind_slab(slab, np.arange(fx.E, dtype=np.int32))
+    plans, bufs = [], []
+    with torch.cuda.stream(stream):
+        for B in (1, 3, 40):
+            x = fx.port.gen_normal(11, 70 + B, 1.0, B * fx.H).reshape(B, fx.H)
+            xd = torch.from_numpy(x).cuda()
+            out = torch.empty(B, fx.H, device="cuda")
+            plans.append(osm.Plan(layer, B, xd, out))
+            bufs.append((B, xd, out))
+        for p in plans:
+            p.launch()
+        stream.synchronize()
+        for (B, xd, out) in bufs:
+            ref = torch.empty(B, fx.H, device="cuda")
+            layer.run_qwen_sparse_moe(xd, B, ref)
+            stream.synchronize()
+            assert torch.equal(out, ref), B
+    assert ctx.status()[0] == 0
+    for p in plans:
+        p.close()
