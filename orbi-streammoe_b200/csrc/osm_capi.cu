@@ -459,7 +459,10 @@ bool grouped_path(osm_layer* L, osm::GrpArgs* a, size_t* smem_gu, size_t* smem_d
   return osm::grouped_configure(*a, ctx->max_smem, smem_gu, smem_dn);
 }
 
-int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
+// picks_from_ids: one token whose picks the decode kernels resolve through
+// the slot table themselves (no binding step ran)
+int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
+                bool picks_from_ids = false) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
   const osm_expert_layout& R = L->slab->layout;
@@ -477,7 +480,8 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual) {
     g.tp_pos = s.tp_pos;
     g.direct = T == 1 ? 1 : 0;
     g.ids = s.ids;
-    g.pick_ptr = s.pick_ptr;
+    g.pick_ptr = picks_from_ids ? nullptr : s.pick_ptr;
+    g.mass = s.mass;
     g.slot_of = L->slot_of;
     g.status = s.status;
     g.h = s.partial;
@@ -1422,20 +1426,22 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   //    the reference's expert_cache.get calls, routed_moe.cpp:319-327)
   rc = osm_cache_acquire(cache, layer_id, ctx->picks_host, (uint32_t)nk);
   if (rc) return fail(ctx, rc, std::string("cached forward: ") + cache->err);
-  // 4. bind the picks to their slots (and group them), then the experts
+  // 4. bind the picks to their slots and group them, then the experts; one
+  //    token on the decode kernels needs neither (they read the slot table)
+  const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
+  if (!prefill && T == 1 && dec) return run_experts(L, T, out, res, true);
   a.skip_route = 1;
   a.ids_out = nullptr;
   a.weights_out = nullptr;
   a.sgate_out = nullptr;
   a.pick_ptr = s.pick_ptr;
-  a.do_group = (!prefill && T == 1 && dec) ? 0 : 1;
+  a.do_group = 1;
   {
     Prof p(ctx, kKRouterSelect);
     osm::launch_group(a, ctx->stream, &ctx->launches);
   }
   rc = check_launch(ctx, "pick binding");
   if (rc) return rc;
-  const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
   if (prefill) return run_prefill(L, T, out, res, pa, psm);
   return run_experts(L, T, out, res);
 }

@@ -155,11 +155,27 @@ __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
   en.tg0 = 0;
   en.pad0 = en.pad1 = 0;
   if (j < a.k) {
-    // the router wrote the slot base of each pick (null: bad or not resident)
     en.kind = 0;
-    en.ptr = CG ? reinterpret_cast<const uint8_t*>(__ldcg(
-                      reinterpret_cast<const unsigned long long*>(a.pick_ptr + j)))
-                : a.pick_ptr[j];
+    if (a.pick_ptr != nullptr) {
+      // the router wrote the slot base of each pick (null: bad or not resident)
+      en.ptr = CG ? reinterpret_cast<const uint8_t*>(__ldcg(
+                        reinterpret_cast<const unsigned long long*>(a.pick_ptr + j)))
+                  : a.pick_ptr[j];
+    } else {
+      // the same resolution as the router's: slot of the picked expert
+      en.ptr = nullptr;
+      const float m = CG ? __ldcg(a.mass) : a.mass[0];
+      if (m > 0.0f) {
+        const uint32_t id = CG ? __ldcg(a.ids + j) : a.ids[j];
+        if (id >= (uint32_t)a.E) {
+          atomicOr(a.status, kStatusBadSlot);
+        } else {
+          const int slot = CG ? __ldcg(a.slot_of + id) : a.slot_of[id];
+          if (slot < 0) atomicOr(a.status, kStatusNotResident);
+          else en.ptr = a.slab + (size_t)slot * a.slab_stride;
+        }
+      }
+    }
   } else {
     en.kind = 1;
     en.ptr = a.shared_ptr;

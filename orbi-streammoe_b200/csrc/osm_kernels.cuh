@@ -155,7 +155,10 @@ struct GemvArgs {
   // routing, entry k the shared expert
   int direct;
   const uint32_t* ids;           // [k]
-  const uint8_t* const* pick_ptr;  // [k] slot base of each pick (router-written)
+  // [k] slot base of each pick (router-written); null: resolved here from
+  // ids through slot_of (a token whose mass the router set to 0 has none)
+  const uint8_t* const* pick_ptr;
+  const float* mass;             // [1] with pick_ptr null
   int E;                         // experts (ids >= E are rejected)
   const int* slot_of;            // [E]
   const uint8_t* slab;
