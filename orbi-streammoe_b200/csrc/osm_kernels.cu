@@ -40,8 +40,10 @@ __global__ void combine_kernel(CombineArgs a) {
   a.out[(size_t)b * a.H + i] = acc;
 }
 
-__global__ void rmsnorm_kernel(const float* __restrict__ in, float* __restrict__ out, int dim,
-                               const float* __restrict__ w, float eps, int exact) {
+// in == out is allowed (osm_rms_norm normalises in place): no __restrict__
+// on them; each element is read before its own write
+__global__ void rmsnorm_kernel(const float* in, float* out, int dim, const float* __restrict__ w,
+                               float eps, int exact) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
