@@ -543,6 +543,136 @@ def run_prefill(args, rank, world, local_rank):
 
 
 # ----------------------------------------------------------------------------
+# Qwen3-30B-A3B-shaped sublayer at 1, 64 and 8192 tokens (--workload q30)
+# ----------------------------------------------------------------------------
+Q30_H, Q30_E, Q30_I, Q30_K = 2048, 128, 768, 8
+Q30_T = (1, 64, 8192)
+
+
+def run_q30(args, rank, world, local_rank):
+    import torch
+
+    import osm_b200 as osm
+
+    if world > 1:
+        raise SystemExit("--workload q30 runs on one GPU")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    ctx = osm.Context(local_rank, max_tokens=max(Q30_T))
+    ctx.set_stream(stream.cuda_stream)
+    lay = osm.expert_layout(Q30_H, Q30_I, GROUP)
+    slab = osm.Slab(ctx, lay, Q30_E)
+    slab.generate(SEED + 3, 1000, 0.02, 0, Q30_E)
+    buf = torch.empty(Q30_E * Q30_H, device=dev)
+    ctx.gen_normal(SEED + 3, 1, 0.02, buf)
+    W = bf16_round(buf.cpu().numpy()).reshape(Q30_E, Q30_H)
+    layer = osm.Layer(ctx, W, Q30_K, True)
+    layer.bind_slab(slab, np.arange(Q30_E, dtype=np.int32))
+    xs, outs, hx, hout = {}, {}, {}, {}
+    for T in Q30_T:
+        xs[T] = torch.empty(T, Q30_H, device=dev)
+        ctx.gen_normal(SEED + 3, 9000 + T, 1.0, xs[T])
+        outs[T] = torch.empty(T, Q30_H, device=dev)
+        hx[T] = xs[T].cpu().pin_memory()
+        hout[T] = torch.empty(T, Q30_H).pin_memory()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    dec = [T for T in Q30_T if T < 1024]
+    plans = {T: osm.Plan(layer, T, xs[T], outs[T]) for T in sorted(dec, reverse=True)}
+    plans_e2e = {T: osm.Plan(layer, T, xs[T], outs[T], x_host=hx[T], out_host=hout[T])
+                 for T in sorted(dec, reverse=True)}
+
+    def call(T, e2e):
+        if T in plans:
+            (plans_e2e if e2e else plans)[T].launch()
+            return
+        if e2e:
+            xs[T].copy_(hx[T], non_blocking=True)
+        layer.run_qwen_sparse_moe(xs[T], T, outs[T], prefill=True)
+        if e2e:
+            hout[T].copy_(outs[T], non_blocking=True)
+
+    def timed_pass(steps, e2e):
+        per = {T: 0.0 for T in Q30_T}
+        for _ in range(steps):
+            for T in Q30_T:
+                flush.zero_()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                call(T, e2e)
+                b.record(stream)
+                b.synchronize()
+                per[T] += a.elapsed_time(b)
+        return per
+
+    gpu_uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local_rank))
+    if gpu_uuid and not gpu_uuid.startswith("GPU-") and len(gpu_uuid) > 8:
+        gpu_uuid = "GPU-" + gpu_uuid
+    clocks = ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else str(local_rank))
+    timed_pass(args.warmup, False)
+    timed_pass(max(1, args.warmup // 2), True)
+    ctx.status()
+    clocks.start()
+    l0 = ctx.launches
+    per = timed_pass(args.steps, False)
+    launches = ctx.launches - l0
+    per_e2e = timed_pass(args.steps, True)
+    for p in list(plans.values()) + list(plans_e2e.values()):
+        p.close()
+    ctx.profile_read()
+    ctx.profile(True)
+    prof_steps = max(1, min(args.steps, 10))
+    for _ in range(prof_steps):
+        flush.zero_()
+        call(Q30_T[-1], False)
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    clk = clocks.stop()
+    status, exact_tokens = ctx.status()
+    if status:
+        raise RuntimeError(f"device status {status} during the q30 benchmark")
+    tokens = sum(Q30_T)
+    total_ms, total_e2e = sum(per.values()), sum(per_e2e.values())
+    value = tokens * args.steps / (total_ms / 1e3)
+    peaks = load_peaks()
+    Tp = Q30_T[-1]
+    gemm_ms = (prof.get("proj_gate_up", (0.0, 0))[0] + prof.get("proj_down", (0.0, 0))[0]) / prof_steps
+    tflops = Tp * Q30_K * 3 * 2 * Q30_H * Q30_I / (gemm_ms / 1e3) / 1e12
+    cases = {str(T): {"us_per_call": round(per[T] / args.steps * 1e3, 2),
+                      "tokens_per_s": round(T * args.steps / (per[T] / 1e3), 1),
+                      "path": "graph plan, decode kernels" if T in plans else "tensor-core prefill"}
+             for T in Q30_T}
+    kernels = {k: {"ms_per_call": round(v[0] / prof_steps, 4), "launches": int(v[1]),
+                   "share": round(v[0] / sum(x[0] for x in prof.values()), 3)} for k, v in prof.items()}
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 (1 and 64 tokens); fp16 operands, fp32 accumulation (8192-token experts)",
+        "data": "synthetic (seeded N(0,0.02) weights, reference quantiser, bf16 scale/bias; x~N(0,1))",
+        "config": {"workload": "configs[3]: Qwen3-30B-A3B-shaped routed-MoE sublayer (hidden 2048, "
+                               "128 experts, top-8, moe_inter 768, no shared expert), 1, 64 and 8192 "
+                               "tokens per step",
+                   "tokens_per_step": tokens, "parallelism": "single GPU",
+                   "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
+                   "timing": "sum of per-call CUDA-event intervals on the launching stream",
+                   "exact_route_tokens": int(exact_tokens), "per_case": cases,
+                   "kernels_8192": kernels},
+        "e2e": {"value": round(tokens * args.steps / (total_e2e / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": tokens * Q30_H * 4, "d2h_bytes_per_step": tokens * Q30_H * 4},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": "pf_gemm (gate/up + down), 8192 tokens",
+                     "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops"], 3), "traffic": None,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, burst)"},
+        "clocks": clk,
+    }
+
+
+# ----------------------------------------------------------------------------
 # 48-layer batch-1 decode streaming experts from pinned host memory
 # into an 8 GB HBM cache (--workload stream)
 # ----------------------------------------------------------------------------
@@ -800,9 +930,9 @@ def main():
     ap.add_argument("--prefill", action="store_true",
                     help="with --single: the config-2 sublayer on the tensor-core prefill path")
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--workload", choices=("decode", "prefill", "stream"), default="decode",
+    ap.add_argument("--workload", choices=("decode", "prefill", "q30", "stream"), default="decode",
                     help="decode: configs[1] sweep (the headline line); prefill: configs[2]; "
-                         "stream: configs[4]")
+                         "q30: configs[3] (one GPU); stream: configs[4]")
     ap.add_argument("--eager", dest="graphs", action="store_false",
                     help="decode sweep: launch each call's kernels one by one instead of "
                          "replaying a CUDA-graph plan")
@@ -834,6 +964,8 @@ def main():
             line = run_prefill(args, rank, world, local_rank)
         elif args.workload == "stream":
             line = run_stream(args, rank, world, local_rank)
+        elif args.workload == "q30":
+            line = run_q30(args, rank, world, local_rank)
         else:
             line = run_ours(args, rank, world, local_rank)
     finally:
