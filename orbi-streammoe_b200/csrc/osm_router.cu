@@ -49,7 +49,8 @@ constexpr int kLogitWarps = 4;
 constexpr int kMaxVec = 8;                    // H <= 2048 on the register path
 constexpr int kSelThreads = 512;
 constexpr int kMaxCand = 16;                  // candidates of the partial exact path
-constexpr int kFullTile = 32;                 // h per tile on the full exact path
+constexpr int kPartChunk = 512;               // h staged at a time on the partial exact path
+constexpr int kFullTile = 16;                 // h per tile on the full exact path
 
 __device__ __forceinline__ void unpack8(const uint4 q, float w[8]) {
   const uint32_t ww[4] = {q.x, q.y, q.z, q.w};
@@ -710,7 +711,8 @@ __device__ __forceinline__ bool distinct_p(float hi, float lo, float mx) {
   return __fsub_rd(hi, lo) > 1e-6f + 3e-7f * (fabsf(hi - mx) + fabsf(lo - mx));
 }
 
-__global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArgs a) {
+template <int TPB>
+__global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterArgs a) {
   extern __shared__ float4 smem4[];
   float* xs = reinterpret_cast<float*>(smem4);  // [H]
   char* uni = reinterpret_cast<char*>(xs + ((a.g.H + 3) & ~3));
@@ -721,9 +723,9 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
   __shared__ float cand_l[kMaxCand];
   __shared__ int s_flag, s_ncand;
   __shared__ float s_bm, s_bcast, s_sum, s_mx;
-  __shared__ float sg_part[kSelThreads / 32];
-  __shared__ float s_red2[kSelThreads / 32];
-  __shared__ unsigned long long s_top[kSelThreads];
+  __shared__ float sg_part[TPB / 32];
+  __shared__ float s_red2[TPB / 32];
+  __shared__ unsigned long long s_top[TPB];
   const RouterGeom g = a.g;
   const int tok = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -739,7 +741,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
   float sgw[kSgRegs];
 #pragma unroll
   for (int j = 0; j < kSgRegs; ++j) {
-    const int h = tid + j * kSelThreads;
+    const int h = tid + j * TPB;
     sgw[j] = (a.sgate_w != nullptr && h < g.H) ? a.sgate_w[h] : 0.0f;
   }
   pdl_wait();
@@ -749,13 +751,13 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
   OSM_STAMP(1);
   TL_WAITED(1);
   const float* x = a.x + (size_t)tok * g.H;
-  // this thread's experts: tid and tid + kSelThreads (E <= 2 * kSelThreads)
+  // this thread's experts: tid and tid + TPB (E <= 2 * TPB)
   float lv[2] = {-INFINITY, -INFINITY};
   float bmax = 0.0f;
   if (!a.skip_route) {
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int e = tid + r * kSelThreads;
+      const int e = tid + r * TPB;
       if (e < g.E) {
         lv[r] = a.logits[(size_t)tok * g.E + e];
         bmax = fmaxf(bmax, a.bounds[(size_t)tok * g.E + e]);
@@ -802,8 +804,8 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
   if (route) {
     const int e0 = warp * 32 + lane;
     top = warp_sort_desc(e0 < g.E ? sel_key(lv[0], e0) : 0ull);
-    if (nl > kSelThreads / 32) {  // E > 512: fold in the second list
-      const int e1 = e0 + kSelThreads;
+    if (nl > TPB / 32) {  // E > 512: fold in the second list
+      const int e1 = e0 + TPB;
       const unsigned long long k1 = warp_sort_desc(e1 < g.E ? sel_key(lv[1], e1) : 0ull);
       top = merge_top(top, __shfl_sync(0xFFFFFFFFu, k1, 31 - lane));
     }
@@ -836,16 +838,16 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
     float d = 0.0f;
 #pragma unroll
     for (int j = 0; j < kSgRegs; ++j) {
-      const int h = tid + j * kSelThreads;
+      const int h = tid + j * TPB;
       if (h < g.H) d = fmaf(sgw[j], xs[h], d);
     }
-    for (int h = tid + kSgRegs * kSelThreads; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
+    for (int h = tid + kSgRegs * TPB; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
     d = warp_sum(d);
     if (lane == 0) sg_part[warp] = d;
   }
   __syncthreads();
   OSM_STAMP(3);
-  for (int step = 1; step < kSelThreads / 32; step <<= 1) {
+  for (int step = 1; step < TPB / 32; step <<= 1) {
     if (route && (warp & (2 * step - 1)) == 0) {
       top = merge_top(top, s_top[(warp + step) * 32 + 31 - lane]);
       s_top[warp * 32 + lane] = top;
@@ -877,7 +879,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
     float es = 0.0f;
 #pragma unroll
     for (int r = 0; r < 2; ++r)
-      if (tid + r * kSelThreads < g.E) es += __expf(__fsub_rn(lv[r], mx));
+      if (tid + r * TPB < g.E) es += __expf(__fsub_rn(lv[r], mx));
     es = warp_sum(es);
     if (lane == 0) red[warp] = es;
   }
@@ -922,35 +924,44 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
     if (nc > kMaxCand || g.f32w || nc < k) {
       if (tid == 0) s_flag = 2;
     } else {
-      // rows of the candidates, transposed: wt[h * kMaxCand + j] (bf16)
+      // rows of the candidates, kPartChunk values of h at a time, transposed:
+      // wt[(h - hc) * kMaxCand + j] (bf16)
       uint16_t* wt = reinterpret_cast<uint16_t*>(uni);
-      const int vpr = g.Hp >> 3;  // 8-element vectors per row
-      for (int i = tid; i < nc * vpr; i += blockDim.x) {
-        const int j = i / vpr, vi = i - j * vpr;
-        const int m = vi >> 5, l = vi & 31;
-        const uint4 q = __ldg(a.wp + ((size_t)cand_id[j] * g.nvec + m) * 32 + l);
-        const uint32_t ww[4] = {q.x, q.y, q.z, q.w};
-        const int h0 = l * g.c + 8 * m;
+      constexpr int vpc = kPartChunk / 8;  // 8-element vectors per row and chunk
+      // the reference's sequential sum, carried across the chunks in h order:
+      // products are independent of the running sum, so a batch of them is
+      // formed ahead of the add chain
+      float acc = 0.0f;
+      for (int hc = 0; hc < g.H; hc += kPartChunk) {
+        for (int i = tid; i < nc * vpc; i += blockDim.x) {
+          const int j = i / vpc, h0 = hc + 8 * (i - j * vpc);
+          if (h0 >= g.H) continue;
+          const int l = h0 / g.c, m = (h0 - l * g.c) >> 3;
+          const uint4 q = __ldg(a.wp + ((size_t)cand_id[j] * g.nvec + m) * 32 + l);
+          const uint32_t ww[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj)
-          if (h0 + jj < g.H) wt[(h0 + jj) * kMaxCand + j] = (uint16_t)((ww[jj >> 1] >> ((jj & 1) * 16)) & 0xFFFFu);
-      }
-      __syncthreads();
-      if (tid < nc) {
-        // the reference's sequential sum: products are independent of the
-        // running sum, so a batch of them is formed ahead of the add chain
-        float acc = 0.0f;
-        int h = 0;
-        for (; h + 64 <= g.H; h += 64) {
-          float pr[64];
-#pragma unroll
-          for (int u = 0; u < 64; ++u)
-            pr[u] = __fmul_rn(bf16_bits_to_f32(wt[(h + u) * kMaxCand + tid]), xs[h + u]);
-#pragma unroll
-          for (int u = 0; u < 64; ++u) acc = __fadd_rn(acc, pr[u]);
+          for (int jj = 0; jj < 8; ++jj)
+            if (h0 + jj < g.H)
+              wt[(h0 - hc + jj) * kMaxCand + j] = (uint16_t)((ww[jj >> 1] >> ((jj & 1) * 16)) & 0xFFFFu);
         }
-        for (; h < g.H; ++h)
-          acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wt[h * kMaxCand + tid]), xs[h]));
+        __syncthreads();
+        if (tid < nc) {
+          const int he = min(g.H, hc + kPartChunk);
+          int h = hc;
+          for (; h + 64 <= he; h += 64) {
+            float pr[64];
+#pragma unroll
+            for (int u = 0; u < 64; ++u)
+              pr[u] = __fmul_rn(bf16_bits_to_f32(wt[(h - hc + u) * kMaxCand + tid]), xs[h + u]);
+#pragma unroll
+            for (int u = 0; u < 64; ++u) acc = __fadd_rn(acc, pr[u]);
+          }
+          for (; h < he; ++h)
+            acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wt[(h - hc) * kMaxCand + tid]), xs[h]));
+        }
+        __syncthreads();  // the chunk's rows are read before the next overwrite
+      }
+      if (tid < nc) {
         if (a.bias != nullptr) acc = __fadd_rn(acc, a.bias[cand_id[tid]]);
         cand_l[tid] = acc;
       }
@@ -1006,7 +1017,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
       __syncthreads();
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        const int e = tid + r * kSelThreads;
+        const int e = tid + r * TPB;
         if (e < g.E) {
           const int nh = min(kFullTile, g.H - h0);
           float pr[kFullTile];
@@ -1024,7 +1035,7 @@ __global__ void __launch_bounds__(kSelThreads, 2) router_select_kernel(RouterArg
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int e = tid + r * kSelThreads;
+      const int e = tid + r * TPB;
       if (e < g.E) lex[e] = a.bias != nullptr ? __fadd_rn(acc[r], a.bias[e]) : acc[r];
     }
     __syncthreads();
@@ -1192,7 +1203,7 @@ void launch_logits_t(const RouterArgs& a, cudaStream_t s) {
 
 size_t select_smem(const RouterGeom& g) {
   const size_t xs = (size_t)((g.H + 3) & ~3) * sizeof(float);
-  const size_t partial = (size_t)g.H * kMaxCand * sizeof(uint16_t);
+  const size_t partial = (size_t)kPartChunk * kMaxCand * sizeof(uint16_t);
   const size_t full = (size_t)g.E * sizeof(float) + (size_t)kFullTile * g.E * sizeof(float);
   const size_t grp = (size_t)5 * (g.E + 1) * sizeof(int);
   size_t u = partial;
@@ -1232,9 +1243,16 @@ void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launche
   if (launches) *launches += 1;
 }
 
+// One token per block: 512 threads while the tokens fit one wave of such
+// blocks (two per SM on 148 SMs), 256 beyond (twice the tokens resident per
+// SM, more work per thread); 256 threads take up to 512 experts.
+constexpr int kSelWideTokens = 2 * 148;
 void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
   const size_t sm = select_smem(a.g);
-  launch_pdl(router_select_kernel, dim3(a.B), dim3(kSelThreads), sm, s, a);
+  if (a.B <= kSelWideTokens || a.g.E > 2 * 256)
+    launch_pdl(router_select_kernel<512>, dim3(a.B), dim3(512), sm, s, a);
+  else
+    launch_pdl(router_select_kernel<256>, dim3(a.B), dim3(256), sm, s, a);
   if (launches) *launches += 1;
   if (a.defer_scatter && a.do_group) {
     const int n = a.B * (a.g.k + 1);
@@ -1252,7 +1270,8 @@ void init_router_attributes(int max_smem) {
   cudaFuncSetAttribute(router_exact_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_select_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
 }
 
