@@ -410,14 +410,14 @@ def run_prefill(args, rank, world, local_rank):
     # N > 1: expert parallelism over the ranks (E/N experts each) on the same
     # 4096 tokens, T/N routed per rank (strong scaling)
     t_local = PF_T // world
-    ctx = osm.Context(local_rank, max_tokens=t_local * (K * world + 1) if world > 1 else PF_T)
+    ctx = osm.Context(local_rank, max_tokens=t_local * (K * world + 1) if args.ep else PF_T)
     ctx.set_stream(stream.cuda_stream)
     x_all = torch.empty(PF_T, H, device=dev)
     ctx.gen_normal(SEED, 7000, 1.0, x_all)
     x = x_all[rank * t_local:(rank + 1) * t_local].contiguous()
     del x_all
     out = torch.empty(t_local, H, device=dev)
-    if world > 1:
+    if args.ep:
         from osm_b200 import ep as osm_ep
 
         e_count = E // world
@@ -437,7 +437,7 @@ def run_prefill(args, rank, world, local_rank):
     def call(e2e):
         if e2e:
             x.copy_(hx, non_blocking=True)
-        if world > 1:
+        if args.ep:
             moe.forward(x, out)
         else:
             layer.run_qwen_sparse_moe(x, PF_T, out, prefill=True)
@@ -458,7 +458,7 @@ def run_prefill(args, rank, world, local_rank):
         return ms
 
     def barrier():
-        if world > 1:
+        if args.ep:
             torch.distributed.barrier()
 
     def max_over_ranks(v: float) -> float:
@@ -517,7 +517,7 @@ def run_prefill(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(total_ms / args.steps, 4),
         "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak",
+        "scaling": "strong" if args.ep else "weak",
         "vs_baseline": None,
         "dtype": "fp16 operands, fp32 accumulation (experts); fp32 exact routing",
         "data": "synthetic (seeded N(0,0.02) weights, reference quantiser, bf16 scale/bias; x~N(0,1))",
@@ -527,7 +527,7 @@ def run_prefill(args, rank, world, local_rank):
                    "moe_inter": I, "shared_inter": SHI,
                    "parallelism": (f"expert parallel x{world} ({E // world} experts and "
                                    f"{t_local} tokens per rank, NCCL all-to-all dispatch/combine)"
-                                   if world > 1 else "single GPU"),
+                                   if args.ep else "single GPU"),
                    "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
                    "timing": "sum of per-call CUDA-event intervals on the launching stream",
                    "exact_route_tokens": int(exact_tokens), "kernels": kernels},
@@ -549,13 +549,138 @@ Q30_H, Q30_E, Q30_I, Q30_K = 2048, 128, 768, 8
 Q30_T = (1, 64, 8192)
 
 
+def run_q30_ep(args, rank, world, local_rank):
+    """configs[3] 8192-token case, expert parallel: rank r owns experts
+    [r 128/N, (r+1) 128/N) and routes 8192/N of the tokens (strong scaling);
+    NCCL all-to-all dispatch and combine (osm_b200.ep)."""
+    import torch
+
+    import osm_b200 as osm
+    from osm_b200 import ep as osm_ep
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    stream = torch.cuda.Stream(device=dev)
+    torch.cuda.set_stream(stream)
+    T = Q30_T[-1]
+    t_local, e_count = T // world, Q30_E // world
+    e0 = rank * e_count
+    # rows a rank can receive: every pick of every token
+    ctx = osm.Context(local_rank, max_tokens=T * Q30_K)
+    ctx.set_stream(stream.cuda_stream)
+    lay = osm.expert_layout(Q30_H, Q30_I, GROUP)
+    slab = osm.Slab(ctx, lay, e_count)
+    slab.generate(SEED + 3, 1000 + 3 * e0, 0.02, 0, e_count)  # the one-GPU leg's experts e0..
+    buf = torch.empty(Q30_E * Q30_H, device=dev)
+    ctx.gen_normal(SEED + 3, 1, 0.02, buf)
+    W = bf16_round(buf.cpu().numpy()).reshape(Q30_E, Q30_H)
+    moe = osm_ep.ExpertParallelMoE(ctx, W, Q30_K, True, lay, slab, e0, e_count)
+    x_all = torch.empty(T, Q30_H, device=dev)
+    ctx.gen_normal(SEED + 3, 9000 + T, 1.0, x_all)
+    x = x_all[rank * t_local:(rank + 1) * t_local].contiguous()
+    del x_all
+    out = torch.empty(t_local, Q30_H, device=dev)
+    hx = x.cpu().pin_memory()
+    hout = torch.empty(t_local, Q30_H).pin_memory()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+
+    def call(e2e):
+        if e2e:
+            x.copy_(hx, non_blocking=True)
+        moe.forward(x, out)
+        if e2e:
+            hout.copy_(out, non_blocking=True)
+
+    def timed_pass(steps, e2e):
+        ms = 0.0
+        for _ in range(steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            call(e2e)
+            b.record(stream)
+            b.synchronize()
+            ms += a.elapsed_time(b)
+        return ms
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    gpu_uuid = str(getattr(torch.cuda.get_device_properties(dev), "uuid", local_rank))
+    if gpu_uuid and not gpu_uuid.startswith("GPU-") and len(gpu_uuid) > 8:
+        gpu_uuid = "GPU-" + gpu_uuid
+    clocks = ClockSampler(gpu_uuid if gpu_uuid.startswith("GPU-") else str(local_rank))
+    timed_pass(args.warmup, False)
+    timed_pass(max(1, args.warmup // 2), True)
+    ctx.status()
+    clocks.start()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    l0 = ctx.launches
+    total_ms = timed_pass(args.steps, False)
+    torch.distributed.barrier()
+    launches = ctx.launches - l0
+    total_e2e = timed_pass(args.steps, True)
+    torch.distributed.barrier()
+    ctx.profile_read()
+    ctx.profile(True)
+    prof_steps = max(1, min(args.steps, 10))
+    for _ in range(prof_steps):
+        flush.zero_()
+        call(False)
+    torch.cuda.synchronize()
+    prof = ctx.profile_read()
+    ctx.profile(False)
+    clk = clocks.stop()
+    status, exact_tokens = ctx.status()
+    if status:
+        raise RuntimeError(f"device status {status} during the q30 expert-parallel benchmark")
+    total_ms = max_over_ranks(total_ms)
+    total_e2e = max_over_ranks(total_e2e)
+    peaks = load_peaks()
+    gemm_ms = (prof.get("proj_gate_up", (0.0, 0))[0] + prof.get("proj_down", (0.0, 0))[0]) / prof_steps
+    # this rank's share of the expert GEMM work (its tokens' picks, on average)
+    tflops = t_local * Q30_K * 3 * 2 * Q30_H * Q30_I / (gemm_ms / 1e3) / 1e12
+    kernels = {k: {"ms_per_call": round(v[0] / prof_steps, 4), "launches": int(v[1]),
+                   "share": round(v[0] / sum(q[0] for q in prof.values()), 3)} for k, v in prof.items()}
+    return {
+        "metric": METRIC, "value": round(T * args.steps / (total_ms / 1e3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp16 operands, fp32 accumulation (experts); fp32 exact routing",
+        "data": "synthetic (seeded N(0,0.02) weights, reference quantiser, bf16 scale/bias; x~N(0,1))",
+        "config": {"workload": "configs[3]: Qwen3-30B-A3B-shaped routed-MoE sublayer, 8192-token "
+                               "case, expert parallel",
+                   "tokens_per_step": T,
+                   "parallelism": (f"expert parallel x{world} ({e_count} experts and {t_local} "
+                                   "tokens per rank, NCCL all-to-all dispatch/combine)"),
+                   "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
+                   "timing": "sum of per-call CUDA-event intervals on the launching stream, max "
+                             "over ranks",
+                   "exact_route_tokens": int(exact_tokens), "kernels": kernels},
+        "e2e": {"value": round(T * args.steps / (total_e2e / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": t_local * Q30_H * 4, "d2h_bytes_per_step": t_local * Q30_H * 4},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "kernel": "pf_gemm (gate/up + down), this rank",
+                     "achieved": round(tflops, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": round(tflops / peaks["bf16_tflops"], 3), "traffic": None,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json bf16_tflops, burst)"},
+        "clocks": clk,
+    }
+
+
 def run_q30(args, rank, world, local_rank):
     import torch
 
     import osm_b200 as osm
 
-    if world > 1:
-        raise SystemExit("--workload q30 runs on one GPU")
+    if args.ep:
+        return run_q30_ep(args, rank, world, local_rank)
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
     stream = torch.cuda.Stream(device=dev)
@@ -932,10 +1057,14 @@ def main():
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--workload", choices=("decode", "prefill", "q30", "stream"), default="decode",
                     help="decode: configs[1] sweep (the headline line); prefill: configs[2]; "
-                         "q30: configs[3] (one GPU); stream: configs[4]")
+                         "q30: configs[3] (one GPU: 1, 64 and 8192 tokens; expert parallel: "
+                         "8192 tokens); stream: configs[4]")
     ap.add_argument("--eager", dest="graphs", action="store_false",
                     help="decode sweep: launch each call's kernels one by one instead of "
                          "replaying a CUDA-graph plan")
+    ap.add_argument("--ep", action="store_true",
+                    help="prefill and q30 workloads: the expert-parallel path even on one rank "
+                         "(a one-rank NCCL group); under torchrun with N > 1 it is always used")
     ap.add_argument("--stream-layers", type=int, default=48,
                     help="with --workload stream: layers in the stack")
     args = ap.parse_args()
@@ -951,11 +1080,17 @@ def main():
         if line is not None:
             print(json.dumps(line), flush=True)
         return
-    if world > 1:
+    args.ep = args.ep or world > 1
+    use_group = world > 1 or (args.ep and args.workload in ("prefill", "q30"))
+    if use_group:
         import datetime
 
         import torch
 
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29531")
+        os.environ.setdefault("RANK", str(rank))
+        os.environ.setdefault("WORLD_SIZE", str(world))
         torch.cuda.set_device(local_rank)
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=torch.device("cuda", local_rank))
@@ -969,7 +1104,7 @@ def main():
         else:
             line = run_ours(args, rank, world, local_rank)
     finally:
-        if world > 1:
+        if use_group:
             import torch
 
             torch.distributed.destroy_process_group()

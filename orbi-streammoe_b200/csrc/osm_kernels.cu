@@ -27,8 +27,8 @@ namespace {
 // ----------------------------------------------------------------------------
 __global__ void combine_kernel(CombineArgs a) {
   pdl_wait();
-  const int b = blockIdx.y;
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.x;  // rows in x: more than 65535 of them are allowed
+  const int i = blockIdx.y * blockDim.x + threadIdx.x;
   if (i >= a.H) return;
   const int kp1 = a.k + 1;
   const float* P = a.partial + (size_t)b * kp1 * a.H + i;
@@ -214,7 +214,7 @@ void launch_slot_updates(const SlotUpdates& u, cudaStream_t s, uint64_t* launche
 }
 
 void launch_combine(const CombineArgs& a, cudaStream_t s, uint64_t* launches) {
-  const dim3 grid((a.H + 255) / 256, a.B);
+  const dim3 grid(a.B, (a.H + 255) / 256);
   combine_kernel<<<grid, 256, 0, s>>>(a);
   if (launches) *launches += 1;
 }

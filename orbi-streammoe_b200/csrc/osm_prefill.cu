@@ -397,8 +397,8 @@ __global__ void __launch_bounds__(256) combine_bf16_kernel(
     const float* __restrict__ sg, const float* __restrict__ res, void* __restrict__ out, int H, int k,
     unsigned int* status) {
   pdl_wait();
-  const int b = blockIdx.y;
-  const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  const int b = blockIdx.x;  // rows in x: more than 65535 of them are allowed
+  const int i = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
   if (i >= H) return;
   const int kp = k + (sg != nullptr ? 1 : 0);
   const int* tp = tp_pos + (size_t)b * kp;
@@ -495,7 +495,7 @@ void launch_combine_bf16(const uint16_t* pb, const int* tp_pos, const float* wei
                          const float* sgate, const float* residual, void* out, bool f16_out,
                          unsigned int* status, int B, int H, int k, cudaStream_t s,
                          uint64_t* launches) {
-  const dim3 grid((H / 8 + 255) / 256, B);
+  const dim3 grid(B, (H / 8 + 255) / 256);
   if (f16_out)
     launch_pdl_pf(combine_bf16_kernel<true>, grid, dim3(256), 0, s, pb, tp_pos, weights, sgate,
                   residual, out, H, k, status);

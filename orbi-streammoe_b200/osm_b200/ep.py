@@ -7,9 +7,10 @@ single-GPU path), then:
   2. exchanges pair counts, then the pairs' activation rows (fp16) with the
      owner-local expert id and routing weight, in one all-to-all each;
   3. runs the owned experts on the rows it received, together with its own
-     tokens routed to the shared expert (held in the slab's spare last slot,
-     weighted by its sigmoid gate): one tensor-core prefill call on the fp16
-     rows, one pick per row, each row scaled by its weight, fp16 rows out;
+     tokens routed to the shared expert when the layer has one (held in the
+     slab's spare last slot, weighted by its sigmoid gate): one tensor-core
+     prefill call on the fp16 rows, one pick per row, each row scaled by its
+     weight, fp16 rows out;
   4. sends the weighted fp16 rows back with the reverse all-to-all;
   5. adds each token's rows in pick order, then the shared expert (replicated,
      computed locally for the rank's own tokens) scaled by its sigmoid gate --
@@ -92,31 +93,36 @@ def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float1
 class ExpertParallelMoE:
     """The Q4 routed-MoE sublayer with its experts spread over the ranks of a
     process group (NCCL, one GPU per rank).  `slab` holds this rank's experts
-    [e_first, e_first + e_count) in slots 0..e_count-1 and has one more slot,
-    which receives the shared expert; the router weight, the shared expert and
-    its gate row are replicated.  The context's max_tokens must cover the rows
-    a rank can receive plus its own tokens."""
+    [e_first, e_first + e_count) in slots 0..e_count-1; for a layer with a
+    shared expert (Qwen3-Next) it has one more slot, which receives it, and
+    the shared expert and its gate row are replicated like the router weight.
+    Layers without one (Qwen3-30B-A3B) pass shared_slot=None.  The context's
+    max_tokens must cover the rows a rank can receive plus its own tokens."""
 
     def __init__(self, ctx, W: np.ndarray, k: int, norm: bool, layout, slab, e_first: int,
-                 e_count: int, shared_slot: np.ndarray, shared_gate: np.ndarray, bias=None,
-                 group=None):
+                 e_count: int, shared_slot=None, shared_gate=None, bias=None, group=None):
         import osm_b200 as osm
 
         self.ctx, self.k, self.group = ctx, k, group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.e_first, self.e_count = e_first, e_count
+        self.has_shared = shared_slot is not None
+        if self.has_shared and shared_gate is None:
+            raise ValueError("a shared expert needs its gate row")
         H = W.shape[1]
-        if slab.slots < e_count + 1:
-            raise ValueError("the slab needs one slot beyond the rank's experts (shared expert)")
+        n_local = e_count + (1 if self.has_shared else 0)
+        if slab.slots < n_local:
+            raise ValueError("the slab needs a slot per owned expert, plus one for a shared expert")
         self.router = osm.Layer(ctx, W, k, norm, logit_bias=bias)
-        self._sh_host = torch.from_numpy(np.ascontiguousarray(shared_slot).reshape(-1)).pin_memory()
-        slab.fill_async(e_count, self._sh_host.data_ptr())
-        slab.fill_wait()
+        if self.has_shared:
+            self._sh_host = torch.from_numpy(np.ascontiguousarray(shared_slot).reshape(-1)).pin_memory()
+            slab.fill_async(e_count, self._sh_host.data_ptr())
+            slab.fill_wait()
+            self.gate = torch.from_numpy(np.asarray(shared_gate, np.float32)).cuda()
         # local experts 0..e_count-1, then the shared expert as local id e_count
-        self.experts = osm.Layer(ctx, np.zeros((e_count + 1, H), np.float32), 1, False)
-        self.experts.bind_slab(slab, np.arange(e_count + 1, dtype=np.int32))
-        self.gate = torch.from_numpy(np.asarray(shared_gate, np.float32)).cuda()
+        self.experts = osm.Layer(ctx, np.zeros((n_local, H), np.float32), 1, False)
+        self.experts.bind_slab(slab, np.arange(n_local, dtype=np.int32))
 
     def forward(self, x: torch.Tensor, out: torch.Tensor, ids: torch.Tensor | None = None,
                 weights: torch.Tensor | None = None):
@@ -126,17 +132,23 @@ class ExpertParallelMoE:
         w = weights if weights is not None else torch.empty(T, self.k, device=dev)
         self.router.route_qwen_top_k(x, T, ids, w)
         x16 = x.to(torch.float16)
+        ns = T if self.has_shared else 0
         # received rows, then this rank's own tokens for the shared expert
         rows, recv_ids, recv_w, state = dispatch_rows(x16, ids, w, self.e_count, self.world,
-                                                      self.group, extra_rows=T)
-        n = rows.shape[0] - T
-        rows[n:].copy_(x16)
-        rid = torch.cat([recv_ids, torch.full((T,), self.e_count, dtype=torch.int32, device=dev)])
-        sg = torch.sigmoid(x @ self.gate)
-        rw = torch.cat([recv_w, sg]).contiguous()
-        y = torch.empty(n + T, H, dtype=torch.float16, device=dev)   # fp16 rows out
-        self.experts.run_experts(rows, n + T, rid.view(-1, 1).contiguous(), rw.view(-1, 1), y,
-                                 prefill=True)
+                                                      self.group, extra_rows=ns)
+        n = rows.shape[0] - ns
+        rid, rw = recv_ids, recv_w
+        if self.has_shared:
+            rows[n:].copy_(x16)
+            rid = torch.cat([recv_ids, torch.full((T,), self.e_count, dtype=torch.int32, device=dev)])
+            rw = torch.cat([recv_w, torch.sigmoid(x @ self.gate)]).contiguous()
+        y = torch.empty(n + ns, H, dtype=torch.float16, device=dev)   # fp16 rows out
+        if n + ns > 0:  # a rank may own no picked expert and have no shared expert
+            self.experts.run_experts(rows, n + ns, rid.view(-1, 1).contiguous(), rw.view(-1, 1), y,
+                                     prefill=True)
         routed = combine_rows(y[:n], state, self.group)
-        torch.add(routed, y[n:], out=out)  # the shared expert last
+        if self.has_shared:
+            torch.add(routed, y[n:], out=out)  # the shared expert last
+        else:
+            out.copy_(routed)
         return ids, w
