@@ -303,6 +303,16 @@ int osm_moe_forward_cached(osm_layer* layer, osm_cache* cache, uint32_t layer_id
                            float* shared_gate_dev, const float* residual_dev,
                            uint32_t flags);
 
+/* No counterpart in the reference (its MoE runs on one device): the return
+ * step of an expert-parallel exchange.  out[t] (fp32, [tokens][hidden]) =
+ * the sum, in order p = 0..k-1, of the fp16 rows rows_f16[pos[t k + p]]
+ * (already weighted by their owners), then + extra_f16[t] when given (the
+ * token's own shared-expert row); fp32 adds, one rounding each.  hidden % 8
+ * == 0; rows, extra and out 16-byte aligned. */
+int osm_gather_sum_rows(osm_context* ctx, const void* rows_f16, const int64_t* pos,
+                        uint32_t tokens, uint32_t k, uint32_t hidden,
+                        const void* extra_f16, float* out);
+
 /* QwenCheckpointMoeSublayer::run (include/orbi/streammoe/model/
  * checkpoint_moe_sublayer.hpp:55-58): normalized = RMSNorm(residual),
  * out = residual + MoE(normalized).  normalized_dev may be NULL. */

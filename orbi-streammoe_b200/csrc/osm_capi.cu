@@ -1446,6 +1446,22 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   return run_experts(L, T, out, res);
 }
 
+int osm_gather_sum_rows(osm_context* ctx, const void* rows_f16, const int64_t* pos, uint32_t tokens,
+                        uint32_t k, uint32_t hidden, const void* extra_f16, float* out) {
+  if (!ctx) return OSM_EINVAL;
+  if (tokens == 0) return OSM_OK;
+  if (!out || (k && (!rows_f16 || !pos))) return fail(ctx, OSM_EINVAL, "gather_sum_rows: null argument");
+  if (hidden == 0 || hidden % 8) return fail(ctx, OSM_EINVAL, "gather_sum_rows: hidden must be a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(rows_f16) | reinterpret_cast<uintptr_t>(extra_f16) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(ctx, OSM_EINVAL, "gather_sum_rows: rows, extra and out must be 16-byte aligned");
+  DeviceGuard dg(ctx->device);
+  osm::launch_gather_sum_rows(static_cast<const uint16_t*>(rows_f16), pos,
+                              static_cast<const uint16_t*>(extra_f16), out, (int)tokens, (int)hidden,
+                              (int)k, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "gather_sum_rows");
+}
+
 int osm_moe_sublayer_forward(osm_layer* L, const float* residual, uint32_t T, float* out,
                              float* normalized, uint32_t* ids, float* w, float* mass,
                              float* sgate, uint32_t flags) {

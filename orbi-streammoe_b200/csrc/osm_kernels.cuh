@@ -245,6 +245,10 @@ bool prefill_configure(const PfArgs& a, int has_shared, int max_smem, size_t* sm
 void init_prefill_attributes(int max_smem);
 void launch_prefill_gateup(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches);
 void launch_prefill_down(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches);
+// out[t] = sum over p < k in order of rows[pos[t k + p]] (fp16 rows, fp32 sums),
+// then + extra[t] (fp16, may be null); H % 8 == 0, all pointers 16-byte aligned
+void launch_gather_sum_rows(const uint16_t* rows, const int64_t* pos, const uint16_t* extra,
+                            float* out, int T, int H, int k, cudaStream_t s, uint64_t* launches);
 // out[b] = sum over picks of w * pb[tp_pos[b][j]] in pick order, then sgate * the
 // shared row, then the residual; H % 8 == 0, out and residual 16-byte aligned;
 // f16_out: out holds fp16 rows

@@ -440,6 +440,32 @@ __global__ void __launch_bounds__(256) combine_bf16_kernel(
   }
 }
 
+// out[t] = sum over p < k, in order, of row(pos[t k + p]), then + extra[t]:
+// fp16 rows, fp32 sums with one rounding per add; eight elements per thread.
+__global__ void __launch_bounds__(256) gather_sum_rows_kernel(
+    const uint16_t* __restrict__ rows, const int64_t* __restrict__ pos, const uint16_t* __restrict__ extra,
+    float* __restrict__ out, int H, int k) {
+  const int t = blockIdx.x;
+  const int i = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (i >= H) return;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  auto add_row = [&](const uint16_t* r) {
+    const uint4 q = *reinterpret_cast<const uint4*>(r + i);
+    const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&qq[u]));
+      acc[2 * u] = __fadd_rn(acc[2 * u], v.x);
+      acc[2 * u + 1] = __fadd_rn(acc[2 * u + 1], v.y);
+    }
+  };
+  for (int p = 0; p < k; ++p) add_row(rows + (size_t)pos[(size_t)t * k + p] * H);
+  if (extra) add_row(extra + (size_t)t * H);
+  float* op = out + (size_t)t * H + i;
+  *reinterpret_cast<float4*>(op) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  *reinterpret_cast<float4*>(op + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
 template <typename Kern, typename... Args>
 void launch_pdl_pf(Kern kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg{};
@@ -488,6 +514,12 @@ void launch_prefill_gateup(const PfArgs& a, int grid, size_t smem, cudaStream_t 
 
 void launch_prefill_down(const PfArgs& a, int grid, size_t smem, cudaStream_t s, uint64_t* launches) {
   launch_pdl_pf(pf_gemm_kernel<true>, dim3(grid), dim3(kPfThreads), smem, s, a);
+  if (launches) *launches += 1;
+}
+
+void launch_gather_sum_rows(const uint16_t* rows, const int64_t* pos, const uint16_t* extra,
+                            float* out, int T, int H, int k, cudaStream_t s, uint64_t* launches) {
+  gather_sum_rows_kernel<<<dim3(T, (H / 8 + 255) / 256), 256, 0, s>>>(rows, pos, extra, out, H, k);
   if (launches) *launches += 1;
 }
 

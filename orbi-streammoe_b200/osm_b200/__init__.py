@@ -128,6 +128,13 @@ class Context:
         self.check(lib().osm_expert_forward(self.h, C.c_void_p(slot_ptr), C.byref(layout), _ptr(x),
                                             tokens, _ptr(out)), "expert_forward")
 
+    def gather_sum_rows(self, rows, pos, tokens, k, out, extra=None):
+        """out[t] = sum over p < k of rows[pos[t k + p]] in pick order, then +
+        extra[t] (fp16 rows, int64 positions, fp32 out): the return step of an
+        expert-parallel exchange."""
+        self.check(lib().osm_gather_sum_rows(self.h, _ptr(rows), _ptr(pos), tokens, k, out.shape[1],
+                                             _ptr(extra), _ptr(out)), "gather_sum_rows")
+
     def gen_normal(self, seed, tensor, sigma, out, first=0):
         self.check(lib().osm_gen_normal(self.h, seed, tensor, sigma, _ptr(out), out.numel(), first),
                    "gen_normal")

@@ -106,6 +106,7 @@ _SIGS = {
     "osm_moe_route": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, C.c_uint32]),
     "osm_moe_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_experts": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, C.c_uint32]),
+    "osm_gather_sum_rows": (C.c_int, [_P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P]),
     "osm_moe_forward_cached": (C.c_int, [_P, _P, C.c_uint32, _P, C.c_uint32, _P, _P, _P, _P, _P,
                                          C.c_uint32]),
     "osm_moe_sublayer_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),

@@ -72,10 +72,15 @@ def dispatch_rows(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, e_local: 
     return recv_x, recv_meta[:, 0].to(torch.int32), recv_meta[:, 1].contiguous(), state
 
 
-def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float16):
-    """Steps 4-5 (routed part): the weighted rows back to their tokens (sent as
-    `row_dtype`), put in (token, pick) order by the inverse of the dispatch
-    permutation and summed in pick order in fp32.  Returns [T, H] fp32."""
+def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float16, extra=None,
+                 out=None, ctx=None):
+    """Steps 4-5: the weighted rows back to their tokens (sent as `row_dtype`),
+    each token's rows summed in pick order in fp32, then + extra[t] (the
+    token's own shared-expert row) when given.  Returns [T, H] fp32 (`out`
+    when given).  With a library context and fp16 CUDA rows the sum reads the
+    returned rows in place through the inverse of the dispatch permutation
+    (osm_gather_sum_rows); otherwise torch gathers them first: the same adds
+    in the same order."""
     order, ss, rs, T, k = state
     H = y_recv.shape[1]
     back = torch.empty(len(order), H, dtype=row_dtype, device=y_recv.device)
@@ -83,10 +88,19 @@ def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float1
     dist.all_to_all_single(back, send.contiguous(), ss, rs, group=group)
     inv = torch.empty_like(order)
     inv[order] = torch.arange(len(order), device=order.device, dtype=order.dtype)
+    if ctx is not None and back.is_cuda and row_dtype == torch.float16:
+        res = out if out is not None else torch.empty(T, H, dtype=torch.float32, device=back.device)
+        ctx.gather_sum_rows(back, inv, T, k, res, extra=extra)
+        return res
     y = back.index_select(0, inv).view(T, k, H)
     acc = y[:, 0].to(torch.float32, copy=True)
     for p in range(1, k):
         acc.add_(y[:, p])
+    if extra is not None:
+        acc.add_(extra)
+    if out is not None:
+        out.copy_(acc)
+        return out
     return acc
 
 
@@ -146,9 +160,7 @@ class ExpertParallelMoE:
         if n + ns > 0:  # a rank may own no picked expert and have no shared expert
             self.experts.run_experts(rows, n + ns, rid.view(-1, 1).contiguous(), rw.view(-1, 1), y,
                                      prefill=True)
-        routed = combine_rows(y[:n], state, self.group)
-        if self.has_shared:
-            torch.add(routed, y[n:], out=out)  # the shared expert last
-        else:
-            out.copy_(routed)
+        # routed rows in pick order, then the shared expert's row
+        combine_rows(y[:n], state, self.group, extra=y[n:] if self.has_shared else None, out=out,
+                     ctx=self.ctx)
         return ids, w

@@ -102,3 +102,30 @@ def test_ep_ranks_match_oracle(world, with_shared):
         assert ids_ok, rank
         assert worst <= 2e-3, (rank, worst)
         assert status == 0, (rank, status)
+
+
+@pytest.mark.parametrize("with_extra", [True, False])
+def test_gather_sum_rows_equals_the_torch_sum(with_extra):
+    """osm_gather_sum_rows (the return step of the exchange) gives the bits of
+    the torch path: rows gathered by position, summed in pick order in fp32,
+    then the extra row."""
+    torch = require_cuda()
+    import osm_b200 as osm
+
+    T, k, Hh = 300, 5, 512
+    g = torch.Generator().manual_seed(7)
+    rows = torch.randn(T * k, Hh, generator=g).half().cuda()
+    pos = torch.randperm(T * k, generator=g).cuda()
+    extra = torch.randn(T, Hh, generator=g).half().cuda() if with_extra else None
+    ctx = osm.Context(0, max_tokens=8)
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    out = torch.empty(T, Hh, device="cuda")
+    ctx.gather_sum_rows(rows, pos, T, k, out, extra=extra)
+    y = rows.index_select(0, pos).view(T, k, Hh)
+    ref = y[:, 0].float()
+    for p in range(1, k):
+        ref = ref + y[:, p].float()
+    if with_extra:
+        ref = ref + extra.float()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
