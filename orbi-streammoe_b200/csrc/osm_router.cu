@@ -107,22 +107,24 @@ __device__ __forceinline__ float2 fadd2_rn(float2 a, float2 b) {
   return r;
 }
 
-template <int TT, bool F32>
+// STG: stages of the router-tile ring (fewer for more tokens per thread, so
+// that two blocks still fit an SM)
+template <int TT, bool F32, int STG = kExStages>
 __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) {
   constexpr int EPC = F32 ? 4 : 8;  // weights per 16-byte chunk
   constexpr int HPT = 8 * EPC;      // h per tile
   extern __shared__ __align__(128) unsigned char exsm[];
-  __shared__ __align__(8) uint64_t full[kExStages];
+  __shared__ __align__(8) uint64_t full[STG];
   unsigned char* ring = exsm;
-  float* xs = reinterpret_cast<float*>(exsm + kExStages * kExTile);  // [H][TT]
+  float* xs = reinterpret_cast<float*>(exsm + STG * kExTile);  // [H][TT]
   const int E = a.g.E, H = a.g.H, nht = H / HPT;
   const int tid = threadIdx.x, e = blockIdx.x * kExThreads + tid, t0 = blockIdx.y * TT;
   const unsigned char* src = static_cast<const unsigned char*>(a.wx) + (size_t)blockIdx.x * nht * kExTile;
   TL_START(0);
   if (tid == 0) {
-    for (int s = 0; s < kExStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < STG; ++s) mbar_init(&full[s], 1);
     mbar_init_fence();
-    for (int s = 0; s < kExStages && s < nht; ++s) {
+    for (int s = 0; s < STG && s < nht; ++s) {
       mbar_arrive_expect(&full[s], kExTile);
       bulk_load(ring + s * kExTile, src + (size_t)s * kExTile, kExTile, &full[s]);
     }
@@ -140,8 +142,8 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
   for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
   const int sw = tid & 7;
   for (int j = 0; j < nht; ++j) {
-    const int s = j % kExStages;
-    const uint32_t par = (uint32_t)(j / kExStages) & 1u;
+    const int s = j % STG;
+    const uint32_t par = (uint32_t)(j / STG) & 1u;
     if (!mbar_wait(&full[s], par)) {
       if (tid == 0) atomicOr(a.status, kStatusCopyTimeout);
       mbar_wait(&full[s], par);  // the copy may still land: wait once more
@@ -187,9 +189,9 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
       }
     }
     __syncthreads();  // every thread is done with stage s
-    if (tid == 0 && j + kExStages < nht) {
+    if (tid == 0 && j + STG < nht) {
       mbar_arrive_expect(&full[s], kExTile);
-      bulk_load(ring + s * kExTile, src + (size_t)(j + kExStages) * kExTile, kExTile, &full[s]);
+      bulk_load(ring + s * kExTile, src + (size_t)(j + STG) * kExTile, kExTile, &full[s]);
     }
   }
   if (e < E) {
@@ -1212,11 +1214,11 @@ size_t select_smem(const RouterGeom& g) {
   return xs + u;
 }
 
-template <int TT, bool F32>
+template <int TT, bool F32, int STG = kExStages>
 void launch_exact_t(const RouterArgs& a, cudaStream_t s) {
   const dim3 grid((a.g.E + kExThreads - 1) / kExThreads, (a.B + TT - 1) / TT);
-  const size_t sm = (size_t)kExStages * kExTile + (size_t)TT * a.g.H * sizeof(float);
-  launch_pdl(router_exact_kernel<TT, F32>, grid, dim3(kExThreads), sm, s, a);
+  const size_t sm = (size_t)STG * kExTile + (size_t)TT * a.g.H * sizeof(float);
+  launch_pdl(router_exact_kernel<TT, F32, STG>, grid, dim3(kExThreads), sm, s, a);
 }
 
 template <bool F32>
@@ -1225,7 +1227,8 @@ void launch_exact(const RouterArgs& a, cudaStream_t s) {
   // (H dependent adds) bounds small batches
   if (a.B <= 16) launch_exact_t<1, F32>(a, s);
   else if (a.B <= 64) launch_exact_t<2, F32>(a, s);
-  else launch_exact_t<4, F32>(a, s);
+  else if (a.B < 2048) launch_exact_t<4, F32>(a, s);
+  else launch_exact_t<8, F32, 2>(a, s);
 }
 
 }  // namespace
@@ -1270,6 +1273,8 @@ void init_router_attributes(int max_smem) {
   cudaFuncSetAttribute(router_exact_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<8, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact_kernel<8, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
