@@ -982,9 +982,10 @@ def run_reference(args, rank, world):
     sg = bf16_round(port.gen_normal(SEED, 2, 0.02, H))
     bias = zipf_bias(E, ZIPF_S, SEED)
     shared = port.gen_expert_slot(SEED, 1000 + 3 * E, 0.02, H, I)
-    # bounded sample: the B=1, B=8 and B=32 batches of the sweep (41 tokens)
+    # the whole sweep of our arm's step (B = 1, 8, 32, 64, 128, 256: 489
+    # tokens, the same inputs), run token-parallel over all host threads
     x = np.concatenate([port.gen_normal(SEED, 5000 + B, 1.0, B * H).reshape(B, H)
-                        for B in (1, 8, 32)])
+                        for B in SWEEP])
     stride = pyoracle.slot_stride(H, I)
     slots = np.zeros((E, stride), np.uint8)
     sub = cb.Sublayer(slots, shared, W, sg, bias, H, I, K, threads)
@@ -1008,10 +1009,11 @@ def run_reference(args, rank, world):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "impl": "reference",
         "data": "synthetic (same seeds as our arm)",
         "config": {"workload": WORKLOAD, "tokens_per_step": int(x.shape[0]),
-                   "sample": "B=1, 8 and 32 batches of the sweep per step"},
+                   "sample": "the full sweep (B=1,8,32,64,128,256) per step, all tokens "
+                             "token-parallel over the host threads"},
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads,
                          "kind": sub.kind,
-                         "sample": f"{x.shape[0]} tokens per step (B=1,8,32 batches), "
+                         "sample": f"{x.shape[0]} tokens per step (the whole sweep), "
                                    f"{len(sub.deq)} experts dequantised once "
                                    f"({sub.dequant_s:.1f} s, excluded)",
                          "cpu_model": cb.cpu_model()},

@@ -3,9 +3,7 @@
  *
  * Plain pointers, sizes and int status codes; no C++ or torch types.  Every
  * entry point names the interface of the reference (ingeniusvictor/
- * orbi-streammoe, paths inside that project) that it replaces.  The C++
- * drop-in layer (orbi-streammoe_b200/host) implements the reference's own
- * class and function names on top of these calls.
+ * orbi-streammoe, paths inside that project) that it replaces.
  *
  * Conventions
  *  - Return 0 on success, a negative OSM_E* code on failure; the text of the
@@ -238,8 +236,10 @@ typedef struct {
   uint32_t experts;         /* E (<= 1024)                               */
   uint32_t top_k;           /* k (<= 32)                                 */
   uint32_t norm_topk_prob;  /* renormalise the selected weights          */
-  const float* router_weight_host;   /* [E][H] fp32, row-major; values
-                                        must be bf16-representable       */
+  const float* router_weight_host;   /* [E][H] fp32, row-major; kept as
+                                        bf16 on the device when every
+                                        value is bf16-representable, else
+                                        as fp32 (a dequantised Q8 router) */
   const float* logit_bias_host;      /* [E] or NULL                      */
   const void* shared_slot_host;      /* one slot of shared_layout or NULL */
   osm_expert_layout shared_layout;   /* ignored without a shared expert  */

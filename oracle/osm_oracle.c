@@ -421,6 +421,60 @@ int osm_oracle_moe_token(const float* hidden, const float* router_weight,
   return rc;
 }
 
+/* osm_oracle_moe_token over Q4 expert slots: routes, dequantises only the
+ * picked experts (and the shared expert) with osm_oracle_dequant_slot, then
+ * runs osm_oracle_moe_token on them -- the same arithmetic without holding
+ * every expert in fp32.  slots: expert e at slots + e * slot_stride. */
+int osm_oracle_moe_token_slots(const float* hidden, const float* router_weight,
+                               const float* logit_bias, size_t hidden_size,
+                               size_t expert_count, size_t top_k,
+                               int norm_topk_prob, size_t inter,
+                               const uint8_t* slots, size_t slot_stride,
+                               const uint8_t* shared_slot,
+                               const float* scalar_gate, float* out,
+                               uint32_t* experts, float* weights,
+                               float* selected_mass, float* shared_scale) {
+  const size_t H = hidden_size, I = inter, per = 2 * I * H + H * I;
+  float* logits = (float*)malloc(expert_count * sizeof(float));
+  const float** g = (const float**)calloc(expert_count, sizeof(float*));
+  const float** u = (const float**)calloc(expert_count, sizeof(float*));
+  const float** d = (const float**)calloc(expert_count, sizeof(float*));
+  float* deq = (float*)malloc((top_k + 1) * per * sizeof(float));
+  int rc = (logits && g && u && d && deq) ? OK : ERUNTIME;
+  if (rc == OK)
+    rc = osm_oracle_route_qwen_top_k(hidden, router_weight, logit_bias, H,
+                                     expert_count, top_k, norm_topk_prob,
+                                     logits, experts, weights, selected_mass);
+  for (size_t k = 0; rc == OK && k < top_k; ++k) {
+    const uint32_t e = experts[k];
+    if (g[e] != NULL) continue;
+    float* base = deq + k * per;
+    rc = osm_oracle_dequant_slot(slots + (size_t)e * slot_stride, H, I, 64,
+                                 base, base + I * H, base + 2 * I * H);
+    g[e] = base;
+    u[e] = base + I * H;
+    d[e] = base + 2 * I * H;
+  }
+  float* sh = deq + top_k * per;
+  if (rc == OK && shared_slot != NULL)
+    rc = osm_oracle_dequant_slot(shared_slot, H, I, 64, sh, sh + I * H,
+                                 sh + 2 * I * H);
+  if (rc == OK)
+    rc = osm_oracle_moe_token(hidden, router_weight, logit_bias, H,
+                              expert_count, top_k, norm_topk_prob, I, g, u, d,
+                              shared_slot ? sh : NULL,
+                              shared_slot ? sh + I * H : NULL,
+                              shared_slot ? sh + 2 * I * H : NULL, scalar_gate,
+                              I, out, experts, weights, selected_mass,
+                              shared_scale);
+  free(logits);
+  free(g);
+  free(u);
+  free(d);
+  free(deq);
+  return rc;
+}
+
 int osm_oracle_add_residual(const float* residual, const float* branch,
                             float* out, size_t n) {
   for (size_t i = 0; i < n; ++i) out[i] = residual[i] + branch[i];

@@ -124,6 +124,21 @@ int osm_oracle_moe_token(const float* hidden, const float* router_weight,
                          float* weights, float* selected_mass,
                          float* shared_scale);
 
+/* osm_oracle_moe_token over Q4 expert slots (expert e at slots + e *
+ * slot_stride; shared_slot may be NULL): dequantises only the picked experts
+ * with osm_oracle_dequant_slot, then runs osm_oracle_moe_token -- the same
+ * arithmetic without every expert in fp32.  The shared expert has the routed
+ * experts' intermediate size. */
+int osm_oracle_moe_token_slots(const float* hidden, const float* router_weight,
+                               const float* logit_bias, size_t hidden_size,
+                               size_t expert_count, size_t top_k,
+                               int norm_topk_prob, size_t inter,
+                               const uint8_t* slots, size_t slot_stride,
+                               const uint8_t* shared_slot,
+                               const float* scalar_gate, float* out,
+                               uint32_t* experts, float* weights,
+                               float* selected_mass, float* shared_scale);
+
 /* checkpoint_moe_sublayer.cpp:21-33 */
 int osm_oracle_add_residual(const float* residual, const float* branch,
                             float* out, size_t n);

@@ -98,6 +98,10 @@ class Oracle:
             L.osm_oracle_hash.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
             L.osm_oracle_hash.restype = C.c_uint64
             L.osm_oracle_add_residual.argtypes = [_f32p, _f32p, _f32p, _sz]
+            L.osm_oracle_moe_token_slots.argtypes = [
+                _f32p, _f32p, C.c_void_p, _sz, _sz, _sz, C.c_int, _sz, C.c_void_p, _sz,
+                C.c_void_p, C.c_void_p, _f32p, _u32p, _f32p, C.POINTER(C.c_float),
+                C.POINTER(C.c_float)]
         mt = getattr(L, p + "moe_token")
         mt.argtypes = [_f32p, _f32p, C.c_void_p, _sz, _sz, _sz, C.c_int, _sz,
                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -267,6 +271,33 @@ class Oracle:
         return out, ids, w, mass.value, ss.value
 
     # --- port-only helpers ---------------------------------------------------
+    def moe_token_slots(self, x, router_weight, k, norm, slots, inter, shared_slot=None,
+                        scalar_gate=None, bias=None):
+        """moe_token with the experts given as Q4 slots: ``slots`` is a
+        C-contiguous uint8 array [E][stride]; only the picked experts are
+        dequantised.  Releases the GIL (ctypes), so threads run tokens in
+        parallel."""
+        x = np.ascontiguousarray(x, np.float32)
+        W = np.ascontiguousarray(router_weight, np.float32)
+        H = x.size
+        E = W.size // H
+        assert slots.flags["C_CONTIGUOUS"] and slots.dtype == np.uint8
+        out = np.zeros(H, np.float32)
+        ids = np.zeros(k, np.uint32)
+        w = np.zeros(k, np.float32)
+        mass = C.c_float(0)
+        ss = C.c_float(0)
+        b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        sh = None if shared_slot is None else np.ascontiguousarray(shared_slot, np.uint8)
+        sg = None if scalar_gate is None else np.ascontiguousarray(scalar_gate, np.float32)
+        rc = self.lib.osm_oracle_moe_token_slots(
+            x, W.reshape(-1), None if b is None else b.ctypes.data, H, E, k, int(norm), inter,
+            slots.ctypes.data, slots.shape[1], None if sh is None else sh.ctypes.data,
+            None if sg is None else sg.ctypes.data, out, ids, w, C.byref(mass), C.byref(ss))
+        if rc:
+            raise OracleError(rc, "moe_token_slots")
+        return out, ids, w, mass.value, ss.value
+
     def dequant_slot(self, slot, H, I, group=64):
         gate = np.zeros((I, H), np.float32)
         up = np.zeros((I, H), np.float32)

@@ -1647,10 +1647,14 @@ void cache_bind_slot(osm_cache* c, osm_layer* L, uint32_t expert, int32_t slot) 
 }
 
 // One get() of the reference: a hit refreshes frequency and recency; a miss
-// evicts the entry with the smallest (frequency, last use, key) until the
-// newcomer fits, then queues the expert's copy into a free slot.  Entries
-// touched in the current acquire (epoch) are not evicted.  The victim is the
-// first unprotected entry of an ordered index, the same entry as the
+// asks the host source for the expert first (the reference fetches from its
+// host cache and uploads before it evicts anything,
+// vulkan_resident_expert_cache.cpp:101-140), so a failing source leaves the
+// residency as it was (only the use count and the miss are recorded, as
+// there); then it evicts the entry with the smallest (frequency, last use,
+// key) until the newcomer fits and queues the expert's copy into a free slot.
+// Entries touched in the current acquire (epoch) are not evicted.  The victim
+// is the first unprotected entry of an ordered index, the same entry as the
 // reference's linear scan (vulkan_resident_expert_cache.cpp:58-69) picks.
 int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) {
   ++c->tick;
@@ -1668,6 +1672,11 @@ int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) 
     return OSM_OK;
   }
   ++c->misses;
+  const void* src = nullptr;
+  if (c->slab || c->source) {
+    if (!c->source || c->source(c->user, layer, expert, &src) != 0 || (c->slab && !src))
+      return cache_fail(c, OSM_ERUNTIME, "cache: the host source could not provide the expert");
+  }
   if (c->accounted > c->budget) return cache_fail(c, OSM_EINVAL, "cache: one expert exceeds the budget");
   while (!c->entries.empty() &&
          (c->resident_bytes + c->accounted > c->budget || (c->slab && c->free_slots.empty()))) {
@@ -1694,18 +1703,11 @@ int cache_get(osm_cache* c, uint32_t layer, uint32_t expert, int32_t* slot_out) 
   int32_t slot = -1;
   if (c->slab) {
     if (c->free_slots.empty()) return cache_fail(c, OSM_ENOMEM, "cache: no free slot");
-    const void* src = nullptr;
-    if (!c->source || c->source(c->user, layer, expert, &src) != 0 || !src)
-      return cache_fail(c, OSM_ERUNTIME, "cache: the host source could not provide the expert");
     slot = c->free_slots.back();
     c->free_slots.pop_back();
     c->fills.emplace_back((uint32_t)slot, src);
     auto lit = c->layers.find(layer);
     if (lit != c->layers.end()) cache_bind_slot(c, lit->second, expert, slot);
-  } else if (c->source) {
-    const void* src = nullptr;
-    if (c->source(c->user, layer, expert, &src) != 0)
-      return cache_fail(c, OSM_ERUNTIME, "cache: the host source could not provide the expert");
   }
   osm_cache::Node n;
   n.slot = slot;
@@ -1887,6 +1889,16 @@ int osm_cache_get(osm_cache* c, uint32_t layer_id, uint32_t expert, int32_t* slo
 
 int osm_cache_acquire(osm_cache* c, uint32_t layer_id, const uint32_t* experts, uint32_t n) {
   if (!c || (n && !experts)) return OSM_EINVAL;
+  // a call whose distinct experts cannot all be resident at once is refused
+  // before anything changes (ExpertCache::fetch, src/cache/expert_cache.cpp:
+  // 108-111, rejects an oversized request the same way)
+  {
+    std::vector<uint32_t> distinct(experts, experts + n);
+    std::sort(distinct.begin(), distinct.end());
+    const uint64_t d = (uint64_t)(std::unique(distinct.begin(), distinct.end()) - distinct.begin());
+    if (d * c->accounted > c->budget || (c->slab && d > c->slab->slots))
+      return cache_fail(c, OSM_ENOMEM, "cache: the experts of one call do not fit in the budget");
+  }
   ++c->epoch;
   int rc = OSM_OK;
   for (uint32_t i = 0; i < n && rc == OSM_OK; ++i) rc = cache_get(c, layer_id, experts[i], nullptr);
@@ -1971,18 +1983,17 @@ int na_device(int dev, NaDevice** out) {
   NaDevice& d = g_na[dev];
   if (!d.ready) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
-      cudaGetLastError();
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr)
       return OSM_ECUDA;
-    }
     int sms = 0, optin = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) {
-      cudaGetLastError();
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
       return OSM_ECUDA;
-    }
-    osm::init_expert_attributes(optin > 64 * 1024 ? optin - 16 * 1024 : 48 * 1024);
-    if (cudaGetLastError() != cudaSuccess) return OSM_ECUDA;
+    // the result of each call is checked directly: an error the caller left
+    // pending is neither taken for this call's nor cleared
+    if (osm::init_expert_attributes(optin > 64 * 1024 ? optin - 16 * 1024 : 48 * 1024) !=
+        cudaSuccess)
+      return OSM_ECUDA;
     d.base = static_cast<uint8_t*>(p);
     d.grid_cap = (sms > 0 ? sms : 148) * 4;
     d.ready = true;
@@ -2001,10 +2012,7 @@ extern "C" int osm_expert_forward_noalloc(const void* slot_dev, const osm_expert
       layout->inter > kNaMaxInter)
     return OSM_EINVAL;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) {
-    cudaGetLastError();
-    return OSM_ECUDA;
-  }
+  if (cudaGetDevice(&dev) != cudaSuccess) return OSM_ECUDA;
   NaDevice* d = nullptr;
   int rc = na_device(dev, &d);
   if (rc) return rc;
@@ -2014,10 +2022,7 @@ extern "C" int osm_expert_forward_noalloc(const void* slot_dev, const osm_expert
   auto at = [&](size_t off) { return b + off; };
   // every intermediate of the call starts cleared: the previous call's
   // contents stay in the array
-  if (cudaMemsetAsync(b, 0, kNaBytes, st) != cudaSuccess) {
-    cudaGetLastError();
-    return OSM_ECUDA;
-  }
+  if (cudaMemsetAsync(b, 0, kNaBytes, st) != cudaSuccess) return OSM_ECUDA;
   uint4* xfrag = reinterpret_cast<uint4*>(at(kNaXfrag));
   float* xfsum = reinterpret_cast<float*>(at(kNaXsum));
   int* n_active = reinterpret_cast<int*>(at(kNaNact));
@@ -2030,9 +2035,12 @@ extern "C" int osm_expert_forward_noalloc(const void* slot_dev, const osm_expert
   int* out_row = reinterpret_cast<int*>(at(kNaOrow));
   uint4* hfrag = reinterpret_cast<uint4*>(at(kNaHfrag));
   float* hfsum = reinterpret_cast<float*>(at(kNaHsum));
-  osm::launch_frag_prep(x_dev, (int)tokens, (int)L.hidden, xfrag, xfsum, st, nullptr);
-  osm::launch_setup_single((int)tokens, static_cast<const uint8_t*>(slot_dev), n_active, act, n_tg,
-                           tg_expert, tg_begin, pair_tok, pair_pick, out_row, st, nullptr);
+  if (osm::launch_frag_prep(x_dev, (int)tokens, (int)L.hidden, xfrag, xfsum, st, nullptr) !=
+          cudaSuccess ||
+      osm::launch_setup_single((int)tokens, static_cast<const uint8_t*>(slot_dev), n_active, act,
+                               n_tg, tg_expert, tg_begin, pair_tok, pair_pick, out_row, st,
+                               nullptr) != cudaSuccess)
+    return OSM_ECUDA;
   osm::ProjArgs gu{};
   fill_sections(gu.sec, L, L, true);
   gu.n_tg = n_tg;
@@ -2048,7 +2056,9 @@ extern "C" int osm_expert_forward_noalloc(const void* slot_dev, const osm_expert
   gu.hK = (int)L.inter;
   const int ntg = (int)((tokens + osm::kTokGroup - 1) / osm::kTokGroup);
   const int tch = (int)std::min<uint32_t>(tokens, 8);
-  osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, ntg, d->grid_cap, tch, st, nullptr);
+  if (osm::launch_proj(gu, osm::ProjKind::kGateUp, (int)L.inter, ntg, d->grid_cap, tch, st,
+                       nullptr) != cudaSuccess)
+    return OSM_ECUDA;
   osm::ProjArgs dn = gu;
   fill_sections(dn.sec, L, L, false);
   dn.frag_by_pair = 1;
@@ -2060,8 +2070,8 @@ extern "C" int osm_expert_forward_noalloc(const void* slot_dev, const osm_expert
   dn.pair_pick = pair_pick;
   dn.kp1 = 1;
   dn.ostride = (int)L.hidden;
-  osm::launch_proj(dn, L.inter <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12,
-                   (int)L.hidden, ntg, d->grid_cap, tch, st, nullptr);
-  if (cudaGetLastError() != cudaSuccess) return OSM_ECUDA;
+  if (osm::launch_proj(dn, L.inter <= 512 ? osm::ProjKind::kDown : osm::ProjKind::kDown12,
+                       (int)L.hidden, ntg, d->grid_cap, tch, st, nullptr) != cudaSuccess)
+    return OSM_ECUDA;
   return OSM_OK;
 }

@@ -324,7 +324,7 @@ __global__ void setup_single_kernel(int T, const uint8_t* ptr, int* n_active, Ac
 }
 
 template <typename K, typename... Args>
-void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -335,7 +335,7 @@ void launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s, Ar
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, kernel, args...);
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 int grid_for(size_t n, int threads) {
@@ -347,15 +347,18 @@ int grid_for(size_t n, int threads) {
 
 }  // namespace
 
-void launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8, cudaStream_t s,
-                      uint64_t* launches) {
+cudaError_t launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8,
+                             cudaStream_t s, uint64_t* launches) {
   const size_t n = (size_t)rows * (K >> 3);
-  launch_pdl(frag_prep_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, rows, K, frag, fsum8);
+  const cudaError_t e =
+      launch_pdl(frag_prep_kernel, dim3(grid_for(n, 256)), dim3(256), 0, s, x, rows, K, frag, fsum8);
   if (launches) *launches += 1;
+  return e;
 }
 
-void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
-                 int max_tokens_chunk, cudaStream_t s, uint64_t* launches) {
+cudaError_t launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
+                        int max_tokens_chunk, cudaStream_t s, uint64_t* launches) {
+  cudaError_t err = cudaSuccess;
   auto go = [&](auto kernel, int rows_per_cta, int K, int ctas_per_sm) {
     const int tiles = (max_rows + rows_per_cta - 1) / rows_per_cta;
     const int tc = max_tokens_chunk < 8 ? (max_tokens_chunk < 1 ? 1 : max_tokens_chunk) : 8;
@@ -368,7 +371,7 @@ void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int
     long long items = (long long)tiles * max_tg;
     int grid = (int)(items < cap ? items : cap);
     if (grid < 1) grid = 1;
-    launch_pdl(kernel, dim3(grid), dim3(kWarps * 32), smem, s, a, tiles);
+    err = launch_pdl(kernel, dim3(grid), dim3(kWarps * 32), smem, s, a, tiles);
   };
   const int Kmax = a.sec.K[0] > a.sec.K[1] ? a.sec.K[0] : a.sec.K[1];
   switch (kind) {
@@ -386,21 +389,26 @@ void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int
       break;
   }
   if (launches) *launches += 1;
+  return err;
 }
 
-void init_expert_attributes(int max_smem) {
-  cudaFuncSetAttribute(proj_kernel<true, 4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(proj_kernel<false, 1, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(proj_kernel<false, 1, 12>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(proj_kernel<false, 4, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+cudaError_t init_expert_attributes(int max_smem) {
+  const auto attr = cudaFuncAttributeMaxDynamicSharedMemorySize;
+  cudaError_t e = cudaFuncSetAttribute(proj_kernel<true, 4, 8>, attr, max_smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(proj_kernel<false, 1, 8>, attr, max_smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(proj_kernel<false, 1, 12>, attr, max_smem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(proj_kernel<false, 4, 8>, attr, max_smem);
+  return e;
 }
 
-void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
-                         int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
-                         int* out_row, cudaStream_t s, uint64_t* launches) {
-  launch_pdl(setup_single_kernel, dim3(grid_for((size_t)T, 256)), dim3(256), 0, s, T, ptr,
-             n_active, act, n_tg, tg_expert, tg_begin, pair_tok, pair_pick, out_row);
+cudaError_t launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
+                                int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
+                                int* out_row, cudaStream_t s, uint64_t* launches) {
+  const cudaError_t e =
+      launch_pdl(setup_single_kernel, dim3(grid_for((size_t)T, 256)), dim3(256), 0, s, T, ptr,
+                 n_active, act, n_tg, tg_expert, tg_begin, pair_tok, pair_pick, out_row);
   if (launches) *launches += 1;
+  return e;
 }
 
 }  // namespace osm

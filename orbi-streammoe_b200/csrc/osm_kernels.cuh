@@ -85,7 +85,7 @@ struct RouterArgs {
 // Allow up to max_smem bytes of dynamic shared memory for every kernel that
 // uses it (once per device, before any launch or capture).
 void init_router_attributes(int max_smem);
-void init_expert_attributes(int max_smem);
+cudaError_t init_expert_attributes(int max_smem);
 
 void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
 void launch_router_select(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
@@ -96,7 +96,7 @@ void launch_group(const RouterArgs& a, cudaStream_t s, uint64_t* launches);
 // Fragments of activations for the projection kernel: per 8-element chunk
 // c of row r, two uint4 (hi, lo) holding bf16x2 pairs (x0,x4) (x1,x5)
 // (x2,x6) (x3,x7), and the fp32 sequential sum of the 8 values.
-void launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8,
+cudaError_t launch_frag_prep(const float* x, int rows, int K, uint4* frag, float* fsum8,
                       cudaStream_t s, uint64_t* launches);
 
 // Section offsets of one projection (weight, scales, biases) for the two
@@ -139,7 +139,7 @@ enum class ProjKind { kGateUp, kDown, kDown12, kSingle };
 // grid_cap: resident CTAs the device holds (SMs x CTAs per SM); the grid is
 // persistent and strides over (active expert, tile) items.
 // max_tg: upper bound of the call's token groups (grid sizing only).
-void launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
+cudaError_t launch_proj(const ProjArgs& a, ProjKind kind, int max_rows, int max_tg, int grid_cap,
                  int max_tokens_chunk, cudaStream_t s, uint64_t* launches);
 
 // The 1-2 token path (osm_gemv.cu).
@@ -291,7 +291,7 @@ struct SlotUpdates {
   int32_t* ptr[kMax];
 };
 void launch_slot_updates(const SlotUpdates& u, cudaStream_t s, uint64_t* launches);
-void launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
+cudaError_t launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
                          int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
                          int* out_row, cudaStream_t s, uint64_t* launches);
 

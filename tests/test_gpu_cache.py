@@ -133,3 +133,96 @@ def test_cached_forward_rejects_an_unbound_layer(torch):
     torch.cuda.synchronize()
     assert cache.stats()["loads"] == K
     cache.close()
+
+
+def test_failing_source_mid_acquire_keeps_slab_and_slot_table_consistent(torch):
+    """A slab-backed cache whose host source fails on the third pick of an
+    acquire: the first two picks are copied and bound, the failing expert is
+    neither bound nor resident and frees or evicts nothing, and a later call
+    with a working source loads it and computes the right output."""
+    import osm_b200 as osm
+
+    H, E, I, K, SLOTS = 256, 8, 128, 4, 4
+    f = MoeFixture(torch, H, E, I, K, seed=191, max_tokens=1)
+    lay = osm.expert_layout(H, I)
+    slab = osm.Slab(f.ctx, lay, SLOTS)
+    L = osm.Layer(f.ctx, f.W, K, True, shared_slot=f.shared_slot, shared_layout=lay,
+                  shared_gate=f.sg)
+    L.bind_slab(slab, np.full(E, -1, np.int32))
+    broken = {6}
+
+    def source(layer, expert):
+        if expert in broken:
+            raise RuntimeError("storage read failed")
+        return f.pinned.data_ptr() + expert * lay.stride
+
+    cache = osm.ExpertCache(slab, SLOTS * lay.stride, source=source)
+    cache.bind_layer(0, L)
+    model = Model(SLOTS * lay.stride, lay.stride)
+    cache.acquire(0, [0, 1, 2, 3])
+    model.acquire(0, [0, 1, 2, 3])
+    with pytest.raises(osm.OsmError) as e:
+        cache.acquire(0, [4, 5, 6])
+    assert e.value.code == -2
+    with pytest.raises(RuntimeError):
+        model.acquire(0, [4, 5, 6], failing=broken)
+    assert cache.stats() == model.stats()
+    resident = [e for e in range(E) if cache.contains(0, e)]
+    assert sorted(resident) == [2, 3, 4, 5]
+    # the device slot table agrees with the policy: the resident experts give
+    # the bits of the fully resident fixture layer, and a routing to 6 is
+    # reported as not resident
+    x = f.port.gen_normal(192, 0, 1.0, H).reshape(1, H)
+    xd = torch.from_numpy(x).cuda()
+    w = torch.full((1, K), 0.25, device="cuda")
+    ids = torch.tensor([resident], dtype=torch.int32, device="cuda")
+    out = torch.empty(1, H, device="cuda")
+    ref = torch.empty(1, H, device="cuda")
+    L.run_experts(xd, 1, ids, w, out)
+    f.layer.run_experts(xd, 1, ids, w, ref)
+    torch.cuda.synchronize()
+    assert f.ctx.status()[0] == 0
+    assert torch.equal(out, ref)
+    L.run_experts(xd, 1, torch.tensor([[2, 3, 4, 6]], dtype=torch.int32, device="cuda"), w, out)
+    torch.cuda.synchronize()
+    assert f.ctx.status()[0] & 4
+    # with the source working again the expert loads and routes normally
+    broken.clear()
+    ids = torch.empty(1, K, dtype=torch.int32, device="cuda")
+    L.route_qwen_top_k(xd, 1, ids, w)
+    picks = ids.cpu().numpy().astype(np.uint32).reshape(-1)
+    cache.acquire(0, [6])
+    assert cache.contains(0, 6)
+    cache.acquire(0, picks)
+    L.run_experts(xd, 1, ids, w, out)
+    torch.cuda.synchronize()
+    rout, rids, _, _, _ = f.oracle_token(x[0])
+    assert np.array_equal(picks, rids)
+    assert normwise_rel(out.cpu().numpy()[0], rout) <= 1e-4
+    assert f.ctx.status()[0] == 0
+    cache.close()
+
+
+def test_slab_fill_wait_times_out_on_a_pending_fill(torch):
+    """osm_slab_fill_wait with a 0 ms limit on a fill that cannot have landed
+    (the context stream is held by a bounded spin that the fill is ordered
+    after) returns OSM_ETIMEOUT; a longer limit then returns OK."""
+    import osm_b200 as osm
+
+    H, I = 256, 128
+    lay = osm.expert_layout(H, I)
+    ctx = osm.Context(0, max_tokens=1)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    slab = osm.Slab(ctx, lay, 2)
+    host = torch.zeros(lay.stride, dtype=torch.uint8).pin_memory()
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(400_000_000)   # a bounded spin, ~0.2 s at 1.9 GHz
+    slab.fill_async(0, host.data_ptr())
+    with pytest.raises(osm.OsmError) as e:
+        slab.fill_wait(0)
+    assert e.value.code == -6            # OSM_ETIMEOUT
+    slab.fill_wait(10_000)
+    stream.synchronize()
+    slab.close()
+    ctx.close()

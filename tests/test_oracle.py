@@ -245,3 +245,28 @@ def test_generator_is_deterministic_and_normal(port):
     assert np.array_equal(s1, s2) and s1.size == pyoracle.slot_stride(256, 64)
     assert pyoracle.slot_stride(2048, 512) == 1769472
     assert pyoracle.slot_stride(2048, 768) == 2654208
+
+
+def test_moe_token_slots_equals_moe_token_bitwise(port):
+    """The slot-based oracle entry (dequantise only the picked experts) gives
+    the bits of moe_token on fully dequantised experts, with and without a
+    shared expert and a logit bias."""
+    H, E, I, K = 256, 12, 128, 4
+    slots = np.stack([port.gen_expert_slot(9, 300 + 3 * e, 0.02, H, I) for e in range(E)])
+    shared = port.gen_expert_slot(9, 290, 0.02, H, I)
+    W = pyoracle.bf16_widen(port.bf16_round(port.gen_normal(9, 1, 0.05, E * H))).reshape(E, H)
+    sg = port.gen_normal(9, 2, 0.02, H)
+    bias = port.gen_normal(9, 3, 0.5, E)
+    experts = {e: port.dequant_slot(slots[e], H, I) for e in range(E)}
+    sh = port.dequant_slot(shared, H, I)
+    for t in range(4):
+        x = port.gen_normal(9, 10 + t, 1.0, H)
+        for b, with_shared in ((None, True), (bias, False)):
+            a = port.moe_token(x, W, K, True, experts, shared=sh if with_shared else None,
+                               scalar_gate=sg if with_shared else None, bias=b)
+            s = port.moe_token_slots(x, W, K, True, slots, I,
+                                     shared_slot=shared if with_shared else None,
+                                     scalar_gate=sg if with_shared else None, bias=b)
+            assert np.array_equal(a[0].view(np.uint32), s[0].view(np.uint32))
+            assert np.array_equal(a[1], s[1]) and np.array_equal(a[2], s[2])
+            assert a[3] == s[3] and a[4] == s[4]
