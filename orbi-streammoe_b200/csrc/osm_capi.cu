@@ -7,6 +7,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <set>
@@ -111,6 +112,8 @@ struct osm_context {
   uint32_t* picks_dev = nullptr;    // the same memory as the kernels address it
   size_t picks_cap = 0;
   cudaEvent_t picks_ev = nullptr;
+  bool tc_enabled = true;           // tensor-core expert kernels (OSM_DISABLE_TC=1: off)
+  bool tc_decode = false;           // also for fp32 calls of 3+ tokens (OSM_TC_DECODE=1)
 };
 
 struct osm_slab {
@@ -121,6 +124,10 @@ struct osm_slab {
   cudaStream_t side = nullptr;
   cudaEvent_t ev = nullptr;
   uint64_t h2d_bytes = 0;
+  // TMA tensor maps over the gate, up and down weight sections of every slot
+  // (the tensor-core expert kernels); tc_ok false: the layout does not suit them
+  alignas(64) unsigned char tc_maps[3][128];
+  bool tc_ok = false;
 };
 
 // Expert residency over one slab: LFU + recency entries keyed (layer, expert).
@@ -176,6 +183,9 @@ struct osm_layer {
   int* slot_of = nullptr;
   std::vector<int32_t> slot_host;
   osm_slab* slab = nullptr;
+  // TMA tensor maps over the shared expert's weight sections
+  alignas(64) unsigned char tc_shared[3][128];
+  bool tc_shared_ok = false;
 };
 
 namespace {
@@ -459,6 +469,120 @@ bool grouped_path(osm_layer* L, osm::GrpArgs* a, size_t* smem_gu, size_t* smem_d
   return osm::grouped_configure(*a, ctx->max_smem, smem_gu, smem_dn);
 }
 
+// TMA tensor maps over the weight sections of an expert layout at `base`.
+bool encode_expert_maps(unsigned char (*dst)[128], const uint8_t* base, const osm_expert_layout& L,
+                        uint32_t slots) {
+  const uint64_t off[3] = {L.gate_w, L.up_w, L.down_w};
+  const int rows[3] = {(int)L.inter, (int)L.inter, (int)L.hidden};
+  const int words[3] = {(int)L.hidden / 8, (int)L.hidden / 8, (int)L.inter / 8};
+  return osm::tc_encode_maps(dst, base, off, rows, words, (int)slots, L.stride);
+}
+
+// The tensor-core expert kernels (osm_tc.cu): fills the call-independent
+// fields of ta and the tensor maps; false when the layer's shapes or
+// alignment do not suit them (the older kernels run instead).
+bool tc_path(osm_layer* L, osm::TcArgs* ta, osm::TcMaps* maps) {
+  osm_context* ctx = L->ctx;
+  if (!ctx->tc_enabled || !L->slab || !L->slab->tc_ok) return false;
+  if (L->shared_slot && !L->tc_shared_ok) return false;
+  const osm_expert_layout& R = L->slab->layout;
+  const osm_expert_layout& S = L->shared_slot ? L->shared_layout : R;
+  *ta = osm::TcArgs{};
+  fill_sections(ta->gu, R, S, true);
+  fill_sections(ta->dn, R, S, false);
+  ta->H = L->g.H;
+  ta->Imax = (int)std::max(R.inter, L->shared_slot ? S.inter : 0u);
+  ta->kp1 = (int)L->g.k + 1;
+  ta->slab = L->slab->base;
+  ta->slab_stride = R.stride;
+  if (!osm::tc_configure(*ta, L->shared_slot ? 1 : 0, ctx->max_smem)) return false;
+  std::memcpy(maps->m[0], L->slab->tc_maps, sizeof(L->slab->tc_maps));
+  if (L->shared_slot) std::memcpy(maps->m[1], L->tc_shared, sizeof(L->tc_shared));
+  else std::memcpy(maps->m[1], L->slab->tc_maps, sizeof(L->slab->tc_maps));
+  return true;
+}
+
+// Whether a call of T tokens runs its experts on the tensor-core kernels of
+// osm_tc.cu.  Prefill: while the routed experts average at most 128 pairs
+// (the older prefill kernel, which converts each weight tile once per 128
+// pairs instead of per 96, is faster beyond that).  fp32 calls of 3+ tokens:
+// only when the context enables it (OSM_TC_DECODE=1; the grouped decode
+// kernels are faster at the decode batch sizes measured so far).
+bool tc_use(osm_layer* L, uint32_t T, bool prefill, osm::TcArgs* ta, osm::TcMaps* maps) {
+  osm_context* ctx = L->ctx;
+  if (prefill) {
+    if ((uint64_t)T * (uint64_t)L->g.k > 128ull * (uint64_t)L->g.E) return false;
+  } else if (!ctx->tc_decode) {
+    return false;
+  }
+  return tc_path(L, ta, maps);
+}
+
+// Pairs per chunk of the grouping for a call of T tokens: the tensor-core
+// kernels take 32 (fp32 calls) or 96 (prefill), the older grouped kernels 8
+// and the older prefill kernel 128.
+int chunk_pairs_for(osm_layer* L, uint32_t T, bool prefill) {
+  osm::TcArgs ta;
+  osm::TcMaps maps;
+  const bool tc = tc_use(L, T, prefill, &ta, &maps);
+  if (prefill) return tc ? osm::kTcChunkFast : 128;
+  return tc ? osm::kTcChunkPrecise : 8;
+}
+
+// Runs the tensor-core gate/up and down kernels, then the combine.
+int run_tc(osm_layer* L, uint32_t T, float* out, const float* residual, osm::TcArgs ta,
+           const osm::TcMaps& maps, bool precise, const uint16_t* xb, bool f16_out) {
+  osm_context* ctx = L->ctx;
+  Scratch& s = ctx->sc;
+  ta.x = ctx->cur_x;
+  ta.xb = xb;
+  ta.h = reinterpret_cast<float*>(s.hfrag);
+  ta.hb = reinterpret_cast<uint16_t*>(s.hfrag);
+  ta.partial = s.partial;
+  ta.pb = reinterpret_cast<uint16_t*>(s.partial);
+  ta.n_ch = s.n_ch;
+  ta.chunks = s.chunks;
+  ta.act = s.act;
+  ta.pair_tok = s.pair_tok;
+  ta.pair_pick = s.pair_pick;
+  ta.status = s.status;
+  {
+    Prof p(ctx, kKGateUp);
+    const cudaError_t e = osm::launch_tc_gateup(ta, maps, precise, ctx->num_sms, ctx->stream, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "tensor-core gate/up");
+  }
+  {
+    Prof p(ctx, kKDown);
+    const cudaError_t e = osm::launch_tc_down(ta, maps, precise, ctx->num_sms, ctx->stream, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "tensor-core down");
+  }
+  if (precise) {
+    osm::CombineArgs c{};
+    c.partial = s.partial;
+    c.weights = s.weights;
+    c.sgate = L->shared_slot ? s.sgate : nullptr;
+    c.residual = residual;
+    c.out = out;
+    c.B = (int)T;
+    c.H = L->g.H;
+    c.k = L->g.k;
+    {
+      Prof p(ctx, kKCombine);
+      osm::launch_combine(c, ctx->stream, &ctx->launches);
+    }
+    return check_launch(ctx, "combine");
+  }
+  if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
+    return fail(ctx, OSM_EINVAL, "prefill: out and residual must be 16-byte aligned");
+  {
+    Prof p(ctx, kKCombine);
+    osm::launch_combine_bf16(ta.pb, s.tp_pos, s.weights, L->shared_slot ? s.sgate : nullptr, residual,
+                             out, f16_out, s.status, (int)T, L->g.H, L->g.k, ctx->stream,
+                             &ctx->launches);
+  }
+  return check_launch(ctx, "prefill combine");
+}
+
 // picks_from_ids: one token whose picks the decode kernels resolve through
 // the slot table themselves (no binding step ran)
 int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
@@ -500,6 +624,12 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
       osm::launch_gemv_down(g, gl, ctx->stream, &ctx->launches);
     }
     return check_launch(ctx, "down gemv + combine");
+  }
+  {
+    // 3+ tokens: the tensor-core kernels over 32-pair chunks of each expert
+    osm::TcArgs ta;
+    osm::TcMaps maps;
+    if (tc_use(L, T, false, &ta, &maps)) return run_tc(L, T, out, residual, ta, maps, true, nullptr, false);
   }
   {
     // 3+ tokens: grouped projections over 8-token chunks of each expert
@@ -629,6 +759,12 @@ int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm
   Scratch& s = ctx->sc;
   if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
     return fail(ctx, OSM_EINVAL, "prefill: out and residual must be 16-byte aligned");
+  {
+    osm::TcArgs ta;
+    osm::TcMaps maps;
+    if (tc_use(L, T, true, &ta, &maps))
+      return run_tc(L, T, out, residual, ta, maps, false, x_given ? pa.xb : s.xbf, f16_out);
+  }
   if (!x_given) pa.xb = s.xbf;
   pa.hb = reinterpret_cast<uint16_t*>(s.hfrag);
   pa.pb = reinterpret_cast<uint16_t*>(s.partial);
@@ -738,6 +874,13 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   osm::init_gemv_attributes(ctx->max_smem);
   osm::init_grouped_attributes(ctx->max_smem);
   osm::init_prefill_attributes(ctx->max_smem);
+  osm::init_tc_attributes(ctx->max_smem);
+  {
+    const char* v = std::getenv("OSM_DISABLE_TC");
+    ctx->tc_enabled = !(v && v[0] && v[0] != '0');
+    const char* d = std::getenv("OSM_TC_DECODE");
+    ctx->tc_decode = d && d[0] && d[0] != '0';
+  }
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {
     cudaFree(ctx->status_blk);
@@ -1037,6 +1180,7 @@ int osm_slab_create(osm_context* ctx, const osm_expert_layout* layout, uint32_t 
     delete s;
     return fail(ctx, OSM_ECUDA, "slab: stream/event creation failed");
   }
+  s->tc_ok = encode_expert_maps(s->tc_maps, s->base, s->layout, slots);
   *out = s;
   return OSM_OK;
 }
@@ -1163,6 +1307,7 @@ int osm_layer_create(osm_context* ctx, const osm_layer_desc* d, osm_layer** out)
       return cleanup(OSM_ENOMEM, "layer: shared expert allocation failed");
     cudaMemcpy(L->shared_slot, d->shared_slot_host, d->shared_layout.stride, cudaMemcpyHostToDevice);
     cudaMemcpy(L->sgate_w, d->shared_gate_host, d->hidden * 4, cudaMemcpyHostToDevice);
+    L->tc_shared_ok = encode_expert_maps(L->tc_shared, L->shared_slot, L->shared_layout, 1);
   }
   if (d->norm_weight_host) {
     if (cudaMalloc(&L->norm_w, d->hidden * 4) != cudaSuccess)
@@ -1265,7 +1410,7 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
     a.do_group = 1;
     a.xfrag = nullptr;
     a.xbf = ctx->sc.xbf;
-    a.chunk_pairs = 128;
+    a.chunk_pairs = chunk_pairs_for(L, T, true);
     ctx->cur_x = x;
     launch_router_pair(ctx, a);
     rc = check_launch(ctx, "router");
@@ -1281,6 +1426,7 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   osm::GrpArgs ga;
   size_t sgu = 0, sdn = 0;
   if (dec || grouped_path(L, &ga, &sgu, &sdn)) a.xfrag = nullptr;  // only the older kernels read it
+  a.chunk_pairs = chunk_pairs_for(L, T, false);
   ctx->cur_x = x;
   launch_router_pair(ctx, a);
   rc = check_launch(ctx, "router");
@@ -1322,8 +1468,8 @@ int experts_impl(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, 
     if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
     a.xfrag = nullptr;
     a.xbf = s.xbf;
-    a.chunk_pairs = 128;
   }
+  a.chunk_pairs = chunk_pairs_for(L, T, prefill);
   ctx->cur_x = x;
   if (f16) {
     // the rows are the GEMM's operand already: only the grouping runs first
@@ -1401,11 +1547,11 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
     if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
     a.xfrag = nullptr;
     a.xbf = s.xbf;
-    a.chunk_pairs = 128;
   } else {
     dec = gemv_path(L, T, &g, &gl);
     if (dec || grouped_path(L, &ga, &sgu, &sdn)) a.xfrag = nullptr;  // only the older kernels read it
   }
+  a.chunk_pairs = chunk_pairs_for(L, T, prefill);
   // 1. route, with the shared gate and the activation operands; the picks go
   //    straight to mapped host memory
   a.force_exact = (flags & OSM_ROUTE_EXACT) ? 1 : 0;

@@ -257,6 +257,49 @@ void launch_combine_bf16(const uint16_t* pb, const int* tp_pos, const float* wei
                          unsigned int* status, int B, int H, int k, cudaStream_t s,
                          uint64_t* launches);
 
+// ---- tensor-core grouped experts with warp specialisation (osm_tc.cu) ----
+// Items are (chunk of pairs sharing an expert, 128 weight rows).  PRECISE:
+// bf16 operand planes (A = s q as hi + lo, exact; B = activations as hi +
+// mid), three passes plus a bias step, outputs within 1e-4 of the fp32 path;
+// chunks of kTcChunkPrecise pairs.  FAST: fp16 operands (A = fp16(s q + b)),
+// one pass, outputs within 2e-3; chunks of kTcChunkFast pairs.
+constexpr int kTcChunkPrecise = 32;
+constexpr int kTcChunkFast = 96;
+// TMA tensor maps (CUtensorMap, 128 bytes each) over the Q4 weight sections:
+// [kind: 0 routed experts in the slab, 1 the shared expert][0 gate, 1 up,
+// 2 down]; each map is words x rows x slots with an 8-word x 128-row box.
+struct alignas(64) TcMaps {
+  unsigned char m[2][3][128];
+};
+struct TcArgs {
+  ProjSections gu, dn;
+  const float* x;                // PRECISE gate/up: [T][H] fp32 rows
+  const uint16_t* xb;            // FAST gate/up: [T][H] fp16 rows
+  float* h;                      // PRECISE: [pairs][Imax] SwiGLU output
+  uint16_t* hb;                  // FAST: [pairs][Imax] fp16 SwiGLU output
+  float* partial;                // PRECISE down: [T][kp1][H] expert rows
+  uint16_t* pb;                  // FAST down: [pairs][H] fp16 expert rows
+  const int* n_ch;
+  const int2* chunks;            // {active entry, first pair within it}
+  const ActEntry* act;
+  const int* pair_tok;
+  const int* pair_pick;
+  const uint8_t* slab;           // routed slots: slot = (ptr - slab) / slab_stride
+  uint64_t slab_stride;
+  int H, Imax, kp1, nmt_gu, nmt_dn;
+  uint32_t* status;
+};
+// Encodes the three maps of one expert source: sections at base + off[s] with
+// rows[s] rows of words[s] u32 words, `slots` slots slot_stride bytes apart.
+bool tc_encode_maps(unsigned char (*dst)[128], const uint8_t* base, const uint64_t off[3],
+                    const int rows[3], const int words[3], int slots, uint64_t slot_stride);
+void init_tc_attributes(int max_smem);
+bool tc_configure(TcArgs& a, int has_shared, int max_smem);
+cudaError_t launch_tc_gateup(const TcArgs& a, const TcMaps& maps, bool precise, int grid,
+                             cudaStream_t s, uint64_t* launches);
+cudaError_t launch_tc_down(const TcArgs& a, const TcMaps& maps, bool precise, int grid,
+                           cudaStream_t s, uint64_t* launches);
+
 void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float* w,
                     float eps, bool exact, cudaStream_t s, uint64_t* launches);
 void launch_dequant(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi,
