@@ -17,6 +17,11 @@
  *  - Geometry: Q4 = MLX affine 4-bit, eight nibbles per uint32 LSB first,
  *    group 64 along the input dimension, BF16 scale and bias
  *    (src/cpu/reference_ops.cpp:11-67, shaders/q4_gemv.comp:32-63).
+ *  - The reference's C++ classes (VulkanComputeContext, VulkanFloatBuffer,
+ *    VulkanResidentExpertCache, ... under include/orbi/streammoe/backend/)
+ *    are implemented over this ABI by the C++ drop-in layer in
+ *    orbi-streammoe_b200/host (headers with the reference's exact public
+ *    declarations, sources replacing src/backend/*.cpp).
  */
 #ifndef OSM_B200_H
 #define OSM_B200_H
@@ -74,6 +79,10 @@ int osm_expert_layout_packed(uint32_t hidden, uint32_t inter, uint32_t group,
 /* ---- context: replaces VulkanComputeContext
  *      (include/orbi/streammoe/backend/vulkan_compute_context.hpp:19-49) ---- */
 int osm_context_create(int device, uint32_t max_tokens, osm_context** out);
+/* The device's name and SM count, for VulkanComputeContext::info()
+ * (include/orbi/streammoe/backend/vulkan_compute_context.hpp:33). */
+int osm_device_info(int device, char* name, size_t name_bytes, uint32_t* sms,
+                    uint32_t* runtime_version);
 int osm_context_destroy(osm_context* ctx);
 const char* osm_last_error(const osm_context* ctx);
 int osm_context_device(const osm_context* ctx);
@@ -106,7 +115,8 @@ int osm_host_free_pinned(void* host);
 
 /* run_vulkan_q4_dequant (src/backend/vulkan_q4_dequant.cpp:270,
  * shaders/q4_dequant.comp): out[r][c] = scale*q + bias, bit-exact with
- * cpu::dequantize_affine_rows (separate multiply and add, no FMA). */
+ * cpu::dequantize_affine_rows (separate multiply and add, no FMA).  Any
+ * group size that divides in_dim; in_dim a multiple of 8. */
 int osm_q4_dequant(osm_context* ctx, const uint32_t* packed_dev,
                    const uint16_t* scales_bf16_dev,
                    const uint16_t* biases_bf16_dev, uint32_t rows,
@@ -114,7 +124,11 @@ int osm_q4_dequant(osm_context* ctx, const uint32_t* packed_dev,
 
 /* run_vulkan_q4_gemv_preloaded (include/orbi/streammoe/backend/
  * vulkan_q4_gemv.hpp:53-57): y[t][r] = sum_c w[r][c] * x[t][c] for `tokens`
- * input vectors (batched; the reference is tokens == 1). */
+ * input vectors (batched; the reference is tokens == 1).  Group 64, in_dim a
+ * multiple of 64 up to 2048, out_dim a multiple of 16 and tokens up to the
+ * context's max_tokens run on the row-tiled projection kernel; any other
+ * geometry (group dividing in_dim, in_dim a multiple of 8) on a one-warp-per-
+ * row kernel. */
 int osm_q4_gemv(osm_context* ctx, const uint32_t* packed_dev,
                 const uint16_t* scales_bf16_dev,
                 const uint16_t* biases_bf16_dev, uint32_t out_dim,

@@ -892,6 +892,23 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   return OSM_OK;
 }
 
+int osm_device_info(int device, char* name, size_t name_bytes, uint32_t* sms,
+                    uint32_t* runtime_version) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return OSM_ECUDA;
+  cudaDeviceProp prop{};
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return OSM_ECUDA;
+  if (name && name_bytes) {
+    std::strncpy(name, prop.name, name_bytes - 1);
+    name[name_bytes - 1] = '\0';
+  }
+  if (sms) *sms = (uint32_t)prop.multiProcessorCount;
+  int rv = 0;
+  cudaRuntimeGetVersion(&rv);
+  if (runtime_version) *runtime_version = (uint32_t)rv;
+  return OSM_OK;
+}
+
 int osm_context_destroy(osm_context* ctx) {
   if (!ctx) return OSM_EINVAL;
   DeviceGuard dg(ctx->device);
@@ -1026,10 +1043,15 @@ int osm_q4_dequant(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
                    const uint16_t* bi, uint32_t rows, uint32_t in_dim, uint32_t group,
                    float* out) {
   if (!ctx) return OSM_EINVAL;
-  if (group != 64 || in_dim % 64 || rows == 0 || !packed || !sc || !bi || !out)
-    return fail(ctx, OSM_EINVAL, "q4 dequant: group must be 64 and in_dim a multiple of 64");
+  if (group == 0 || in_dim == 0 || in_dim % 8 || in_dim % group || rows == 0 || !packed || !sc ||
+      !bi || !out)
+    return fail(ctx, OSM_EINVAL,
+                "q4 dequant: in_dim must be a non-zero multiple of 8 and of the group size");
+  if ((uint64_t)rows * in_dim > (uint64_t)INT32_MAX * 8)
+    return fail(ctx, OSM_EINVAL, "q4 dequant: matrix too large");
   DeviceGuard dg(ctx->device);
-  osm::launch_dequant(packed, sc, bi, (int)rows, (int)in_dim, out, ctx->stream, &ctx->launches);
+  osm::launch_dequant(packed, sc, bi, (int)rows, (int)in_dim, (int)group, out, ctx->stream,
+                      &ctx->launches);
   return check_launch(ctx, "q4 dequant");
 }
 
@@ -1037,12 +1059,19 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
                 const uint16_t* bi, uint32_t out_dim, uint32_t in_dim, uint32_t group,
                 const float* x, uint32_t tokens, float* y) {
   if (!ctx) return OSM_EINVAL;
-  if (group != 64 || in_dim % 64 || in_dim > 2048 || out_dim % 16 || out_dim == 0 || !packed ||
+  if (group == 0 || in_dim == 0 || in_dim % 8 || in_dim % group || out_dim == 0 || !packed ||
       !sc || !bi || !x || !y || tokens == 0)
     return fail(ctx, OSM_EINVAL,
-                "q4 gemv: group 64, in_dim a multiple of 64 (<= 2048), out_dim a multiple of 16");
-  if (tokens > ctx->max_tokens) return fail(ctx, OSM_EINVAL, "q4 gemv: tokens > max_tokens");
+                "q4 gemv: in_dim must be a non-zero multiple of 8 and of the group size");
   DeviceGuard dg(ctx->device);
+  if (group != 64 || in_dim % 64 || in_dim > 2048 || out_dim % 16 || tokens > ctx->max_tokens) {
+    // shapes the row-tiled projection kernel does not take
+    if ((uint64_t)out_dim * tokens > (uint64_t)INT32_MAX / 32)
+      return fail(ctx, OSM_EINVAL, "q4 gemv: out_dim * tokens too large");
+    osm::launch_gemv_any(packed, sc, bi, (int)out_dim, (int)in_dim, (int)group, x, (int)tokens, y,
+                         ctx->stream, &ctx->launches);
+    return check_launch(ctx, "q4 gemv");
+  }
   int rc = ensure_scratch(ctx, tokens, 0, 1, 1, 64, in_dim);
   if (rc) return rc;
   Scratch& s = ctx->sc;

@@ -73,18 +73,52 @@ __global__ void rmsnorm_kernel(const float* in, float* out, int dim, const float
 }
 
 __global__ void dequant_kernel(const uint32_t* __restrict__ packed, const uint16_t* __restrict__ sc,
-                               const uint16_t* __restrict__ bi, int rows, int K,
+                               const uint16_t* __restrict__ bi, int rows, int K, int group,
                                float* __restrict__ out) {
   const size_t total = (size_t)rows * K;
-  const int G = K >> 6;
+  const int G = K / group;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
        i += (size_t)gridDim.x * blockDim.x) {
     const size_t row = i / K;
     const int col = (int)(i - row * K);
     const uint32_t q = (packed[row * (K >> 3) + (col >> 3)] >> ((col & 7) * 4)) & 0xFu;
-    const float s = bf16_bits_to_f32(sc[row * G + (col >> 6)]);
-    const float b = bf16_bits_to_f32(bi[row * G + (col >> 6)]);
+    const float s = bf16_bits_to_f32(sc[row * G + col / group]);
+    const float b = bf16_bits_to_f32(bi[row * G + col / group]);
     out[i] = __fadd_rn(__fmul_rn(s, (float)q), b);
+  }
+}
+
+// Any-geometry affine Q4 GEMV (group dividing K, K a multiple of 8): one warp
+// per (token, row), each lane a strided run of packed words, the dequantised
+// weight formed as in dequant_kernel.  Serves the small and odd shapes the
+// row-tiled projection kernels do not take (group sizes other than 64, K not
+// a multiple of 64); not a hot path.
+__global__ void gemv_any_kernel(const uint32_t* __restrict__ packed,
+                                const uint16_t* __restrict__ sc,
+                                const uint16_t* __restrict__ bi, int rows, int K, int group,
+                                const float* __restrict__ x, int tokens, float* __restrict__ y) {
+  const int lane = threadIdx.x & 31;
+  const size_t warps = ((size_t)gridDim.x * blockDim.x) >> 5;
+  const int W = K >> 3, G = K / group;
+  for (size_t w = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5; w < (size_t)rows * tokens;
+       w += warps) {
+    const int t = (int)(w / rows), r = (int)(w - (size_t)t * rows);
+    const uint32_t* pr = packed + (size_t)r * W;
+    const float* xt = x + (size_t)t * K;
+    float acc = 0.0f;
+    for (int word = lane; word < W; word += 32) {
+      const uint32_t p = pr[word];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = word * 8 + j, g = c / group;
+        const float s = bf16_bits_to_f32(sc[(size_t)r * G + g]);
+        const float b = bf16_bits_to_f32(bi[(size_t)r * G + g]);
+        acc = fmaf(__fadd_rn(__fmul_rn(s, (float)((p >> (4 * j)) & 0xFu)), b), xt[c], acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[(size_t)t * rows + r] = acc;
   }
 }
 
@@ -226,8 +260,17 @@ void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float*
 }
 
 void launch_dequant(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi, int rows,
-                    int K, float* out, cudaStream_t s, uint64_t* launches) {
-  dequant_kernel<<<grid_for((size_t)rows * K, 256), 256, 0, s>>>(packed, sc, bi, rows, K, out);
+                    int K, int group, float* out, cudaStream_t s, uint64_t* launches) {
+  dequant_kernel<<<grid_for((size_t)rows * K, 256), 256, 0, s>>>(packed, sc, bi, rows, K, group,
+                                                                 out);
+  if (launches) *launches += 1;
+}
+
+void launch_gemv_any(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi, int rows,
+                     int K, int group, const float* x, int tokens, float* y, cudaStream_t s,
+                     uint64_t* launches) {
+  gemv_any_kernel<<<grid_for((size_t)rows * tokens * 32, 256), 256, 0, s>>>(
+      packed, sc, bi, rows, K, group, x, tokens, y);
   if (launches) *launches += 1;
 }
 

@@ -67,6 +67,8 @@ _P = C.c_void_p
 _SIGS = {
     "osm_expert_layout_packed": (C.c_int, [C.c_uint32, C.c_uint32, C.c_uint32, C.POINTER(ExpertLayout)]),
     "osm_context_create": (C.c_int, [C.c_int, C.c_uint32, C.POINTER(_P)]),
+    "osm_device_info": (C.c_int, [C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_uint32),
+                                  C.POINTER(C.c_uint32)]),
     "osm_context_destroy": (C.c_int, [_P]),
     "osm_last_error": (C.c_char_p, [_P]),
     "osm_context_device": (C.c_int, [_P]),

@@ -51,11 +51,51 @@ def test_q4_dequant_bit_exact(torch, ctx, port):
 
 
 def test_q4_dequant_rejects_bad_group(torch, ctx):
+    """A group that does not divide the row (tests/vulkan_q4_dequant_test.cpp:
+    38-53 asks for group 3 on an 8-column row) is refused before any launch."""
     import osm_b200 as osm
 
     z = torch.zeros(64, dtype=torch.int32, device="cuda")
     with pytest.raises(osm.OsmError):
-        ctx.q4_dequant(z, z, z, 1, 64, torch.empty(64, device="cuda"), group=32)
+        ctx.q4_dequant(z, z, z, 1, 8, torch.empty(64, device="cuda"), group=3)
+    with pytest.raises(osm.OsmError):
+        ctx.q4_gemv(z, z, z, 1, 8, torch.zeros(8, device="cuda"), 1,
+                    torch.empty(1, device="cuda"), group=3)
+
+
+def _proj_g(port, rows, cols, group, seed):
+    vals = port.gen_normal(seed, 1, 0.02, rows * cols)
+    pk, sc, bi = port.quantize_q4(vals, rows, cols, group)
+    return pk, port.bf16_round(sc).reshape(rows, -1), port.bf16_round(bi).reshape(rows, -1)
+
+
+@pytest.mark.parametrize("rows,cols,group,tokens", [
+    (8, 8, 4, 1),       # the checkpoint fixtures' geometry (hidden 8, group 4)
+    (24, 96, 32, 3),    # rows not a multiple of 16, group 32
+    (40, 8, 8, 2),
+    (130, 64, 64, 70),  # more tokens than the context's max_tokens (64)
+    (16, 4096, 64, 2),  # K above the row-tiled kernel's 2048
+])
+def test_q4_any_geometry(torch, ctx, port, rows, cols, group, tokens):
+    """Shapes outside the row-tiled projection kernel run on the
+    any-geometry dequant / GEMV kernels: dequant bit-exact, GEMV within the
+    same bounds as above."""
+    pk, sb, bb = _proj_g(port, rows, cols, group, rows * 7 + cols + group)
+    W = port.dequantize_affine_rows(pk, rows, cols // 8, pyoracle.bf16_widen(sb),
+                                    pyoracle.bf16_widen(bb), 4, group)
+    pkd, sbd, bbd = (torch.from_numpy(a).cuda() for a in (pk, sb, bb))
+    out = torch.empty(rows, cols, device="cuda")
+    ctx.q4_dequant(pkd, sbd, bbd, rows, cols, out, group=group)
+    x = port.gen_normal(6, rows + tokens, 1.0, tokens * cols).reshape(tokens, cols)
+    y = torch.empty(tokens, rows, device="cuda")
+    ctx.q4_gemv(pkd, sbd, bbd, rows, cols, torch.from_numpy(x).cuda(), tokens, y, group=group)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), W.view(np.uint32))
+    got = y.cpu().numpy()
+    for t in range(tokens):
+        ref = port.matvec(W, x[t])
+        assert normwise_rel(got[t], ref) <= 1e-4
+        assert float(np.abs(got[t] - ref).max()) <= 5e-4
 
 
 @pytest.mark.parametrize("rows,cols", [(64, 128), (512, 2048), (2048, 512), (2048, 768), (16, 64)])
