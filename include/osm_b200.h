@@ -21,7 +21,7 @@
  *    VulkanResidentExpertCache, ... under include/orbi/streammoe/backend/)
  *    are implemented over this ABI by the C++ drop-in layer in
  *    orbi-streammoe_b200/host (headers with the reference's exact public
- *    declarations, sources replacing src/backend/*.cpp).
+ *    declarations, sources replacing the .cpp files of src/backend).
  */
 #ifndef OSM_B200_H
 #define OSM_B200_H
