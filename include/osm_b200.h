@@ -122,6 +122,14 @@ int osm_q4_dequant(osm_context* ctx, const uint32_t* packed_dev,
                    const uint16_t* biases_bf16_dev, uint32_t rows,
                    uint32_t in_dim, uint32_t group, float* out_dev);
 
+/* The same with fp32 scale and bias (the reference's device format,
+ * src/backend/vulkan_q4_weights.cpp), for metadata bf16 cannot hold exactly;
+ * any-geometry kernel. */
+int osm_q4_dequant_f32(osm_context* ctx, const uint32_t* packed_dev,
+                       const float* scales_dev, const float* biases_dev,
+                       uint32_t rows, uint32_t in_dim, uint32_t group,
+                       float* out_dev);
+
 /* run_vulkan_q4_gemv_preloaded (include/orbi/streammoe/backend/
  * vulkan_q4_gemv.hpp:53-57): y[t][r] = sum_c w[r][c] * x[t][c] for `tokens`
  * input vectors (batched; the reference is tokens == 1).  Group 64, in_dim a
@@ -134,6 +142,11 @@ int osm_q4_gemv(osm_context* ctx, const uint32_t* packed_dev,
                 const uint16_t* biases_bf16_dev, uint32_t out_dim,
                 uint32_t in_dim, uint32_t group, const float* x_dev,
                 uint32_t tokens, float* y_dev);
+/* osm_q4_gemv with fp32 scale and bias (see osm_q4_dequant_f32). */
+int osm_q4_gemv_f32(osm_context* ctx, const uint32_t* packed_dev,
+                    const float* scales_dev, const float* biases_dev,
+                    uint32_t out_dim, uint32_t in_dim, uint32_t group,
+                    const float* x_dev, uint32_t tokens, float* y_dev);
 
 /* run_vulkan_swiglu_buffers (include/orbi/streammoe/backend/
  * vulkan_swiglu.hpp:26-30): out = silu(gate) * up. */

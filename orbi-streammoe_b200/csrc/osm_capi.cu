@@ -1039,39 +1039,74 @@ int osm_host_free_pinned(void* host) {
   return cudaFreeHost(host) == cudaSuccess ? OSM_OK : OSM_ECUDA;
 }
 
+namespace {
+
+// The Q4 geometry every dequant / GEMV entry accepts.
+int check_q4(osm_context* ctx, const char* what, const void* packed, const void* sc,
+             const void* bi, uint32_t rows, uint32_t in_dim, uint32_t group) {
+  if (group == 0 || in_dim == 0 || in_dim % 8 || in_dim % group || rows == 0 || !packed || !sc ||
+      !bi)
+    return fail(ctx, OSM_EINVAL,
+                std::string(what) +
+                    ": in_dim must be a non-zero multiple of 8 and of the group size");
+  if ((uint64_t)rows * in_dim > (uint64_t)INT32_MAX * 8)
+    return fail(ctx, OSM_EINVAL, std::string(what) + ": matrix too large");
+  return OSM_OK;
+}
+
+int q4_dequant_any(osm_context* ctx, const uint32_t* packed, const void* sc, const void* bi,
+                   bool f32, uint32_t rows, uint32_t in_dim, uint32_t group, float* out) {
+  if (!ctx) return OSM_EINVAL;
+  if (int rc = check_q4(ctx, "q4 dequant", packed, sc, bi, rows, in_dim, group)) return rc;
+  if (!out) return fail(ctx, OSM_EINVAL, "q4 dequant: null output");
+  DeviceGuard dg(ctx->device);
+  osm::launch_dequant(packed, sc, bi, f32, (int)rows, (int)in_dim, (int)group, out, ctx->stream,
+                      &ctx->launches);
+  return check_launch(ctx, "q4 dequant");
+}
+
+int q4_gemv_any(osm_context* ctx, const uint32_t* packed, const void* sc, const void* bi, bool f32,
+                uint32_t out_dim, uint32_t in_dim, uint32_t group, const float* x,
+                uint32_t tokens, float* y) {
+  if ((uint64_t)out_dim * tokens > (uint64_t)INT32_MAX / 32)
+    return fail(ctx, OSM_EINVAL, "q4 gemv: out_dim * tokens too large");
+  DeviceGuard dg(ctx->device);
+  osm::launch_gemv_any(packed, sc, bi, f32, (int)out_dim, (int)in_dim, (int)group, x, (int)tokens,
+                       y, ctx->stream, &ctx->launches);
+  return check_launch(ctx, "q4 gemv");
+}
+
+}  // namespace
+
 int osm_q4_dequant(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
                    const uint16_t* bi, uint32_t rows, uint32_t in_dim, uint32_t group,
                    float* out) {
+  return q4_dequant_any(ctx, packed, sc, bi, false, rows, in_dim, group, out);
+}
+
+int osm_q4_dequant_f32(osm_context* ctx, const uint32_t* packed, const float* sc, const float* bi,
+                       uint32_t rows, uint32_t in_dim, uint32_t group, float* out) {
+  return q4_dequant_any(ctx, packed, sc, bi, true, rows, in_dim, group, out);
+}
+
+int osm_q4_gemv_f32(osm_context* ctx, const uint32_t* packed, const float* sc, const float* bi,
+                    uint32_t out_dim, uint32_t in_dim, uint32_t group, const float* x,
+                    uint32_t tokens, float* y) {
   if (!ctx) return OSM_EINVAL;
-  if (group == 0 || in_dim == 0 || in_dim % 8 || in_dim % group || rows == 0 || !packed || !sc ||
-      !bi || !out)
-    return fail(ctx, OSM_EINVAL,
-                "q4 dequant: in_dim must be a non-zero multiple of 8 and of the group size");
-  if ((uint64_t)rows * in_dim > (uint64_t)INT32_MAX * 8)
-    return fail(ctx, OSM_EINVAL, "q4 dequant: matrix too large");
-  DeviceGuard dg(ctx->device);
-  osm::launch_dequant(packed, sc, bi, (int)rows, (int)in_dim, (int)group, out, ctx->stream,
-                      &ctx->launches);
-  return check_launch(ctx, "q4 dequant");
+  if (int rc = check_q4(ctx, "q4 gemv", packed, sc, bi, out_dim, in_dim, group)) return rc;
+  if (!x || !y || tokens == 0) return fail(ctx, OSM_EINVAL, "q4 gemv: null vector or no tokens");
+  return q4_gemv_any(ctx, packed, sc, bi, true, out_dim, in_dim, group, x, tokens, y);
 }
 
 int osm_q4_gemv(osm_context* ctx, const uint32_t* packed, const uint16_t* sc,
                 const uint16_t* bi, uint32_t out_dim, uint32_t in_dim, uint32_t group,
                 const float* x, uint32_t tokens, float* y) {
   if (!ctx) return OSM_EINVAL;
-  if (group == 0 || in_dim == 0 || in_dim % 8 || in_dim % group || out_dim == 0 || !packed ||
-      !sc || !bi || !x || !y || tokens == 0)
-    return fail(ctx, OSM_EINVAL,
-                "q4 gemv: in_dim must be a non-zero multiple of 8 and of the group size");
+  if (int rc = check_q4(ctx, "q4 gemv", packed, sc, bi, out_dim, in_dim, group)) return rc;
+  if (!x || !y || tokens == 0) return fail(ctx, OSM_EINVAL, "q4 gemv: null vector or no tokens");
+  if (group != 64 || in_dim % 64 || in_dim > 2048 || out_dim % 16 || tokens > ctx->max_tokens)
+    return q4_gemv_any(ctx, packed, sc, bi, false, out_dim, in_dim, group, x, tokens, y);
   DeviceGuard dg(ctx->device);
-  if (group != 64 || in_dim % 64 || in_dim > 2048 || out_dim % 16 || tokens > ctx->max_tokens) {
-    // shapes the row-tiled projection kernel does not take
-    if ((uint64_t)out_dim * tokens > (uint64_t)INT32_MAX / 32)
-      return fail(ctx, OSM_EINVAL, "q4 gemv: out_dim * tokens too large");
-    osm::launch_gemv_any(packed, sc, bi, (int)out_dim, (int)in_dim, (int)group, x, (int)tokens, y,
-                         ctx->stream, &ctx->launches);
-    return check_launch(ctx, "q4 gemv");
-  }
   int rc = ensure_scratch(ctx, tokens, 0, 1, 1, 64, in_dim);
   if (rc) return rc;
   Scratch& s = ctx->sc;

@@ -72,8 +72,15 @@ __global__ void rmsnorm_kernel(const float* in, float* out, int dim, const float
   }
 }
 
-__global__ void dequant_kernel(const uint32_t* __restrict__ packed, const uint16_t* __restrict__ sc,
-                               const uint16_t* __restrict__ bi, int rows, int K, int group,
+// Affine metadata element i: bf16 bits (the slot format) or fp32.
+__device__ __forceinline__ float meta_at(const uint16_t* p, size_t i) {
+  return bf16_bits_to_f32(p[i]);
+}
+__device__ __forceinline__ float meta_at(const float* p, size_t i) { return p[i]; }
+
+template <typename M>
+__global__ void dequant_kernel(const uint32_t* __restrict__ packed, const M* __restrict__ sc,
+                               const M* __restrict__ bi, int rows, int K, int group,
                                float* __restrict__ out) {
   const size_t total = (size_t)rows * K;
   const int G = K / group;
@@ -82,8 +89,8 @@ __global__ void dequant_kernel(const uint32_t* __restrict__ packed, const uint16
     const size_t row = i / K;
     const int col = (int)(i - row * K);
     const uint32_t q = (packed[row * (K >> 3) + (col >> 3)] >> ((col & 7) * 4)) & 0xFu;
-    const float s = bf16_bits_to_f32(sc[row * G + col / group]);
-    const float b = bf16_bits_to_f32(bi[row * G + col / group]);
+    const float s = meta_at(sc, row * G + col / group);
+    const float b = meta_at(bi, row * G + col / group);
     out[i] = __fadd_rn(__fmul_rn(s, (float)q), b);
   }
 }
@@ -92,10 +99,10 @@ __global__ void dequant_kernel(const uint32_t* __restrict__ packed, const uint16
 // per (token, row), each lane a strided run of packed words, the dequantised
 // weight formed as in dequant_kernel.  Serves the small and odd shapes the
 // row-tiled projection kernels do not take (group sizes other than 64, K not
-// a multiple of 64); not a hot path.
-__global__ void gemv_any_kernel(const uint32_t* __restrict__ packed,
-                                const uint16_t* __restrict__ sc,
-                                const uint16_t* __restrict__ bi, int rows, int K, int group,
+// a multiple of 64, fp32 metadata); not a hot path.
+template <typename M>
+__global__ void gemv_any_kernel(const uint32_t* __restrict__ packed, const M* __restrict__ sc,
+                                const M* __restrict__ bi, int rows, int K, int group,
                                 const float* __restrict__ x, int tokens, float* __restrict__ y) {
   const int lane = threadIdx.x & 31;
   const size_t warps = ((size_t)gridDim.x * blockDim.x) >> 5;
@@ -111,8 +118,8 @@ __global__ void gemv_any_kernel(const uint32_t* __restrict__ packed,
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int c = word * 8 + j, g = c / group;
-        const float s = bf16_bits_to_f32(sc[(size_t)r * G + g]);
-        const float b = bf16_bits_to_f32(bi[(size_t)r * G + g]);
+        const float s = meta_at(sc, (size_t)r * G + g);
+        const float b = meta_at(bi, (size_t)r * G + g);
         acc = fmaf(__fadd_rn(__fmul_rn(s, (float)((p >> (4 * j)) & 0xFu)), b), xt[c], acc);
       }
     }
@@ -259,18 +266,31 @@ void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float*
   if (launches) *launches += 1;
 }
 
-void launch_dequant(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi, int rows,
-                    int K, int group, float* out, cudaStream_t s, uint64_t* launches) {
-  dequant_kernel<<<grid_for((size_t)rows * K, 256), 256, 0, s>>>(packed, sc, bi, rows, K, group,
-                                                                 out);
+void launch_dequant(const uint32_t* packed, const void* sc, const void* bi, bool f32_meta,
+                    int rows, int K, int group, float* out, cudaStream_t s, uint64_t* launches) {
+  const int grid = grid_for((size_t)rows * K, 256);
+  if (f32_meta)
+    dequant_kernel<float><<<grid, 256, 0, s>>>(packed, static_cast<const float*>(sc),
+                                               static_cast<const float*>(bi), rows, K, group, out);
+  else
+    dequant_kernel<uint16_t><<<grid, 256, 0, s>>>(packed, static_cast<const uint16_t*>(sc),
+                                                  static_cast<const uint16_t*>(bi), rows, K, group,
+                                                  out);
   if (launches) *launches += 1;
 }
 
-void launch_gemv_any(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi, int rows,
-                     int K, int group, const float* x, int tokens, float* y, cudaStream_t s,
-                     uint64_t* launches) {
-  gemv_any_kernel<<<grid_for((size_t)rows * tokens * 32, 256), 256, 0, s>>>(
-      packed, sc, bi, rows, K, group, x, tokens, y);
+void launch_gemv_any(const uint32_t* packed, const void* sc, const void* bi, bool f32_meta,
+                     int rows, int K, int group, const float* x, int tokens, float* y,
+                     cudaStream_t s, uint64_t* launches) {
+  const int grid = grid_for((size_t)rows * tokens * 32, 256);
+  if (f32_meta)
+    gemv_any_kernel<float><<<grid, 256, 0, s>>>(packed, static_cast<const float*>(sc),
+                                                static_cast<const float*>(bi), rows, K, group, x,
+                                                tokens, y);
+  else
+    gemv_any_kernel<uint16_t><<<grid, 256, 0, s>>>(packed, static_cast<const uint16_t*>(sc),
+                                                   static_cast<const uint16_t*>(bi), rows, K, group,
+                                                   x, tokens, y);
   if (launches) *launches += 1;
 }
 

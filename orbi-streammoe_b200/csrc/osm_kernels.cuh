@@ -302,11 +302,12 @@ cudaError_t launch_tc_down(const TcArgs& a, const TcMaps& maps, bool precise, in
 
 void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float* w,
                     float eps, bool exact, cudaStream_t s, uint64_t* launches);
-void launch_dequant(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi,
+// sc/bi: bf16 bits, or fp32 when f32_meta
+void launch_dequant(const uint32_t* packed, const void* sc, const void* bi, bool f32_meta,
                     int rows, int K, int group, float* out, cudaStream_t s, uint64_t* launches);
-void launch_gemv_any(const uint32_t* packed, const uint16_t* sc, const uint16_t* bi, int rows,
-                     int K, int group, const float* x, int tokens, float* y, cudaStream_t s,
-                     uint64_t* launches);
+void launch_gemv_any(const uint32_t* packed, const void* sc, const void* bi, bool f32_meta,
+                     int rows, int K, int group, const float* x, int tokens, float* y,
+                     cudaStream_t s, uint64_t* launches);
 void launch_swiglu(const float* g, const float* u, float* out, size_t n, cudaStream_t s,
                    uint64_t* launches);
 void launch_waccum(const float* src, float w, float* acc, size_t n, cudaStream_t s,

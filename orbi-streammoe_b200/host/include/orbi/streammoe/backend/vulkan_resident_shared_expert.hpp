@@ -1,7 +1,7 @@
 // The always-on Qwen shared expert resident in HBM; its scalar gate stays on
 // the host (sigmoid(gate . hidden) in the reference's operation order).  As
 // include/orbi/streammoe/backend/vulkan_resident_shared_expert.hpp of the
-// reference.  Projection scales/biases must be bf16-representable.
+// reference.
 #pragma once
 
 #include <cstddef>

@@ -422,21 +422,28 @@ VulkanQ4DequantResult run_vulkan_q4_dequant(VulkanComputeContext& context,
                    &r.diagnostic))
     return r;
   try {
+    // bf16 metadata (the slot format) when it holds the values exactly, else fp32
     std::vector<std::uint16_t> sb, bb;
-    if (!osmh::narrow_bf16(scales, sb, &r.diagnostic, "Q4 dequant") ||
-        !osmh::narrow_bf16(biases, bb, &r.diagnostic, "Q4 dequant"))
-      return r;
+    const bool bf16 = osmh::narrow_bf16(scales, sb, nullptr, "") &&
+                      osmh::narrow_bf16(biases, bb, nullptr, "");
     osm_context* ctx = context.osm();
     DeviceVec p, s, b, o;
     const std::size_t cols = packed_cols * 8;
     int rc = p.put(ctx, packed.data(), packed.size_bytes());
-    if (rc == OSM_OK) rc = s.put(ctx, sb.data(), sb.size() * 2);
-    if (rc == OSM_OK) rc = b.put(ctx, bb.data(), bb.size() * 2);
+    if (rc == OSM_OK)
+      rc = bf16 ? s.put(ctx, sb.data(), sb.size() * 2) : s.put(ctx, scales.data(), scales.size_bytes());
+    if (rc == OSM_OK)
+      rc = bf16 ? b.put(ctx, bb.data(), bb.size() * 2) : b.put(ctx, biases.data(), biases.size_bytes());
     if (rc == OSM_OK) rc = o.alloc(ctx, rows * cols * sizeof(float));
     if (rc == OSM_OK)
-      rc = osm_q4_dequant(ctx, static_cast<const uint32_t*>(p.p), static_cast<const uint16_t*>(s.p),
-                          static_cast<const uint16_t*>(b.p), (uint32_t)rows, (uint32_t)cols,
-                          (uint32_t)group_size, static_cast<float*>(o.p));
+      rc = bf16 ? osm_q4_dequant(ctx, static_cast<const uint32_t*>(p.p),
+                                 static_cast<const uint16_t*>(s.p), static_cast<const uint16_t*>(b.p),
+                                 (uint32_t)rows, (uint32_t)cols, (uint32_t)group_size,
+                                 static_cast<float*>(o.p))
+                : osm_q4_dequant_f32(ctx, static_cast<const uint32_t*>(p.p),
+                                     static_cast<const float*>(s.p), static_cast<const float*>(b.p),
+                                     (uint32_t)rows, (uint32_t)cols, (uint32_t)group_size,
+                                     static_cast<float*>(o.p));
     r.values.resize(rows * cols);
     if (rc == OSM_OK) rc = osm_download(ctx, r.values.data(), o.p, r.values.size() * sizeof(float));
     if (rc != OSM_OK) {
@@ -496,12 +503,11 @@ std::optional<VulkanQ4ProjectionWeights> VulkanQ4ProjectionWeights::create(
     return std::nullopt;
   }
   try {
+    // bf16 copies of the metadata (read by the row-tiled kernel) when bf16
+    // holds the values exactly; the fp32 buffers below serve the rest
     std::vector<std::uint16_t> sb, bb;
-    if (!osmh::narrow_bf16(scales, sb, &local, "Q4 weights") ||
-        !osmh::narrow_bf16(biases, bb, &local, "Q4 weights")) {
-      osmh::set(diagnostic, local);
-      return std::nullopt;
-    }
+    const bool bf16 = osmh::narrow_bf16(scales, sb, nullptr, "") &&
+                      osmh::narrow_bf16(biases, bb, nullptr, "");
     auto impl = std::make_unique<Impl>();
     osm_context* ctx = context.osm();
     impl->ctx = ctx;
@@ -510,10 +516,12 @@ std::optional<VulkanQ4ProjectionWeights> VulkanQ4ProjectionWeights::create(
     impl->group = group_size;
     int rc = osm_device_alloc(ctx, packed.size_bytes(), &impl->packed);
     if (rc == OSM_OK) rc = osm_upload(ctx, impl->packed, packed.data(), packed.size_bytes());
-    if (rc == OSM_OK) rc = osm_device_alloc(ctx, sb.size() * 2, &impl->s16);
-    if (rc == OSM_OK) rc = osm_upload(ctx, impl->s16, sb.data(), sb.size() * 2);
-    if (rc == OSM_OK) rc = osm_device_alloc(ctx, bb.size() * 2, &impl->b16);
-    if (rc == OSM_OK) rc = osm_upload(ctx, impl->b16, bb.data(), bb.size() * 2);
+    if (bf16) {
+      if (rc == OSM_OK) rc = osm_device_alloc(ctx, sb.size() * 2, &impl->s16);
+      if (rc == OSM_OK) rc = osm_upload(ctx, impl->s16, sb.data(), sb.size() * 2);
+      if (rc == OSM_OK) rc = osm_device_alloc(ctx, bb.size() * 2, &impl->b16);
+      if (rc == OSM_OK) rc = osm_upload(ctx, impl->b16, bb.data(), bb.size() * 2);
+    }
     if (rc != OSM_OK) {
       osmh::set(diagnostic, osmh::err(ctx, rc, "Q4 weights upload failed"));
       return std::nullopt;
@@ -533,7 +541,9 @@ std::optional<VulkanQ4ProjectionWeights> VulkanQ4ProjectionWeights::create(
   }
 }
 
-bool VulkanQ4ProjectionWeights::valid() const noexcept { return impl_ && impl_->packed && impl_->s16; }
+bool VulkanQ4ProjectionWeights::valid() const noexcept {
+  return impl_ && impl_->packed && impl_->scales && impl_->biases;
+}
 std::size_t VulkanQ4ProjectionWeights::out_dim() const noexcept { return impl_ ? impl_->out_dim : 0; }
 std::size_t VulkanQ4ProjectionWeights::packed_cols() const noexcept {
   return impl_ ? impl_->packed_cols : 0;
@@ -585,10 +595,16 @@ VulkanBufferDispatchResult run_vulkan_q4_gemv_preloaded(VulkanComputeContext& co
     return r;
   }
   osm_context* ctx = context.osm();
-  int rc = osm_q4_gemv(ctx, weights.device_packed(), weights.device_scales_bf16(),
-                       weights.device_biases_bf16(), (uint32_t)weights.out_dim(),
-                       (uint32_t)weights.in_dim(), (uint32_t)weights.group_size(), x.device_data(), 1,
-                       y.device_data());
+  const auto od = (uint32_t)weights.out_dim(), id = (uint32_t)weights.in_dim(),
+             gs = (uint32_t)weights.group_size();
+  int rc = weights.device_scales_bf16()
+               ? osm_q4_gemv(ctx, weights.device_packed(), weights.device_scales_bf16(),
+                             weights.device_biases_bf16(), od, id, gs, x.device_data(), 1,
+                             y.device_data())
+               : osm_q4_gemv_f32(ctx, weights.device_packed(),
+                                 weights.scales_buffer().device_data(),
+                                 weights.biases_buffer().device_data(), od, id, gs,
+                                 x.device_data(), 1, y.device_data());
   if (rc == OSM_OK) rc = osm_context_synchronize(ctx);
   if (rc != OSM_OK) {
     r.diagnostic = osmh::err(ctx, rc, "Q4 GEMV failed");

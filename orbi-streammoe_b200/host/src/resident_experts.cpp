@@ -134,6 +134,29 @@ bool bind_expert(const QpackReader& reader, const ExpertCacheEntry& entry, Qpack
   return true;
 }
 
+bool metadata_bf16(const QpackExpertQ4View& v) {
+  std::uint16_t b;
+  for (const float f : v.scales)
+    if (!osmh::bf16_exact(f, &b)) return false;
+  for (const float f : v.biases)
+    if (!osmh::bf16_exact(f, &b)) return false;
+  return true;
+}
+
+// Whether the expert can live in a slab slot: a geometry the fused expert
+// kernels take and metadata the slot's bf16 format holds exactly.
+bool slab_eligible(const QpackExpertQ4View& gate, const QpackExpertQ4View& up,
+                   const QpackExpertQ4View& down, const Geometry& g, osm_expert_layout* L) {
+  return slab_layout(g, L) && metadata_bf16(gate) && metadata_bf16(up) && metadata_bf16(down);
+}
+
+bool slab_eligible(const QpackReader& reader, const ExpertCacheEntry& entry, Geometry* geo,
+                   osm_expert_layout* L) {
+  QpackExpertQ4View g, u, d;
+  std::string ignored;
+  return bind_expert(reader, entry, g, u, d, *geo, &ignored) && slab_eligible(g, u, d, *geo, L);
+}
+
 }  // namespace
 
 std::optional<VulkanResidentExpert> VulkanResidentExpert::create(VulkanComputeContext& context,
@@ -159,9 +182,10 @@ std::optional<VulkanResidentExpert> VulkanResidentExpert::create_in_slab(
     std::string local;
 
     osm_expert_layout L{};
-    const bool slab_ok = slab_layout(g, &L);
+    const bool slab_ok = slab_eligible(gate, up, down, g, &L);
     if (slab && !slab_ok) {
-      osmh::set(diagnostic, "resident expert: geometry has no slab layout");
+      osmh::set(diagnostic,
+                "resident expert: geometry or non-bf16 metadata has no slab slot format");
       return std::nullopt;
     }
     if (slab_ok) {
@@ -418,21 +442,22 @@ struct VulkanResidentExpertCache::Impl {
     if (r.slab_slot() >= 0) free_slots.push_back(static_cast<std::uint32_t>(r.slab_slot()));
   }
 
-  // Creates the slab sized for this geometry when it has a slab layout.
-  bool ensure_slab(const ExpertCacheEntry& entry, std::string* d) {
-    if (slab) return true;
-    QpackExpertQ4View g, u, dn;
+  // Whether this entry goes into a slab slot; creates the slab, sized for
+  // its geometry, at the first such entry.
+  bool use_slab(const ExpertCacheEntry& entry) {
     Geometry geo;
-    if (!bind_expert(reader, entry, g, u, dn, geo, d)) return false;
-    if (!slab_layout(geo, &layout)) return true;  // any-geometry residents
+    osm_expert_layout L{};
+    if (!slab_eligible(reader, entry, &geo, &L)) return false;
+    if (slab) return std::memcmp(&L, &layout, sizeof(L)) == 0 && !free_slots.empty();
+    layout = L;
     const std::size_t per = accounted(geo);
     const std::size_t fit = per ? budget / per : 0;
     const std::size_t slots = std::min<std::size_t>(fit, 1u << 20) + 1;
     const int rc = osm_slab_create(context.osm(), &layout, static_cast<std::uint32_t>(slots), &slab);
     if (rc != OSM_OK) {
       slab = nullptr;
-      osmh::set(d, osmh::err(context.osm(), rc, "resident expert cache: slab allocation failed"));
-      return false;
+      throw std::runtime_error(
+          osmh::err(context.osm(), rc, "resident expert cache: slab allocation failed"));
     }
     free_slots.clear();
     for (std::size_t s = slots; s-- > 0;) free_slots.push_back(static_cast<std::uint32_t>(s));
@@ -477,12 +502,8 @@ VulkanResidentExpert* VulkanResidentExpertCache::get(std::uint32_t layer, std::u
       return nullptr;
     }
     std::string local;
-    if (!m.ensure_slab(host_entries.front(), &local)) {
-      osmh::set(diagnostic, "resident expert cache: upload failed: " + local);
-      return nullptr;
-    }
     std::optional<VulkanResidentExpert> resident;
-    if (m.slab && !m.free_slots.empty()) {
+    if (m.use_slab(host_entries.front())) {
       const std::uint32_t slot = m.free_slots.back();
       resident = VulkanResidentExpert::create_in_slab(m.context, m.reader, host_entries.front(),
                                                       m.slab, slot, &local);

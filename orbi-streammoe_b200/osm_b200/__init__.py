@@ -113,6 +113,17 @@ class Context:
         self.check(lib().osm_q4_gemv(self.h, _ptr(packed), _ptr(scales_bf16), _ptr(biases_bf16),
                                      out_dim, in_dim, group, _ptr(x), tokens, _ptr(y)), "q4_gemv")
 
+    def q4_dequant_f32(self, packed, scales, biases, rows, in_dim, out, group=64):
+        """q4_dequant with fp32 scale and bias."""
+        self.check(lib().osm_q4_dequant_f32(self.h, _ptr(packed), _ptr(scales), _ptr(biases),
+                                            rows, in_dim, group, _ptr(out)), "q4_dequant_f32")
+
+    def q4_gemv_f32(self, packed, scales, biases, out_dim, in_dim, x, tokens, y, group=64):
+        """q4_gemv with fp32 scale and bias."""
+        self.check(lib().osm_q4_gemv_f32(self.h, _ptr(packed), _ptr(scales), _ptr(biases),
+                                         out_dim, in_dim, group, _ptr(x), tokens, _ptr(y)),
+                   "q4_gemv_f32")
+
     def swiglu(self, gate, up, out):
         self.check(lib().osm_swiglu(self.h, _ptr(gate), _ptr(up), _ptr(out), gate.numel()), "swiglu")
 

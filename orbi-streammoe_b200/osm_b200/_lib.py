@@ -89,6 +89,8 @@ _SIGS = {
     "osm_host_free_pinned": (C.c_int, [_P]),
     "osm_q4_dequant": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P]),
     "osm_q4_gemv": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P]),
+    "osm_q4_dequant_f32": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P]),
+    "osm_q4_gemv_f32": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P]),
     "osm_swiglu": (C.c_int, [_P, _P, _P, _P, C.c_size_t]),
     "osm_weighted_accumulate": (C.c_int, [_P, _P, C.c_float, _P, C.c_size_t]),
     "osm_rms_norm": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _P, C.c_float, C.c_uint32]),

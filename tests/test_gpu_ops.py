@@ -215,3 +215,25 @@ def test_gpu_generator_matches_cpu_quantiser(torch, ctx, port):
         cpu = port.gen_expert_slot(5, 40 + 3 * i, 0.02, H, I)
         mismatch = np.count_nonzero(host != cpu)
         assert mismatch <= 8, mismatch  # double-precision log/cos may differ in the last place
+
+
+@pytest.mark.parametrize("rows,cols,group", [(64, 128, 64), (8, 8, 4), (33, 96, 32)])
+def test_q4_fp32_metadata(torch, ctx, port, rows, cols, group):
+    """fp32 scale and bias that bf16 cannot hold (the reference's own device
+    format): dequant bit-exact with the oracle, GEMV within the bounds above."""
+    vals = port.gen_normal(rows + 5 * cols, 1, 0.02, rows * cols)
+    pk, sc, bi = port.quantize_q4(vals, rows, cols, group)  # fp32, not bf16-rounded
+    assert not np.array_equal(sc, pyoracle.bf16_widen(port.bf16_round(sc)).reshape(sc.shape))
+    W = port.dequantize_affine_rows(pk, rows, cols // 8, sc, bi, 4, group)
+    pkd, scd, bid = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (pk, sc, bi))
+    out = torch.empty(rows, cols, device="cuda")
+    ctx.q4_dequant_f32(pkd, scd, bid, rows, cols, out, group=group)
+    x = port.gen_normal(8, rows, 1.0, 2 * cols).reshape(2, cols)
+    y = torch.empty(2, rows, device="cuda")
+    ctx.q4_gemv_f32(pkd, scd, bid, rows, cols, torch.from_numpy(x).cuda(), 2, y, group=group)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), W.view(np.uint32))
+    got = y.cpu().numpy()
+    for t in range(2):
+        ref = port.matvec(W, x[t])
+        assert normwise_rel(got[t], ref) <= 1e-4
