@@ -1045,6 +1045,33 @@ def run_single(B: int, reps: int, prefill: bool = False):
     print(json.dumps({"single": B, "reps": reps, "status": list(ctx.status())}))
 
 
+SUB_KEYS = ("value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scaling", "dtype",
+            "e2e", "gpu_launches", "roofline", "clocks")
+
+
+def sub_workloads(args, rank, world, local_rank):
+    """configs[2] (4096-token prefill) and configs[3] (Qwen3-30B-A3B shape)
+    timed in the same run as the headline sweep, each with its own steps,
+    timing rules and roofline; under torchrun both run expert parallel over
+    the ranks (strong scaling), as the configs ask."""
+    import copy
+
+    sub = copy.copy(args)
+    sub.steps = max(3, min(args.steps, 20))
+    sub.warmup = 3
+    out = {}
+    for key, fn in (("configs[2]", run_prefill), ("configs[3]", run_q30)):
+        line = fn(sub, rank, world, local_rank)
+        d = {k: line[k] for k in SUB_KEYS if k in line}
+        d["workload"] = line["config"]["workload"]
+        d["parallelism"] = line["config"]["parallelism"]
+        for extra in ("per_case", "kernels", "kernels_8192"):
+            if extra in line["config"]:
+                d[extra] = line["config"][extra]
+        out[key] = d
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1067,6 +1094,9 @@ def main():
     ap.add_argument("--ep", action="store_true",
                     help="prefill and q30 workloads: the expert-parallel path even on one rank "
                          "(a one-rank NCCL group); under torchrun with N > 1 it is always used")
+    ap.add_argument("--no-sub", dest="sub", action="store_false",
+                    help="decode workload: skip the configs[2] and configs[3] sub-runs whose "
+                         "results the line carries under 'workloads'")
     ap.add_argument("--stream-layers", type=int, default=48,
                     help="with --workload stream: layers in the stack")
     args = ap.parse_args()
@@ -1105,6 +1135,8 @@ def main():
             line = run_q30(args, rank, world, local_rank)
         else:
             line = run_ours(args, rank, world, local_rank)
+            if args.sub:
+                line["workloads"] = sub_workloads(args, rank, world, local_rank)
     finally:
         if use_group:
             import torch

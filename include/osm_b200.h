@@ -52,6 +52,11 @@ extern "C" {
                                      [tokens][hidden] (layers without a shared expert) */
 #define OSM_OUTPUT_F16 0x20u      /* osm_moe_experts with OSM_PREFILL_BF16: out_dev receives fp16
                                      rows [tokens][hidden] (each fp32 sum rounded once) */
+#define OSM_PREFILL_NO_CHECK 0x40u /* osm_moe_forward with OSM_PREFILL_BF16: skip the range check.
+                                     By default (and never inside stream capture) the call ends
+                                     with a stream synchronisation that reads its status; when a
+                                     value left the fp16 range it runs again on the fp32 path
+                                     (status bit 6 then reports it) */
 
 typedef struct osm_context osm_context;
 typedef struct osm_layer osm_layer;
@@ -97,10 +102,20 @@ int osm_context_synchronize(osm_context* ctx);
  * non-finite router input, bit 1 invalid softmax/mass, bit 2 non-resident
  * expert, bit 3 bad slot, bit 4 a bounded wait on an asynchronous weight
  * copy gave up, bit 5 an activation left the fp16 range on the
- * OSM_PREFILL_BF16 path, whose outputs are then invalid); the count of tokens
+ * OSM_PREFILL_BF16 path, whose outputs are then invalid, bit 6 a checked
+ * OSM_PREFILL_BF16 call found bit 5 and re-ran on the fp32 path, whose
+ * outputs stand); the count of tokens
  * routed on the exact path. */
 int osm_context_status(osm_context* ctx, uint32_t* status,
                        uint64_t* exact_tokens);
+
+/* Test hook (no counterpart in the reference): the number of polls of the
+ * first bounded wait a kernel makes on an asynchronous weight copy, on
+ * `device`, for every later launch in this process.  When that wait gives up
+ * the kernel sets status bit 4 and waits again with the full bound, so the
+ * results stand; 0 makes every first wait give up at once, UINT32_MAX
+ * restores the default. */
+int osm_test_set_copy_wait_polls(int device, uint32_t polls);
 
 /* ---- buffers: replaces VulkanFloatBuffer
  *      (include/orbi/streammoe/backend/vulkan_float_buffer.hpp:23-58) ---- */

@@ -63,6 +63,7 @@ struct Scratch {
   float* partial = nullptr;
   float* normalized = nullptr;
   uint32_t* status = nullptr;
+  uint32_t* range_status = nullptr;  // status of one checked prefill call
   unsigned long long* exact_count = nullptr;
   const uint8_t** pick_ptr = nullptr;
 };
@@ -112,6 +113,7 @@ struct osm_context {
   uint32_t* picks_dev = nullptr;    // the same memory as the kernels address it
   size_t picks_cap = 0;
   cudaEvent_t picks_ev = nullptr;
+  uint32_t pending_status = 0;      // status bits read by checked calls, reported next
   bool tc_enabled = true;           // tensor-core expert kernels (OSM_DISABLE_TC=1: off)
   bool tc_decode = false;           // also for fp32 calls of 3+ tokens (OSM_TC_DECODE=1)
 };
@@ -857,6 +859,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
     return OSM_ENOMEM;
   }
   ctx->sc.status = static_cast<uint32_t*>(ctx->status_blk);
+  ctx->sc.range_status = static_cast<uint32_t*>(ctx->status_blk) + 1;
   ctx->sc.exact_count = reinterpret_cast<unsigned long long*>(static_cast<char*>(ctx->status_blk) + 8);
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) {
@@ -992,8 +995,22 @@ int osm_context_status(osm_context* ctx, uint32_t* status, uint64_t* exact_token
   OSM_CUDA(ctx, cudaMemcpy(&ex, ctx->sc.exact_count, 8, cudaMemcpyDeviceToHost));
   OSM_CUDA(ctx, cudaMemset(ctx->sc.status, 0, 4));
   OSM_CUDA(ctx, cudaMemset(ctx->sc.exact_count, 0, 8));
+  st |= ctx->pending_status;
+  ctx->pending_status = 0;
   if (status) *status = st;
   if (exact_tokens) *exact_tokens = ex;
+  return OSM_OK;
+}
+
+int osm_test_set_copy_wait_polls(int device, uint32_t polls) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return OSM_EINVAL;
+  DeviceGuard dg(device);
+  const uint32_t v = polls == UINT32_MAX ? osm::kCopyPolls : polls;
+  if (osm::set_first_wait_polls_gemv(v) != cudaSuccess ||
+      osm::set_first_wait_polls_prefill(v) != cudaSuccess ||
+      osm::set_first_wait_polls_router(v) != cudaSuccess)
+    return OSM_ECUDA;
   return OSM_OK;
 }
 
@@ -1471,15 +1488,39 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
     osm::PfArgs pa;
     size_t psm = 0;
     if (!prefill_path(L, &pa, &psm)) return fail(ctx, OSM_EINVAL, "prefill: layer shapes not supported");
+    // Checked (the default outside stream capture): this call's status bits
+    // go to a word of their own, read back when the call ends; if a value
+    // left the fp16 range the call runs again on the fp32 path.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    OSM_CUDA(ctx, cudaStreamIsCapturing(ctx->stream, &cap));
+    const bool checked = !(flags & OSM_PREFILL_NO_CHECK) && cap == cudaStreamCaptureStatusNone;
+    Scratch& sc = ctx->sc;
+    uint32_t* const main_status = sc.status;
+    if (checked) {
+      OSM_CUDA(ctx, cudaMemsetAsync(sc.range_status, 0, 4, ctx->stream));
+      sc.status = sc.range_status;
+    }
+    a.status = sc.status;
     a.do_group = 1;
     a.xfrag = nullptr;
-    a.xbf = ctx->sc.xbf;
+    a.xbf = sc.xbf;
     a.chunk_pairs = chunk_pairs_for(L, T, true);
     ctx->cur_x = x;
     launch_router_pair(ctx, a);
     rc = check_launch(ctx, "router");
-    if (rc) return rc;
-    return run_prefill(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr, pa, psm);
+    if (!rc) rc = run_prefill(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr, pa, psm);
+    sc.status = main_status;
+    if (rc || !checked) return rc;
+    uint32_t st = 0;
+    OSM_CUDA(ctx, cudaMemcpyAsync(&st, sc.range_status, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    OSM_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+    if (!(st & osm::kStatusF16Range)) {
+      ctx->pending_status |= st;
+      return OSM_OK;
+    }
+    ctx->pending_status |= (st & ~osm::kStatusF16Range) | osm::kStatusPrefillFallback;
+    flags &= ~(OSM_PREFILL_BF16 | OSM_PREFILL_NO_CHECK);
+    return osm_moe_forward(L, x, T, out, ids, w, mass, sgate, residual, flags);
   }
   // one token: the expert kernels read the picks directly (no grouping, no
   // tensor-core fragments)

@@ -19,6 +19,7 @@ constexpr uint32_t kStatusNotResident = 1u << 2;
 constexpr uint32_t kStatusBadSlot = 1u << 3;
 constexpr uint32_t kStatusCopyTimeout = 1u << 4;  // a bounded wait on an async copy gave up
 constexpr uint32_t kStatusF16Range = 1u << 5;     // prefill: a value left the fp16 range
+constexpr uint32_t kStatusPrefillFallback = 1u << 6;  // host: a checked prefill call re-ran in fp32
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);
@@ -173,6 +174,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   for (uint32_t i = 0; i < kCopyPolls; ++i)
     if (mbar_test(bar, parity)) return true;
   return false;
+}
+
+// The first bounded wait of a consumer on a copy polls g_first_polls times
+// (kCopyPolls unless lowered through osm_test_set_copy_wait_polls); when it
+// gives up the caller records kStatusCopyTimeout and waits again with the
+// full bound (mbar_wait), so the copies have landed before the data is read
+// or the block exits.  One variable per translation unit, set by
+// set_first_wait_polls() of that unit.
+static __device__ uint32_t g_first_polls = kCopyPolls;
+__device__ __forceinline__ bool mbar_wait_first(uint64_t* bar, uint32_t parity) {
+  const uint32_t n = *reinterpret_cast<volatile uint32_t*>(&g_first_polls);
+  for (uint32_t i = 0; i < n; ++i)
+    if (mbar_test(bar, parity)) return true;
+  return false;
+}
+static inline cudaError_t set_first_wait_polls(uint32_t n) {
+  return cudaMemcpyToSymbol(g_first_polls, &n, sizeof(n));
 }
 
 // Monotone map of finite floats (and -inf) to unsigned keys.

@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
   for (int item = warp; item < ntile * ks; item += kDecWarps) {
     const int tl = item / ks, q = item - tl * ks;
     const int g0 = q * gpc, g1 = min(G, g0 + gpc);
-    if (!mbar_wait(&bars[tl], 0)) {
+    if (!mbar_wait_first(&bars[tl], 0)) {
       if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
       mbar_wait(&bars[tl], 0);  // the copies may still land: wait once more
     }
@@ -655,7 +655,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_down_kernel(GemvArgs a)
     const int jj = item / ksd, half = item - jj * ksd;
     const DecMeta m = meta[jj];
     if (m.ptr == nullptr) continue;
-    if (!mbar_wait(&bars[jj], 0)) {
+    if (!mbar_wait_first(&bars[jj], 0)) {
       if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
       mbar_wait(&bars[jj], 0);  // the copies may still land: wait once more
     }
@@ -1053,7 +1053,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_gateup_kernel(GrpArgs a) {
   for (;; ++n) {
     const int s = (int)(n % Ly.nst);
     bool bad = false;
-    if (!mbar_wait(&full[s], (n / Ly.nst) & 1)) {
+    if (!mbar_wait_first(&full[s], (n / Ly.nst) & 1)) {
       if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
       bad = !mbar_wait(&full[s], (n / Ly.nst) & 1);
     }
@@ -1188,7 +1188,7 @@ __global__ void __launch_bounds__(kGrpThreads, 1) grp_down_kernel(GrpArgs a) {
   for (;; ++n) {
     const int s = (int)(n % Ly.nst);
     bool bad = false;
-    if (!mbar_wait(&full[s], (n / Ly.nst) & 1)) {
+    if (!mbar_wait_first(&full[s], (n / Ly.nst) & 1)) {
       if (lane == 0) atomicOr(a.status, kStatusCopyTimeout);
       bad = !mbar_wait(&full[s], (n / Ly.nst) & 1);
     }
@@ -1450,3 +1450,7 @@ extern "C" int osm_dbg_cycles_gemv(long long* out) {
   return (int)cudaMemcpyFromSymbol(out, osm::g_cyc, 64 * sizeof(long long));
 }
 #endif
+
+namespace osm {
+cudaError_t set_first_wait_polls_gemv(uint32_t polls) { return set_first_wait_polls(polls); }
+}  // namespace osm

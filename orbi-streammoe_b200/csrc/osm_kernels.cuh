@@ -300,6 +300,11 @@ cudaError_t launch_tc_gateup(const TcArgs& a, const TcMaps& maps, bool precise, 
 cudaError_t launch_tc_down(const TcArgs& a, const TcMaps& maps, bool precise, int grid,
                            cudaStream_t s, uint64_t* launches);
 
+// Test hook: polls of the first bounded copy wait in each kernel file.
+cudaError_t set_first_wait_polls_gemv(uint32_t polls);
+cudaError_t set_first_wait_polls_prefill(uint32_t polls);
+cudaError_t set_first_wait_polls_router(uint32_t polls);
+
 void launch_rmsnorm(const float* in, float* out, int rows, int dim, const float* w,
                     float eps, bool exact, cudaStream_t s, uint64_t* launches);
 // sc/bi: bf16 bits, or fp32 when f32_meta

@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
         // stage (s - 2) and A buffer s & 1 were last read by the MMAs of step s - 2
         if (s >= 2) {
           const uint32_t ps = s - 2;
-          if (!mbar_wait(&bar_mma[ps % kPfStages], (ps / kPfStages) & 1)) {
+          if (!mbar_wait_first(&bar_mma[ps % kPfStages], (ps / kPfStages) & 1)) {
             if (t == 0) atomicOr(a.status, kStatusCopyTimeout);
             mbar_wait(&bar_mma[ps % kPfStages], (ps / kPfStages) & 1);
           }
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) pf_gemm_kernel(PfArgs a) {
       for (int r = 0; r < NARR; ++r) sc_cur[r] = sc_nxt[r];
     }
     // ---- epilogue: accumulators -> fp16 rows ----
-    if (!mbar_wait(&bar_acc, nacc & 1)) {
+    if (!mbar_wait_first(&bar_acc, nacc & 1)) {
       if (t == 0) atomicOr(a.status, kStatusCopyTimeout);
       mbar_wait(&bar_acc, nacc & 1);
     }
@@ -537,4 +537,8 @@ void launch_combine_bf16(const uint16_t* pb, const int* tp_pos, const float* wei
   if (launches) *launches += 1;
 }
 
+}  // namespace osm
+
+namespace osm {
+cudaError_t set_first_wait_polls_prefill(uint32_t polls) { return set_first_wait_polls(polls); }
 }  // namespace osm

@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
   for (int j = 0; j < nht; ++j) {
     const int s = j % STG;
     const uint32_t par = (uint32_t)(j / STG) & 1u;
-    if (!mbar_wait(&full[s], par)) {
+    if (!mbar_wait_first(&full[s], par)) {
       if (tid == 0) atomicOr(a.status, kStatusCopyTimeout);
       mbar_wait(&full[s], par);  // the copy may still land: wait once more
     }
@@ -1304,3 +1304,7 @@ extern "C" int osm_dbg_timeline_router(unsigned long long* out) {
   return (int)cudaMemcpyToSymbol(osm::g_tl, init, sizeof(init));
 }
 #endif
+
+namespace osm {
+cudaError_t set_first_wait_polls_router(uint32_t polls) { return set_first_wait_polls(polls); }
+}  // namespace osm

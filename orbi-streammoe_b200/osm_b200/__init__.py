@@ -253,11 +253,15 @@ class Layer:
                                            _ptr(mass), OSM_ROUTE_EXACT if exact else 0), "route")
 
     def run_qwen_sparse_moe(self, x, tokens, out, ids=None, weights=None, mass=None,
-                            shared_gate=None, residual=None, exact_route=False, prefill=False):
-        """prefill=True: experts as the bf16 tcgen05 grouped GEMM (outputs within
-        bf16 rounding of the fp32 path; for prefill-sized batches)."""
+                            shared_gate=None, residual=None, exact_route=False, prefill=False,
+                            check_range=True):
+        """prefill=True: experts as the 16-bit tcgen05 grouped GEMM (outputs
+        within 2e-3 of the fp32 path; for prefill-sized batches).  With
+        check_range (the default) the call synchronises at its end and re-runs
+        on the fp32 path when a value left the fp16 range (status bit 6)."""
         flags = ((OSM_ROUTE_EXACT if exact_route else 0) | (OSM_ADD_RESIDUAL if residual is not None else 0)
-                 | (OSM_PREFILL_BF16 if prefill else 0))
+                 | (OSM_PREFILL_BF16 if prefill else 0)
+                 | (0 if check_range else _lib.OSM_PREFILL_NO_CHECK))
         self.ctx.check(lib().osm_moe_forward(self.h, _ptr(x), tokens, _ptr(out), _ptr(ids),
                                              _ptr(weights), _ptr(mass), _ptr(shared_gate),
                                              _ptr(residual), flags), "moe_forward")

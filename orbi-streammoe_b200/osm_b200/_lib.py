@@ -24,6 +24,7 @@ OSM_ADD_RESIDUAL = 0x4
 OSM_PREFILL_BF16 = 0x8
 OSM_INPUT_F16 = 0x10
 OSM_OUTPUT_F16 = 0x20
+OSM_PREFILL_NO_CHECK = 0x40
 OSM_PLAN_SUBLAYER = 0x100
 OSM_PLAN_PROFILE = 0x200
 
@@ -89,6 +90,7 @@ _SIGS = {
     "osm_host_free_pinned": (C.c_int, [_P]),
     "osm_q4_dequant": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P]),
     "osm_q4_gemv": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P]),
+    "osm_test_set_copy_wait_polls": (C.c_int, [C.c_int, C.c_uint32]),
     "osm_q4_dequant_f32": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P]),
     "osm_q4_gemv_f32": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P]),
     "osm_swiglu": (C.c_int, [_P, _P, _P, _P, C.c_size_t]),

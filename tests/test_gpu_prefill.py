@@ -100,3 +100,29 @@ def test_prefill_experts_write_fp16_rows(torch):
     torch.cuda.synchronize()
     assert torch.equal(o32.half(), o16)
     assert f.ctx.status()[0] == 0
+
+
+def test_prefill_out_of_fp16_range_falls_back_to_fp32(torch):
+    """Activations beyond the fp16 range (x scaled by 1e5): the checked
+    prefill call (the default) re-runs on the fp32 path -- its output is that
+    path's, bit for bit, and the status word reports bit 6, not bit 5; with
+    the check off the call reports bit 5 (outputs invalid)."""
+    H, E, I, K, T = 256, 12, 256, 3, 150
+    f = MoeFixture(torch, H, E, I, K, seed=95, max_tokens=T)
+    x = torch.from_numpy(f.port.gen_normal(95, 2, 1.0, T * H).reshape(T, H) * 1e5).cuda()
+    f.ctx.status()
+    ref = torch.empty(T, H, device="cuda")
+    f.layer.run_qwen_sparse_moe(x, T, ref)
+    assert f.ctx.status()[0] == 0
+    out = torch.empty(T, H, device="cuda")
+    f.layer.run_qwen_sparse_moe(x, T, out, prefill=True)
+    st = f.ctx.status()[0]
+    assert st == 1 << 6, st
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref.cpu().numpy().view(np.uint32))
+    f.layer.run_qwen_sparse_moe(x, T, out, prefill=True, check_range=False)
+    st = f.ctx.status()[0]
+    assert st & (1 << 5) and not st & (1 << 6), st
+    # in range, the checked call reports nothing and stays on the fp16 path
+    xs = x / 1e5
+    f.layer.run_qwen_sparse_moe(xs, T, out, prefill=True)
+    assert f.ctx.status()[0] == 0
