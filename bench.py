@@ -410,7 +410,9 @@ def run_prefill(args, rank, world, local_rank):
     # N > 1: expert parallelism over the ranks (E/N experts each) on the same
     # 4096 tokens, T/N routed per rank (strong scaling)
     t_local = PF_T // world
-    ctx = osm.Context(local_rank, max_tokens=t_local * (K * world + 1) if args.ep else PF_T)
+    if args.ep:
+        from osm_b200 import ep as osm_ep
+    ctx = osm.Context(local_rank, max_tokens=osm_ep.context_rows(world, t_local, K) if args.ep else PF_T)
     ctx.set_stream(stream.cuda_stream)
     x_all = torch.empty(PF_T, H, device=dev)
     ctx.gen_normal(SEED, 7000, 1.0, x_all)
@@ -418,15 +420,14 @@ def run_prefill(args, rank, world, local_rank):
     del x_all
     out = torch.empty(t_local, H, device=dev)
     if args.ep:
-        from osm_b200 import ep as osm_ep
-
         e_count = E // world
         e0 = rank * e_count
         lay = osm.expert_layout(H, I, GROUP)
         slab = osm.Slab(ctx, lay, e_count + 1)  # + the shared expert's slot
         slab.generate(SEED, 1000 + 3 * e0, 0.02, 0, e_count)
         W, sg, shared = replicated_weights(torch, ctx, osm)
-        moe = osm_ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg)
+        moe = osm_ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg,
+                                       tokens_per_rank=t_local)
     else:
         layer = build_sublayer(torch, ctx, osm, zipf=False)[0]
     hx = x.cpu().pin_memory()
@@ -495,6 +496,8 @@ def run_prefill(args, rank, world, local_rank):
     ctx.profile(False)
     clk = clocks.stop()
     status, exact_tokens = ctx.status()
+    if args.ep:
+        moe.close()
     if status:
         raise RuntimeError(f"device status {status} during the prefill benchmark")
     total_ms = max_over_ranks(total_ms)
@@ -526,7 +529,8 @@ def run_prefill(args, rank, world, local_rank):
                    "tokens_per_step": PF_T, "hidden": H, "experts": E, "top_k": K,
                    "moe_inter": I, "shared_inter": SHI,
                    "parallelism": (f"expert parallel x{world} ({E // world} experts and "
-                                   f"{t_local} tokens per rank, NCCL all-to-all dispatch/combine)"
+                                   f"{t_local} tokens per rank, dispatch/combine by stores into "
+                                   "peer memory over NVLink, device-side barriers)"
                                    if args.ep else "single GPU"),
                    "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
                    "timing": "sum of per-call CUDA-event intervals on the launching stream",
@@ -552,7 +556,7 @@ Q30_T = (1, 64, 8192)
 def run_q30_ep(args, rank, world, local_rank):
     """configs[3] 8192-token case, expert parallel: rank r owns experts
     [r 128/N, (r+1) 128/N) and routes 8192/N of the tokens (strong scaling);
-    NCCL all-to-all dispatch and combine (osm_b200.ep)."""
+    dispatch and combine by stores into peer memory (osm_b200.ep)."""
     import torch
 
     import osm_b200 as osm
@@ -565,8 +569,8 @@ def run_q30_ep(args, rank, world, local_rank):
     T = Q30_T[-1]
     t_local, e_count = T // world, Q30_E // world
     e0 = rank * e_count
-    # rows a rank can receive: every pick of every token
-    ctx = osm.Context(local_rank, max_tokens=T * Q30_K)
+    # rows an owner runs its experts over: a receive region per rank
+    ctx = osm.Context(local_rank, max_tokens=osm_ep.context_rows(world, t_local, Q30_K))
     ctx.set_stream(stream.cuda_stream)
     lay = osm.expert_layout(Q30_H, Q30_I, GROUP)
     slab = osm.Slab(ctx, lay, e_count)
@@ -574,7 +578,8 @@ def run_q30_ep(args, rank, world, local_rank):
     buf = torch.empty(Q30_E * Q30_H, device=dev)
     ctx.gen_normal(SEED + 3, 1, 0.02, buf)
     W = bf16_round(buf.cpu().numpy()).reshape(Q30_E, Q30_H)
-    moe = osm_ep.ExpertParallelMoE(ctx, W, Q30_K, True, lay, slab, e0, e_count)
+    moe = osm_ep.ExpertParallelMoE(ctx, W, Q30_K, True, lay, slab, e0, e_count,
+                                   tokens_per_rank=t_local)
     x_all = torch.empty(T, Q30_H, device=dev)
     ctx.gen_normal(SEED + 3, 9000 + T, 1.0, x_all)
     x = x_all[rank * t_local:(rank + 1) * t_local].contiguous()
@@ -637,6 +642,7 @@ def run_q30_ep(args, rank, world, local_rank):
     ctx.profile(False)
     clk = clocks.stop()
     status, exact_tokens = ctx.status()
+    moe.close()
     if status:
         raise RuntimeError(f"device status {status} during the q30 expert-parallel benchmark")
     total_ms = max_over_ranks(total_ms)
@@ -658,7 +664,8 @@ def run_q30_ep(args, rank, world, local_rank):
                                "case, expert parallel",
                    "tokens_per_step": T,
                    "parallelism": (f"expert parallel x{world} ({e_count} experts and {t_local} "
-                                   "tokens per rank, NCCL all-to-all dispatch/combine)"),
+                                   "tokens per rank, dispatch/combine by stores into peer "
+                                   "memory over NVLink, device-side barriers)"),
                    "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
                    "timing": "sum of per-call CUDA-event intervals on the launching stream, max "
                              "over ranks",

@@ -61,6 +61,9 @@ extern "C" {
 typedef struct osm_context osm_context;
 typedef struct osm_layer osm_layer;
 typedef struct osm_slab osm_slab;
+typedef struct osm_ep osm_ep;
+
+#define OSM_IPC_HANDLE_BYTES 64
 
 /* Byte offsets of the nine qpack sections inside one expert slot
  * (gate_proj/up_proj/down_proj . weight/scales/biases; the section table of
@@ -104,7 +107,8 @@ int osm_context_synchronize(osm_context* ctx);
  * copy gave up, bit 5 an activation left the fp16 range on the
  * OSM_PREFILL_BF16 path, whose outputs are then invalid, bit 6 a checked
  * OSM_PREFILL_BF16 call found bit 5 and re-ran on the fp32 path, whose
- * outputs stand); the count of tokens
+ * outputs stand, bit 7 an expert-parallel barrier gave up waiting for a
+ * rank, whose outputs are then invalid); the count of tokens
  * routed on the exact path. */
 int osm_context_status(osm_context* ctx, uint32_t* status,
                        uint64_t* exact_tokens);
@@ -208,6 +212,40 @@ int osm_expert_forward_noalloc(const void* slot_dev,
                                const osm_expert_layout* layout,
                                const float* x_dev, uint32_t tokens,
                                float* out_dev, void* cuda_stream);
+
+/* ---- expert parallelism over NVLink peer memory (configs 2 and 3 across
+ *      the GPUs of one box; no counterpart in the reference, whose sublayer
+ *      runs on one device).  Rank r of W owns experts [r E/W, (r+1) E/W).
+ *      Each rank allocates one EP block (receive regions, back rows,
+ *      barrier flags), exports it with osm_ep_ipc_handle, and maps every
+ *      other rank's block with osm_ep_open_peers (the handles gathered on the
+ *      host, e.g. by torch.distributed.all_gather_object).  osm_ep_forward is
+ *      then one call per step with no host synchronisation: route (ids exact
+ *      as on one GPU), store each pick's fp16 row into its owner's block,
+ *      barrier, run the owned experts (and this rank's shared-expert rows) on
+ *      the tensor-core prefill path, store each weighted fp16 result into the
+ *      source's back rows, barrier, sum each token's rows in pick order and
+ *      its shared row (fp32).  Every rank must call it the same number of
+ *      times.  A barrier waits at most the block's timeout (default 2 s,
+ *      osm_ep_set_timeout) and then sets status bit 7.  Destroy the blocks
+ *      only after every rank has finished using them (a host barrier). ---- */
+int osm_ep_create(osm_context* ctx, uint32_t world, uint32_t rank,
+                  uint32_t tokens_per_rank, uint32_t k, uint32_t hidden,
+                  uint32_t experts_per_rank, int has_shared, osm_ep** out);
+int osm_ep_ipc_handle(const osm_ep* ep, unsigned char* handle /* OSM_IPC_HANDLE_BYTES */);
+/* handles: world x OSM_IPC_HANDLE_BYTES, rank order (this rank's is ignored) */
+int osm_ep_open_peers(osm_ep* ep, const unsigned char* handles);
+int osm_ep_set_timeout(osm_ep* ep, uint32_t timeout_ms);
+int osm_ep_destroy(osm_ep* ep);
+/* router: the full router (E = experts_per_rank * world, top-k; with
+ * has_shared it holds the shared expert, whose gate it computes).  experts:
+ * k = 1 over this rank's experts in slots 0..experts_per_rank-1 and, with
+ * has_shared, the shared expert as local id experts_per_rank.  x_dev/out_dev
+ * [tokens][hidden] fp32 (tokens <= tokens_per_rank); ids/weights outputs may
+ * be NULL.  Flags: OSM_ROUTE_EXACT. */
+int osm_ep_forward(osm_ep* ep, osm_layer* router, osm_layer* experts,
+                   const float* x_dev, uint32_t tokens, float* out_dev,
+                   uint32_t* ids_dev, float* weights_dev, uint32_t flags);
 
 /* ---- expert slab: the HBM side of VulkanResidentExpertCache
  *      (include/orbi/streammoe/backend/vulkan_resident_expert_cache.hpp:

@@ -114,6 +114,7 @@ struct osm_context {
   size_t picks_cap = 0;
   cudaEvent_t picks_ev = nullptr;
   uint32_t pending_status = 0;      // status bits read by checked calls, reported next
+  uint64_t pairs_hint = 0;          // expected real pairs of a call with empty slots (0: T * k)
   bool tc_enabled = true;           // tensor-core expert kernels (OSM_DISABLE_TC=1: off)
   bool tc_decode = false;           // also for fp32 calls of 3+ tokens (OSM_TC_DECODE=1)
 };
@@ -130,6 +131,18 @@ struct osm_slab {
   // (the tensor-core expert kernels); tc_ok false: the layout does not suit them
   alignas(64) unsigned char tc_maps[3][128];
   bool tc_ok = false;
+};
+
+// One rank's expert-parallel block and the peers' blocks as mapped here.
+struct osm_ep {
+  osm_context* ctx = nullptr;
+  osm::EpLayout lay{};
+  unsigned char* own = nullptr;
+  unsigned char* peer[osm::kEpMaxWorld] = {};
+  bool opened = false;
+  float* sgate = nullptr;  // [T_r] shared-expert gates of this rank's tokens
+  uint32_t epoch = 0;
+  uint64_t timeout_ns = 2000000000ull;
 };
 
 // Expert residency over one slab: LFU + recency entries keyed (layer, expert).
@@ -513,7 +526,8 @@ bool tc_path(osm_layer* L, osm::TcArgs* ta, osm::TcMaps* maps) {
 bool tc_use(osm_layer* L, uint32_t T, bool prefill, osm::TcArgs* ta, osm::TcMaps* maps) {
   osm_context* ctx = L->ctx;
   if (prefill) {
-    if ((uint64_t)T * (uint64_t)L->g.k > 128ull * (uint64_t)L->g.E) return false;
+    const uint64_t pairs = ctx->pairs_hint ? ctx->pairs_hint : (uint64_t)T * (uint64_t)L->g.k;
+    if (pairs > 128ull * (uint64_t)L->g.E) return false;
   } else if (!ctx->tc_decode) {
     return false;
   }
@@ -533,7 +547,8 @@ int chunk_pairs_for(osm_layer* L, uint32_t T, bool prefill) {
 
 // Runs the tensor-core gate/up and down kernels, then the combine.
 int run_tc(osm_layer* L, uint32_t T, float* out, const float* residual, osm::TcArgs ta,
-           const osm::TcMaps& maps, bool precise, const uint16_t* xb, bool f16_out) {
+           const osm::TcMaps& maps, bool precise, const uint16_t* xb, bool f16_out,
+           bool combine = true) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
   ta.x = ctx->cur_x;
@@ -558,6 +573,7 @@ int run_tc(osm_layer* L, uint32_t T, float* out, const float* residual, osm::TcA
     const cudaError_t e = osm::launch_tc_down(ta, maps, precise, ctx->num_sms, ctx->stream, &ctx->launches);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "tensor-core down");
   }
+  if (!combine) return OSM_OK;  // the caller reads the pair rows (expert parallelism)
   if (precise) {
     osm::CombineArgs c{};
     c.partial = s.partial;
@@ -756,7 +772,7 @@ bool prefill_path(osm_layer* L, osm::PfArgs* pa, size_t* smem) {
 }
 
 int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm::PfArgs pa,
-                size_t smem, bool x_given = false, bool f16_out = false) {
+                size_t smem, bool x_given = false, bool f16_out = false, bool combine = true) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
   if ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(residual)) & 15)
@@ -765,7 +781,8 @@ int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm
     osm::TcArgs ta;
     osm::TcMaps maps;
     if (tc_use(L, T, true, &ta, &maps))
-      return run_tc(L, T, out, residual, ta, maps, false, x_given ? pa.xb : s.xbf, f16_out);
+      return run_tc(L, T, out, residual, ta, maps, false, x_given ? pa.xb : s.xbf, f16_out,
+                    combine);
   }
   if (!x_given) pa.xb = s.xbf;
   pa.hb = reinterpret_cast<uint16_t*>(s.hfrag);
@@ -786,7 +803,7 @@ int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm
     osm::launch_prefill_down(pa, ctx->num_sms, smem, ctx->stream, &ctx->launches);
   }
   rc = check_launch(ctx, "prefill down");
-  if (rc) return rc;
+  if (rc || !combine) return rc;
   {
     Prof p(ctx, kKCombine);
     osm::launch_combine_bf16(pa.pb, s.tp_pos, s.weights, L->shared_slot ? s.sgate : nullptr, residual,
@@ -1598,6 +1615,58 @@ int experts_impl(osm_layer* L, const float* x, uint32_t T, const uint32_t* ids, 
   return run_experts(L, T, out, (flags & OSM_ADD_RESIDUAL) ? residual : nullptr);
 }
 
+// The owner's experts over every slot of its EP block (fp16 rows, one pick
+// each, empty slots skipped by the grouping): gate/up and down on the
+// tensor-core prefill path, leaving each pair's fp16 result row in the
+// context's pair rows for ep_return_kernel.
+int ep_experts(osm_ep* ep, osm_layer* X) {
+  osm_context* ctx = ep->ctx;
+  Scratch& s = ctx->sc;
+  const osm::EpLayout& Ly = ep->lay;
+  const uint32_t R = (uint32_t)((Ly.world + 1) * Ly.cap);
+  const size_t nk = R;
+  OSM_CUDA(ctx, cudaMemcpyAsync(s.ids, ep->own + Ly.o_ids, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  OSM_CUDA(ctx, cudaMemcpyAsync(s.weights, ep->own + Ly.o_wts, nk * 4, cudaMemcpyDeviceToDevice,
+                                ctx->stream));
+  const float* rows = reinterpret_cast<const float*>(ep->own + Ly.o_rows);
+  osm::RouterArgs a = router_args(X, rows, R);
+  a.skip_route = 1;
+  a.sgate_out = nullptr;
+  a.do_group = 1;
+  a.pick_ptr = nullptr;
+  osm::PfArgs pa;
+  size_t psm = 0;
+  if (!prefill_path(X, &pa, &psm)) return fail(ctx, OSM_EINVAL, "expert parallel: expert shapes not supported");
+  a.xfrag = nullptr;
+  a.xbf = s.xbf;
+  // the real pairs: this rank's share of every rank's picks, plus its own
+  // tokens' shared-expert rows
+  ctx->pairs_hint = (uint64_t)Ly.T_r * Ly.k + (Ly.shared ? Ly.T_r : 0);
+  a.chunk_pairs = chunk_pairs_for(X, R, true);
+  ctx->cur_x = rows;
+  {
+    Prof p(ctx, kKRouterSelect);
+    osm::launch_group(a, ctx->stream, &ctx->launches);
+  }
+  int rc = check_launch(ctx, "expert parallel grouping");
+  if (!rc) {
+    osm::PfArgs pf = pa;
+    pf.xb = reinterpret_cast<const uint16_t*>(rows);
+    rc = run_prefill(X, R, nullptr, nullptr, pf, psm, true, true, false);
+  }
+  ctx->pairs_hint = 0;
+  return rc;
+}
+
+osm::EpArgs ep_args(const osm_ep* ep) {
+  osm::EpArgs e{};
+  e.lay = ep->lay;
+  for (int i = 0; i < osm::kEpMaxWorld; ++i) e.peer[i] = ep->peer[i];
+  e.send_cnt = reinterpret_cast<int*>(ep->own + ep->lay.o_cnt);
+  e.status = ep->ctx->sc.status;
+  return e;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1695,6 +1764,167 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   if (rc) return rc;
   if (prefill) return run_prefill(L, T, out, res, pa, psm);
   return run_experts(L, T, out, res);
+}
+
+int osm_ep_create(osm_context* ctx, uint32_t world, uint32_t rank, uint32_t tokens_per_rank,
+                  uint32_t k, uint32_t hidden, uint32_t experts_per_rank, int has_shared,
+                  osm_ep** out) {
+  if (!ctx || !out) return OSM_EINVAL;
+  *out = nullptr;
+  if (world == 0 || world > (uint32_t)osm::kEpMaxWorld || rank >= world)
+    return fail(ctx, OSM_EINVAL, "expert parallel: 1 to 8 ranks, rank < world");
+  if (tokens_per_rank == 0 || k == 0 || experts_per_rank == 0)
+    return fail(ctx, OSM_EINVAL, "expert parallel: tokens, k and experts must be non-zero");
+  if (hidden == 0 || hidden % 256 || hidden > 8192)
+    return fail(ctx, OSM_EINVAL, "expert parallel: hidden must be a multiple of 256 up to 8192");
+  if ((uint64_t)(world + 1) * tokens_per_rank * k > (1u << 24))
+    return fail(ctx, OSM_EINVAL, "expert parallel: receive regions too large");
+  DeviceGuard dg(ctx->device);
+  auto* ep = new (std::nothrow) osm_ep();
+  if (!ep) return OSM_ENOMEM;
+  ep->ctx = ctx;
+  ep->lay = osm::ep_layout((int)world, (int)rank, (int)tokens_per_rank, (int)k, (int)hidden,
+                           (int)experts_per_rank, has_shared ? 1 : 0);
+  if (cudaMalloc(&ep->own, ep->lay.total) != cudaSuccess ||
+      cudaMalloc(&ep->sgate, (size_t)tokens_per_rank * 4) != cudaSuccess) {
+    if (ep->own) cudaFree(ep->own);
+    delete ep;
+    return fail(ctx, OSM_ENOMEM, "expert parallel: device allocation failed");
+  }
+  // back rows, flags and counters zero; every receive slot empty
+  cudaMemset(ep->own + ep->lay.o_back, 0, ep->lay.total - ep->lay.o_back);
+  cudaMemset(ep->sgate, 0, (size_t)tokens_per_rank * 4);
+  osm::launch_ep_clear_ids(ep->lay, ep->own, nullptr, nullptr);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(ep->own);
+    cudaFree(ep->sgate);
+    delete ep;
+    return fail(ctx, OSM_ECUDA, "expert parallel: block initialisation failed");
+  }
+  ep->peer[rank] = ep->own;
+  *out = ep;
+  return OSM_OK;
+}
+
+int osm_ep_ipc_handle(const osm_ep* ep, unsigned char* handle) {
+  if (!ep || !handle) return OSM_EINVAL;
+  DeviceGuard dg(ep->ctx->device);
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, ep->own) != cudaSuccess)
+    return fail(ep->ctx, OSM_ECUDA, "expert parallel: cudaIpcGetMemHandle failed");
+  static_assert(sizeof(h) == OSM_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return OSM_OK;
+}
+
+int osm_ep_open_peers(osm_ep* ep, const unsigned char* handles) {
+  if (!ep || !handles) return OSM_EINVAL;
+  if (ep->opened) return fail(ep->ctx, OSM_EINVAL, "expert parallel: peers already open");
+  DeviceGuard dg(ep->ctx->device);
+  for (int r = 0; r < ep->lay.world; ++r) {
+    if (r == ep->lay.rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handles + (size_t)r * OSM_IPC_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != ep->lay.rank && ep->peer[q]) {
+          cudaIpcCloseMemHandle(ep->peer[q]);
+          ep->peer[q] = nullptr;
+        }
+      return fail(ep->ctx, OSM_ECUDA, "expert parallel: cudaIpcOpenMemHandle failed");
+    }
+    ep->peer[r] = static_cast<unsigned char*>(p);
+  }
+  ep->opened = true;
+  return OSM_OK;
+}
+
+int osm_ep_set_timeout(osm_ep* ep, uint32_t timeout_ms) {
+  if (!ep || timeout_ms == 0) return OSM_EINVAL;
+  ep->timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+  return OSM_OK;
+}
+
+int osm_ep_destroy(osm_ep* ep) {
+  if (!ep) return OSM_EINVAL;
+  DeviceGuard dg(ep->ctx->device);
+  cudaStreamSynchronize(ep->ctx->stream);
+  for (int r = 0; r < ep->lay.world; ++r)
+    if (r != ep->lay.rank && ep->peer[r]) cudaIpcCloseMemHandle(ep->peer[r]);
+  cudaFree(ep->own);
+  cudaFree(ep->sgate);
+  delete ep;
+  return OSM_OK;
+}
+
+int osm_ep_forward(osm_ep* ep, osm_layer* router, osm_layer* experts, const float* x, uint32_t T,
+                   float* out, uint32_t* ids_out, float* weights_out, uint32_t flags) {
+  if (!ep || !router || !experts) return OSM_EINVAL;
+  osm_context* ctx = ep->ctx;
+  const osm::EpLayout& Ly = ep->lay;
+  if (router->ctx != ctx || experts->ctx != ctx)
+    return fail(ctx, OSM_EINVAL, "expert parallel: layers of another context");
+  if (!ep->opened && Ly.world > 1) return fail(ctx, OSM_EINVAL, "expert parallel: peers not open");
+  if (!x || !out || T == 0 || T > (uint32_t)Ly.T_r)
+    return fail(ctx, OSM_EINVAL, "expert parallel: null input/output or tokens > tokens_per_rank");
+  if (router->g.k != Ly.k || router->g.H != Ly.H || router->g.E != Ly.e_local * Ly.world)
+    return fail(ctx, OSM_EINVAL, "expert parallel: router geometry differs from the block's");
+  if (Ly.shared && !router->shared_slot)
+    return fail(ctx, OSM_EINVAL, "expert parallel: the router layer needs the shared expert's gate");
+  if (experts->g.k != 1 || experts->g.H != Ly.H || experts->g.E < Ly.e_local + Ly.shared ||
+      experts->shared_slot)
+    return fail(ctx, OSM_EINVAL, "expert parallel: experts layer must be k = 1 over the local experts");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(ctx, OSM_EINVAL, "expert parallel: x and out must be 16-byte aligned");
+  const uint32_t R = (uint32_t)((Ly.world + 1) * Ly.cap);
+  // scratch for both calls first, so that nothing moves within this one
+  int rc = layer_ready(experts, R, true);
+  if (!rc) rc = layer_ready(router, T, false);
+  if (rc) return rc;
+  DeviceGuard dg(ctx->device);
+  Scratch& s = ctx->sc;
+  // 1. route, with the shared gate
+  osm::RouterArgs a = router_args(router, x, T);
+  a.force_exact = (flags & OSM_ROUTE_EXACT) ? 1 : 0;
+  a.ids_out = ids_out;
+  a.weights_out = weights_out;
+  a.do_group = 0;
+  a.xfrag = nullptr;
+  a.xbf = nullptr;
+  a.pick_ptr = nullptr;
+  a.sgate_w = Ly.shared ? router->sgate_w : nullptr;
+  a.sgate_out = ep->sgate;
+  launch_router_pair(ctx, a);
+  rc = check_launch(ctx, "expert parallel router");
+  if (rc) return rc;
+  // 2. every pick's row into its owner's region, the shared rows locally
+  osm::EpArgs e = ep_args(ep);
+  e.x = x;
+  e.ids = s.ids;
+  e.w = s.weights;
+  e.sgate = ep->sgate;
+  e.T = (int)T;
+  OSM_CUDA(ctx, cudaMemsetAsync(e.send_cnt, 0, (size_t)Ly.world * 4, ctx->stream));
+  {
+    Prof p(ctx, kKOther);
+    osm::launch_ep_dispatch(e, ctx->num_sms, ctx->stream, &ctx->launches);
+    osm::launch_ep_barrier(e, ++ep->epoch, ep->timeout_ns, ctx->stream, &ctx->launches);
+  }
+  rc = check_launch(ctx, "expert parallel dispatch");
+  if (rc) return rc;
+  // 3. this rank's experts over every region
+  rc = ep_experts(ep, experts);
+  if (rc) return rc;
+  // 4. the weighted rows back to their sources, 5. the combine
+  {
+    Prof p(ctx, kKCombine);
+    osm::launch_ep_return(e, reinterpret_cast<const uint16_t*>(s.partial), s.tp_pos, ctx->stream,
+                          &ctx->launches);
+    osm::launch_ep_barrier(e, ++ep->epoch, ep->timeout_ns, ctx->stream, &ctx->launches);
+    osm::launch_ep_combine(e, out, ctx->stream, &ctx->launches);
+  }
+  return check_launch(ctx, "expert parallel combine");
 }
 
 int osm_gather_sum_rows(osm_context* ctx, const void* rows_f16, const int64_t* pos, uint32_t tokens,

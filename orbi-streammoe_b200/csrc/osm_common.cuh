@@ -20,6 +20,7 @@ constexpr uint32_t kStatusBadSlot = 1u << 3;
 constexpr uint32_t kStatusCopyTimeout = 1u << 4;  // a bounded wait on an async copy gave up
 constexpr uint32_t kStatusF16Range = 1u << 5;     // prefill: a value left the fp16 range
 constexpr uint32_t kStatusPrefillFallback = 1u << 6;  // host: a checked prefill call re-ran in fp32
+constexpr uint32_t kStatusPeerTimeout = 1u << 7;  // expert parallel: a rank did not reach a barrier
 
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
   return __uint_as_float(bits16 << 16);

@@ -300,6 +300,35 @@ cudaError_t launch_tc_gateup(const TcArgs& a, const TcMaps& maps, bool precise, 
 cudaError_t launch_tc_down(const TcArgs& a, const TcMaps& maps, bool precise, int grid,
                            cudaStream_t s, uint64_t* launches);
 
+// ---- expert parallelism over peer memory (osm_ep.cu) ----
+constexpr uint32_t kEpEmpty = 0xFFFFFFFFu;  // id of an empty receive slot
+constexpr int kEpMaxWorld = 8;
+
+// One rank's EP block; the same layout on every rank.  Offsets in bytes.
+struct EpLayout {
+  int world, rank, T_r, k, H, e_local, shared, cap;
+  size_t o_rows, o_ids, o_wts, o_src, o_back, o_flags, o_cnt, total;
+};
+struct EpArgs {
+  EpLayout lay;
+  unsigned char* peer[kEpMaxWorld];  // every rank's block as this GPU addresses it
+  const float* x;                    // [T][H] this rank's tokens
+  const uint32_t* ids;               // [T][k] global expert ids
+  const float* w;                    // [T][k] routing weights
+  const float* sgate;                // [T] shared-expert gate (when lay.shared)
+  int* send_cnt;                     // [world] slots claimed in each owner's region
+  uint32_t* status;
+  int T;
+};
+EpLayout ep_layout(int world, int rank, int T_r, int k, int H, int e_local, int shared);
+void launch_ep_clear_ids(const EpLayout& L, unsigned char* own, cudaStream_t s, uint64_t* launches);
+void launch_ep_dispatch(const EpArgs& a, int num_sms, cudaStream_t s, uint64_t* launches);
+void launch_ep_barrier(const EpArgs& a, uint32_t epoch, uint64_t timeout_ns, cudaStream_t s,
+                       uint64_t* launches);
+void launch_ep_return(const EpArgs& a, const uint16_t* pb, const int* tp_pos, cudaStream_t s,
+                      uint64_t* launches);
+void launch_ep_combine(const EpArgs& a, float* out, cudaStream_t s, uint64_t* launches);
+
 // Test hook: polls of the first bounded copy wait in each kernel file.
 cudaError_t set_first_wait_polls_gemv(uint32_t polls);
 cudaError_t set_first_wait_polls_prefill(uint32_t polls);

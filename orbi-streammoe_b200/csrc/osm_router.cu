@@ -520,7 +520,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
       if (p0 + u * (int)blockDim.x >= B * k) break;
       const uint32_t e = ev[u];
       if (e >= (uint32_t)E) {
-        atomicOr(a.status, kStatusBadSlot);
+        if (e != kEpEmpty) atomicOr(a.status, kStatusBadSlot);  // kEpEmpty: an empty slot
         continue;
       }
       if (atomicAdd(&cnt[e], 1) == 0) actidx[e] = atomicAdd(&s_nact, 1);

@@ -1,120 +1,81 @@
 """Expert parallelism for prefill-sized batches (configs 2 and 3): one process
 per GPU, rank r owning experts [r E/N, (r+1) E/N) in its slab.
 
-Each rank routes its own tokens with the replicated router (ids exact as the
-single-GPU path), then:
-  1. sorts its (token, pick) pairs by the rank that owns the picked expert;
-  2. exchanges pair counts, then the pairs' activation rows (fp16) with the
-     owner-local expert id and routing weight, in one all-to-all each;
-  3. runs the owned experts on the rows it received, together with its own
-     tokens routed to the shared expert when the layer has one (held in the
-     slab's spare last slot, weighted by its sigmoid gate): one tensor-core
-     prefill call on the fp16 rows, one pick per row, each row scaled by its
-     weight, fp16 rows out;
-  4. sends the weighted fp16 rows back with the reverse all-to-all;
-  5. adds each token's rows in pick order, then the shared expert (replicated,
-     computed locally for the rank's own tokens) scaled by its sigmoid gate --
-     the accumulation order of run_qwen_sparse_moe_vulkan_accum
-     (src/model/routed_moe.cpp:396-404).
+The exchange runs inside the library over NVLink peer memory, one call per
+step with no host synchronisation (osm_ep_forward): each rank routes its own
+tokens with the replicated router (ids exact as on one GPU; the shared
+expert's gate comes from the same select kernel), stores each pick's fp16 row
+straight into the owner's receive region, and after a device-side barrier the
+owner runs its experts -- and this rank's own tokens on the shared expert,
+held in the slab's spare last slot -- on the tensor-core prefill path, stores
+each result times its routing weight (fp16) into the source's back rows, and
+after a second barrier every rank sums its tokens' rows in pick order and then
+the shared row, in fp32: the accumulation order of
+run_qwen_sparse_moe_vulkan_accum (src/model/routed_moe.cpp:396-404).
 
-The exchange steps are plain functions of tensors and a process group, so the
-index arithmetic runs unchanged on gloo ranks on the CPU; ExpertParallelMoE
-binds them to the library's kernels on CUDA ranks (NCCL over NVLink)."""
+The host part is the one-time setup done here: every rank creates its EP
+block, exports it as a CUDA IPC handle, and the handles are gathered with the
+rank geometry through torch.distributed (any backend; the checks run on gloo
+ranks on the CPU), then every peer block is mapped."""
 from __future__ import annotations
+
+import ctypes as C
+import datetime
 
 import numpy as np
 import torch
 import torch.distributed as dist
 
-
-def dispatch_plan(ids: torch.Tensor, e_local: int, world: int):
-    """Send order of the flattened (token, pick) pairs grouped by owner rank
-    (stable: token-major, then pick, inside each destination), pairs per
-    destination, and each pair's expert id local to its owner."""
-    flat = ids.reshape(-1).long()
-    owner = flat // e_local
-    if flat.numel() and int(owner.max()) >= world:
-        raise ValueError("expert id beyond the last rank's range")
-    order = torch.sort(owner, stable=True).indices
-    counts = torch.bincount(owner, minlength=world)
-    return order, counts, (flat % e_local)
+IPC_HANDLE_BYTES = 64
+STATUS_PEER_TIMEOUT = 1 << 7
 
 
-def exchange_counts(send_counts: torch.Tensor, group=None) -> torch.Tensor:
-    recv = torch.empty_like(send_counts)
-    dist.all_to_all_single(recv, send_counts, group=group)
-    return recv
+def context_rows(world: int, tokens_per_rank: int, k: int) -> int:
+    """Rows of the receive regions an owner runs its experts over: the
+    context's max_tokens must be at least this."""
+    return (world + 1) * tokens_per_rank * max(k, 1)
 
 
-def dispatch_rows(x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, e_local: int, world: int,
-                  group=None, row_dtype=torch.float16, extra_rows: int = 0):
-    """Steps 1-2: returns (received rows, their local expert ids, their routing
-    weights, state for combine_rows).  The rows are gathered after one
-    conversion of x to `row_dtype` (none when x has it already); the returned
-    row buffer has `extra_rows` more rows after the received ones, left for
-    the caller to fill."""
-    T, k = ids.shape
-    order, send_counts, local = dispatch_plan(ids, e_local, world)
-    recv_counts = exchange_counts(send_counts.to(x.device), group).cpu()
-    send_counts = send_counts.cpu()
-    ss, rs = send_counts.tolist(), recv_counts.tolist()
-    n_recv = int(sum(rs))
-    tok = torch.div(order, k, rounding_mode="floor")
-    xr = x if x.dtype == row_dtype else x.to(row_dtype)
-    send_x = xr.index_select(0, tok)
-    meta = torch.stack([local.index_select(0, order).to(torch.float32),
-                        w.reshape(-1).index_select(0, order).to(torch.float32)], dim=1).contiguous()
-    recv_x = torch.empty(n_recv + extra_rows, x.shape[1], dtype=row_dtype, device=x.device)
-    recv_meta = torch.empty(n_recv, 2, dtype=torch.float32, device=x.device)
-    dist.all_to_all_single(recv_x[:n_recv], send_x, rs, ss, group=group)
-    dist.all_to_all_single(recv_meta, meta, rs, ss, group=group)
-    state = (order, ss, rs, T, k)
-    return recv_x, recv_meta[:, 0].to(torch.int32), recv_meta[:, 1].contiguous(), state
-
-
-def combine_rows(y_recv: torch.Tensor, state, group=None, row_dtype=torch.float16, extra=None,
-                 out=None, ctx=None):
-    """Steps 4-5: the weighted rows back to their tokens (sent as `row_dtype`),
-    each token's rows summed in pick order in fp32, then + extra[t] (the
-    token's own shared-expert row) when given.  Returns [T, H] fp32 (`out`
-    when given).  With a library context and fp16 CUDA rows the sum reads the
-    returned rows in place through the inverse of the dispatch permutation
-    (osm_gather_sum_rows); otherwise torch gathers them first: the same adds
-    in the same order."""
-    order, ss, rs, T, k = state
-    H = y_recv.shape[1]
-    back = torch.empty(len(order), H, dtype=row_dtype, device=y_recv.device)
-    send = y_recv if y_recv.dtype == row_dtype else y_recv.to(row_dtype)
-    dist.all_to_all_single(back, send.contiguous(), ss, rs, group=group)
-    inv = torch.empty_like(order)
-    inv[order] = torch.arange(len(order), device=order.device, dtype=order.dtype)
-    if ctx is not None and back.is_cuda and row_dtype == torch.float16:
-        res = out if out is not None else torch.empty(T, H, dtype=torch.float32, device=back.device)
-        ctx.gather_sum_rows(back, inv, T, k, res, extra=extra)
-        return res
-    y = back.index_select(0, inv).view(T, k, H)
-    acc = y[:, 0].to(torch.float32, copy=True)
-    for p in range(1, k):
-        acc.add_(y[:, p])
-    if extra is not None:
-        acc.add_(extra)
-    if out is not None:
-        out.copy_(acc)
-        return out
-    return acc
+def exchange_handles(handle: bytes, geometry: tuple, group=None,
+                     timeout: datetime.timedelta | None = None) -> list[bytes]:
+    """Every rank's IPC handle in rank order.  All ranks must pass the same
+    geometry (world, tokens per rank, k, hidden, experts per rank, shared);
+    otherwise every rank raises ValueError.  A rank that does not take part
+    makes the others fail with the process group's timeout (RuntimeError)."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("an IPC handle is 64 bytes")
+    world = dist.get_world_size(group)
+    gathered: list = [None] * world
+    try:
+        if timeout is None:
+            dist.all_gather_object(gathered, (tuple(geometry), bytes(handle)), group=group)
+        else:
+            # a bounded exchange: monitored_barrier first, so a missing rank
+            # is named after `timeout` instead of hanging the collective
+            if dist.get_backend(group) == "gloo":
+                dist.monitored_barrier(group=group, timeout=timeout, wait_all_ranks=True)
+            dist.all_gather_object(gathered, (tuple(geometry), bytes(handle)), group=group)
+    except RuntimeError as e:
+        raise RuntimeError(f"expert parallel setup: a rank did not join the handle exchange ({e})") from e
+    geos = {g for g, _ in gathered}
+    if len(geos) != 1:
+        raise ValueError(f"expert parallel setup: ranks disagree on the geometry: {sorted(geos)}")
+    return [h for _, h in gathered]
 
 
 class ExpertParallelMoE:
     """The Q4 routed-MoE sublayer with its experts spread over the ranks of a
-    process group (NCCL, one GPU per rank).  `slab` holds this rank's experts
+    process group, one GPU per rank.  `slab` holds this rank's experts
     [e_first, e_first + e_count) in slots 0..e_count-1; for a layer with a
     shared expert (Qwen3-Next) it has one more slot, which receives it, and
     the shared expert and its gate row are replicated like the router weight.
-    Layers without one (Qwen3-30B-A3B) pass shared_slot=None.  The context's
-    max_tokens must cover the rows a rank can receive plus its own tokens."""
+    Layers without one (Qwen3-30B-A3B) pass shared_slot=None.  Each call
+    routes at most `tokens_per_rank` tokens; the context's max_tokens must be
+    at least context_rows(world, tokens_per_rank, k)."""
 
     def __init__(self, ctx, W: np.ndarray, k: int, norm: bool, layout, slab, e_first: int,
-                 e_count: int, shared_slot=None, shared_gate=None, bias=None, group=None):
+                 e_count: int, shared_slot=None, shared_gate=None, bias=None, group=None,
+                 tokens_per_rank: int | None = None, timeout_ms: int = 2000):
         import osm_b200 as osm
 
         self.ctx, self.k, self.group = ctx, k, group
@@ -124,43 +85,73 @@ class ExpertParallelMoE:
         self.has_shared = shared_slot is not None
         if self.has_shared and shared_gate is None:
             raise ValueError("a shared expert needs its gate row")
-        H = W.shape[1]
+        E, H = W.shape
+        if E != e_count * self.world:
+            raise ValueError("the router covers every rank's experts: E = e_count * world")
         n_local = e_count + (1 if self.has_shared else 0)
         if slab.slots < n_local:
             raise ValueError("the slab needs a slot per owned expert, plus one for a shared expert")
-        self.router = osm.Layer(ctx, W, k, norm, logit_bias=bias)
+        if tokens_per_rank is None:
+            tokens_per_rank = ctx.max_tokens // ((self.world + 1) * k)
+        self.tokens_per_rank = int(tokens_per_rank)
+        if ctx.max_tokens < context_rows(self.world, self.tokens_per_rank, k):
+            raise ValueError("context max_tokens below context_rows(world, tokens_per_rank, k)")
+        # the router computes the shared expert's gate in its select kernel
+        self.router = osm.Layer(ctx, W, k, norm, logit_bias=bias,
+                                shared_slot=shared_slot if self.has_shared else None,
+                                shared_layout=layout if self.has_shared else None,
+                                shared_gate=shared_gate if self.has_shared else None)
         if self.has_shared:
             self._sh_host = torch.from_numpy(np.ascontiguousarray(shared_slot).reshape(-1)).pin_memory()
             slab.fill_async(e_count, self._sh_host.data_ptr())
             slab.fill_wait()
-            self.gate = torch.from_numpy(np.asarray(shared_gate, np.float32)).cuda()
         # local experts 0..e_count-1, then the shared expert as local id e_count
         self.experts = osm.Layer(ctx, np.zeros((n_local, H), np.float32), 1, False)
         self.experts.bind_slab(slab, np.arange(n_local, dtype=np.int32))
+        lib = osm.lib()
+        h = C.c_void_p()
+        ctx.check(lib.osm_ep_create(ctx.h, self.world, self.rank, self.tokens_per_rank, k, H,
+                                    e_count, 1 if self.has_shared else 0, C.byref(h)), "ep_create")
+        self.h = h
+        try:
+            buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+            ctx.check(lib.osm_ep_ipc_handle(self.h, buf), "ep_ipc_handle")
+            geometry = (self.world, self.tokens_per_rank, k, H, e_count, int(self.has_shared))
+            handles = exchange_handles(buf.raw, geometry, group)
+            if self.world > 1:
+                ctx.check(lib.osm_ep_open_peers(self.h, b"".join(handles)), "ep_open_peers")
+            ctx.check(lib.osm_ep_set_timeout(self.h, int(timeout_ms)), "ep_set_timeout")
+        except Exception:
+            lib.osm_ep_destroy(self.h)
+            self.h = None
+            raise
 
     def forward(self, x: torch.Tensor, out: torch.Tensor, ids: torch.Tensor | None = None,
-                weights: torch.Tensor | None = None):
-        T, H = x.shape
+                weights: torch.Tensor | None = None, exact_route: bool = False):
+        """out[t] = the sublayer's output for x[t]; returns (ids, weights).  No
+        host synchronisation; a rank that misses a barrier shows as status bit
+        7 (STATUS_PEER_TIMEOUT) on the others."""
+        import osm_b200 as osm
+
+        T = x.shape[0]
         dev = x.device
         ids = ids if ids is not None else torch.empty(T, self.k, dtype=torch.int32, device=dev)
         w = weights if weights is not None else torch.empty(T, self.k, device=dev)
-        self.router.route_qwen_top_k(x, T, ids, w)
-        x16 = x.to(torch.float16)
-        ns = T if self.has_shared else 0
-        # received rows, then this rank's own tokens for the shared expert
-        rows, recv_ids, recv_w, state = dispatch_rows(x16, ids, w, self.e_count, self.world,
-                                                      self.group, extra_rows=ns)
-        n = rows.shape[0] - ns
-        rid, rw = recv_ids, recv_w
-        if self.has_shared:
-            rows[n:].copy_(x16)
-            rid = torch.cat([recv_ids, torch.full((T,), self.e_count, dtype=torch.int32, device=dev)])
-            rw = torch.cat([recv_w, torch.sigmoid(x @ self.gate)]).contiguous()
-        y = torch.empty(n + ns, H, dtype=torch.float16, device=dev)   # fp16 rows out
-        if n + ns > 0:  # a rank may own no picked expert and have no shared expert
-            self.experts.run_experts(rows, n + ns, rid.view(-1, 1).contiguous(), rw.view(-1, 1), y,
-                                     prefill=True)
-        # routed rows in pick order, then the shared expert's row
-        combine_rows(y[:n], state, self.group, extra=y[n:] if self.has_shared else None, out=out,
-                     ctx=self.ctx)
+        flags = osm.OSM_ROUTE_EXACT if exact_route else 0
+        self.ctx.check(osm.lib().osm_ep_forward(self.h, self.router.h, self.experts.h,
+                                                C.c_void_p(x.data_ptr()), T,
+                                                C.c_void_p(out.data_ptr()),
+                                                C.c_void_p(ids.data_ptr()), C.c_void_p(w.data_ptr()),
+                                                flags), "ep_forward")
         return ids, w
+
+    def close(self):
+        """Frees the EP block once every rank is done with every block."""
+        import osm_b200 as osm
+
+        if self.h is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        osm.lib().osm_ep_destroy(self.h)
+        self.h = None

@@ -1,9 +1,15 @@
-"""Expert parallelism (osm_b200.ep, NCCL): each rank owns E/N of the experts
-and routes T/N of the tokens; ids match the oracle exactly and outputs agree
-with the fp32 oracle within the prefill bound (2e-3, max|a-b| / max|b| per
-token), for a layer with a shared expert (Qwen3-Next) and one without
-(Qwen3-30B-A3B).  One rank runs the same exchange code on one GPU; two ranks
-need two visible GPUs (skipped otherwise)."""
+"""Expert parallelism (osm_b200.ep: the exchange over NVLink peer memory,
+osm_ep_forward): each rank owns E/N of the experts and routes T/N of the
+tokens; ids match the oracle exactly and outputs agree with the fp32 oracle
+within the prefill bound (2e-3, max|a-b| / max|b| per token), for a layer
+with a shared expert (Qwen3-Next) and one without (Qwen3-30B-A3B), over two
+consecutive calls (the receive slots are reused).  One rank runs the same
+code on one GPU; two ranks need two visible GPUs (skipped otherwise).
+
+A rank that skips a step: the other rank's device barriers give up after the
+block's timeout (300 ms here) and its status word reports bit 7; the skipping
+rank stays alive and joins the host barrier afterwards, so no mapped block
+goes away while a peer can still write to it.  NVLS is off in NCCL."""
 import os
 import sys
 
@@ -19,7 +25,7 @@ ROOT = os.path.dirname(HERE)
 H, E, I, K, T, SEED = 256, 16, 256, 4, 160, 61
 
 
-def _worker(rank, world, port, q, with_shared):
+def _worker(rank, world, port, q, with_shared, skip_rank=-1):
     sys.path[:0] = [HERE, os.path.join(ROOT, "oracle"), os.path.join(ROOT, "orbi-streammoe_b200")]
     import torch
     import torch.distributed as dist
@@ -30,6 +36,7 @@ def _worker(rank, world, port, q, with_shared):
 
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
     torch.cuda.set_device(rank)
     import datetime
 
@@ -45,7 +52,7 @@ def _worker(rank, world, port, q, with_shared):
         x_all = port_o.gen_normal(SEED, 1, 1.0, T * H).reshape(T, H)
         e_count, t_count = E // world, T // world
         e0, t0 = rank * e_count, rank * t_count
-        ctx = osm.Context(rank, max_tokens=T * K + T)
+        ctx = osm.Context(rank, max_tokens=ep.context_rows(world, t_count, K))
         ctx.set_stream(torch.cuda.current_stream().cuda_stream)
         lay = osm.expert_layout(H, I)
         slab = osm.Slab(ctx, lay, e_count + (1 if with_shared else 0))
@@ -53,12 +60,23 @@ def _worker(rank, world, port, q, with_shared):
         for e in range(e_count):
             slab.fill_async(e, pinned.data_ptr() + e * lay.stride)
         slab.fill_wait()
+        timeout = 300 if skip_rank >= 0 else 2000
         if with_shared:
-            moe = ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg)
+            moe = ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count, shared, sg,
+                                       tokens_per_rank=t_count, timeout_ms=timeout)
         else:
-            moe = ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count)
+            moe = ep.ExpertParallelMoE(ctx, W, K, True, lay, slab, e0, e_count,
+                                       tokens_per_rank=t_count, timeout_ms=timeout)
         x = torch.from_numpy(x_all[t0:t0 + t_count]).cuda()
         out = torch.empty(t_count, H, device="cuda")
+        if skip_rank >= 0:
+            if rank != skip_rank:
+                moe.forward(x, out)
+                torch.cuda.synchronize()
+            q.put((rank, ctx.status()[0]))
+            moe.close()
+            return
+        moe.forward(torch.zeros_like(x), out)   # a first call: the slots are reused below
         ids, _ = moe.forward(x, out)
         torch.cuda.synchronize()
         o, ih = out.cpu().numpy(), ids.cpu().numpy().astype(np.uint32)
@@ -76,6 +94,7 @@ def _worker(rank, world, port, q, with_shared):
                                    scalar_gate=sg if with_shared else None)[0]
             worst = max(worst, float(np.abs(o[t] - ref).max()) / float(np.abs(ref).max()))
         q.put((rank, ids_ok, worst, ctx.status()[0]))
+        moe.close()
     finally:
         dist.destroy_process_group()
 
@@ -102,6 +121,26 @@ def test_ep_ranks_match_oracle(world, with_shared):
         assert ids_ok, rank
         assert worst <= 2e-3, (rank, worst)
         assert status == 0, (rank, status)
+
+
+def test_ep_rank_that_skips_a_step_times_out():
+    torch = require_cuda()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
+    port = 29900 + os.getpid() % 90
+    procs = [mpc.Process(target=_worker, args=(r, 2, port, q, True, 1)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = sorted(q.get(timeout=5) for _ in range(2))
+    assert res[0][1] & (1 << 7), res   # rank 0 saw its barriers give up
+    assert res[1][1] == 0, res
 
 
 @pytest.mark.parametrize("with_extra", [True, False])
