@@ -1919,8 +1919,8 @@ int osm_ep_forward(osm_ep* ep, osm_layer* router, osm_layer* experts, const floa
   // 4. the weighted rows back to their sources, 5. the combine
   {
     Prof p(ctx, kKCombine);
-    osm::launch_ep_return(e, reinterpret_cast<const uint16_t*>(s.partial), s.tp_pos, ctx->stream,
-                          &ctx->launches);
+    osm::launch_ep_return(e, reinterpret_cast<const uint16_t*>(s.partial), s.tp_pos, ctx->num_sms,
+                          ctx->stream, &ctx->launches);
     osm::launch_ep_barrier(e, ++ep->epoch, ep->timeout_ns, ctx->stream, &ctx->launches);
     osm::launch_ep_combine(e, out, ctx->stream, &ctx->launches);
   }

@@ -114,7 +114,20 @@ __global__ void __launch_bounds__(kDispWarps * 32) ep_dispatch_kernel(EpArgs a) 
     const size_t slot = (size_t)region * L.cap + pos;
     const float4* xr = reinterpret_cast<const float4*>(a.x + (size_t)t * L.H);
     uint4* rr = reinterpret_cast<uint4*>(dst + L.o_rows + slot * (size_t)L.H * 2);
-    for (int c = lane; c < nch; c += 32) rr[c] = to_f16x8(xr[2 * c], xr[2 * c + 1], over);
+    for (int c0 = 0; c0 < nch; c0 += 4 * 32) {  // a lane's loads before its stores
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u * 32 + lane;
+        v[2 * u] = c < nch ? xr[2 * c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[2 * u + 1] = c < nch ? xr[2 * c + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < nch) rr[c] = to_f16x8(v[2 * u], v[2 * u + 1], over);
+      }
+    }
     if (lane == 0) {
       reinterpret_cast<uint32_t*>(dst + L.o_ids)[slot] = le;
       reinterpret_cast<float*>(dst + L.o_wts)[slot] = wgt;
@@ -145,44 +158,61 @@ __global__ void ep_barrier_kernel(EpArgs a, uint32_t epoch, unsigned long long t
   __syncthreads();
 }
 
-// grid (cap, world + 1), H / 8 threads per row (a multiple of 32, <= 1024)
-__global__ void ep_return_kernel(EpArgs a, const uint16_t* __restrict__ pb,
-                                 const int* __restrict__ tp_pos) {
+// One warp per receive slot (grid-stride over all regions): a filled slot's
+// result row (fp16, H / 8 chunks of 16 bytes, all of a lane's loads issued
+// before its stores) times the slot's weight, to the source's back rows.
+constexpr int kRetWarps = 8;
+__global__ void __launch_bounds__(kRetWarps * 32) ep_return_kernel(EpArgs a, const uint16_t* __restrict__ pb,
+                                                              const int* __restrict__ tp_pos) {
   const EpLayout& L = a.lay;
-  const int region = blockIdx.y;
-  const size_t slot = (size_t)region * L.cap + blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const size_t nslots = (size_t)(L.world + 1) * L.cap;
+  const int nch = L.H >> 3;  // <= 1024: at most 32 chunks per lane
   unsigned char* own = a.peer[L.rank];
   uint32_t* ids = reinterpret_cast<uint32_t*>(own + L.o_ids);
-  const uint32_t id = ids[slot];
-  if (id == kEpEmpty) return;
-  if (id >= (uint32_t)(L.e_local + L.shared)) {  // never written by ep_dispatch_kernel
-    if (threadIdx.x == 0) {
-      atomicOr(a.status, kStatusBadSlot);
-      ids[slot] = kEpEmpty;
+  bool over = false, bad = false;
+  for (size_t slot = (size_t)blockIdx.x * kRetWarps + (threadIdx.x >> 5); slot < nslots;
+       slot += (size_t)gridDim.x * kRetWarps) {
+    const uint32_t id = ids[slot];
+    if (id == kEpEmpty) continue;
+    __syncwarp();
+    if (lane == 0) ids[slot] = kEpEmpty;  // empty again for the next call
+    if (id >= (uint32_t)(L.e_local + L.shared)) {  // never written by ep_dispatch_kernel
+      bad = true;
+      continue;
     }
-    return;
-  }
-  const float wgt = reinterpret_cast<const float*>(own + L.o_wts)[slot];
-  const int32_t src = reinterpret_cast<const int32_t*>(own + L.o_src)[slot];
-  const int pos = tp_pos[slot];
-  unsigned char* dst = region < L.world ? a.peer[region] : own;
-  const int c = threadIdx.x;
-  bool over = false;
-  if (c < (L.H >> 3)) {
-    const uint4 q = reinterpret_cast<const uint4*>(pb + (size_t)pos * L.H)[c];
-    const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
-    float v[8];
+    const int region = (int)(slot / L.cap);
+    const float wgt = reinterpret_cast<const float*>(own + L.o_wts)[slot];
+    const int32_t src = reinterpret_cast<const int32_t*>(own + L.o_src)[slot];
+    const uint4* in = reinterpret_cast<const uint4*>(pb + (size_t)tp_pos[slot] * L.H);
+    unsigned char* dst = region < L.world ? a.peer[region] : own;
+    uint4* outp = reinterpret_cast<uint4*>(dst + L.o_back + (size_t)src * L.H * 2);
+    for (int c0 = 0; c0 < nch; c0 += 8 * 32) {
+      uint4 q[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qq[u]));
-      v[2 * u] = __fmul_rn(wgt, f.x);
-      v[2 * u + 1] = __fmul_rn(wgt, f.y);
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        q[u] = c < nch ? in[c] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c >= nch) break;
+        const uint32_t qq[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qq[j]));
+          v[2 * j] = __fmul_rn(wgt, f.x);
+          v[2 * j + 1] = __fmul_rn(wgt, f.y);
+        }
+        outp[c] = to_f16x8(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]),
+                           over);
+      }
     }
-    reinterpret_cast<uint4*>(dst + L.o_back + (size_t)src * L.H * 2)[c] =
-        to_f16x8(make_float4(v[0], v[1], v[2], v[3]), make_float4(v[4], v[5], v[6], v[7]), over);
   }
-  if (__syncthreads_or(over) && threadIdx.x == 0) atomicOr(a.status, kStatusF16Range);
-  if (threadIdx.x == 0) ids[slot] = kEpEmpty;
+  if (__any_sync(0xFFFFFFFFu, over) && lane == 0) atomicOr(a.status, kStatusF16Range);
+  if (__any_sync(0xFFFFFFFFu, bad) && lane == 0) atomicOr(a.status, kStatusBadSlot);
   __threadfence_system();
 }
 
@@ -266,10 +296,12 @@ void launch_ep_barrier(const EpArgs& a, uint32_t epoch, uint64_t timeout_ns, cud
   if (launches) *launches += 1;
 }
 
-void launch_ep_return(const EpArgs& a, const uint16_t* pb, const int* tp_pos, cudaStream_t s,
-                      uint64_t* launches) {
-  const dim3 grid((unsigned)a.lay.cap, (unsigned)(a.lay.world + 1));
-  ep_return_kernel<<<grid, a.lay.H >> 3, 0, s>>>(a, pb, tp_pos);
+void launch_ep_return(const EpArgs& a, const uint16_t* pb, const int* tp_pos, int num_sms,
+                      cudaStream_t s, uint64_t* launches) {
+  const size_t nslots = (size_t)(a.lay.world + 1) * a.lay.cap;
+  size_t blocks = (nslots + kRetWarps - 1) / kRetWarps;
+  if (blocks > (size_t)num_sms * 8) blocks = (size_t)num_sms * 8;
+  ep_return_kernel<<<(unsigned)blocks, kRetWarps * 32, 0, s>>>(a, pb, tp_pos);
   if (launches) *launches += 1;
 }
 

@@ -325,8 +325,8 @@ void launch_ep_clear_ids(const EpLayout& L, unsigned char* own, cudaStream_t s, 
 void launch_ep_dispatch(const EpArgs& a, int num_sms, cudaStream_t s, uint64_t* launches);
 void launch_ep_barrier(const EpArgs& a, uint32_t epoch, uint64_t timeout_ns, cudaStream_t s,
                        uint64_t* launches);
-void launch_ep_return(const EpArgs& a, const uint16_t* pb, const int* tp_pos, cudaStream_t s,
-                      uint64_t* launches);
+void launch_ep_return(const EpArgs& a, const uint16_t* pb, const int* tp_pos, int num_sms,
+                      cudaStream_t s, uint64_t* launches);
 void launch_ep_combine(const EpArgs& a, float* out, cudaStream_t s, uint64_t* launches);
 
 // Test hook: polls of the first bounded copy wait in each kernel file.
