@@ -208,6 +208,143 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
   TL_END(0);
 }
 
+// router_exact2_kernel<TT, F32, STG>: the same sums as router_exact_kernel
+// (one thread per expert and TT tokens, h in order), with the tokens' x
+// streamed beside the router tiles instead of staged whole: each ring stage
+// holds one 16 KB router tile and the matching HPT values of each of the TT
+// rows of x ([t][h], TT bulk copies), filled by a producer warp behind
+// full/empty mbarriers, so a block holds STG * (16 KB + TT * HPT * 4) of
+// shared memory (three or more blocks per SM) and starts computing as soon
+// as its first stage lands.  Needs x 16-byte aligned and H a multiple of
+// HPT.
+constexpr int kEx2Consumers = kExThreads / 32;
+template <int TT, bool F32, int STG>
+__global__ void __launch_bounds__(kExThreads + 32) router_exact2_kernel(RouterArgs a) {
+  constexpr int EPC = F32 ? 4 : 8;   // weights per 16-byte chunk
+  constexpr int HPT = 8 * EPC;       // h per tile
+  constexpr int XB = TT * HPT * 4;   // x bytes per stage
+  constexpr int SB = kExTile + XB;   // stage bytes
+  extern __shared__ __align__(128) unsigned char exsm[];
+  __shared__ __align__(8) uint64_t full[STG], empty[STG];
+  const int E = a.g.E, H = a.g.H, nht = H / HPT;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.y * TT;
+  const int nt = min(TT, a.B - t0);  // rows of x this block copies
+  const unsigned char* src = static_cast<const unsigned char*>(a.wx) + (size_t)blockIdx.x * nht * kExTile;
+  TL_START(0);
+  if (tid == 0) {
+    for (int st = 0; st < STG; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kEx2Consumers);
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (warp == kEx2Consumers) {
+    // ---- producer: router tiles (immutable) may go before the PDL wait;
+    //      x segments after it ----
+    if (lane == 0) {
+      for (int st = 0; st < STG && st < nht; ++st) {
+        mbar_arrive_expect(&full[st], (uint32_t)(kExTile + nt * HPT * 4));
+        bulk_load(exsm + st * SB, src + (size_t)st * kExTile, kExTile, &full[st]);
+      }
+    }
+    pdl_wait();
+    if (lane == 0) {
+      int issued = min(STG, nht);  // stages whose router tile is on its way
+      for (int j = 0; j < nht; ++j) {
+        const int st = j % STG;
+        if (j >= STG) {
+          if (!mbar_wait(&empty[st], (uint32_t)((j / STG) - 1) & 1u)) {
+            atomicOr(a.status, kStatusCopyTimeout);
+            break;
+          }
+          issued = j + 1;
+          mbar_arrive_expect(&full[st], (uint32_t)(kExTile + nt * HPT * 4));
+          bulk_load(exsm + st * SB, src + (size_t)j * kExTile, kExTile, &full[st]);
+        }
+        for (int t = 0; t < nt; ++t)
+          bulk_load(exsm + st * SB + kExTile + t * HPT * 4, a.x + (size_t)(t0 + t) * H + (size_t)j * HPT,
+                    HPT * 4, &full[st]);
+      }
+      // copies of the last stages may still be landing: wait for them
+      for (int j = max(0, issued - STG); j < issued; ++j)
+        mbar_wait(&full[j % STG], (uint32_t)(j / STG) & 1u);
+    }
+    __syncwarp();
+    return;
+  }
+  pdl_trigger();
+  const int e = blockIdx.x * kExThreads + tid;
+  float acc[TT];
+#pragma unroll
+  for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
+  const int sw = tid & 7;
+  for (int j = 0; j < nht; ++j) {
+    const int st = j % STG;
+    const uint32_t par = (uint32_t)(j / STG) & 1u;
+    if (!mbar_wait_first(&full[st], par)) {
+      if (tid == 0) atomicOr(a.status, kStatusCopyTimeout);
+      mbar_wait(&full[st], par);  // the copies may still land: wait once more
+    }
+    const uint4* row = reinterpret_cast<const uint4*>(exsm + st * SB + tid * 128);
+    const float4* xt = reinterpret_cast<const float4*>(exsm + st * SB + kExTile);  // [TT][HPT]
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 q = row[c ^ sw];
+      float w[EPC];
+      if constexpr (F32) {
+        w[0] = __uint_as_float(q.x); w[1] = __uint_as_float(q.y);
+        w[2] = __uint_as_float(q.z); w[EPC - 1] = __uint_as_float(q.w);
+      } else {
+        const uint32_t qq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          w[2 * jj] = __uint_as_float(qq[jj] << 16);
+          w[2 * jj + 1] = __uint_as_float(qq[jj] & 0xFFFF0000u);
+        }
+      }
+      // x of the TT tokens at these EPC values of h (broadcast reads)
+      float xv[TT][EPC];
+#pragma unroll
+      for (int t = 0; t < TT; ++t)
+#pragma unroll
+        for (int u = 0; u < EPC; u += 4) {
+          const float4 x4 = xt[t * (HPT / 4) + c * (EPC / 4) + (u >> 2)];
+          xv[t][u] = x4.x; xv[t][u + 1] = x4.y; xv[t][u + 2] = x4.z; xv[t][u + 3] = x4.w;
+        }
+#pragma unroll
+      for (int jj = 0; jj < EPC; ++jj) {
+        if constexpr (TT == 1) {
+          acc[0] = __fadd_rn(acc[0], __fmul_rn(w[jj], xv[0][jj]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < TT; t += 2) {
+            const float2 p2 = fmul2_rn(make_float2(w[jj], w[jj]), make_float2(xv[t][jj], xv[t + 1][jj]));
+            const float2 s2 = fadd2_rn(make_float2(acc[t], acc[t + 1]), p2);
+            acc[t] = s2.x;
+            acc[t + 1] = s2.y;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (e < E) {
+    const float bias = a.bias != nullptr ? a.bias[e] : 0.0f;
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+      if (t0 + t < a.B) {
+        const float v = a.bias != nullptr ? __fadd_rn(acc[t], bias) : acc[t];
+        a.logits[(size_t)(t0 + t) * E + e] = v;
+        a.bounds[(size_t)(t0 + t) * E + e] = 0.0f;
+      }
+    }
+  }
+  TL_END(0);
+}
+
 // ----------------------------------------------------------------------------
 // logits
 // ----------------------------------------------------------------------------
@@ -1221,8 +1358,25 @@ void launch_exact_t(const RouterArgs& a, cudaStream_t s) {
   launch_pdl(router_exact_kernel<TT, F32, STG>, grid, dim3(kExThreads), sm, s, a);
 }
 
+template <int TT, bool F32, int STG>
+void launch_exact2_t(const RouterArgs& a, cudaStream_t s) {
+  constexpr int HPT = F32 ? 32 : 64;
+  const dim3 grid((a.g.E + kExThreads - 1) / kExThreads, (a.B + TT - 1) / TT);
+  const size_t sm = (size_t)STG * (kExTile + TT * HPT * 4);
+  launch_pdl(router_exact2_kernel<TT, F32, STG>, grid, dim3(kExThreads + 32), sm, s, a);
+}
+
 template <bool F32>
 void launch_exact(const RouterArgs& a, cudaStream_t s) {
+  const int HPT = F32 ? 32 : 64;
+  if ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.g.H % HPT == 0) {
+    // streamed x: the tokens per thread grow with the batch
+    if (a.B <= 16) launch_exact2_t<1, F32, 4>(a, s);
+    else if (a.B <= 64) launch_exact2_t<2, F32, 4>(a, s);
+    else if (a.B <= 512) launch_exact2_t<4, F32, 4>(a, s);
+    else launch_exact2_t<8, F32, 4>(a, s);
+    return;
+  }
   // tokens per thread grow with the batch; the sequential sum's latency
   // (H dependent adds) bounds small batches
   if (a.B <= 16) launch_exact_t<1, F32>(a, s);
@@ -1275,6 +1429,14 @@ void init_router_attributes(int max_smem) {
   cudaFuncSetAttribute(router_exact_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<8, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<8, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
