@@ -208,29 +208,35 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
   TL_END(0);
 }
 
-// router_exact2_kernel<TT, F32, STG>: the same sums as router_exact_kernel
-// (one thread per expert and TT tokens, h in order), with the tokens' x
-// streamed beside the router tiles instead of staged whole: each ring stage
-// holds one 16 KB router tile and the matching HPT values of each of the TT
-// rows of x ([t][h], TT bulk copies), filled by a producer warp behind
-// full/empty mbarriers, so a block holds STG * (16 KB + TT * HPT * 4) of
-// shared memory (three or more blocks per SM) and starts computing as soon
-// as its first stage lands.  Needs x 16-byte aligned and H a multiple of
-// HPT.
-constexpr int kEx2Consumers = kExThreads / 32;
-template <int TT, bool F32, int STG>
-__global__ void __launch_bounds__(kExThreads + 32) router_exact2_kernel(RouterArgs a) {
+// router_exact2_kernel<TT, F32, STG, NW>: the same sums as
+// router_exact_kernel (one thread per expert and TT tokens, h in order), with
+// the tokens' x streamed beside the router rows instead of staged whole.  A
+// block owns 32 * NW experts (NW consumer warps; the rows of 32 NW experts
+// are one contiguous quarter, half or whole of a 16 KB router tile) and TT
+// tokens; each ring stage holds those rows of one tile and the matching HPT
+// values of each of the TT rows of x ([t][h], TT bulk copies), filled by a
+// producer warp behind full/empty mbarriers.  Small batches take one warp of
+// experts per block and one token per thread, so that the 2 * H dependent
+// operations of each sum run on as many SMs as possible.  Needs x 16-byte
+// aligned and H a multiple of HPT.
+template <int TT, bool F32, int STG, int NW>
+__global__ void __launch_bounds__(NW * 32 + 32) router_exact2_kernel(RouterArgs a) {
   constexpr int EPC = F32 ? 4 : 8;   // weights per 16-byte chunk
   constexpr int HPT = 8 * EPC;       // h per tile
+  constexpr int EXPB = 32 * NW;      // experts per block
+  constexpr int WB = EXPB * 128;     // router bytes per stage
   constexpr int XB = TT * HPT * 4;   // x bytes per stage
-  constexpr int SB = kExTile + XB;   // stage bytes
+  constexpr int SB = WB + XB;        // stage bytes
+  constexpr int kEx2Consumers = NW;
   extern __shared__ __align__(128) unsigned char exsm[];
   __shared__ __align__(8) uint64_t full[STG], empty[STG];
   const int E = a.g.E, H = a.g.H, nht = H / HPT;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = blockIdx.y * TT;
   const int nt = min(TT, a.B - t0);  // rows of x this block copies
-  const unsigned char* src = static_cast<const unsigned char*>(a.wx) + (size_t)blockIdx.x * nht * kExTile;
+  const int e0 = blockIdx.x * EXPB;
+  const unsigned char* src = static_cast<const unsigned char*>(a.wx) +
+                             (size_t)(e0 / kExThreads) * nht * kExTile + (size_t)(e0 % kExThreads) * 128;
   TL_START(0);
   if (tid == 0) {
     for (int st = 0; st < STG; ++st) {
@@ -245,8 +251,8 @@ __global__ void __launch_bounds__(kExThreads + 32) router_exact2_kernel(RouterAr
     //      x segments after it ----
     if (lane == 0) {
       for (int st = 0; st < STG && st < nht; ++st) {
-        mbar_arrive_expect(&full[st], (uint32_t)(kExTile + nt * HPT * 4));
-        bulk_load(exsm + st * SB, src + (size_t)st * kExTile, kExTile, &full[st]);
+        mbar_arrive_expect(&full[st], (uint32_t)(WB + nt * HPT * 4));
+        bulk_load(exsm + st * SB, src + (size_t)st * kExTile, WB, &full[st]);
       }
     }
     pdl_wait();
@@ -260,11 +266,11 @@ __global__ void __launch_bounds__(kExThreads + 32) router_exact2_kernel(RouterAr
             break;
           }
           issued = j + 1;
-          mbar_arrive_expect(&full[st], (uint32_t)(kExTile + nt * HPT * 4));
-          bulk_load(exsm + st * SB, src + (size_t)j * kExTile, kExTile, &full[st]);
+          mbar_arrive_expect(&full[st], (uint32_t)(WB + nt * HPT * 4));
+          bulk_load(exsm + st * SB, src + (size_t)j * kExTile, WB, &full[st]);
         }
         for (int t = 0; t < nt; ++t)
-          bulk_load(exsm + st * SB + kExTile + t * HPT * 4, a.x + (size_t)(t0 + t) * H + (size_t)j * HPT,
+          bulk_load(exsm + st * SB + WB + t * HPT * 4, a.x + (size_t)(t0 + t) * H + (size_t)j * HPT,
                     HPT * 4, &full[st]);
       }
       // copies of the last stages may still be landing: wait for them
@@ -275,7 +281,7 @@ __global__ void __launch_bounds__(kExThreads + 32) router_exact2_kernel(RouterAr
     return;
   }
   pdl_trigger();
-  const int e = blockIdx.x * kExThreads + tid;
+  const int e = e0 + tid;
   float acc[TT];
 #pragma unroll
   for (int t = 0; t < TT; ++t) acc[t] = 0.0f;
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(kExThreads + 32) router_exact2_kernel(RouterAr
       mbar_wait(&full[st], par);  // the copies may still land: wait once more
     }
     const uint4* row = reinterpret_cast<const uint4*>(exsm + st * SB + tid * 128);
-    const float4* xt = reinterpret_cast<const float4*>(exsm + st * SB + kExTile);  // [TT][HPT]
+    const float4* xt = reinterpret_cast<const float4*>(exsm + st * SB + WB);  // [TT][HPT]
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const uint4 q = row[c ^ sw];
@@ -1358,23 +1364,23 @@ void launch_exact_t(const RouterArgs& a, cudaStream_t s) {
   launch_pdl(router_exact_kernel<TT, F32, STG>, grid, dim3(kExThreads), sm, s, a);
 }
 
-template <int TT, bool F32, int STG>
+template <int TT, bool F32, int STG, int NW>
 void launch_exact2_t(const RouterArgs& a, cudaStream_t s) {
   constexpr int HPT = F32 ? 32 : 64;
-  const dim3 grid((a.g.E + kExThreads - 1) / kExThreads, (a.B + TT - 1) / TT);
-  const size_t sm = (size_t)STG * (kExTile + TT * HPT * 4);
-  launch_pdl(router_exact2_kernel<TT, F32, STG>, grid, dim3(kExThreads + 32), sm, s, a);
+  const dim3 grid((a.g.E + 32 * NW - 1) / (32 * NW), (a.B + TT - 1) / TT);
+  const size_t sm = (size_t)STG * (32 * NW * 128 + TT * HPT * 4);
+  launch_pdl(router_exact2_kernel<TT, F32, STG, NW>, grid, dim3(NW * 32 + 32), sm, s, a);
 }
 
 template <bool F32>
 void launch_exact(const RouterArgs& a, cudaStream_t s) {
   const int HPT = F32 ? 32 : 64;
-  if ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.g.H % HPT == 0) {
-    // streamed x: the tokens per thread grow with the batch
-    if (a.B <= 16) launch_exact2_t<1, F32, 4>(a, s);
-    else if (a.B <= 64) launch_exact2_t<2, F32, 4>(a, s);
-    else if (a.B <= 512) launch_exact2_t<4, F32, 4>(a, s);
-    else launch_exact2_t<8, F32, 4>(a, s);
+  if ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.g.H % HPT == 0 && a.g.E % 32 == 0) {
+    // streamed x: tokens per thread and experts per block grow with the batch
+    if (a.B <= 16) launch_exact2_t<1, F32, 4, 1>(a, s);
+    else if (a.B <= 64) launch_exact2_t<2, F32, 4, 1>(a, s);
+    else if (a.B <= 512) launch_exact2_t<4, F32, 4, 2>(a, s);
+    else launch_exact2_t<8, F32, 4, 4>(a, s);
     return;
   }
   // tokens per thread grow with the batch; the sequential sum's latency
@@ -1429,14 +1435,14 @@ void init_router_attributes(int max_smem) {
   cudaFuncSetAttribute(router_exact_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<8, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<8, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<1, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<2, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<4, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<8, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<1, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<2, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<4, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<8, true, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, false, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, false, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, false, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, false, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, true, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, true, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, true, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, true, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
