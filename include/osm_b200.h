@@ -335,6 +335,20 @@ int osm_layer_destroy(osm_layer* layer);
  * expert e is not resident (routing to it then fails with OSM_ENOTRES). */
 int osm_layer_bind_slab(osm_layer* layer, osm_slab* slab,
                         const int32_t* slot_of_expert_host);
+/* The router as the checkpoint stores it: MLX-affine 8-bit, group 64
+ * (packed_host: [experts][hidden / 4] u32, four values per word LSB first;
+ * scales/biases: [experts][hidden / 64] bf16), kept 8-bit on the device
+ * (hidden + 4 * hidden / 64 bytes per expert instead of 2 or 4 * hidden) and
+ * dequantised as the kernels read it, in the operation order of
+ * cpu::dequantize_affine_rows (src/cpu/reference_ops.cpp:11-67): the logits
+ * and ids are those of the reference's fp32 router
+ * (src/model/checkpoint_sparse_moe.cpp:159-162 dequantises the same module to
+ * fp32 on the host).  Replaces the router given at creation.  Needs hidden a
+ * multiple of 128, experts a multiple of 32, 16-byte aligned x in later
+ * calls, and no plan of the context alive. */
+int osm_layer_set_router_q8(osm_layer* layer, const uint32_t* packed_host,
+                            const uint16_t* scales_bf16_host,
+                            const uint16_t* biases_bf16_host, uint32_t group);
 /* Rebind a single expert (cache fill / eviction). */
 int osm_layer_set_slot(osm_layer* layer, uint32_t expert, int32_t slot);
 

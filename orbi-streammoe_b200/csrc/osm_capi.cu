@@ -189,6 +189,7 @@ struct osm_layer {
   uint32_t norm = 0;
   void* wp = nullptr;          // permuted router
   void* wx = nullptr;          // router tiles of the exact logits
+  uint32_t* qmeta = nullptr;   // 8-bit router: scale | bias << 16 per (expert, 64-group)
   float* bias = nullptr;
   float* sgate_w = nullptr;
   uint8_t* shared_slot = nullptr;
@@ -395,6 +396,7 @@ osm::RouterArgs router_args(osm_layer* L, const float* x, uint32_t T) {
   a.g = L->g;
   a.wp = static_cast<const uint4*>(L->wp);
   a.wx = L->wx;
+  a.qmeta = L->qmeta;
   a.bias = L->bias;
   a.x = x;
   a.B = (int)T;
@@ -811,6 +813,14 @@ int run_prefill(osm_layer* L, uint32_t T, float* out, const float* residual, osm
                              &ctx->launches);
   }
   return check_launch(ctx, "prefill combine");
+}
+
+// An 8-bit router's exact logits stream x by bulk copies: x must be 16-byte
+// aligned.
+int router_x_ok(osm_layer* L, const float* x) {
+  if (L->g.q8 && (reinterpret_cast<uintptr_t>(x) & 15))
+    return fail(L->ctx, OSM_EINVAL, "8-bit router: x must be 16-byte aligned");
+  return OSM_OK;
 }
 
 int layer_ready(osm_layer* L, uint32_t T, bool need_slab) {
@@ -1428,12 +1438,65 @@ int osm_layer_destroy(osm_layer* L) {
   cudaStreamSynchronize(L->ctx->stream);
   cudaFree(L->wp);
   cudaFree(L->wx);
+  cudaFree(L->qmeta);
   cudaFree(L->bias);
   cudaFree(L->sgate_w);
   cudaFree(L->shared_slot);
   cudaFree(L->norm_w);
   cudaFree(L->slot_of);
   delete L;
+  return OSM_OK;
+}
+
+int osm_layer_set_router_q8(osm_layer* L, const uint32_t* packed, const uint16_t* scales_bf16,
+                            const uint16_t* biases_bf16, uint32_t group) {
+  if (!L || !packed || !scales_bf16 || !biases_bf16) return OSM_EINVAL;
+  osm_context* ctx = L->ctx;
+  if (group != 64) return fail(ctx, OSM_EINVAL, "8-bit router: group must be 64");
+  if (L->g.H % 128 || L->g.E % 32)
+    return fail(ctx, OSM_EINVAL, "8-bit router: hidden must be a multiple of 128, experts of 32");
+  if (ctx->plans_alive > 0) return fail(ctx, OSM_EINVAL, "8-bit router: set it before creating plans");
+  const size_t E = (size_t)L->g.E, H = (size_t)L->g.H, G = H / 64;
+  std::vector<uint32_t> meta(E * G);
+  for (size_t i = 0; i < E * G; ++i) {
+    const uint32_t sb = scales_bf16[i], bb = biases_bf16[i];
+    if ((sb & 0x7F80u) == 0x7F80u || (bb & 0x7F80u) == 0x7F80u)
+      return fail(ctx, OSM_EINVAL, "8-bit router: non-finite scale or bias");
+    meta[i] = sb | (bb << 16);
+  }
+  DeviceGuard dg(ctx->device);
+  osm::RouterGeom g = L->g;
+  g.q8 = 1;
+  g.f32w = 0;
+  void *wp = nullptr, *wx = nullptr, *qm = nullptr, *tmp = nullptr;
+  if (cudaMalloc(&wp, E * g.Hp) != cudaSuccess || cudaMalloc(&wx, osm::router_tile_bytes(g)) != cudaSuccess ||
+      cudaMalloc(&qm, E * G * 4) != cudaSuccess || cudaMalloc(&tmp, E * H) != cudaSuccess) {
+    cudaFree(wp);
+    cudaFree(wx);
+    cudaFree(qm);
+    cudaFree(tmp);
+    return fail(ctx, OSM_ENOMEM, "8-bit router: allocation failed");
+  }
+  cudaStreamSynchronize(ctx->stream);  // no queued call still reads the old router
+  cudaMemcpy(tmp, packed, E * H, cudaMemcpyHostToDevice);  // the words' bytes, element order
+  cudaMemcpy(qm, meta.data(), E * G * 4, cudaMemcpyHostToDevice);
+  osm::launch_router_pack_q8(static_cast<const uint8_t*>(tmp), g, wp, ctx->stream, &ctx->launches);
+  osm::launch_router_tile_q8(static_cast<const uint8_t*>(tmp), g, wx, ctx->stream, &ctx->launches);
+  const cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(tmp);
+  if (e != cudaSuccess) {
+    cudaFree(wp);
+    cudaFree(wx);
+    cudaFree(qm);
+    return cuda_fail(ctx, e, "8-bit router: layout kernels");
+  }
+  cudaFree(L->wp);
+  cudaFree(L->wx);
+  cudaFree(L->qmeta);
+  L->wp = wp;
+  L->wx = wx;
+  L->qmeta = static_cast<uint32_t*>(qm);
+  L->g = g;
   return OSM_OK;
 }
 
@@ -1472,6 +1535,7 @@ int osm_moe_route(osm_layer* L, const float* x, uint32_t T, uint32_t* ids, float
   int rc = layer_ready(L, T, false);
   if (rc) return rc;
   if (!x) return fail(L->ctx, OSM_EINVAL, "route: null input");
+  if (int e = router_x_ok(L, x)) return e;
   osm_context* ctx = L->ctx;
   DeviceGuard dg(ctx->device);
   osm::RouterArgs a = router_args(L, x, T);
@@ -1493,6 +1557,7 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
   if (rc) return rc;
   osm_context* ctx = L->ctx;
   if (!x || !out) return fail(ctx, OSM_EINVAL, "forward: null input/output");
+  if (int e = router_x_ok(L, x)) return e;
   if ((flags & OSM_ADD_RESIDUAL) && !residual) return fail(ctx, OSM_EINVAL, "forward: residual missing");
   DeviceGuard dg(ctx->device);
   osm::RouterArgs a = router_args(L, x, T);
@@ -1688,6 +1753,7 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   if (rc) return rc;
   osm_context* ctx = L->ctx;
   if (!cache || !x || !out) return fail(ctx, OSM_EINVAL, "cached forward: null argument");
+  if (int e = router_x_ok(L, x)) return e;
   if ((flags & OSM_ADD_RESIDUAL) && !residual)
     return fail(ctx, OSM_EINVAL, "cached forward: residual missing");
   if (flags & OSM_INPUT_F16) return fail(ctx, OSM_EINVAL, "cached forward: fp32 rows only");

@@ -233,6 +233,36 @@ __global__ void router_tile_kernel(const float* __restrict__ w, RouterGeom g,
   }
 }
 
+// q8 router layouts, from the byte matrix q [E][H]: the lane-chunk vectors of
+// router_pack_kernel with one byte per element, and 16 KB tiles of 128
+// experts x 128 bytes (128 values of h) with the same 16-byte chunk swizzle.
+__global__ void router_pack_q8_kernel(const uint8_t* __restrict__ q, RouterGeom g,
+                                      uint8_t* __restrict__ wp) {
+  const size_t total = (size_t)g.E * g.Hp;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t e = i / g.Hp;
+    const int h = (int)(i - e * g.Hp);
+    const int l = h / g.c, o = h - l * g.c;
+    wp[((e * g.nvec + (o >> 3)) * 32 + l) * 8 + (o & 7)] = h < g.H ? q[e * g.H + h] : 0;
+  }
+}
+
+__global__ void router_tile_q8_kernel(const uint8_t* __restrict__ q, RouterGeom g,
+                                      unsigned char* __restrict__ wx) {
+  const int nht = g.H / 128;
+  const int Ep = (g.E + 127) & ~127;
+  const size_t total = (size_t)Ep * g.H;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int e = (int)(i / g.H), h = (int)(i - (size_t)e * g.H);
+    const int eb = e >> 7, r = e & 127, ht = h >> 7, hh = h & 127;
+    const int c = hh >> 4, p = hh & 15;
+    wx[(((size_t)eb * nht + ht) * 128 + r) * 128 + (size_t)((c ^ (r & 7)) * 16) + p] =
+        e < g.E ? q[(size_t)e * g.H + h] : 0;
+  }
+}
+
 inline int grid_for(size_t n, int threads) {
   size_t b = (n + threads - 1) / threads;
   if (b > 148 * 64) b = 148 * 64;
@@ -333,7 +363,21 @@ void launch_gen_quant(uint64_t seed, uint64_t tensor, float sigma, int rows, int
 }
 
 size_t router_tile_bytes(const RouterGeom& g) {
-  return (size_t)((g.E + 127) & ~127) * g.H * (g.f32w ? 4 : 2);
+  return (size_t)((g.E + 127) & ~127) * g.H * (g.q8 ? 1 : g.f32w ? 4 : 2);
+}
+
+void launch_router_pack_q8(const uint8_t* q, const RouterGeom& g, void* wp, cudaStream_t s,
+                           uint64_t* launches) {
+  router_pack_q8_kernel<<<grid_for((size_t)g.E * g.Hp, 256), 256, 0, s>>>(q, g,
+                                                                          static_cast<uint8_t*>(wp));
+  if (launches) *launches += 1;
+}
+
+void launch_router_tile_q8(const uint8_t* q, const RouterGeom& g, void* wx, cudaStream_t s,
+                           uint64_t* launches) {
+  router_tile_q8_kernel<<<grid_for((size_t)((g.E + 127) & ~127) * g.H, 256), 256, 0, s>>>(
+      q, g, static_cast<unsigned char*>(wx));
+  if (launches) *launches += 1;
 }
 
 void launch_router_tile(const float* w, const RouterGeom& g, void* wx, cudaStream_t s,

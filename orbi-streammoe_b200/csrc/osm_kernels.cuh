@@ -26,12 +26,16 @@ constexpr int kTokGroup = 32;  // tokens per projection work item
 struct RouterGeom {
   int H, Hp, c, nvec, E, k;
   int f32w;                 // router stored as fp32 (else bf16)
+  int q8;                   // router stored as MLX-affine 8-bit (one byte per weight; scale and
+                            // bias per 64-group in RouterArgs::qmeta); the weight is
+                            // fl(fl(scale * q) + bias), as cpu::dequantize_affine_rows
 };
 
 struct RouterArgs {
   RouterGeom g;
   const uint4* wp;          // permuted router rows (bf16 or fp32)
   const void* wx;           // router in 16 KB tiles (router_tile_kernel)
+  const uint32_t* qmeta;    // q8: [E][H / 64] bf16 scale | bf16 bias << 16
   const float* bias;        // [E] or null
   const float* x;           // [B][H]
   int B;
@@ -358,6 +362,12 @@ void launch_gen_quant(uint64_t seed, uint64_t tensor, float sigma, int rows, int
 // weights), tiles of one 128-expert block consecutive along h; in each
 // 128-byte row the 16-byte chunk c sits at c ^ (row & 7).
 size_t router_tile_bytes(const RouterGeom& g);
+// q8 router: layouts of the byte matrix q [E][H] (the packed words of an
+// 8-bit MLX-affine module are its bytes in element order)
+void launch_router_pack_q8(const uint8_t* q, const RouterGeom& g, void* wp, cudaStream_t s,
+                           uint64_t* launches);
+void launch_router_tile_q8(const uint8_t* q, const RouterGeom& g, void* wx, cudaStream_t s,
+                           uint64_t* launches);
 void launch_router_tile(const float* w, const RouterGeom& g, void* wx, cudaStream_t s,
                         uint64_t* launches);
 void launch_router_pack(const float* w, const RouterGeom& g, void* wp, cudaStream_t s,

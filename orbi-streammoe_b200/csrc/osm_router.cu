@@ -58,9 +58,25 @@ __device__ __forceinline__ void unpack8(const uint4 q, float w[8]) {
   for (int jj = 0; jj < 8; ++jj) w[jj] = bf16_bits_to_f32((ww[jj >> 1] >> ((jj & 1) * 16)) & 0xFFFFu);
 }
 
+// Eight 8-bit affine weights: fl(fl(scale * q) + bias) each, the operation
+// order of cpu::dequantize_affine_rows (reference_ops.cpp:11-67).
+__device__ __forceinline__ void deq8(uint2 q, uint32_t meta, float w[8]) {
+  const float sc = bf16_bits_to_f32(meta & 0xFFFFu), bi = bf16_bits_to_f32(meta >> 16);
+  const uint32_t qq[2] = {q.x, q.y};
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj)
+    w[jj] = __fadd_rn(__fmul_rn(sc, (float)((qq[jj >> 2] >> (8 * (jj & 3))) & 0xFFu)), bi);
+}
+
 // Eight consecutive weights of vector (e, m, lane) of the router layout.
 __device__ __forceinline__ void load8(const RouterArgs& a, int e, int m, int lane, float w[8]) {
   const size_t v = ((size_t)e * a.g.nvec + m) * 32 + lane;
+  if (a.g.q8) {
+    const int h = lane * a.g.c + 8 * m;  // the vector's first h: one 64-group
+    deq8(__ldg(reinterpret_cast<const uint2*>(a.wp) + v),
+         __ldg(a.qmeta + (size_t)e * (a.g.H >> 6) + (h >> 6)), w);
+    return;
+  }
   if (a.g.f32w) {
     const float4* p = reinterpret_cast<const float4*>(a.wp) + 2 * v;
     const float4 x0 = __ldg(p), x1 = __ldg(p + 1);
@@ -208,7 +224,7 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
   TL_END(0);
 }
 
-// router_exact2_kernel<TT, F32, STG, NW>: the same sums as
+// router_exact2_kernel<TT, FMT, STG, NW>: the same sums as
 // router_exact_kernel (one thread per expert and TT tokens, h in order), with
 // the tokens' x streamed beside the router rows instead of staged whole.  A
 // block owns 32 * NW experts (NW consumer warps; the rows of 32 NW experts
@@ -217,11 +233,13 @@ __global__ void __launch_bounds__(kExThreads) router_exact_kernel(RouterArgs a) 
 // values of each of the TT rows of x ([t][h], TT bulk copies), filled by a
 // producer warp behind full/empty mbarriers.  Small batches take one warp of
 // experts per block and one token per thread, so that the 2 * H dependent
-// operations of each sum run on as many SMs as possible.  Needs x 16-byte
-// aligned and H a multiple of HPT.
-template <int TT, bool F32, int STG, int NW>
+// operations of each sum run on as many SMs as possible.  FMT: router
+// weights as bf16 (0), fp32 (1) or 8-bit affine (2, dequantised in the
+// reference's operation order as they are read).  Needs x 16-byte aligned and
+// H a multiple of HPT.
+template <int TT, int FMT, int STG, int NW>
 __global__ void __launch_bounds__(NW * 32 + 32) router_exact2_kernel(RouterArgs a) {
-  constexpr int EPC = F32 ? 4 : 8;   // weights per 16-byte chunk
+  constexpr int EPC = FMT == 1 ? 4 : FMT == 0 ? 8 : 16;  // weights per 16-byte chunk
   constexpr int HPT = 8 * EPC;       // h per tile
   constexpr int EXPB = 32 * NW;      // experts per block
   constexpr int WB = EXPB * 128;     // router bytes per stage
@@ -299,7 +317,12 @@ __global__ void __launch_bounds__(NW * 32 + 32) router_exact2_kernel(RouterArgs 
     for (int c = 0; c < 8; ++c) {
       const uint4 q = row[c ^ sw];
       float w[EPC];
-      if constexpr (F32) {
+      if constexpr (FMT == 2) {
+        const uint32_t meta =
+            __ldg(a.qmeta + (size_t)min(e, E - 1) * (H >> 6) + ((j * HPT + c * EPC) >> 6));
+        deq8(make_uint2(q.x, q.y), meta, w);
+        deq8(make_uint2(q.z, q.w), meta, w + 8);
+      } else if constexpr (FMT == 1) {
         w[0] = __uint_as_float(q.x); w[1] = __uint_as_float(q.y);
         w[2] = __uint_as_float(q.z); w[EPC - 1] = __uint_as_float(q.w);
       } else {
@@ -310,26 +333,29 @@ __global__ void __launch_bounds__(NW * 32 + 32) router_exact2_kernel(RouterArgs 
           w[2 * jj + 1] = __uint_as_float(qq[jj] & 0xFFFF0000u);
         }
       }
-      // x of the TT tokens at these EPC values of h (broadcast reads)
-      float xv[TT][EPC];
+      // four values of h at a time: x of the TT tokens there (broadcast
+      // reads), then the TT sums advance over them in h order
 #pragma unroll
-      for (int t = 0; t < TT; ++t)
+      for (int u = 0; u < EPC; u += 4) {
+        float xv[TT][4];
 #pragma unroll
-        for (int u = 0; u < EPC; u += 4) {
+        for (int t = 0; t < TT; ++t) {
           const float4 x4 = xt[t * (HPT / 4) + c * (EPC / 4) + (u >> 2)];
-          xv[t][u] = x4.x; xv[t][u + 1] = x4.y; xv[t][u + 2] = x4.z; xv[t][u + 3] = x4.w;
+          xv[t][0] = x4.x; xv[t][1] = x4.y; xv[t][2] = x4.z; xv[t][3] = x4.w;
         }
 #pragma unroll
-      for (int jj = 0; jj < EPC; ++jj) {
-        if constexpr (TT == 1) {
-          acc[0] = __fadd_rn(acc[0], __fmul_rn(w[jj], xv[0][jj]));
-        } else {
+        for (int jj = 0; jj < 4; ++jj) {
+          const float wj = w[u + jj];
+          if constexpr (TT == 1) {
+            acc[0] = __fadd_rn(acc[0], __fmul_rn(wj, xv[0][jj]));
+          } else {
 #pragma unroll
-          for (int t = 0; t < TT; t += 2) {
-            const float2 p2 = fmul2_rn(make_float2(w[jj], w[jj]), make_float2(xv[t][jj], xv[t + 1][jj]));
-            const float2 s2 = fadd2_rn(make_float2(acc[t], acc[t + 1]), p2);
-            acc[t] = s2.x;
-            acc[t + 1] = s2.y;
+            for (int t = 0; t < TT; t += 2) {
+              const float2 p2 = fmul2_rn(make_float2(wj, wj), make_float2(xv[t][jj], xv[t + 1][jj]));
+              const float2 s2 = fadd2_rn(make_float2(acc[t], acc[t + 1]), p2);
+              acc[t] = s2.x;
+              acc[t + 1] = s2.y;
+            }
           }
         }
       }
@@ -362,7 +388,7 @@ __global__ void __launch_bounds__(kLogitWarps * 32) router_logits_kernel(RouterA
   float* xs = reinterpret_cast<float*>(smem4);  // [TOKS][32][cp]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e0 = (blockIdx.x * kLogitWarps + warp) * EXP;
-  const bool reg_path = !g.f32w && g.nvec <= kMaxVec;
+  const bool reg_path = !g.f32w && !g.q8 && g.nvec <= kMaxVec;
 #ifdef OSM_PHASE_TIMING
   const unsigned long long lg0 = gtime();
 #endif
@@ -1066,7 +1092,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
     }
     __syncthreads();
     const int nc = s_ncand;
-    if (nc > kMaxCand || g.f32w || nc < k) {
+    if (nc > kMaxCand || g.f32w || g.q8 || nc < k) {
       if (tid == 0) s_flag = 2;
     } else {
       // rows of the candidates, kPartChunk values of h at a time, transposed:
@@ -1155,7 +1181,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
         load8(a, e, o >> 3, l, w8);
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
-          if (g.f32w) tilef[(vv * 8 + jj) * g.E + e] = w8[jj];
+          if (g.f32w || g.q8) tilef[(vv * 8 + jj) * g.E + e] = w8[jj];
           else tile[(vv * 8 + jj) * g.E + e] = (uint16_t)(__float_as_uint(w8[jj]) >> 16);
         }
       }
@@ -1168,7 +1194,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
           float pr[kFullTile];
 #pragma unroll
           for (int hh = 0; hh < kFullTile; ++hh) {
-            const float w = hh < nh ? (g.f32w ? tilef[hh * g.E + e] : bf16_bits_to_f32(tile[hh * g.E + e])) : 0.0f;
+            const float w = hh < nh ? (g.f32w || g.q8 ? tilef[hh * g.E + e] : bf16_bits_to_f32(tile[hh * g.E + e])) : 0.0f;
             pr[hh] = __fmul_rn(w, xs[h0 + (hh < nh ? hh : 0)]);
           }
 #pragma unroll
@@ -1364,23 +1390,28 @@ void launch_exact_t(const RouterArgs& a, cudaStream_t s) {
   launch_pdl(router_exact_kernel<TT, F32, STG>, grid, dim3(kExThreads), sm, s, a);
 }
 
-template <int TT, bool F32, int STG, int NW>
+template <int TT, int FMT, int STG, int NW>
 void launch_exact2_t(const RouterArgs& a, cudaStream_t s) {
-  constexpr int HPT = F32 ? 32 : 64;
+  constexpr int HPT = FMT == 1 ? 32 : FMT == 0 ? 64 : 128;
   const dim3 grid((a.g.E + 32 * NW - 1) / (32 * NW), (a.B + TT - 1) / TT);
   const size_t sm = (size_t)STG * (32 * NW * 128 + TT * HPT * 4);
-  launch_pdl(router_exact2_kernel<TT, F32, STG, NW>, grid, dim3(NW * 32 + 32), sm, s, a);
+  launch_pdl(router_exact2_kernel<TT, FMT, STG, NW>, grid, dim3(NW * 32 + 32), sm, s, a);
+}
+
+template <int FMT>
+void launch_exact2(const RouterArgs& a, cudaStream_t s) {
+  // tokens per thread and experts per block grow with the batch
+  if (a.B <= 16) launch_exact2_t<1, FMT, 4, 1>(a, s);
+  else if (a.B <= 64) launch_exact2_t<2, FMT, 4, 1>(a, s);
+  else if (a.B <= 512) launch_exact2_t<4, FMT, 4, 2>(a, s);
+  else launch_exact2_t<8, FMT, 4, 4>(a, s);
 }
 
 template <bool F32>
 void launch_exact(const RouterArgs& a, cudaStream_t s) {
   const int HPT = F32 ? 32 : 64;
   if ((reinterpret_cast<uintptr_t>(a.x) & 15) == 0 && a.g.H % HPT == 0 && a.g.E % 32 == 0) {
-    // streamed x: tokens per thread and experts per block grow with the batch
-    if (a.B <= 16) launch_exact2_t<1, F32, 4, 1>(a, s);
-    else if (a.B <= 64) launch_exact2_t<2, F32, 4, 1>(a, s);
-    else if (a.B <= 512) launch_exact2_t<4, F32, 4, 2>(a, s);
-    else launch_exact2_t<8, F32, 4, 4>(a, s);
+    launch_exact2<F32 ? 1 : 0>(a, s);
     return;
   }
   // tokens per thread grow with the batch; the sequential sum's latency
@@ -1398,6 +1429,8 @@ void launch_exact(const RouterArgs& a, cudaStream_t s) {
 void launch_router_logits(const RouterArgs& a, cudaStream_t s, uint64_t* launches) {
   if (a.B <= 2) {
     launch_logits_t<1, 1>(a, s);
+  } else if (a.g.q8) {
+    launch_exact2<2>(a, s);  // the layer guarantees H % 128, E % 32 and an aligned x
   } else if (a.g.f32w) {
     launch_exact<true>(a, s);
   } else {
@@ -1435,14 +1468,18 @@ void init_router_attributes(int max_smem) {
   cudaFuncSetAttribute(router_exact_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<8, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_exact_kernel<8, true, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<1, false, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<2, false, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<4, false, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<8, false, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<1, true, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<2, true, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<4, true, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-  cudaFuncSetAttribute(router_exact2_kernel<8, true, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, 0, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, 0, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, 0, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, 0, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, 1, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, 1, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, 1, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, 1, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<1, 2, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<2, 2, 4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<4, 2, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  cudaFuncSetAttribute(router_exact2_kernel<8, 2, 4, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(router_select_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
   cudaFuncSetAttribute(group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);

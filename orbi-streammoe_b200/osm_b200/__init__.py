@@ -248,6 +248,20 @@ class Layer:
     def set_slot(self, expert: int, slot: int):
         self.ctx.check(lib().osm_layer_set_slot(self.h, expert, slot), "set_slot")
 
+    def set_router_q8(self, packed, scales_bf16, biases_bf16, group=64):
+        """Keeps the router 8-bit on the device (MLX affine: packed [E][H/4]
+        uint32, bf16 scale and bias bits [E][H/64]); logits and ids are those
+        of the fp32 router cpu::dequantize_affine_rows would give."""
+        import numpy as np
+
+        pk = np.ascontiguousarray(packed, np.uint32)
+        sc = np.ascontiguousarray(scales_bf16, np.uint16)
+        bi = np.ascontiguousarray(biases_bf16, np.uint16)
+        self.ctx.check(lib().osm_layer_set_router_q8(self.h, C.c_void_p(pk.ctypes.data),
+                                                     C.c_void_p(sc.ctypes.data),
+                                                     C.c_void_p(bi.ctypes.data), group),
+                       "set_router_q8")
+
     def route_qwen_top_k(self, x, tokens, ids, weights, mass=None, exact=False):
         self.ctx.check(lib().osm_moe_route(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
                                            _ptr(mass), OSM_ROUTE_EXACT if exact else 0), "route")

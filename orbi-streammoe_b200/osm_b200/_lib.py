@@ -91,6 +91,7 @@ _SIGS = {
     "osm_q4_dequant": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P]),
     "osm_q4_gemv": (C.c_int, [_P, _P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P]),
     "osm_test_set_copy_wait_polls": (C.c_int, [C.c_int, C.c_uint32]),
+    "osm_layer_set_router_q8": (C.c_int, [_P, _P, _P, _P, C.c_uint32]),
     "osm_ep_create": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
                                 C.c_uint32, C.c_int, C.POINTER(_P)]),
     "osm_ep_ipc_handle": (C.c_int, [_P, C.c_char_p]),
