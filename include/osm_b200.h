@@ -344,7 +344,7 @@ int osm_layer_bind_slab(osm_layer* layer, osm_slab* slab,
  * and ids are those of the reference's fp32 router
  * (src/model/checkpoint_sparse_moe.cpp:159-162 dequantises the same module to
  * fp32 on the host).  Replaces the router given at creation.  Needs hidden a
- * multiple of 128, experts a multiple of 32, 16-byte aligned x in later
+ * multiple of 256, experts a multiple of 32, 16-byte aligned x in later
  * calls, and no plan of the context alive. */
 int osm_layer_set_router_q8(osm_layer* layer, const uint32_t* packed_host,
                             const uint16_t* scales_bf16_host,

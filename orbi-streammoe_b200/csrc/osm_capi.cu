@@ -1453,8 +1453,8 @@ int osm_layer_set_router_q8(osm_layer* L, const uint32_t* packed, const uint16_t
   if (!L || !packed || !scales_bf16 || !biases_bf16) return OSM_EINVAL;
   osm_context* ctx = L->ctx;
   if (group != 64) return fail(ctx, OSM_EINVAL, "8-bit router: group must be 64");
-  if (L->g.H % 128 || L->g.E % 32)
-    return fail(ctx, OSM_EINVAL, "8-bit router: hidden must be a multiple of 128, experts of 32");
+  if (L->g.H % 256 || L->g.E % 32)
+    return fail(ctx, OSM_EINVAL, "8-bit router: hidden must be a multiple of 256, experts of 32");
   if (ctx->plans_alive > 0) return fail(ctx, OSM_EINVAL, "8-bit router: set it before creating plans");
   const size_t E = (size_t)L->g.E, H = (size_t)L->g.H, G = H / 64;
   std::vector<uint32_t> meta(E * G);
