@@ -48,12 +48,10 @@
 namespace osm {
 namespace {
 
-constexpr int kTcConv = 16;                        // converter warps
+constexpr int kTcConv = 8;                         // converter warps
 constexpr int kTcEpi = 4;                          // epilogue warps
 constexpr int kTcMma2 = 2 + kTcConv + kTcEpi;     // the second MMA issuer (gate/up: up)
-constexpr int kTcWarps = kTcMma2 + 2;                // + one idle warp: 24 warps, 6 per scheduler, so
-                                                   // that the 80 registers a thread gets fit one
-                                                   // scheduler's register file
+constexpr int kTcWarps = kTcMma2 + 1;
 constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcM = 128;                          // weight rows per item (MMA M)
 
@@ -69,14 +67,11 @@ struct TcCfg {
   // about an ulp of the accumulator per step, so the small correction terms
   // are summed among themselves and added to the main sum once, in fp32.
   static constexpr int NACC = PRECISE ? 2 : 1;
-  // operand stages (one K group each) and accumulator buffers (deeper rings
-  // measured no faster: the converters set the pace)
-  static constexpr int RO = DOWN ? 3 : 2;
-  static constexpr int NBUF = 2;
+  static constexpr int RO = DOWN ? 3 : 2;               // operand stages (one K group each)
   static constexpr int RQ = DOWN ? 8 : 4;               // weight stages (four K groups each)
   static constexpr uint32_t ACC_COLS = NMAT * NACC * NMAX;  // one accumulator buffer
   static constexpr uint32_t A_COLS = NMAT * PA * 32;    // one operand stage of A
-  static constexpr uint32_t TMEM_A = NBUF * ACC_COLS;
+  static constexpr uint32_t TMEM_A = 2 * ACC_COLS;
   static constexpr uint32_t TMEM_USED = TMEM_A + RO * A_COLS;
   static constexpr uint32_t TMEM_ALLOC = TMEM_USED <= 256 ? 256 : 512;
   static_assert(TMEM_USED <= 512, "tensor memory budget");
@@ -422,8 +417,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const TcArgs a, const
       for (int item = i0; item < i1 && ok; ++item) {
         TcItem it;
         if (!tc_item<PRECISE, DOWN>(a, item, it)) continue;
-        const int b = j % C::NBUF;
-        if (j >= C::NBUF && !tc_wait(&accempty[b], ((j / C::NBUF) - 1) & 1, abort, a.status)) break;
+        const int b = j & 1;
+        if (j >= 2 && !tc_wait(&accempty[b], ((j >> 1) - 1) & 1, abort, a.status)) break;
         fence_after();
         const int npad = (it.ntok + 15) & ~15;
         const uint32_t idesc = idesc16(kTcM, npad, PRECISE);
@@ -757,8 +752,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const TcArgs a, const
         if (inxt < i1) rows_of(nxt, pn);
       }
     }
-  } else if (warp > kTcMma2) {
-    // idle: present only so that the block's register budget fits
   } else {
     // ---------------- epilogue ----------------
     const int row = (warp & 3) * 32 + lane;
@@ -768,8 +761,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const TcArgs a, const
     for (int item = i0; item < i1; ++item) {
       TcItem it;
       if (!tc_item<PRECISE, DOWN>(a, item, it)) continue;
-      const int b = j % C::NBUF;
-      if (!warp_wait(&accfull[b], (j / C::NBUF) & 1, abort, a.status)) break;
+      const int b = j & 1;
+      if (!warp_wait(&accfull[b], (j >> 1) & 1, abort, a.status)) break;
       if (warp == kTcMma2 - 1 && lane == 0) TCT(5, j);
       fence_after();
       const uint32_t acc = tmem + lane_addr + (uint32_t)b * C::ACC_COLS;
