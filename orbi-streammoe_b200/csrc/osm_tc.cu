@@ -583,16 +583,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_kernel(const TcArgs a, const
       constexpr int NW = C::NW;
       uint32_t wv[NW];
       {
-        const unsigned char* qr = q + (size_t)m * C::QMAT + row * 128 + (g & 3) * 32 + part * NW * 4;
-        if constexpr (NW == 4) {
-          const uint4 v0 = *reinterpret_cast<const uint4*>(qr);
+        // the stage is 128-byte swizzled by the TMA copy: 16-byte chunk c of
+        // row r sits at chunk c ^ (r & 7), so a warp's 32 rows spread over
+        // all banks
+        const unsigned char* qrow = q + (size_t)m * C::QMAT + row * 128;
+        const int sw = row & 7;
+        const int c0 = 2 * (g & 3);  // the group's first chunk
+        if constexpr (NW == 8) {
+          const uint4 v0 = *reinterpret_cast<const uint4*>(qrow + ((c0 ^ sw) << 4));
+          const uint4 v1 = *reinterpret_cast<const uint4*>(qrow + (((c0 + 1) ^ sw) << 4));
           wv[0] = v0.x; wv[1] = v0.y; wv[2] = v0.z; wv[3] = v0.w;
-        } else if constexpr (NW == 2) {
-          const uint2 v0 = *reinterpret_cast<const uint2*>(qr);
-          wv[0] = v0.x; wv[1] = v0.y;
+          wv[4 % NW] = v1.x; wv[5 % NW] = v1.y; wv[6 % NW] = v1.z; wv[7 % NW] = v1.w;
+        } else if constexpr (NW == 4) {
+          const uint4 v0 = *reinterpret_cast<const uint4*>(qrow + (((c0 + part) ^ sw) << 4));
+          wv[0] = v0.x; wv[1] = v0.y; wv[2] = v0.z; wv[3] = v0.w;
         } else {
-#pragma unroll
-          for (int w = 0; w < NW; ++w) wv[w] = reinterpret_cast<const uint32_t*>(qr)[w];
+          static_assert(NW == 2, "converter split");
+          const uint2 v0 = *reinterpret_cast<const uint2*>(
+              qrow + (((c0 + (part >> 1)) ^ sw) << 4) + (part & 1) * 8);
+          wv[0] = v0.x; wv[1] = v0.y;
         }
       }
       const uint32_t acol = (uint32_t)(part * NW * 4);
@@ -887,7 +896,7 @@ bool tc_encode_maps(unsigned char (*dst)[128], const uint8_t* base, const uint64
     cuuint32_t es[3] = {1, 1, 1};
     const CUresult r = fn(reinterpret_cast<CUtensorMap*>(dst[s]), CU_TENSOR_MAP_DATA_TYPE_UINT32, 3,
                           const_cast<uint8_t*>(base) + off[s], dims, strides, box, es,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return false;
   }
