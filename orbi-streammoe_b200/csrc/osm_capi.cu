@@ -114,7 +114,6 @@ struct osm_context {
   size_t picks_cap = 0;
   cudaEvent_t picks_ev = nullptr;
   uint32_t pending_status = 0;      // status bits read by checked calls, reported next
-  uint64_t pairs_hint = 0;          // expected real pairs of a call with empty slots (0: T * k)
   bool tc_enabled = true;           // tensor-core expert kernels (OSM_DISABLE_TC=1: off)
   bool tc_decode = false;           // also for fp32 calls of 3+ tokens (OSM_TC_DECODE=1)
 };
@@ -527,10 +526,7 @@ bool tc_path(osm_layer* L, osm::TcArgs* ta, osm::TcMaps* maps) {
 // kernels are faster at the decode batch sizes measured so far).
 bool tc_use(osm_layer* L, uint32_t T, bool prefill, osm::TcArgs* ta, osm::TcMaps* maps) {
   osm_context* ctx = L->ctx;
-  if (prefill) {
-    const uint64_t pairs = ctx->pairs_hint ? ctx->pairs_hint : (uint64_t)T * (uint64_t)L->g.k;
-    if (pairs > 128ull * (uint64_t)L->g.E) return false;
-  } else if (!ctx->tc_decode) {
+  if (!prefill && !ctx->tc_decode) {
     return false;
   }
   return tc_path(L, ta, maps);
@@ -1704,9 +1700,6 @@ int ep_experts(osm_ep* ep, osm_layer* X) {
   if (!prefill_path(X, &pa, &psm)) return fail(ctx, OSM_EINVAL, "expert parallel: expert shapes not supported");
   a.xfrag = nullptr;
   a.xbf = s.xbf;
-  // the real pairs: this rank's share of every rank's picks, plus its own
-  // tokens' shared-expert rows
-  ctx->pairs_hint = (uint64_t)Ly.T_r * Ly.k + (Ly.shared ? Ly.T_r : 0);
   a.chunk_pairs = chunk_pairs_for(X, R, true);
   ctx->cur_x = rows;
   {
@@ -1719,7 +1712,6 @@ int ep_experts(osm_ep* ep, osm_layer* X) {
     pf.xb = reinterpret_cast<const uint16_t*>(rows);
     rc = run_prefill(X, R, nullptr, nullptr, pf, psm, true, true, false);
   }
-  ctx->pairs_hint = 0;
   return rc;
 }
 

@@ -4,8 +4,8 @@ and against the older kernels, through the C ABI.
 * The precise (bf16 operand planes) variant serves fp32 calls of 3+ tokens when
   a context is created with OSM_TC_DECODE=1: every token of Qwen3-Next-shaped
   batches within the 1e-4 normwise bound of the fp32 path, ids bit-exact.
-* The fast (fp16) variant serves prefill calls whose experts average at most
-  128 pairs; with OSM_DISABLE_TC=1 the older prefill kernel runs instead.  Both
+* The fast (fp16) variant serves every prefill call; with OSM_DISABLE_TC=1 the
+  older prefill kernel runs instead.  Both
   stay within the 2e-3 bound of the oracle and within 4e-3 of each other.
 """
 import ctypes
