@@ -518,12 +518,11 @@ bool tc_path(osm_layer* L, osm::TcArgs* ta, osm::TcMaps* maps) {
   return true;
 }
 
-// Whether a call of T tokens runs its experts on the tensor-core kernels of
-// osm_tc.cu.  Prefill: while the routed experts average at most 128 pairs
-// (the older prefill kernel, which converts each weight tile once per 128
-// pairs instead of per 96, is faster beyond that).  fp32 calls of 3+ tokens:
-// only when the context enables it (OSM_TC_DECODE=1; the grouped decode
-// kernels are faster at the decode batch sizes measured so far).
+// Whether a call runs its experts on the tensor-core kernels of osm_tc.cu:
+// every prefill call whose shapes they take (the older prefill kernel of
+// osm_prefill.cu otherwise, or with OSM_DISABLE_TC=1); fp32 calls of 3+
+// tokens only when the context enables it (OSM_TC_DECODE=1; the grouped
+// decode kernels are faster at the decode batch sizes measured so far).
 bool tc_use(osm_layer* L, uint32_t T, bool prefill, osm::TcArgs* ta, osm::TcMaps* maps) {
   osm_context* ctx = L->ctx;
   if (!prefill && !ctx->tc_decode) {
