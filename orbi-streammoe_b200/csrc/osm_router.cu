@@ -298,7 +298,6 @@ __global__ void __launch_bounds__(NW * 32 + 32) router_exact2_kernel(RouterArgs 
     __syncwarp();
     return;
   }
-  pdl_trigger();
   const int e = e0 + tid;
   float acc[TT];
 #pragma unroll
@@ -311,6 +310,10 @@ __global__ void __launch_bounds__(NW * 32 + 32) router_exact2_kernel(RouterArgs 
       if (tid == 0) atomicOr(a.status, kStatusCopyTimeout);
       mbar_wait(&full[st], par);  // the copies may still land: wait once more
     }
+    // the select kernel may launch once x has been read here: its first
+    // stage's x copies were issued after the producer's dependency wait, so
+    // the select can stage x itself before its own wait
+    if (j == 0) pdl_trigger();
     const uint4* row = reinterpret_cast<const uint4*>(exsm + st * SB + tid * 128);
     const float4* xt = reinterpret_cast<const float4*>(exsm + st * SB + WB);  // [TT][HPT]
 #pragma unroll
@@ -915,13 +918,36 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
     const int h = tid + j * TPB;
     sgw[j] = (a.sgate_w != nullptr && h < g.H) ? a.sgate_w[h] : 0.0f;
   }
+  const float* x = a.x + (size_t)tok * g.H;
+  int nonfinite = 0;
+  auto stage_x = [&]() {
+    if ((g.H & 3) == 0) {
+      for (int i = tid; i < (g.H >> 2); i += blockDim.x) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        reinterpret_cast<float4*>(xs)[i] = v;
+        if (!isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w)) nonfinite = 1;
+      }
+    } else {
+      for (int h = tid; h < g.H; h += blockDim.x) {
+        const float v = x[h];
+        xs[h] = v;
+        if (!isfinite(v)) nonfinite = 1;
+      }
+    }
+  };
+  // With routing, this grid follows the logits kernel, which waited for the
+  // producer of x before it let this grid launch: x is complete, and its
+  // staging overlaps the logits.  Given routing (osm_moe_experts), x may come
+  // from the kernel just before: it is read after the wait.
+  const bool early_x = !a.skip_route;
+  if (early_x) stage_x();
   pdl_wait();
   // the expert kernels may launch now: they stage their inputs and prefetch
   // the shared expert while this grid selects, then wait for it
   pdl_trigger();
   OSM_STAMP(1);
   TL_WAITED(1);
-  const float* x = a.x + (size_t)tok * g.H;
+  if (!early_x) stage_x();
   // this thread's experts: tid and tid + TPB (E <= 2 * TPB)
   float lv[2] = {-INFINITY, -INFINITY};
   float bmax = 0.0f;
@@ -933,20 +959,6 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
         lv[r] = a.logits[(size_t)tok * g.E + e];
         bmax = fmaxf(bmax, a.bounds[(size_t)tok * g.E + e]);
       }
-    }
-  }
-  int nonfinite = 0;
-  if ((g.H & 3) == 0) {
-    for (int i = tid; i < (g.H >> 2); i += blockDim.x) {
-      const float4 v = reinterpret_cast<const float4*>(x)[i];
-      reinterpret_cast<float4*>(xs)[i] = v;
-      if (!isfinite(v.x) || !isfinite(v.y) || !isfinite(v.z) || !isfinite(v.w)) nonfinite = 1;
-    }
-  } else {
-    for (int h = tid; h < g.H; h += blockDim.x) {
-      const float v = x[h];
-      xs[h] = v;
-      if (!isfinite(v)) nonfinite = 1;
     }
   }
   if (tid == 0) {
@@ -1248,6 +1260,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
     }
     if (tid == 0 && !a.force_exact) atomicAdd(a.exact_count, 0ull);
   }
+  OSM_STAMP(10);
   if (s_flag == 2 && a.force_exact && tid == 0) atomicAdd(a.exact_count, 1ull);
   if (nonfinite && tid == 0 && !a.skip_route) {
     for (int j = 0; j < k; ++j) {
@@ -1258,6 +1271,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
     a.mass[tok] = 0.0f;
   }
   __syncthreads();
+  OSM_STAMP(11);
   if ((s_flag == 2 || nonfinite) && tid < k && !a.skip_route) {
     if (a.ids_out) a.ids_out[(size_t)tok * k + tid] = a.ids[(size_t)tok * k + tid];
     if (a.weights_out) a.weights_out[(size_t)tok * k + tid] = a.weights[(size_t)tok * k + tid];
@@ -1270,7 +1284,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
   if (!a.do_group) TL_END(1);
 #ifdef OSM_PHASE_TIMING
   if (blockIdx.x == 0 && tid == 0)
-    for (int i = 0; i < 10; ++i) g_rcyc[i] = ts_[i] - ts_[0];
+    for (int i = 0; i < 12; ++i) g_rcyc[i] = ts_[i] - ts_[0];
 #endif
 #ifdef OSM_PHASE_PRINT
   if (!a.do_group && tid == 0) {
