@@ -617,7 +617,7 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
     g.act = s.act;
     g.pair_tok = s.pair_tok;
     g.tp_pos = s.tp_pos;
-    g.direct = T == 1 ? 1 : 0;
+    g.direct = 1;  // the picks of each token in order, no grouping needed
     g.ids = s.ids;
     g.pick_ptr = picks_from_ids ? nullptr : s.pick_ptr;
     g.mass = s.mass;
@@ -1599,12 +1599,12 @@ int osm_moe_forward(osm_layer* L, const float* x, uint32_t T, float* out, uint32
     flags &= ~(OSM_PREFILL_BF16 | OSM_PREFILL_NO_CHECK);
     return osm_moe_forward(L, x, T, out, ids, w, mass, sgate, residual, flags);
   }
-  // one token: the expert kernels read the picks directly (no grouping, no
-  // tensor-core fragments)
+  // one or two tokens: the expert kernels read the picks directly (no
+  // grouping, no tensor-core fragments)
   osm::GemvArgs g;
   osm::GemvLaunch gl;
   const bool dec = gemv_path(L, T, &g, &gl);
-  a.do_group = (T == 1 && dec) ? 0 : 1;
+  a.do_group = dec ? 0 : 1;
   osm::GrpArgs ga;
   size_t sgu = 0, sdn = 0;
   if (dec || grouped_path(L, &ga, &sgu, &sdn)) a.xfrag = nullptr;  // only the older kernels read it
@@ -1806,7 +1806,7 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   // 4. bind the picks to their slots and group them, then the experts; one
   //    token on the decode kernels needs neither (they read the slot table)
   const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
-  if (!prefill && T == 1 && dec) return run_experts(L, T, out, res, true);
+  if (!prefill && dec) return run_experts(L, T, out, res, true);
   a.skip_route = 1;
   a.ids_out = nullptr;
   a.weights_out = nullptr;

@@ -132,8 +132,9 @@ __device__ __forceinline__ Digits make_digits(const float (&v)[8], int e) {
 __host__ __device__ inline int mma_to_row(int R) { return 4 * (R & 3) + (R >> 2); }
 __host__ __device__ inline int row_to_mma(int m) { return 4 * (m & 3) + (m >> 2); }
 
-// Active entry j: from the grouping step, or in direct mode pick j of the one
-// token (j == k: the shared expert).  CG: read through L2 only (the routing
+// Active entry j: from the grouping step, or in direct mode (one or two
+// tokens, no grouping step) pick j % k of token j / k (j == B k: the shared
+// expert, for all B tokens; pad0 holds a routed entry's token).  CG: read through L2 only (the routing
 // may be read before this grid's dependency wait; see dec_down_kernel).
 template <bool CG>
 __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
@@ -154,8 +155,9 @@ __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
   en.cnt = 1;
   en.tg0 = 0;
   en.pad0 = en.pad1 = 0;
-  if (j < a.k) {
+  if (j < a.B * a.k) {
     en.kind = 0;
+    en.pad0 = j / a.k;  // the entry's token
     if (a.pick_ptr != nullptr) {
       // the router wrote the slot base of each pick (null: bad or not resident)
       en.ptr = CG ? reinterpret_cast<const uint8_t*>(__ldcg(
@@ -164,7 +166,7 @@ __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
     } else {
       // the same resolution as the router's: slot of the picked expert
       en.ptr = nullptr;
-      const float m = CG ? __ldcg(a.mass) : a.mass[0];
+      const float m = CG ? __ldcg(a.mass + j / a.k) : a.mass[j / a.k];
       if (m > 0.0f) {
         const uint32_t id = CG ? __ldcg(a.ids + j) : a.ids[j];
         if (id >= (uint32_t)a.E) {
@@ -179,13 +181,14 @@ __device__ __forceinline__ ActEntry gemv_entry(const GemvArgs& a, int j) {
   } else {
     en.kind = 1;
     en.ptr = a.shared_ptr;
+    en.cnt = a.B;
   }
   return en;
 }
 
 template <bool CG>
 __device__ __forceinline__ int gemv_entries(const GemvArgs& a) {
-  if (a.direct) return a.k + a.has_shared;
+  if (a.direct) return a.B * a.k + a.has_shared;
   return CG ? __ldcg(a.n_active) : *a.n_active;
 }
 
@@ -193,6 +196,7 @@ __device__ __forceinline__ int gemv_entries(const GemvArgs& a) {
 struct DecMeta {
   const uint8_t* ptr;  // slot base (null: nothing to compute)
   int off, cnt, row, kind;
+  int tok;             // direct mode: a routed entry's token
 };
 
 // ---- shared-memory plans (host and device agree on them) ----
@@ -248,13 +252,13 @@ __device__ __forceinline__ int pair_entry(const GemvArgs& a, int p, bool shared_
   const int rs = a.has_shared ? a.gu.rows[1] : 0;
   if (p < rs) {
     row = p;
-    return a.direct ? a.k : 0;
+    return a.direct ? a.B * a.k : 0;
   }
   if (shared_only) return -1;
   const int q = (p - rs) / a.gu.rows[0];
   row = (p - rs) - q * a.gu.rows[0];
   const int j = a.direct ? q : a.has_shared + q;
-  return (a.direct ? q < a.k : j < n_ent) ? j : -1;
+  return (a.direct ? q < a.B * a.k : j < n_ent) ? j : -1;
 }
 
 // int8 A fragment halves of one 32-bit word of 8 nibbles
@@ -404,11 +408,12 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
     m.ptr = nullptr;
     m.kind = 0;
     m.off = m.cnt = 0;
+    m.tok = 0;
     if (pair_entry(a, c0 + p, true, 0, row) >= 0) {
       m.ptr = a.shared_ptr;
       m.kind = 1;
-      m.off = a.direct ? a.k : 0;
-      m.cnt = a.direct ? 1 : a.B;
+      m.off = a.direct ? a.B * a.k : 0;
+      m.cnt = a.B;
     }
     m.row = row;
     meta[p] = m;
@@ -440,12 +445,14 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
       m.kind = 0;
       m.row = row;
       m.off = m.cnt = 0;
+      m.tok = 0;
       if (j >= 0) {
         const ActEntry en = gemv_entry<false>(a, j);
         m.ptr = en.ptr;
         m.kind = en.kind;
         m.off = en.off;
         m.cnt = en.cnt;
+        m.tok = en.pad0;
       }
       meta[p] = m;
     }
@@ -532,7 +539,9 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_gateup_kernel(GemvArgs 
     if (m.ptr == nullptr) continue;
     int pos = -1;
     if (a.direct) {
-      pos = m.off;
+      // the shared entry holds every token's pair; a routed entry one token's
+      if (m.kind == 1) pos = m.off + tk;
+      else if (m.tok == tk) pos = m.off;
     } else {
       for (int i = 0; i < m.cnt; ++i)
         if (a.pair_tok[m.off + i] == tk) pos = m.off + i;
@@ -585,7 +594,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_down_kernel(GemvArgs a)
     for (int q = tid; q < a.B * kp1; q += blockDim.x) {
       const int t = q / kp1, p = q - t * kp1;
       rwt[q] = p < a.k ? __ldcg(a.weights + t * a.k + p) : __ldcg(a.sgate + t);
-      rpos[q] = a.direct ? p : __ldcg(a.tp_pos + t * kp1 + p);
+      rpos[q] = a.direct ? (p < a.k ? t * a.k + p : a.B * a.k + t) : __ldcg(a.tp_pos + t * kp1 + p);
     }
   }
   for (int jj = tid; jj < ne; jj += blockDim.x) {
@@ -596,6 +605,7 @@ __global__ void __launch_bounds__(kDecWarps * 32, 2) dec_down_kernel(GemvArgs a)
     m.off = en.off;
     m.cnt = en.cnt;
     m.row = 0;
+    m.tok = en.pad0;
     meta[jj] = m;
   }
   CYC(17);
