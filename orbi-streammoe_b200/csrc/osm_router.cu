@@ -935,19 +935,87 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
       }
     }
   };
+  // Everything that needs only x: staging, the finiteness check, the fp16 /
+  // fragment copies for the expert kernels and the shared expert's gate.
+  auto prologue = [&]() {
+    stage_x();
+    if (tid == 0) {
+      s_flag = 0;
+      s_ncand = 0;
+    }
+    nonfinite = __syncthreads_or(nonfinite);
+    if (a.xbf != nullptr) {  // fp16 copy of x for the prefill tensor-core path
+      bool over = false;
+      for (int h = tid; h < g.H; h += blockDim.x) {
+        const float v = xs[h];
+        over |= fabsf(v) >= 65504.0f;
+        a.xbf[(size_t)tok * g.H + h] = __half_as_ushort(__float2half_rn(v));
+      }
+      if (over) atomicOr(a.status, kStatusF16Range);
+    }
+    if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
+    // activation fragments of the tensor-core path
+    if (a.xfrag != nullptr) {
+      const int nch = g.H >> 3;
+      for (int c = tid; c < nch; c += blockDim.x) {
+        const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
+        const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
+        const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+        uint32_t hi[8], lo[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
+        float fs = xc[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
+        uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
+        dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
+                            pack2(hi[3], hi[7]));
+        dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
+                            pack2(lo[3], lo[7]));
+        a.xfsum8[(size_t)tok * nch + c] = fs;
+      }
+    }
+    if (a.sgate_w != nullptr) {
+      float d = 0.0f;
+#pragma unroll
+      for (int j = 0; j < kSgRegs; ++j) {
+        const int h = tid + j * TPB;
+        if (h < g.H) d = fmaf(sgw[j], xs[h], d);
+      }
+      for (int h = tid + kSgRegs * TPB; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
+      d = warp_sum(d);
+      if (lane == 0) sg_part[warp] = d;
+    }
+    __syncthreads();
+    // ---- shared expert scalar gate ----
+    if (tid == blockDim.x - 32) {
+      if (a.sgate_w != nullptr) {
+        float dot = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) dot += sg_part[w];
+        const float sgv = ref_sigmoid(dot);
+        a.sgate[tok] = sgv;
+        if (a.sgate_out) a.sgate_out[tok] = sgv;
+      } else {
+        if (a.sgate) a.sgate[tok] = 0.0f;
+        if (a.sgate_out) a.sgate_out[tok] = 0.0f;
+      }
+    }
+  };
   // With routing, this grid follows the logits kernel, which waited for the
-  // producer of x before it let this grid launch: x is complete, and its
-  // staging overlaps the logits.  Given routing (osm_moe_experts), x may come
-  // from the kernel just before: it is read after the wait.
+  // producer of x before it let this grid launch: x is complete, and the
+  // prologue overlaps the logits (the scratch it writes is no longer read by
+  // the previous call, whose kernels ended before the logits kernel waited).
+  // Given routing (osm_moe_experts), x may come from the kernel just before:
+  // the prologue runs after the wait.
   const bool early_x = !a.skip_route;
-  if (early_x) stage_x();
+  if (early_x) prologue();
   pdl_wait();
   // the expert kernels may launch now: they stage their inputs and prefetch
   // the shared expert while this grid selects, then wait for it
   pdl_trigger();
   OSM_STAMP(1);
   TL_WAITED(1);
-  if (!early_x) stage_x();
+  if (!early_x) prologue();
   // this thread's experts: tid and tid + TPB (E <= 2 * TPB)
   float lv[2] = {-INFINITY, -INFINITY};
   float bmax = 0.0f;
@@ -961,22 +1029,7 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
       }
     }
   }
-  if (tid == 0) {
-    s_flag = 0;
-    s_ncand = 0;
-  }
-  nonfinite = __syncthreads_or(nonfinite);
   OSM_STAMP(2);
-  if (a.xbf != nullptr) {  // fp16 copy of x for the prefill tensor-core path
-    bool over = false;
-    for (int h = tid; h < g.H; h += blockDim.x) {
-      const float v = xs[h];
-      over |= fabsf(v) >= 65504.0f;
-      a.xbf[(size_t)tok * g.H + h] = __half_as_ushort(__float2half_rn(v));
-    }
-    if (over) atomicOr(a.status, kStatusF16Range);
-  }
-  if (nonfinite && tid == 0) atomicOr(a.status, kStatusNonFinite);
   const bool route = !nonfinite && !a.skip_route;  // block-uniform
   const int nsel = k + 1 <= g.E ? k + 1 : k;
   const int nl = (g.E + 31) >> 5;  // lists of 32 experts
@@ -996,38 +1049,6 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
   bmax = warp_max(bmax);
     if (lane == 0) s_red2[warp] = bmax;
   }
-  // activation fragments of the tensor-core path
-  if (a.xfrag != nullptr) {
-    const int nch = g.H >> 3;
-    for (int c = tid; c < nch; c += blockDim.x) {
-      const float4 p = reinterpret_cast<const float4*>(xs)[2 * c];
-      const float4 q = reinterpret_cast<const float4*>(xs)[2 * c + 1];
-      const float xc[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
-      uint32_t hi[8], lo[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) split_bf16(xc[j], hi[j], lo[j]);
-      float fs = xc[0];
-#pragma unroll
-      for (int j = 1; j < 8; ++j) fs = __fadd_rn(fs, xc[j]);
-      uint4* dst = a.xfrag + ((size_t)tok * nch + c) * 2;
-      dst[0] = make_uint4(pack2(hi[0], hi[4]), pack2(hi[1], hi[5]), pack2(hi[2], hi[6]),
-                          pack2(hi[3], hi[7]));
-      dst[1] = make_uint4(pack2(lo[0], lo[4]), pack2(lo[1], lo[5]), pack2(lo[2], lo[6]),
-                          pack2(lo[3], lo[7]));
-      a.xfsum8[(size_t)tok * nch + c] = fs;
-    }
-  }
-  if (a.sgate_w != nullptr) {
-    float d = 0.0f;
-#pragma unroll
-    for (int j = 0; j < kSgRegs; ++j) {
-      const int h = tid + j * TPB;
-      if (h < g.H) d = fmaf(sgw[j], xs[h], d);
-    }
-    for (int h = tid + kSgRegs * TPB; h < g.H; h += blockDim.x) d = fmaf(a.sgate_w[h], xs[h], d);
-    d = warp_sum(d);
-    if (lane == 0) sg_part[warp] = d;
-  }
   __syncthreads();
   OSM_STAMP(3);
   for (int step = 1; step < TPB / 32; step <<= 1) {
@@ -1040,19 +1061,6 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
   if (route && warp == 0 && lane < nsel && nsel <= 32) {
     sel_id[lane] = key_id(top);
     sel_v[lane] = key_value(top);
-  }
-  // ---- shared expert scalar gate ----
-  if (tid == blockDim.x - 32) {
-    if (a.sgate_w != nullptr) {
-      float dot = 0.0f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) dot += sg_part[w];
-      const float sgv = ref_sigmoid(dot);
-      a.sgate[tok] = sgv;
-      if (a.sgate_out) a.sgate_out[tok] = sgv;
-    } else {
-      if (a.sgate) a.sgate[tok] = 0.0f;
-      if (a.sgate_out) a.sgate_out[tok] = 0.0f;
-    }
   }
   __syncthreads();
   OSM_STAMP(4);
