@@ -185,7 +185,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // set_first_wait_polls() of that unit.
 static __device__ uint32_t g_first_polls = kCopyPolls;
 __device__ __forceinline__ bool mbar_wait_first(uint64_t* bar, uint32_t parity) {
-  const uint32_t n = *reinterpret_cast<volatile uint32_t*>(&g_first_polls);
+  // read-only while kernels run (set from the host between launches): a
+  // cached load, not one to memory on every wait
+  const uint32_t n = __ldg(&g_first_polls);
   for (uint32_t i = 0; i < n; ++i)
     if (mbar_test(bar, parity)) return true;
   return false;
