@@ -255,6 +255,8 @@ int osm_slab_create(osm_context* ctx, const osm_expert_layout* layout,
 int osm_slab_destroy(osm_slab* slab);
 uint32_t osm_slab_slots(const osm_slab* slab);
 void* osm_slab_slot_ptr(const osm_slab* slab, uint32_t slot);
+/* The expert layout the slab was created with. */
+int osm_slab_layout(const osm_slab* slab, osm_expert_layout* out);
 /* Copy one slot's bytes from (ideally pinned) host memory on the slab's side
  * stream; the copy is ordered before the next kernel on the context stream
  * that reads the slab (an event is recorded and waited on). */
@@ -359,6 +361,16 @@ int osm_layer_set_slot(osm_layer* layer, uint32_t expert, int32_t slot);
 int osm_moe_route(osm_layer* layer, const float* x_dev, uint32_t tokens,
                   uint32_t* ids_dev, float* weights_dev, float* mass_dev,
                   uint32_t flags);
+
+/* route_qwen_top_k_cpu with its QwenRouterResult::logits: as osm_moe_route
+ * with every token on the reference's own arithmetic (OSM_ROUTE_EXACT), and
+ * the fp32 logits the softmax sees (W x, plus the layer's logit bias when it
+ * has one) written to logits_dev [tokens][experts].  Inputs with a
+ * non-finite value leave logits_dev unwritten and route to expert 0 with
+ * weight 0, as osm_moe_route does. */
+int osm_moe_route_logits(osm_layer* layer, const float* x_dev, uint32_t tokens,
+                         float* logits_dev, uint32_t* ids_dev, float* weights_dev,
+                         float* mass_dev);
 
 /* run_qwen_sparse_moe_vulkan_accum (include/orbi/streammoe/model/
  * routed_moe.hpp:58-65), batched: route, run the picked experts and the

@@ -1302,6 +1302,12 @@ int osm_slab_destroy(osm_slab* s) {
 
 uint32_t osm_slab_slots(const osm_slab* s) { return s ? s->slots : 0; }
 
+int osm_slab_layout(const osm_slab* s, osm_expert_layout* out) {
+  if (!s || !out) return OSM_EINVAL;
+  *out = s->layout;
+  return OSM_OK;
+}
+
 void* osm_slab_slot_ptr(const osm_slab* s, uint32_t slot) {
   if (!s || slot >= s->slots) return nullptr;
   return s->base + (size_t)slot * s->layout.stride;
@@ -1542,6 +1548,28 @@ int osm_moe_route(osm_layer* L, const float* x, uint32_t T, uint32_t* ids, float
   a.xfrag = nullptr;
   a.sgate_w = nullptr;
   a.pick_ptr = nullptr;  // routing only: residency is the caller's next step
+  launch_router_pair(ctx, a);
+  return check_launch(ctx, "router");
+}
+
+int osm_moe_route_logits(osm_layer* L, const float* x, uint32_t T, float* logits, uint32_t* ids,
+                         float* w, float* mass) {
+  int rc = layer_ready(L, T, false);
+  if (rc) return rc;
+  if (!x || !logits) return fail(L->ctx, OSM_EINVAL, "route: null input/logits");
+  if (int e = router_x_ok(L, x)) return e;
+  osm_context* ctx = L->ctx;
+  DeviceGuard dg(ctx->device);
+  osm::RouterArgs a = router_args(L, x, T);
+  a.force_exact = 1;  // every token on the reference's arithmetic: its logits are the reference's
+  a.ids_out = ids;
+  a.weights_out = w;
+  a.mass_out = mass;
+  a.logits_out = logits;
+  a.do_group = 0;
+  a.xfrag = nullptr;
+  a.sgate_w = nullptr;
+  a.pick_ptr = nullptr;
   launch_router_pair(ctx, a);
   return check_launch(ctx, "router");
 }

@@ -50,6 +50,7 @@ struct RouterArgs {
   uint32_t* ids_out;        // optional user copies
   float* weights_out;
   float* mass_out;
+  float* logits_out;        // optional [B][E]: the full exact path's logits (W x + bias)
   // shared expert scalar gate
   const float* sgate_w;     // [H] or null
   float* sgate;             // scratch [B]

@@ -1227,7 +1227,10 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int e = tid + r * TPB;
-      if (e < g.E) lex[e] = a.bias != nullptr ? __fadd_rn(acc[r], a.bias[e]) : acc[r];
+      if (e < g.E) {
+        lex[e] = a.bias != nullptr ? __fadd_rn(acc[r], a.bias[e]) : acc[r];
+        if (a.logits_out) a.logits_out[(size_t)tok * g.E + e] = lex[e];
+      }
     }
     __syncthreads();
     float m = -INFINITY;

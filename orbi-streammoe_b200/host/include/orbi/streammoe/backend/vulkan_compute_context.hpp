@@ -9,9 +9,11 @@
 #include <cstdint>
 #include <memory>
 #include <optional>
+#include <span>
 #include <string>
 
 struct osm_context;
+struct osm_layer;
 
 namespace orbi::streammoe {
 
@@ -52,6 +54,20 @@ class VulkanComputeContext {
 
   // CUDA-side handle for the other backend classes (not in the reference).
   [[nodiscard]] osm_context* osm() const noexcept;
+
+  // The device router for a router weight (not in the reference): a
+  // libosm_b200 layer holding `weight` ([experts][hidden], row-major), made
+  // at the first call for that span and reused while the span's address,
+  // size, geometry and contents stay the same (the contents are compared
+  // with a host copy at every call, so a caller that rewrites its router in
+  // place gets a new layer).  Owned by this context; nullptr with a
+  // diagnostic when the library rejects the router.
+  [[nodiscard]] osm_layer* router_layer(std::span<const float> weight,
+                                        std::uint32_t hidden,
+                                        std::uint32_t experts,
+                                        std::uint32_t top_k,
+                                        bool norm_topk_prob,
+                                        std::string* diagnostic = nullptr) noexcept;
 
  private:
   struct Impl;

@@ -81,6 +81,9 @@ class VulkanResidentExpert {
 
   // The slab slot holding this expert (not in the reference).
   [[nodiscard]] std::int32_t slab_slot() const noexcept;
+  // The slab holding this expert: the cache's, or one of its own (not in
+  // the reference).
+  [[nodiscard]] osm_slab* slab() const noexcept;
 
  private:
   struct Impl;

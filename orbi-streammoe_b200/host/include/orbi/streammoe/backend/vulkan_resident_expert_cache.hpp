@@ -64,6 +64,8 @@ class VulkanResidentExpertCache {
 
   // The slab every resident expert lives in (not in the reference).
   [[nodiscard]] osm_slab* slab() const noexcept;
+  // The compute context the cache uploads into (not in the reference).
+  [[nodiscard]] VulkanComputeContext& context() const noexcept;
 
  private:
   struct Impl;

@@ -68,7 +68,24 @@ bool narrow_bf16(std::span<const float> in, std::vector<std::uint16_t>& out, std
 struct VulkanComputeContext::Impl {
   osm_context* ctx = nullptr;
   VulkanComputeContextInfo info;
+
+  // Device routers of the router weights this context has routed with, the
+  // least recently used dropped past kMaxRouters.
+  struct Router {
+    const float* data = nullptr;
+    std::size_t size = 0;
+    std::uint32_t hidden = 0, experts = 0, top_k = 0;
+    bool norm = false;
+    std::vector<float> copy;  // contents at upload, compared at every use
+    osm_layer* layer = nullptr;
+    std::uint64_t last_use = 0;
+  };
+  static constexpr std::size_t kMaxRouters = 256;
+  std::vector<Router> routers;
+  std::uint64_t tick = 0;
+
   ~Impl() {
+    for (auto& r : routers) osm_layer_destroy(r.layer);
     if (ctx) osm_context_destroy(ctx);
   }
 };
@@ -133,6 +150,69 @@ std::uintptr_t VulkanComputeContext::native_queue() const noexcept {
 }
 std::uintptr_t VulkanComputeContext::native_command_pool() const noexcept { return native_queue(); }
 osm_context* VulkanComputeContext::osm() const noexcept { return impl_ ? impl_->ctx : nullptr; }
+
+osm_layer* VulkanComputeContext::router_layer(std::span<const float> weight, std::uint32_t hidden,
+                                              std::uint32_t experts, std::uint32_t top_k,
+                                              bool norm_topk_prob, std::string* diagnostic) noexcept {
+  if (!valid()) {
+    osmh::set(diagnostic, "device router requires a valid compute context");
+    return nullptr;
+  }
+  auto& m = *impl_;
+  try {
+    ++m.tick;
+    for (auto it = m.routers.begin(); it != m.routers.end(); ++it) {
+      if (it->data != weight.data() || it->size != weight.size() || it->hidden != hidden ||
+          it->experts != experts || it->top_k != top_k || it->norm != norm_topk_prob)
+        continue;
+      if (std::memcmp(it->copy.data(), weight.data(), weight.size_bytes()) == 0) {
+        it->last_use = m.tick;
+        return it->layer;
+      }
+      osm_layer_destroy(it->layer);  // rewritten in place: upload it again
+      m.routers.erase(it);
+      break;
+    }
+    if (m.routers.size() >= Impl::kMaxRouters) {
+      auto lru = m.routers.begin();
+      for (auto it = m.routers.begin(); it != m.routers.end(); ++it)
+        if (it->last_use < lru->last_use) lru = it;
+      osm_layer_destroy(lru->layer);
+      m.routers.erase(lru);
+    }
+    if (weight.size() != static_cast<std::size_t>(hidden) * experts) {
+      osmh::set(diagnostic, "device router: weight size does not match experts x hidden");
+      return nullptr;
+    }
+    osm_layer_desc d{};
+    d.hidden = hidden;
+    d.experts = experts;
+    d.top_k = top_k;
+    d.norm_topk_prob = norm_topk_prob ? 1u : 0u;
+    d.router_weight_host = weight.data();
+    osm_layer* layer = nullptr;
+    const int rc = osm_layer_create(m.ctx, &d, &layer);
+    if (rc != OSM_OK || !layer) {
+      osmh::set(diagnostic, osmh::err(m.ctx, rc, "device router upload failed"));
+      return nullptr;
+    }
+    Impl::Router r;
+    r.data = weight.data();
+    r.size = weight.size();
+    r.hidden = hidden;
+    r.experts = experts;
+    r.top_k = top_k;
+    r.norm = norm_topk_prob;
+    r.copy.assign(weight.begin(), weight.end());
+    r.layer = layer;
+    r.last_use = m.tick;
+    m.routers.push_back(std::move(r));
+    return layer;
+  } catch (const std::exception& e) {
+    osmh::set(diagnostic, std::string("device router exception: ") + e.what());
+    return nullptr;
+  }
+}
 
 // ---------------------------------------------------------------------------
 // VulkanFloatBuffer

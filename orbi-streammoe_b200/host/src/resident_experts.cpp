@@ -288,6 +288,8 @@ std::uintptr_t VulkanResidentExpert::native_device() const noexcept {
 std::int32_t VulkanResidentExpert::slab_slot() const noexcept {
   return impl_ && impl_->slab_mode() ? impl_->slot : -1;
 }
+
+osm_slab* VulkanResidentExpert::slab() const noexcept { return impl_ ? impl_->slab : nullptr; }
 const VulkanFloatBuffer* VulkanResidentExpert::output_buffer() const noexcept {
   return valid() ? &*impl_->output : nullptr;
 }
@@ -438,8 +440,11 @@ struct VulkanResidentExpertCache::Impl {
     return v;
   }
 
+  // Returns a resident's slot to the free list when it lives in this cache's
+  // slab (an expert of another geometry holds a one-slot slab of its own).
   void release(const VulkanResidentExpert& r) {
-    if (r.slab_slot() >= 0) free_slots.push_back(static_cast<std::uint32_t>(r.slab_slot()));
+    if (slab && r.slab() == slab && r.slab_slot() >= 0)
+      free_slots.push_back(static_cast<std::uint32_t>(r.slab_slot()));
   }
 
   // Whether this entry goes into a slab slot; creates the slab, sized for
@@ -577,6 +582,8 @@ ExpertCacheStats VulkanResidentExpertCache::host_stats() const noexcept {
 }
 
 osm_slab* VulkanResidentExpertCache::slab() const noexcept { return impl_->slab; }
+
+VulkanComputeContext& VulkanResidentExpertCache::context() const noexcept { return impl_->context; }
 
 // ---------------------------------------------------------------------------
 // VulkanResidentSharedExpert

@@ -266,6 +266,13 @@ class Layer:
         self.ctx.check(lib().osm_moe_route(self.h, _ptr(x), tokens, _ptr(ids), _ptr(weights),
                                            _ptr(mass), OSM_ROUTE_EXACT if exact else 0), "route")
 
+    def route_qwen_top_k_logits(self, x, tokens, logits, ids=None, weights=None, mass=None):
+        """Every token on the reference's own arithmetic, with its logits
+        (W x, plus the logit bias when the layer has one) in `logits`
+        [tokens][experts] fp32."""
+        self.ctx.check(lib().osm_moe_route_logits(self.h, _ptr(x), tokens, _ptr(logits), _ptr(ids),
+                                                  _ptr(weights), _ptr(mass)), "route_logits")
+
     def run_qwen_sparse_moe(self, x, tokens, out, ids=None, weights=None, mass=None,
                             shared_gate=None, residual=None, exact_route=False, prefill=False,
                             check_range=True):

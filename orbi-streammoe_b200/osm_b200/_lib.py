@@ -109,6 +109,7 @@ _SIGS = {
     "osm_slab_create": (C.c_int, [_P, C.POINTER(ExpertLayout), C.c_uint32, C.POINTER(_P)]),
     "osm_slab_destroy": (C.c_int, [_P]),
     "osm_slab_slots": (C.c_uint32, [_P]),
+    "osm_slab_layout": (C.c_int, [_P, _P]),
     "osm_slab_slot_ptr": (_P, [_P, C.c_uint32]),
     "osm_slab_fill_async": (C.c_int, [_P, C.c_uint32, _P]),
     "osm_slab_fill_wait": (C.c_int, [_P, C.c_uint32]),
@@ -118,6 +119,7 @@ _SIGS = {
     "osm_layer_bind_slab": (C.c_int, [_P, _P, _P]),
     "osm_layer_set_slot": (C.c_int, [_P, C.c_uint32, C.c_int32]),
     "osm_moe_route": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, C.c_uint32]),
+    "osm_moe_route_logits": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P]),
     "osm_moe_forward": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_moe_experts": (C.c_int, [_P, _P, C.c_uint32, _P, _P, _P, _P, _P, C.c_uint32]),
     "osm_gather_sum_rows": (C.c_int, [_P, _P, _P, C.c_uint32, C.c_uint32, C.c_uint32, _P, _P]),

@@ -120,6 +120,36 @@ def test_router_golden_q3n_with_bias(torch, golden_dir, exact):
         np.testing.assert_allclose(w, z["weights"][sel], atol=1e-6, rtol=0)
 
 
+def test_router_logits_q3n_match_reference(torch, golden_dir):
+    """osm_moe_route_logits, the C++ drop-in's router: the logits the reference
+    library returned (router_q3n.npz, with and without the Zipf bias) bit for
+    bit, the same ids, weights and mass within 1e-6."""
+    import osm_b200 as osm
+
+    z = np.load(os.path.join(golden_dir, "router_q3n.npz"))
+    W = pyoracle.bf16_widen(z["Wbits"])
+    k = int(z["k"])
+    for sel, bias in ((slice(0, None, 2), None), (slice(1, None, 2), z["bias"])):
+        x = z["x"][sel]
+        B, E = x.shape[0], W.shape[0]
+        ctx = osm.Context(0, max_tokens=B)
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        layer = osm.Layer(ctx, W, k, True, logit_bias=bias)
+        xd = torch.from_numpy(np.ascontiguousarray(x, np.float32)).cuda()
+        logits = torch.empty(B, E, device="cuda")
+        ids = torch.empty(B, k, dtype=torch.int32, device="cuda")
+        w = torch.empty(B, k, device="cuda")
+        m = torch.empty(B, device="cuda")
+        layer.route_qwen_top_k_logits(xd, B, logits, ids, w, m)
+        torch.cuda.synchronize()
+        st, ex = ctx.status()
+        assert st == 0 and ex == B
+        assert np.array_equal(logits.cpu().numpy().view(np.uint32), z["logits"][sel].view(np.uint32))
+        assert np.array_equal(ids.cpu().numpy().astype(np.uint32), z["ids"][sel])
+        np.testing.assert_allclose(w.cpu().numpy(), z["weights"][sel], atol=1e-6, rtol=0)
+        np.testing.assert_allclose(m.cpu().numpy(), z["mass"][sel], atol=1e-6, rtol=0)
+
+
 def test_router_q3n_many_tokens_ids_bit_exact(torch, port):
     """Size-independent check at the decode batch size: every token's ids
     equal the oracle's (256 tokens, Zipf-biased and unbiased)."""

@@ -19,8 +19,11 @@ HOST = os.path.join(ROOT, "orbi-streammoe_b200", "host")
 BIN = os.path.join(HOST, "_build", "bin")
 REF = os.environ.get("OSM_REFERENCE_ROOT", "/root/reference")
 HEADERS = sorted(os.listdir(os.path.join(HOST, "include", "orbi", "streammoe", "backend")))
-TESTS = re.search(r"TESTS := \\\n(.*?)\n\n", open(os.path.join(HOST, "Makefile")).read(),
-                  re.S).group(1).replace("\\", " ").split()
+_MAKEFILE = open(os.path.join(HOST, "Makefile")).read()
+TESTS = re.search(r"\nTESTS := \\\n(.*?)\n\n", _MAKEFILE, re.S).group(1).replace("\\", " ").split()
+# this layer's own tests (host/tests/*.cpp): the drop-in against the
+# reference's CPU path
+OWN_TESTS = re.search(r"\nOWN_TESTS := ([^\n]*)", _MAKEFILE).group(1).split()
 
 
 def _drop_private(text):
@@ -79,7 +82,7 @@ def test_dropin_binaries_built_and_skip_without_gpu():
 
     if torch.cuda.is_available():
         pytest.skip("a GPU is present: test_gpu_host_dropin.py runs the binaries")
-    for t in TESTS:
+    for t in TESTS + OWN_TESTS:
         path = os.path.join(BIN, t)
         assert os.access(path, os.X_OK), f"{t} not built (make -C orbi-streammoe_b200/host)"
         r = subprocess.run([path], capture_output=True, text=True, timeout=120)
@@ -87,7 +90,8 @@ def test_dropin_binaries_built_and_skip_without_gpu():
         assert "PASS (no compute device on host)" in r.stdout, (t, r.stdout)
         # and where the test honours it, a required device that is missing is
         # an error, not a pass
-        if "ORBI_REQUIRE_VULKAN_COMPUTE" not in open(os.path.join(REF, "tests", t + ".cpp")).read():
+        src = os.path.join(HOST, "tests", t + ".cpp") if t in OWN_TESTS else os.path.join(REF, "tests", t + ".cpp")
+        if "ORBI_REQUIRE_VULKAN_COMPUTE" not in open(src).read():
             continue
         env = dict(os.environ, ORBI_REQUIRE_VULKAN_COMPUTE="1")
         r = subprocess.run([path], capture_output=True, text=True, timeout=120, env=env)
