@@ -62,6 +62,10 @@ struct Scratch {
   float* hfsum8 = nullptr;
   float* partial = nullptr;
   float* normalized = nullptr;
+  uint8_t* xd = nullptr;        // digit planes of each pair's x row / of h (osm_tcd.cu)
+  float2* xq = nullptr;
+  uint8_t* hd = nullptr;
+  float2* hq = nullptr;
   uint32_t* status = nullptr;
   uint32_t* range_status = nullptr;  // status of one checked prefill call
   unsigned long long* exact_count = nullptr;
@@ -116,6 +120,10 @@ struct osm_context {
   uint32_t pending_status = 0;      // status bits read by checked calls, reported next
   bool tc_enabled = true;           // tensor-core expert kernels (OSM_DISABLE_TC=1: off)
   bool tc_decode = false;           // also for fp32 calls of 3+ tokens (OSM_TC_DECODE=1)
+  bool dg_decode = true;            // int8 digit-plane tensor-core kernels for fp32 calls
+                                    // (OSM_DG_DECODE=0: the mma.sync kernels throughout)
+  uint32_t dg_min_tokens = 96;      // ... of at least this many tokens (OSM_DG_MIN_TOKENS;
+                                    // below it the mma.sync grouped kernels are faster)
 };
 
 struct osm_slab {
@@ -305,6 +313,8 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   const size_t o_hf = take(P * (I / 8) * 32), o_hs = take(P * (I / 8) * 4);
   const size_t o_part = take(P * H * 4), o_norm = take(T * H * 4);
   const size_t o_pptr = take(T * k * sizeof(void*));
+  const size_t o_xd = take(P * 3 * Kx), o_xq = take(P * (Kx / 64) * 8);
+  const size_t o_hd = take(P * 3 * I), o_hq = take(P * (I / 64) * 8);
   void* base = nullptr;
   cudaError_t e = cudaMalloc(&base, off);
   if (e != cudaSuccess) return fail(ctx, OSM_ENOMEM, "scratch allocation failed");
@@ -351,6 +361,10 @@ int ensure_scratch(osm_context* ctx, size_t T, size_t H, size_t E, size_t k, siz
   s.partial = reinterpret_cast<float*>(b + o_part);
   s.normalized = reinterpret_cast<float*>(b + o_norm);
   s.pick_ptr = reinterpret_cast<const uint8_t**>(b + o_pptr);
+  s.xd = reinterpret_cast<uint8_t*>(b + o_xd);
+  s.xq = reinterpret_cast<float2*>(b + o_xq);
+  s.hd = reinterpret_cast<uint8_t*>(b + o_hd);
+  s.hq = reinterpret_cast<float2*>(b + o_hq);
   return OSM_OK;
 }
 
@@ -531,12 +545,32 @@ bool tc_use(osm_layer* L, uint32_t T, bool prefill, osm::TcArgs* ta, osm::TcMaps
   return tc_path(L, ta, maps);
 }
 
+// Whether an fp32 call of T tokens runs its experts on the int8 digit-plane
+// tensor-core kernels of osm_tcd.cu: from dg_min_tokens tokens (96 by default,
+// where they overtake the mma.sync grouped kernels of osm_gemv.cu on the
+// Qwen3-Next sublayer; OSM_DG_MIN_TOKENS moves the threshold, OSM_DG_DECODE=0
+// turns them off).  The shapes are those of the 16-bit tensor-core
+// kernels (same tensor maps, same item geometry); scale and bias rows arrive
+// by bulk copies, so their sections must be 16-byte aligned.
+bool dg_use(osm_layer* L, uint32_t T, osm::TcArgs* ta, osm::TcMaps* maps) {
+  osm_context* ctx = L->ctx;
+  if (!ctx->dg_decode || T < 3 || T < ctx->dg_min_tokens || !osm::dg_fits(ctx->max_smem)) return false;
+  if (!tc_path(L, ta, maps)) return false;
+  for (int kd = 0; kd < 2; ++kd) {
+    const uint64_t o[6] = {ta->gu.s[kd], ta->gu.b[kd], ta->gu.s2[kd], ta->gu.b2[kd], ta->dn.s[kd], ta->dn.b[kd]};
+    for (uint64_t v : o)
+      if (v % 16) return false;
+  }
+  return ta->H % 128 == 0 && ta->Imax % 128 == 0;
+}
+
 // Pairs per chunk of the grouping for a call of T tokens: the tensor-core
 // kernels take 32 (fp32 calls) or 96 (prefill), the older grouped kernels 8
 // and the older prefill kernel 128.
 int chunk_pairs_for(osm_layer* L, uint32_t T, bool prefill) {
   osm::TcArgs ta;
   osm::TcMaps maps;
+  if (!prefill && dg_use(L, T, &ta, &maps)) return osm::kDgChunk;
   const bool tc = tc_use(L, T, prefill, &ta, &maps);
   if (prefill) return tc ? osm::kTcChunkFast : 128;
   return tc ? osm::kTcChunkPrecise : 8;
@@ -598,6 +632,63 @@ int run_tc(osm_layer* L, uint32_t T, float* out, const float* residual, osm::TcA
   return check_launch(ctx, "prefill combine");
 }
 
+// The digit-plane tensor-core path: digit planes of each pair's x row,
+// gate/up (+ SwiGLU), digit planes of h, down, then the pick-order combine.
+int run_dg(osm_layer* L, uint32_t T, float* out, const float* residual, const osm::TcArgs& ta0,
+           const osm::TcMaps& maps) {
+  osm_context* ctx = L->ctx;
+  Scratch& s = ctx->sc;
+  osm::DgArgs d{};
+  d.t = ta0;
+  osm::TcArgs& ta = d.t;
+  ta.x = ctx->cur_x;
+  ta.h = reinterpret_cast<float*>(s.hfrag);
+  ta.partial = s.partial;
+  ta.n_ch = s.n_ch;
+  ta.chunks = s.chunks;
+  ta.act = s.act;
+  ta.pair_tok = s.pair_tok;
+  ta.pair_pick = s.pair_pick;
+  ta.status = s.status;
+  d.xq = s.xq;
+  d.hq = s.hq;
+  const int H = L->g.H, Imax = ta.Imax;
+  // pair positions of the call: k per token, plus the shared expert's
+  const int P = (int)T * (int)L->g.k + (L->shared_slot ? (int)T : 0);
+  osm::DgMaps dm;
+  std::memcpy(&dm.q, &maps, sizeof(maps));
+  for (int i = 0; i < 3; ++i)
+    if (!osm::tc_encode_u8_rows(dm.xd[i], s.xd, (uint64_t)P * 3, (uint64_t)H, 16 * (i + 1)) ||
+        !osm::tc_encode_u8_rows(dm.hd[i], s.hd, (uint64_t)P * 3, (uint64_t)Imax, 16 * (i + 1)))
+      return fail(ctx, OSM_ECUDA, "digit-plane tensor maps");
+  {
+    Prof p(ctx, kKGateUp);
+    osm::launch_digits(ctx->cur_x, s.pair_tok, (int)T, P, H, H, s.xd, s.xq, ctx->stream, &ctx->launches);
+    const cudaError_t e = osm::launch_dg_gateup(d, dm, ctx->num_sms, ctx->stream, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "digit-plane gate/up");
+  }
+  {
+    Prof p(ctx, kKDown);
+    osm::launch_digits(ta.h, nullptr, P, P, Imax, Imax, s.hd, s.hq, ctx->stream, &ctx->launches);
+    const cudaError_t e = osm::launch_dg_down(d, dm, ctx->num_sms, ctx->stream, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "digit-plane down");
+  }
+  osm::CombineArgs c{};
+  c.partial = s.partial;
+  c.weights = s.weights;
+  c.sgate = L->shared_slot ? s.sgate : nullptr;
+  c.residual = residual;
+  c.out = out;
+  c.B = (int)T;
+  c.H = H;
+  c.k = L->g.k;
+  {
+    Prof p(ctx, kKCombine);
+    osm::launch_combine(c, ctx->stream, &ctx->launches);
+  }
+  return check_launch(ctx, "combine");
+}
+
 // picks_from_ids: one token whose picks the decode kernels resolve through
 // the slot table themselves (no binding step ran)
 int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
@@ -641,7 +732,13 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
     return check_launch(ctx, "down gemv + combine");
   }
   {
-    // 3+ tokens: the tensor-core kernels over 32-pair chunks of each expert
+    // dg_min_tokens+ tokens: the int8 digit-plane tensor-core kernels over 16-pair chunks
+    osm::TcArgs ta;
+    osm::TcMaps maps;
+    if (dg_use(L, T, &ta, &maps)) return run_dg(L, T, out, residual, ta, maps);
+  }
+  {
+    // 3+ tokens: the 16-bit tensor-core kernels over 32-pair chunks of each expert
     osm::TcArgs ta;
     osm::TcMaps maps;
     if (tc_use(L, T, false, &ta, &maps)) return run_tc(L, T, out, residual, ta, maps, true, nullptr, false);
@@ -900,11 +997,16 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   osm::init_grouped_attributes(ctx->max_smem);
   osm::init_prefill_attributes(ctx->max_smem);
   osm::init_tc_attributes(ctx->max_smem);
+  osm::init_dg_attributes(ctx->max_smem);
   {
     const char* v = std::getenv("OSM_DISABLE_TC");
     ctx->tc_enabled = !(v && v[0] && v[0] != '0');
     const char* d = std::getenv("OSM_TC_DECODE");
     ctx->tc_decode = d && d[0] && d[0] != '0';
+    const char* g = std::getenv("OSM_DG_DECODE");
+    ctx->dg_decode = !(g && g[0] == '0');
+    const char* gm = std::getenv("OSM_DG_MIN_TOKENS");
+    if (gm && gm[0]) ctx->dg_min_tokens = (uint32_t)std::strtoul(gm, nullptr, 10);
   }
   const cudaError_t ae = cudaGetLastError();
   if (ae != cudaSuccess) {

@@ -196,6 +196,43 @@ static inline cudaError_t set_first_wait_polls(uint32_t n) {
   return cudaMemcpyToSymbol(g_first_polls, &n, sizeof(n));
 }
 
+// Block-floating-point int8 digits of 8 consecutive activations (physical
+// inputs k0..k0+7 of one group) for the B fragments: b0 takes the even
+// positions, b1 the odd ones.  s = 2^e with 127 s > max|x_group|.
+struct Digits {
+  uint32_t b0[3], b1[3];
+};
+__device__ __forceinline__ int group_exponent(float m) {
+  int E = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+  if (E < -100) E = -100;   // zero / tiny groups: digits are 0 anyway
+  if (E > 120) E = 120;     // keeps 2^-e finite
+  return E - 5;             // |x| < 2^(E+1) = 64 s
+}
+// y = rint(x 2^(14-e)) (|y| < 2^20) split into balanced base-128 digits:
+// y = d0 2^14 + d1 2^7 + d2 with |d| <= 64.
+__device__ __forceinline__ Digits make_digits(const float (&v)[8], int e) {
+  const float sc = __uint_as_float((uint32_t)(127 + 14 - e) << 23);  // 2^(14-e)
+  uint32_t p[3][8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int y = __float2int_rn(v[m] * sc);
+    const int d2 = ((y + 64) & 127) - 64;
+    const int y1 = (y - d2) >> 7;
+    const int d1 = ((y1 + 64) & 127) - 64;
+    const int d0 = (y1 - d1) >> 7;
+    p[0][m] = (uint32_t)d0 & 0xFFu;
+    p[1][m] = (uint32_t)d1 & 0xFFu;
+    p[2][m] = (uint32_t)d2 & 0xFFu;
+  }
+  Digits D;
+#pragma unroll
+  for (int d = 0; d < 3; ++d) {
+    D.b0[d] = p[d][0] | (p[d][2] << 8) | (p[d][4] << 16) | (p[d][6] << 24);
+    D.b1[d] = p[d][1] | (p[d][3] << 8) | (p[d][5] << 16) | (p[d][7] << 24);
+  }
+  return D;
+}
+
 // Monotone map of finite floats (and -inf) to unsigned keys.
 __device__ __forceinline__ uint32_t ord_key(float v) {
   const uint32_t u = __float_as_uint(v);

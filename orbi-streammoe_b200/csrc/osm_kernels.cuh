@@ -305,6 +305,45 @@ cudaError_t launch_tc_gateup(const TcArgs& a, const TcMaps& maps, bool precise, 
 cudaError_t launch_tc_down(const TcArgs& a, const TcMaps& maps, bool precise, int grid,
                            cudaStream_t s, uint64_t* launches);
 
+// 2-D tensor map over `rows` rows of row_bytes bytes (uint8, 128-byte
+// swizzle, box 128 bytes x box_rows rows): the digit planes of osm_tcd.cu.
+bool tc_encode_u8_rows(unsigned char* dst, const uint8_t* base, uint64_t rows, uint64_t row_bytes,
+                       int box_rows);
+
+// ---- tensor-core grouped experts on int8 digit planes (osm_tcd.cu) ----
+// fp32 calls of 3+ tokens: Q4 nibbles (exact int8) against block-floating-
+// point activations split into three int8 digit planes, tcgen05.mma
+// kind::i8 with one s32 accumulator per 64-wide K group, the group scales
+// applied in fp32 by the epilogue; outputs within 1e-4 of the fp32 path.
+// Items are (chunk of <= kDgChunk pairs of one active entry, 128 rows).
+constexpr int kDgChunk = 16;
+struct DgArgs {
+  TcArgs t;                      // sections, grouping, h / partial outputs, status
+  const float2* xq;              // [pairs][H/64] {s 2^-14, group sum} of each pair's x row
+  const float2* hq;              // [pairs][Imax/64] the same for h
+};
+// Tensor maps: the Q4 sections (TcMaps) and the digit planes of x per pair
+// ([pairs * 3][H] bytes) and of h ([pairs * 3][Imax]), box 128 bytes x
+// 16 (i + 1) rows for map i (an item of n pairs reads 16 ceil(3 n / 16) rows).
+struct alignas(64) DgMaps {
+  TcMaps q;
+  unsigned char xd[3][128];
+  unsigned char hd[3][128];
+};
+// Digit planes of `rows` fp32 rows of K inputs (K a multiple of 64): row r
+// reads src row rowmap[r] (clamped to [0, nsrc)) or r, row stride ld floats;
+// dst[r][d][K] int8, per 8 inputs the digits of the even positions then the
+// odd ones (the A operand's nibble order); q[r][K/64] = {s 2^-14, sum of the
+// group's inputs}.
+void launch_digits(const float* src, const int* rowmap, int nsrc, int rows, int K, int ld,
+                   uint8_t* dst, float2* q, cudaStream_t s, uint64_t* launches);
+void init_dg_attributes(int max_smem);
+bool dg_fits(int max_smem);
+cudaError_t launch_dg_gateup(const DgArgs& a, const DgMaps& maps, int grid, cudaStream_t s,
+                             uint64_t* launches);
+cudaError_t launch_dg_down(const DgArgs& a, const DgMaps& maps, int grid, cudaStream_t s,
+                           uint64_t* launches);
+
 // ---- expert parallelism over peer memory (osm_ep.cu) ----
 constexpr uint32_t kEpEmpty = 0xFFFFFFFFu;  // id of an empty receive slot
 constexpr int kEpMaxWorld = 8;

@@ -11,8 +11,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(HERE, "libosm_b200.so")
 
 SOURCES = ["osm_capi.cu", "osm_kernels.cu", "osm_router.cu", "osm_experts.cu", "osm_gemv.cu",
-           "osm_prefill.cu", "osm_tc.cu", "osm_ep.cu"]
-HEADERS = ["osm_common.cuh", "osm_kernels.cuh"]
+           "osm_prefill.cu", "osm_tc.cu", "osm_tcd.cu", "osm_ep.cu"]
+HEADERS = ["osm_common.cuh", "osm_kernels.cuh", "osm_tcgen05.cuh"]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-shared"]
 
