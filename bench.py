@@ -46,10 +46,11 @@ S_GATEUP = 1179648   # gate + up sections
 S_DOWN = 589824
 S_ROUTER = E * H * 2
 S_SGATE = H * 2
-# DRAM traffic (read + write) of one grouped gate/up launch at B = 256, from
-# the ncu capture summarised in profiles/grp_gateup_q3n_b256.md (algorithmic
-# bytes of that launch: 105.8 MB).
-NCU_GATEUP_TRAFFIC_B256 = 107_173_888 + 4_133_632
+# DRAM traffic (read + write) of one gate/up launch at B = 256 (the digit-plane
+# tensor-core kernel, dg_kernel<0>), from the ncu capture summarised in
+# profiles/dg_kernel_gateup_down_q3n_b256.md (algorithmic bytes of that
+# launch: 105.8 MB).
+NCU_GATEUP_TRAFFIC_B256 = 128_601_088 + 4_684_288
 
 
 def bf16_round(v: np.ndarray) -> np.ndarray:
