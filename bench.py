@@ -877,7 +877,7 @@ def run_stream(args, rank, world, local_rank):
         t0.record(stream)
         for l, layer in enumerate(layers):
             x, out = bufs[l & 1], bufs[(l + 1) & 1]
-            layer.run_cached(cache, l, x, 1, out)
+            layer.run_cached(cache, l, x, 1, out, early=args.stream_early)
             ctx.rms_norm(out, 1, H, ones, 1e-6)
         if L & 1:
             bufs.reverse()
@@ -925,6 +925,10 @@ def run_stream(args, rank, world, local_rank):
                    "timing": "per-token CUDA events on the launching stream (the host's wait "
                              "for each layer's picks included); inputs: each token streams its "
                              "layers' weights (>1 GB) through HBM",
+                   "expert_launch": ("early: queued behind the router before the picks reach "
+                                     "the host, run again after a miss (OSM_CACHED_EARLY)"
+                                     if args.stream_early else
+                                     "after the picks are resident"),
                    "cache_hit_rate": round(hits / max(1, hits + misses), 4),
                    "cache_loads": int(s1["loads"] - s0["loads"]),
                    "cache_evictions": int(s1["evictions"] - s0["evictions"]),
@@ -1057,6 +1061,10 @@ SUB_KEYS = ("value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "scalin
             "e2e", "gpu_launches", "roofline", "clocks")
 
 
+STREAM_SUB_TOKENS = 128   # configs[4] sub-run of the default line
+STREAM_SUB_WARMUP = 8
+
+
 def sub_workloads(args, rank, world, local_rank):
     """configs[2] (4096-token prefill) and configs[3] (Qwen3-30B-A3B shape)
     timed in the same run as the headline sweep, each with its own steps,
@@ -1077,6 +1085,21 @@ def sub_workloads(args, rank, world, local_rank):
             if extra in line["config"]:
                 d[extra] = line["config"][extra]
         out[key] = d
+    if world == 1 and args.stream_sub:
+        # configs[4] on one GPU only: every rank would pin its own 43.5 GB
+        # host copy of the 48 layers' experts
+        s4 = copy.copy(args)
+        s4.steps = STREAM_SUB_TOKENS
+        s4.warmup = STREAM_SUB_WARMUP
+        line = run_stream(s4, rank, world, local_rank)
+        d = {k: line[k] for k in SUB_KEYS if k in line}
+        for extra in ("workload", "layers", "cache_slots", "cache_hit_rate", "cache_loads",
+                      "cache_evictions", "h2d_bytes_per_token", "exposed_h2d_ms_per_token",
+                      "expert_launch"):
+            d[extra] = line["config"][extra]
+        d["sample"] = (f"{STREAM_SUB_TOKENS} decode tokens after {STREAM_SUB_WARMUP} warm-up "
+                       "tokens (the cache fills during the warm-up and the first timed tokens)")
+        out["configs[4]"] = d
     return out
 
 
@@ -1103,8 +1126,13 @@ def main():
                     help="prefill and q30 workloads: the expert-parallel path even on one rank "
                          "(a one-rank NCCL group); under torchrun with N > 1 it is always used")
     ap.add_argument("--no-sub", dest="sub", action="store_false",
-                    help="decode workload: skip the configs[2] and configs[3] sub-runs whose "
-                         "results the line carries under 'workloads'")
+                    help="decode workload: skip the configs[2], configs[3] (and configs[4]) sub-runs "
+                         "whose results the line carries under 'workloads'")
+    ap.add_argument("--no-stream-sub", dest="stream_sub", action="store_false",
+                    help="decode workload on one GPU: skip the configs[4] streaming sub-run")
+    ap.add_argument("--stream-late", dest="stream_early", action="store_false",
+                    help="configs[4]: queue each layer's expert kernels only after its picks "
+                         "are resident (default: early, OSM_CACHED_EARLY)")
     ap.add_argument("--stream-layers", type=int, default=48,
                     help="with --workload stream: layers in the stack")
     args = ap.parse_args()

@@ -57,6 +57,10 @@ extern "C" {
                                      with a stream synchronisation that reads its status; when a
                                      value left the fp16 range it runs again on the fp32 path
                                      (status bit 6 then reports it) */
+#define OSM_CACHED_EARLY 0x80u    /* osm_moe_forward_cached, one or two tokens: queue the expert
+                                     kernels right behind the router, before the host has the
+                                     picks; when the acquire finds every pick resident their
+                                     output stands, otherwise they run again behind the copies */
 
 typedef struct osm_context osm_context;
 typedef struct osm_layer osm_layer;
@@ -402,7 +406,8 @@ int osm_moe_experts(osm_layer* layer, const float* x_dev, uint32_t tokens,
  * call returns once the picks are known and the copies and kernels are
  * queued; outputs as for osm_moe_forward (ids_dev, weights_dev,
  * shared_gate_dev may be NULL).  Flags: OSM_ROUTE_EXACT, OSM_PREFILL_BF16,
- * OSM_ADD_RESIDUAL. */
+ * OSM_ADD_RESIDUAL, OSM_CACHED_EARLY (the result is the same; the early
+ * run's non-resident picks do not reach osm_context_status). */
 int osm_moe_forward_cached(osm_layer* layer, osm_cache* cache, uint32_t layer_id,
                            const float* x_dev, uint32_t tokens, float* out_dev,
                            uint32_t* ids_dev, float* weights_dev,

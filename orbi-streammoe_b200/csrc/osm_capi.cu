@@ -68,6 +68,7 @@ struct Scratch {
   float2* hq = nullptr;
   uint32_t* status = nullptr;
   uint32_t* range_status = nullptr;  // status of one checked prefill call
+  uint32_t* early_status = nullptr;  // status of a cached call's early expert run
   unsigned long long* exact_count = nullptr;
   const uint8_t** pick_ptr = nullptr;
 };
@@ -110,7 +111,7 @@ struct osm_context {
   const float* cur_x = nullptr;  // activations of the call in flight (expert kernels)
   std::vector<cudaEvent_t> ev_pool;
   std::vector<ProfRec> recs;
-  void* status_blk = nullptr;       // status word + exact-route counter: never moves
+  void* status_blk = nullptr;       // status words + exact-route counter: never moves
   int plans_alive = 0;              // captured graphs hold scratch pointers
   std::vector<void*> retired;       // scratch blocks a live plan may still use
   uint32_t* picks_host = nullptr;   // mapped pinned: the picks a cached call reads back
@@ -691,8 +692,10 @@ int run_dg(osm_layer* L, uint32_t T, float* out, const float* residual, const os
 
 // picks_from_ids: one token whose picks the decode kernels resolve through
 // the slot table themselves (no binding step ran)
+// status: where the decode kernels report (the context's status word when
+// null)
 int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
-                bool picks_from_ids = false) {
+                bool picks_from_ids = false, uint32_t* status = nullptr) {
   osm_context* ctx = L->ctx;
   Scratch& s = ctx->sc;
   const osm_expert_layout& R = L->slab->layout;
@@ -713,7 +716,7 @@ int run_experts(osm_layer* L, uint32_t T, float* out, const float* residual,
     g.pick_ptr = picks_from_ids ? nullptr : s.pick_ptr;
     g.mass = s.mass;
     g.slot_of = L->slot_of;
-    g.status = s.status;
+    g.status = status ? status : s.status;
     g.h = s.partial;
     g.weights = s.weights;
     g.sgate = s.sgate;
@@ -971,7 +974,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
     return OSM_ECUDA;
   }
   ctx->stream = ctx->own_stream;
-  if (cudaMalloc(&ctx->status_blk, 16) != cudaSuccess || cudaMemset(ctx->status_blk, 0, 16) != cudaSuccess) {
+  if (cudaMalloc(&ctx->status_blk, 32) != cudaSuccess || cudaMemset(ctx->status_blk, 0, 32) != cudaSuccess) {
     if (ctx->status_blk) cudaFree(ctx->status_blk);
     cudaStreamDestroy(ctx->own_stream);
     delete ctx;
@@ -980,6 +983,7 @@ int osm_context_create(int device, uint32_t max_tokens, osm_context** out) {
   ctx->sc.status = static_cast<uint32_t*>(ctx->status_blk);
   ctx->sc.range_status = static_cast<uint32_t*>(ctx->status_blk) + 1;
   ctx->sc.exact_count = reinterpret_cast<unsigned long long*>(static_cast<char*>(ctx->status_blk) + 8);
+  ctx->sc.early_status = static_cast<uint32_t*>(ctx->status_blk) + 4;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0) {
     ctx->grid_cap = sms * 4;
@@ -1927,15 +1931,31 @@ int osm_moe_forward_cached(osm_layer* L, osm_cache* cache, uint32_t layer_id, co
   if (rc) return rc;
   OSM_CUDA(ctx, cudaEventRecord(ctx->picks_ev, ctx->stream));
   if (ids) OSM_CUDA(ctx, cudaMemcpyAsync(ids, s.ids, nk * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
+  // 1b. early experts (one or two tokens): queued before the host has the
+  //     picks, resolving them through the slot table as it stands, so the
+  //     device runs them right behind the router while the host waits and
+  //     acquires.  Their non-resident picks go to a side status word.
+  const bool early = !prefill && dec && (flags & OSM_CACHED_EARLY);
+  if (early) {
+    OSM_CUDA(ctx, cudaMemsetAsync(s.early_status, 0, 4, ctx->stream));
+    rc = run_experts(L, T, out, res, true, s.early_status);
+    if (rc) return rc;
+  }
   // 2. the host needs the picks to make them resident
   OSM_CUDA(ctx, cudaEventSynchronize(ctx->picks_ev));
   // 3. one acquire over the picks in token-major pick order (the order of
   //    the reference's expert_cache.get calls, routed_moe.cpp:319-327)
+  const uint64_t misses0 = cache->misses;
   rc = osm_cache_acquire(cache, layer_id, ctx->picks_host, (uint32_t)nk);
   if (rc) return fail(ctx, rc, std::string("cached forward: ") + cache->err);
+  // every pick was resident before the acquire: the early run used the
+  // right slots and its output stands
+  if (early && cache->misses == misses0) return OSM_OK;
   // 4. bind the picks to their slots and group them, then the experts; one
-  //    token on the decode kernels needs neither (they read the slot table)
-  const float* res = (flags & OSM_ADD_RESIDUAL) ? residual : nullptr;
+  //    token on the decode kernels needs neither (they read the slot table).
+  //    After an early run with a miss this runs the experts again, behind
+  //    the acquire's copies and slot-table writes.
   if (!prefill && dec) return run_experts(L, T, out, res, true);
   a.skip_route = 1;
   a.ids_out = nullptr;

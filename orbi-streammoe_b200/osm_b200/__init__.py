@@ -12,7 +12,7 @@ from __future__ import annotations
 import ctypes as C
 
 from . import _lib
-from ._lib import (OSM_ADD_RESIDUAL, OSM_INPUT_F16, OSM_OUTPUT_F16, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT,  # noqa: F401
+from ._lib import (OSM_ADD_RESIDUAL, OSM_CACHED_EARLY, OSM_INPUT_F16, OSM_OUTPUT_F16, OSM_PREFILL_BF16, OSM_RMSNORM_EXACT,  # noqa: F401
                    OSM_ROUTE_EXACT, ExpertLayout, LayerDesc)
 
 
@@ -302,12 +302,14 @@ class Layer:
 
     def run_cached(self, cache: "ExpertCache", layer_id: int, x, tokens, out, ids=None,
                    weights=None, shared_gate=None, residual=None, exact_route=False,
-                   prefill=False):
+                   prefill=False, early=False):
         """run_qwen_sparse_moe_vulkan_accum with its expert cache: route, make
         the picks resident through ``cache`` (this layer bound as
-        ``layer_id``), run the experts."""
+        ``layer_id``), run the experts.  early: one or two tokens, the
+        experts are queued behind the router before the picks reach the host
+        (OSM_CACHED_EARLY; same result)."""
         flags = ((OSM_ROUTE_EXACT if exact_route else 0) | (OSM_ADD_RESIDUAL if residual is not None else 0)
-                 | (OSM_PREFILL_BF16 if prefill else 0))
+                 | (OSM_PREFILL_BF16 if prefill else 0) | (OSM_CACHED_EARLY if early else 0))
         rc = lib().osm_moe_forward_cached(self.h, cache.h, layer_id, _ptr(x), tokens, _ptr(out),
                                           _ptr(ids), _ptr(weights), _ptr(shared_gate),
                                           _ptr(residual), flags)

@@ -25,6 +25,7 @@ OSM_PREFILL_BF16 = 0x8
 OSM_INPUT_F16 = 0x10
 OSM_OUTPUT_F16 = 0x20
 OSM_PREFILL_NO_CHECK = 0x40
+OSM_CACHED_EARLY = 0x80
 OSM_PLAN_SUBLAYER = 0x100
 OSM_PLAN_PROFILE = 0x200
 

@@ -112,6 +112,66 @@ def test_cached_forward_matches_oracle_and_policy(torch, E, SLOTS, B):
     cache.close()
 
 
+@pytest.mark.parametrize("B", [1, 2])
+def test_cached_forward_early_experts_match_the_ordinary_call(torch, B):
+    """OSM_CACHED_EARLY: the one/two-token expert kernels are queued behind the
+    router before the host has the picks and resolve them through the slot
+    table as it stands; a call whose picks were all resident keeps that
+    output, a call with a miss runs them again behind the copies.  Over a
+    stream with hits, misses and evictions (two layers through a small slab),
+    every output is bit-identical to the ordinary cached call's, the cache
+    counts equal the policy model's, and the context status stays clean (the
+    early run's non-resident picks go to a side word)."""
+    import osm_b200 as osm
+
+    H, I, K, E, SLOTS = 512, 256, 4, 20, 8
+    fx = [MoeFixture(torch, H, E, I, K, seed=210 + l, max_tokens=B) for l in range(2)]
+    lay = osm.expert_layout(H, I)
+    runs = []
+    for early in (False, True):
+        ctx = osm.Context(0, max_tokens=B)
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        slab = osm.Slab(ctx, lay, SLOTS)
+        pinned = [torch.from_numpy(np.ascontiguousarray(f.slots).reshape(-1)).pin_memory()
+                  for f in fx]
+        layers = []
+        for f in fx:
+            L = osm.Layer(ctx, f.W, K, True, shared_slot=f.shared_slot, shared_layout=lay,
+                          shared_gate=f.sg)
+            L.bind_slab(slab, np.full(E, -1, np.int32))
+            layers.append(L)
+        cache = osm.ExpertCache(slab, SLOTS * lay.stride,
+                                source=lambda l, e, p=pinned: p[l].data_ptr() + e * lay.stride)
+        for l, L in enumerate(layers):
+            cache.bind_layer(l, L)
+        model = Model(SLOTS * lay.stride, lay.stride)
+        outs = []
+        for step in range(12):
+            for l, (f, L) in enumerate(zip(fx, layers)):
+                x = f.port.gen_normal(220 + l, step, 1.0, B * H).reshape(B, H)
+                xd = torch.from_numpy(x).cuda()
+                ids = torch.empty(B, K, dtype=torch.int32, device="cuda")
+                out = torch.empty(B, H, device="cuda")
+                L.run_cached(cache, l, xd, B, out, ids=ids, early=early)
+                torch.cuda.synchronize()
+                got_ids = ids.cpu().numpy().astype(np.uint32)
+                model.acquire(l, [int(e) for e in got_ids.reshape(-1)])
+                outs.append(out.cpu().numpy())
+                if step % 4 == 0:
+                    for t in range(B):
+                        ref, rids, _, _, _ = f.oracle_token(x[t])
+                        assert np.array_equal(got_ids[t], rids)
+                        assert normwise_rel(outs[-1][t], ref) <= 1e-4
+        s = cache.stats()
+        assert s == model.stats()
+        assert s["evictions"] > 0 and s["hits"] > 0
+        assert ctx.status()[0] == 0
+        cache.close()
+        runs.append(outs)
+    for a, b in zip(*runs):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 def test_cached_forward_rejects_an_unbound_layer(torch):
     import osm_b200 as osm
 
