@@ -42,6 +42,10 @@ namespace {
 #ifdef OSM_PHASE_TIMING
 __device__ unsigned long long g_tl[OSM_TL_SLOTS];
 __device__ long long g_rcyc[16];
+__device__ long long g_gts[12];
+#define GRP_STAMP(i) do { if (threadIdx.x == 0) g_gts[(i)] = clock64(); } while (0)
+#else
+#define GRP_STAMP(i) do { } while (0)
 #endif
 
 constexpr float kU = 5.9604644775390625e-8f;  // 2^-24
@@ -634,20 +638,32 @@ __device__ int block_exclusive_scan(int* v, int n, int* red) {
   return total;
 }
 
-// Exclusive scan of n ints in smem; one warp when n <= 32.  Returns the total.
+// Exclusive scan of n ints in smem by warp 0 (each lane a run of ceil(n/32)
+// consecutive values, one shuffle scan over the lanes' sums); a block-wide
+// scan beyond 1024 values.  The caller has synchronised after writing v.
+// Returns the total.
 __device__ int small_or_block_scan(int* v, int n, int* red) {
-  if (n > 32) return block_exclusive_scan(v, n, red);
+  if (n > 1024) return block_exclusive_scan(v, n, red);
   __shared__ int s_tot;
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
-    const int x = lane < n ? v[lane] : 0;
-    int incl = x;
+    const int per = (n + 31) >> 5;
+    const int i0 = lane * per;
+    const int i1 = min(n, i0 + per);
+    int sum = 0;
+    for (int i = i0; i < i1; ++i) sum += v[i];
+    int incl = sum;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int y = __shfl_up_sync(0xFFFFFFFFu, incl, o);
       if (lane >= o) incl += y;
     }
-    if (lane < n) v[lane] = incl - x;
+    int run = incl - sum;
+    for (int i = i0; i < i1; ++i) {
+      const int x = v[i];
+      v[i] = run;
+      run += x;
+    }
     if (lane == 31) s_tot = incl;
   }
   __syncthreads();
@@ -668,6 +684,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
   int* expert_of = sm + 3 * NE;
   int* off = sm + 4 * NE;
   __shared__ int s_nact;
+  GRP_STAMP(0);
   for (int i = threadIdx.x; i < NE; i += blockDim.x) {
     cnt[i] = 0;
     cur[i] = 0;
@@ -699,6 +716,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     }
   }
   __syncthreads();
+  GRP_STAMP(1);
   const int n_active = s_nact;
   for (int e = threadIdx.x; e < NE; e += blockDim.x)
     if (actidx[e] >= 0) expert_of[actidx[e]] = e;
@@ -711,6 +729,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     cur[j] = (cnt[expert_of[j]] + kTokGroup - 1) / kTokGroup;
   __syncthreads();
   const int n_tg = small_or_block_scan(cur, n_active, red);
+  GRP_STAMP(2);
   for (int j = threadIdx.x; j < n_active; j += blockDim.x) {
     const int e = expert_of[j];
     ActEntry en;
@@ -739,6 +758,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     }
   }
   __syncthreads();
+  GRP_STAMP(3);
   if (a.chunks) {
     // chunks of chunk_pairs pairs of each active entry, in entry order
     const int cp = a.chunk_pairs > 0 ? a.chunk_pairs : 8;
@@ -753,6 +773,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
     if (threadIdx.x == 0) *a.n_ch = n_ch;
     __syncthreads();
   }
+  GRP_STAMP(4);
   if (a.defer_scatter) {
     // many pairs: each expert's first position and a zero cursor for
     // scatter_pairs_kernel, which places the pairs across the whole GPU
@@ -789,6 +810,7 @@ __device__ void group_pairs(const RouterArgs& a, int* sm, int* red) {
         if (a.tp_pos) a.tp_pos[t * (k + 1) + k] = off[0] + t;
       }
   }
+  GRP_STAMP(5);
   if (threadIdx.x == 0) {
     *a.n_active = n_active;
     *a.n_tg = n_tg;
@@ -1329,6 +1351,8 @@ __global__ void __launch_bounds__(TPB, 1024 / TPB) router_select_kernel(RouterAr
   if (tid == 0) {
     printf("select tok %d:", tok);
     for (int i = 1; i < 14; ++i) printf(" %d:%lld", i, ts_[i] - ts_[0]);
+    printf(" | group:");
+    for (int i = 1; i < 6; ++i) printf(" %d:%lld", i, g_gts[i] - g_gts[0]);
     printf("\n");
   }
 #endif
