@@ -292,7 +292,10 @@ def run_ours(args, rank, world, local_rank):
     evs2 = timed_pass(args.steps, True)
     torch.cuda.synchronize()
     barrier()
-    total_ms_e2e = sum(a.elapsed_time(b) for _, a, b in evs2)
+    e2e_b = {B: 0.0 for B in SWEEP}
+    for B, a, b in evs2:
+        e2e_b[B] += a.elapsed_time(b)
+    total_ms_e2e = sum(e2e_b.values())
     # ---- the same calls launched one by one (no graph), for comparison ----
     eager_b = {B: 0.0 for B in SWEEP}
     if args.graphs:
@@ -340,7 +343,8 @@ def run_ours(args, rank, world, local_rank):
         byt = sublayer_bytes(B, uniq[B])
         sweep[str(B)] = {"us_per_call": round(us, 2), "distinct_experts": uniq[B],
                          "alg_bytes": byt, "gbs": round(byt / us / 1e3, 1),
-                         "frac_hbm": round(byt / us / 1e3 / peaks["hbm_gbs"], 3)}
+                         "frac_hbm": round(byt / us / 1e3 / peaks["hbm_gbs"], 3),
+                         "e2e_us_per_call": round(e2e_b[B] / args.steps * 1e3, 2)}
         if args.graphs:
             sweep[str(B)]["eager_us_per_call"] = round(eager_b[B] / args.steps * 1e3, 2)
     kernels = {k: {"ms": round(v[0], 3), "launches": int(v[1]),
@@ -370,7 +374,8 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "flushed before every call (256 MiB write, outside the timed intervals)",
                    "timing": "sum of per-call CUDA-event intervals on the launching stream",
                    "calls": ("one CUDA-graph plan launch per call (osm_plan_launch; e2e plans hold "
-                             "the pinned-host copies); eager_us_per_call: the same call through "
+                             "the pinned-host copies, made by the SMs through the GPU's mapping of "
+                             "the pinned buffers); eager_us_per_call: the same call through "
                              "osm_moe_forward, kernels launched one by one") if args.graphs
                             else "osm_moe_forward, kernels launched one by one",
                    "bracket_wall_s": round(bracket_s, 3),

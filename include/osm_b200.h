@@ -439,8 +439,10 @@ int osm_moe_sublayer_forward(osm_layer* layer, const float* residual_dev,
  *      osm_moe_forward (or, with OSM_PLAN_SUBLAYER, osm_moe_sublayer_forward)
  *      on fixed device buffers with one graph launch.  When x_host / out_host
  *      (pinned) are given, the H2D copy of x and the D2H copy of out are part
- *      of the plan.  With OSM_PLAN_PROFILE each kernel is bracketed by event
- *      nodes, read by osm_plan_profile_read. ---- */
+ *      of the plan: copied by the SMs through the GPU's mapping of the pinned
+ *      buffer when it is mapped, 16-byte aligned and at most 2 MiB, by
+ *      copy-engine nodes otherwise.  With OSM_PLAN_PROFILE each kernel is
+ *      bracketed by event nodes, read by osm_plan_profile_read. ---- */
 #define OSM_PLAN_SUBLAYER 0x100u
 #define OSM_PLAN_PROFILE 0x200u
 typedef struct osm_plan osm_plan;

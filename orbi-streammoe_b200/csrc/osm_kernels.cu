@@ -10,6 +10,8 @@
 //   gen_*            seeded synthetic weights, quantised like
 //                    src/conversion/single_expert_pilot.cpp:276-346
 //   router_pack      the router weight layout of osm_kernels.cuh
+//   host_copy        a plan's input / output copy through pinned host memory
+//                    mapped into the GPU (loads and stores by the SMs)
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -276,6 +278,42 @@ __global__ void slot_updates_kernel(const SlotUpdates u) {
   // in order: a later write to the same entry wins
   if (threadIdx.x == 0)
     for (int i = 0; i < u.n; ++i) *u.ptr[i] = u.val[i];
+}
+
+// Copies n16 16-byte words between this GPU's memory and pinned host memory
+// that the GPU maps (unified addressing: the host pointer is the device
+// pointer).  One word per thread per pass; each warp's 512 bytes go over PCIe
+// as full-line reads or posted writes.  after_pdl: the kernel was launched as
+// a programmatic dependent and waits for its predecessor before it reads.
+__global__ void __launch_bounds__(256) host_copy_kernel(const uint4* __restrict__ src,
+                                                        uint4* __restrict__ dst, size_t n16,
+                                                        int after_pdl) {
+  if (after_pdl) pdl_wait();
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += stride)
+    dst[i] = src[i];
+}
+
+cudaError_t launch_host_copy(void* dst, const void* src, size_t bytes, bool after_pdl, int num_sms,
+                             cudaStream_t s, uint64_t* launches) {
+  const size_t n16 = bytes / 16;
+  if (n16 == 0) return cudaSuccess;
+  size_t blocks = (n16 + 255) / 256;
+  const size_t cap = (size_t)2 * (num_sms > 0 ? num_sms : 148);
+  if (blocks > cap) blocks = cap;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = after_pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, host_copy_kernel, static_cast<const uint4*>(src),
+                                           static_cast<uint4*>(dst), n16, after_pdl ? 1 : 0);
+  if (e == cudaSuccess && launches) *launches += 1;
+  return e;
 }
 
 void launch_slot_updates(const SlotUpdates& u, cudaStream_t s, uint64_t* launches) {

@@ -422,6 +422,10 @@ struct SlotUpdates {
   int32_t* ptr[kMax];
 };
 void launch_slot_updates(const SlotUpdates& u, cudaStream_t s, uint64_t* launches);
+// bytes (a multiple of 16, both pointers 16-byte aligned) between device
+// memory and mapped pinned host memory, copied by the SMs.
+cudaError_t launch_host_copy(void* dst, const void* src, size_t bytes, bool after_pdl, int num_sms,
+                             cudaStream_t s, uint64_t* launches);
 cudaError_t launch_setup_single(int T, const uint8_t* ptr, int* n_active, ActEntry* act, int* n_tg,
                          int* tg_expert, int* tg_begin, int* pair_tok, int* pair_pick,
                          int* out_row, cudaStream_t s, uint64_t* launches);

@@ -355,7 +355,10 @@ def test_sublayer_rmsnorm_residual(torch, port):
 
 def test_plan_replay_matches_direct_call(torch):
     """A captured plan (CUDA graph) gives bit-identical results to the direct
-    call, with and without host buffers inside the plan."""
+    call, with and without host buffers inside the plan.  With host buffers the
+    plan itself must bring x in (the device input is cleared first) and out
+    back, both for aligned pinned buffers (copied by the SMs through the
+    mapping) and for buffers 4 bytes off alignment (copy-engine nodes)."""
     import osm_b200 as osm
 
     fx = _q3n_fixture(torch)
@@ -375,14 +378,27 @@ def test_plan_replay_matches_direct_call(torch):
                 torch.cuda.synchronize()
                 assert np.array_equal(out.cpu().numpy().view(np.uint32), out_ref.view(np.uint32))
                 assert np.array_equal(ids.cpu().numpy().astype(np.uint32), ids_ref)
-                xh = torch.from_numpy(x).pin_memory()
-                oh = torch.empty(B, fx.H).pin_memory()
-                plan2 = osm.Plan(fx.layer, B, xd, out, x_host=xh, out_host=oh)
-                plan2.launch()
-                torch.cuda.synchronize()
-                assert np.array_equal(oh.numpy().view(np.uint32), out_ref.view(np.uint32))
                 plan.close()
-                plan2.close()
+                n = B * fx.H
+                for off in (0, 1):  # element offset into the pinned buffers
+                    xbuf = torch.zeros(n + 4).pin_memory()
+                    obuf = torch.zeros(n + 4).pin_memory()
+                    xh = xbuf[off:off + n].view(B, fx.H)
+                    oh = obuf[off:off + n].view(B, fx.H)
+                    xh.copy_(torch.from_numpy(x))
+                    xd.zero_()
+                    out.zero_()
+                    torch.cuda.synchronize()
+                    plan2 = osm.Plan(fx.layer, B, xd, out, x_host=xh, out_host=oh)
+                    for _ in range(2):
+                        plan2.launch()
+                    torch.cuda.synchronize()
+                    assert np.array_equal(xd.cpu().numpy(), x)
+                    assert np.array_equal(out.cpu().numpy().view(np.uint32), out_ref.view(np.uint32))
+                    assert np.array_equal(oh.numpy().view(np.uint32), out_ref.view(np.uint32))
+                    assert float(obuf[:off].abs().sum()) == 0.0
+                    assert float(obuf[off + n:].abs().sum()) == 0.0
+                    plan2.close()
         finally:
             fx.ctx.set_stream(torch.cuda.current_stream().cuda_stream)
 
